@@ -1,0 +1,93 @@
+"""Build libcusr_b200.so (sm_100a) in-tree.
+
+    python -m cusr_b200.build            # incremental
+    python -m cusr_b200.build --force    # rebuild everything
+
+The library is also exposed under the file names the CuSR ctypes loader looks for
+(libcusr_co_ad.so, libcusr_co_fd.so), so the reference's `co_inproc.InProcessCO` can bind it
+unchanged.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+INCLUDE = HERE.parent / "include"
+OBJ = HERE / "_build"
+LIB = HERE / "libcusr_b200.so"
+ALIASES = ("libcusr_co_ad.so", "libcusr_co_fd.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
+                     "-Xcompiler", "-O3", f"-I{INCLUDE}"]
+SOURCES = ["eval_f32.cu", "eval_f64.cu", "engine.cu", "pack.cpp", "debug_api.cpp"]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _headers() -> list[Path]:
+    return sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    nvcc = _nvcc()
+    OBJ.mkdir(exist_ok=True)
+    hdrs = _headers()
+    jobs = []
+    for src in SOURCES:
+        s = CSRC / src
+        o = OBJ / (s.stem + ".o")
+        if force or _stale(o, [s, *hdrs, Path(__file__)]):
+            jobs.append([nvcc, *NVCC_FLAGS, "-c", str(s), "-o", str(o)])
+
+    def run(cmd):
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"compile failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+        if verbose and (r.stdout or r.stderr):
+            print(r.stdout, r.stderr, file=sys.stderr)
+
+    with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
+        list(ex.map(run, jobs))
+    objs = [OBJ / (Path(s).stem + ".o") for s in SOURCES]
+    if force or jobs or _stale(LIB, objs):
+        run([nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"])
+    for alias in ALIASES:
+        a = HERE / alias
+        if a.is_symlink() or a.exists():
+            if a.is_symlink() and os.readlink(a) == LIB.name:
+                continue
+            a.unlink()
+        a.symlink_to(LIB.name)
+    return LIB
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.verbose))
+
+
+if __name__ == "__main__":
+    main()

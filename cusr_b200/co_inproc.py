@@ -1,0 +1,386 @@
+"""In-process ctypes binding of libcusr_b200.so — the drop-in for CuSR's co_inproc module.
+
+Same surface as the reference (cusr/kernel/co_inproc.py:29-295): `InProcessCO(device_id,
+lib_path, variant).optimize(pop, max_iter)` returning {'c_final', 'status', 'loss_init',
+'loss_final'}, the process-wide `get_inproc_co(device_id, variant)` singleton, `COError`
+with the same return-code messages, and the `PopHeader` / `TreeMeta` ctypes mirrors.
+
+Additions: `optimize_ex` (fp64 arithmetic, shared targets, lambda0 / xtol knobs, fp64
+outputs, per-tree iteration counts) and `stats()` (phase timings and work counters of the
+last call). There is no fallback path: if the shared library is missing the constructor
+raises, and every fit runs on the GPU.
+"""
+from __future__ import annotations
+
+import atexit
+import ctypes
+import threading
+from pathlib import Path
+
+import numpy as np
+
+POP_MAGIC = 0x4D4C344D
+POP_VERSION = 1
+
+CO_OK = 0
+CO_ERR_BOUNDS = 2
+CO_ERR_CUDA = -1
+CO_ERR_SUM_C = -2
+CO_ERR_SUM_NODES = -3
+CO_ERR_NULLARG = -4
+CO_ERR_OOM = -5
+CO_ERR_BADTREE = -6
+
+CO_PREC_FP32 = 0
+CO_PREC_FP64 = 1
+
+STATUS_CONVERGED, STATUS_MAXITER, STATUS_FAIL_NAN, STATUS_K0_SKIP, STATUS_FAIL_CHOLESKY = range(5)
+
+_ERR_MSG = {
+    CO_ERR_BOUNDS: "K_max > MAX_K(32) or max_stack > MAX_STACK(64) (caller must pre-filter)",
+    CO_ERR_CUDA: "CUDA error inside co_optimize",
+    CO_ERR_SUM_C: "sum(metas.K) != header.total_c (pop inconsistent)",
+    CO_ERR_SUM_NODES: "sum(metas.n_nodes) != header.total_nodes (pop inconsistent)",
+    CO_ERR_NULLARG: "null pointer / bad argument",
+    CO_ERR_OOM: "out of memory growing a device buffer",
+    CO_ERR_BADTREE: "malformed tree bytecode (node type, stack, var index or const rank)",
+}
+
+
+class COError(RuntimeError):
+    """Raised when co_init / co_optimize returns a non-OK code."""
+
+    def __init__(self, code: int, where: str):
+        self.code = code
+        msg = _ERR_MSG.get(code, f"unknown code {code}")
+        super().__init__(f"{where}: {msg} (code={code})")
+
+
+class PopHeader(ctypes.Structure):
+    _fields_ = [
+        ("magic", ctypes.c_int32), ("version", ctypes.c_int32), ("M_prob", ctypes.c_int32),
+        ("total_nodes", ctypes.c_int32), ("total_c", ctypes.c_int32), ("N", ctypes.c_int32),
+        ("n_vars", ctypes.c_int32), ("K_max", ctypes.c_int32), ("max_stack", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 7),
+    ]
+
+
+class TreeMeta(ctypes.Structure):
+    _fields_ = [("node_offset", ctypes.c_int32), ("n_nodes", ctypes.c_int32),
+                ("c_offset", ctypes.c_int32), ("K", ctypes.c_int32)]
+
+
+class CoOptions(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", ctypes.c_int32), ("precision", ctypes.c_int32),
+        ("max_iter", ctypes.c_int32), ("y_shared", ctypes.c_int32),
+        ("lambda0", ctypes.c_double), ("xtol", ctypes.c_double),
+        ("fp64_audit", ctypes.c_int32), ("early_exit", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 8),
+    ]
+
+
+class CoStats(ctypes.Structure):
+    _fields_ = [
+        ("setup_ms", ctypes.c_double), ("loop_ms", ctypes.c_double),
+        ("finish_ms", ctypes.c_double), ("eval_ms", ctypes.c_double),
+        ("step_ms", ctypes.c_double),
+        ("node_evals", ctypes.c_int64), ("sample_evals", ctypes.c_int64),
+        ("eval_launches", ctypes.c_int64), ("kernel_launches", ctypes.c_int64),
+        ("iters_run", ctypes.c_int32), ("n_bins", ctypes.c_int32),
+        ("y_shared", ctypes.c_int32), ("precision", ctypes.c_int32),
+        ("n_reverted", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7),
+    ]
+
+
+assert ctypes.sizeof(PopHeader) == 64
+assert ctypes.sizeof(TreeMeta) == 16
+
+_F32 = ctypes.POINTER(ctypes.c_float)
+_F64 = ctypes.POINTER(ctypes.c_double)
+_I32 = ctypes.POINTER(ctypes.c_int32)
+
+_HERE = Path(__file__).resolve().parent
+LIB_NAME = "libcusr_b200.so"
+
+# Every symbol include/cusr_co.h declares, with its ctypes signature.
+SIGNATURES = {
+    "co_init": ([ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "co_optimize": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
+                     ctypes.POINTER(TreeMeta), _F32, _F32, _F32, ctypes.c_int,
+                     _F32, _I32, _F32, _F32], ctypes.c_int),
+    "co_last_split": ([ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)],
+                      ctypes.c_int),
+    "co_teardown": ([ctypes.c_void_p], None),
+    "co_default_options": ([ctypes.POINTER(CoOptions)], None),
+    "co_optimize_ex": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
+                        ctypes.POINTER(TreeMeta), _F32, _F32, _F32,
+                        ctypes.POINTER(CoOptions), _F64, _I32, _F64, _F64, _I32], ctypes.c_int),
+    "co_get_stats": ([ctypes.c_void_p, ctypes.POINTER(CoStats)], ctypes.c_int),
+    "co_strerror": ([ctypes.c_int], ctypes.c_char_p),
+    "co_evaluate": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
+                     ctypes.POINTER(TreeMeta), _F64, _F32, _F32, ctypes.c_int, ctypes.c_int,
+                     _F64, _F64, _F64], ctypes.c_int),
+}
+
+
+def default_lib_path() -> Path:
+    return _HERE / LIB_NAME
+
+
+def load_library(lib_path: str | Path | None = None) -> ctypes.CDLL:
+    """Load the engine library and bind every exported C-ABI symbol."""
+    path = Path(lib_path) if lib_path else default_lib_path()
+    if not path.exists():
+        raise FileNotFoundError(
+            f"{path} is not built; run `python -m cusr_b200.build` (needs nvcc)")
+    lib = ctypes.CDLL(str(path.resolve()))
+    for name, (argtypes, restype) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    return lib
+
+
+def _c_ptr(arr, dtype):
+    a = np.ascontiguousarray(arr, dtype=dtype)
+    return a.ctypes.data_as(ctypes.POINTER(np.ctypeslib.as_ctypes_type(dtype))), a
+
+
+def build_header(pop: dict) -> PopHeader:
+    """Full 64-byte header from a pop dict (key 'M', no magic/version)."""
+    h = PopHeader()
+    h.magic = POP_MAGIC
+    h.version = POP_VERSION
+    h.M_prob = int(pop["M"])
+    h.total_nodes = int(pop["total_nodes"])
+    h.total_c = int(pop["total_c"])
+    h.N = int(pop["N"])
+    h.n_vars = int(pop["n_vars"])
+    h.K_max = int(pop["K_max"])
+    h.max_stack = int(pop["max_stack"])
+    for i in range(7):
+        h.reserved[i] = 0
+    return h
+
+
+class InProcessCO:
+    """One persistent engine context on one device. CUDA context creation is paid once in
+    __init__; every optimize() starts from the pop's c_init."""
+
+    def __init__(self, device_id: int = 0, lib_path: str | None = None, variant: str = "ad"):
+        self.variant = variant
+        self.device_id = int(device_id)
+        self._lib = load_library(lib_path)
+        self._handle = ctypes.c_void_p()
+        self._torn = False
+        rc = self._lib.co_init(self.device_id, ctypes.byref(self._handle))
+        if rc != CO_OK:
+            raise COError(rc, "co_init")
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.teardown()
+        return False
+
+    _build_header = staticmethod(build_header)
+
+    def _inputs(self, pop: dict, y_shared: bool = False):
+        M = int(pop["M"])
+        keep = []
+
+        def ptr(key, dtype):
+            p, a = _c_ptr(pop[key], dtype)
+            keep.append(a)
+            return p
+
+        ym = np.asarray(pop["ym"], np.float32)
+        if y_shared:
+            ym = ym.reshape(-1)[: int(pop["N"])]
+        elif ym.ndim == 1:
+            # the reference ABI takes [M][N] targets: replicate a shared row
+            ym = np.broadcast_to(ym, (M, int(pop["N"])))
+        ym_p, ym_a = _c_ptr(ym, np.float32)
+        keep.append(ym_a)
+        metas_np = np.ascontiguousarray(pop["metas"], dtype=np.int32).reshape(M, 4)
+        metas_buf = (TreeMeta * max(M, 1))()
+        if M:
+            ctypes.memmove(metas_buf, metas_np.ctypes.data, M * 16)
+        keep.append(metas_buf)
+        return (ptr("nt", np.int32), ptr("nv", np.float32), ptr("ci", np.int32), metas_buf,
+                ptr("c_init", np.float32), ptr("xs", np.float32), ym_p), keep
+
+    def optimize(self, pop: dict, max_iter: int = 50):
+        """Reference-compatible fit (fp32). Returns {'c_final','status','loss_init',
+        'loss_final'} sliced to this pop's sizes; raises COError on a non-OK code."""
+        if self._torn:
+            raise RuntimeError("InProcessCO used after teardown()")
+        M, total_c = int(pop["M"]), int(pop["total_c"])
+        hdr = build_header(pop)
+        args, keep = self._inputs(pop)
+        c_final = np.zeros(total_c, np.float32)
+        status = np.zeros(M, np.int32)
+        loss_init = np.zeros(M, np.float32)
+        loss_final = np.zeros(M, np.float32)
+        rc = self._lib.co_optimize(
+            self._handle, ctypes.byref(hdr), *args, int(max_iter),
+            c_final.ctypes.data_as(_F32), status.ctypes.data_as(_I32),
+            loss_init.ctypes.data_as(_F32), loss_final.ctypes.data_as(_F32))
+        del keep
+        if rc != CO_OK:
+            raise COError(rc, "co_optimize")
+        out = {"c_final": c_final, "status": status}
+        if self.variant == "ad":
+            out["loss_init"] = loss_init
+            out["loss_final"] = loss_final
+        return out
+
+    def optimize_ex(self, pop: dict, max_iter: int = 50, precision: str = "fp32",
+                    y_shared: bool | None = None, lambda0: float = 1e-3, xtol: float = 1e-6,
+                    fp64_audit: int = -1, early_exit: bool = True):
+        """Extended fit: precision 'fp32' | 'fp64'; y_shared=True passes one target row
+        (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a 1-D ym).
+        Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters."""
+        if self._torn:
+            raise RuntimeError("InProcessCO used after teardown()")
+        M, total_c = int(pop["M"]), int(pop["total_c"])
+        if y_shared is None:
+            y_shared = np.asarray(pop["ym"]).ndim == 1
+        hdr = build_header(pop)
+        args, keep = self._inputs(pop, y_shared=bool(y_shared))
+        opt = CoOptions()
+        self._lib.co_default_options(ctypes.byref(opt))
+        opt.precision = CO_PREC_FP64 if precision == "fp64" else CO_PREC_FP32
+        opt.max_iter = int(max_iter)
+        opt.y_shared = 1 if y_shared else 0
+        opt.lambda0 = float(lambda0)
+        opt.xtol = float(xtol)
+        opt.fp64_audit = int(fp64_audit)
+        opt.early_exit = 1 if early_exit else 0
+        c_final = np.zeros(total_c, np.float64)
+        status = np.zeros(M, np.int32)
+        loss_init = np.zeros(M, np.float64)
+        loss_final = np.zeros(M, np.float64)
+        iters = np.zeros(M, np.int32)
+        rc = self._lib.co_optimize_ex(
+            self._handle, ctypes.byref(hdr), *args, ctypes.byref(opt),
+            c_final.ctypes.data_as(_F64), status.ctypes.data_as(_I32),
+            loss_init.ctypes.data_as(_F64), loss_final.ctypes.data_as(_F64),
+            iters.ctypes.data_as(_I32))
+        del keep
+        if rc != CO_OK:
+            raise COError(rc, "co_optimize_ex")
+        return {"c_final": c_final, "status": status, "loss_init": loss_init,
+                "loss_final": loss_final, "iters": iters}
+
+    def evaluate(self, pop: dict, c=None, precision: str = "fp32", values: bool = True,
+                 jacobian: bool = False, blocks: bool = False) -> dict:
+        """One fused device pass at constants c (default c_init): per-sample values [M, N],
+        Jacobian [M, K_max, N] (df/dc_k), normal-equation blocks (list of per-tree arrays:
+        JtJ lower triangle packed, Jtr, 0.5*sum r^2)."""
+        if self._torn:
+            raise RuntimeError("InProcessCO used after teardown()")
+        M, N, K_max = int(pop["M"]), int(pop["N"]), int(pop["K_max"])
+        y_shared = np.asarray(pop["ym"]).ndim == 1
+        hdr = build_header(pop)
+        args, keep = self._inputs(pop, y_shared=y_shared)
+        nt_p, nv_p, ci_p, metas_buf, _c0, xs_p, ym_p = args
+        c = np.ascontiguousarray(pop["c_init"] if c is None else c, np.float64)
+        vals = np.zeros((M, N), np.float64) if values else None
+        jac = np.zeros((M, max(K_max, 1), N), np.float64) if jacobian else None
+        Ks = np.asarray(pop["metas"], np.int64).reshape(-1, 4)[:, 3]
+        nblk = int(np.sum((Ks + 1) * (Ks + 2) // 2))
+        blk = np.zeros(max(nblk, 1), np.float64) if blocks else None
+
+        def p64(a):
+            return a.ctypes.data_as(_F64) if a is not None else None
+
+        rc = self._lib.co_evaluate(
+            self._handle, ctypes.byref(hdr), nt_p, nv_p, ci_p, metas_buf, p64(c), xs_p, ym_p,
+            CO_PREC_FP64 if precision == "fp64" else CO_PREC_FP32, 1 if y_shared else 0,
+            p64(vals), p64(jac), p64(blk))
+        del keep
+        if rc != CO_OK:
+            raise COError(rc, "co_evaluate")
+        out: dict = {}
+        if values:
+            out["values"] = vals
+        if jacobian:
+            out["jacobian"] = jac
+        if blocks:
+            parts, o = [], 0
+            for K in Ks:
+                n = int((K + 1) * (K + 2) // 2)
+                parts.append(blk[o:o + n])
+                o += n
+            out["blocks"] = parts
+        return out
+
+    def stats(self) -> dict:
+        st = CoStats()
+        rc = self._lib.co_get_stats(self._handle, ctypes.byref(st))
+        if rc != CO_OK:
+            raise COError(rc, "co_get_stats")
+        return {name: getattr(st, name) for name, _ in CoStats._fields_ if name != "reserved"}
+
+    def last_split(self):
+        s = ctypes.c_double(-1.0)
+        l = ctypes.c_double(-1.0)
+        rc = self._lib.co_last_split(ctypes.byref(s), ctypes.byref(l))
+        if rc != 0:
+            return (None, None)
+        return (s.value, l.value)
+
+    def teardown(self):
+        if self._torn:
+            return
+        if self._handle:
+            self._lib.co_teardown(self._handle)
+            self._handle = ctypes.c_void_p()
+        self._torn = True
+
+    def __del__(self):
+        try:
+            self.teardown()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+_SINGLETONS: dict[tuple[int, str], InProcessCO] = {}
+_SINGLETON_LOCK = threading.Lock()
+_ATEXIT_REGISTERED = False
+
+
+def _so_path(variant: str) -> Path:
+    """libcusr_co_{variant}.so next to this module (aliases of libcusr_b200.so)."""
+    return _HERE / f"libcusr_co_{variant}.so"
+
+
+def _teardown_all() -> None:
+    for co in list(_SINGLETONS.values()):
+        try:
+            co.teardown()
+        except Exception:  # noqa: BLE001
+            pass
+    _SINGLETONS.clear()
+
+
+def get_inproc_co(device_id: int = 0, variant: str = "ad") -> InProcessCO:
+    """Process-wide InProcessCO per (device_id, variant); torn down at exit."""
+    global _ATEXIT_REGISTERED
+    key = (int(device_id), str(variant))
+    with _SINGLETON_LOCK:
+        co = _SINGLETONS.get(key)
+        if co is None or co._torn:
+            so = _so_path(variant)
+            if not so.exists():
+                raise FileNotFoundError(
+                    f"{so.name} not built — run `python -m cusr_b200.build` in {_HERE.parent}")
+            co = InProcessCO(device_id=device_id, lib_path=str(so), variant=variant)
+            _SINGLETONS[key] = co
+            if not _ATEXIT_REGISTERED:
+                atexit.register(_teardown_all)
+                _ATEXIT_REGISTERED = True
+        return co

@@ -1,0 +1,768 @@
+// engine.cu — persistent per-device context, the per-call LM driver, and the C ABI
+// (include/cusr_co.h).
+//
+// Per call (co_optimize / co_optimize_ex):
+//   1. argument, sum and structure checks (before any device work; co_lib.cu:195-220);
+//   2. compile every tree to a register-stack program and build the cost-binned schedule;
+//   3. H2D of programs, inputs (transposed on device to [n_vars][N]) and targets (one row
+//      when every tree shares it);
+//   4. initial fused pass at c_init, then max_iter LM iterations, each
+//        build work items of the pending trees -> one fused evaluation launch per bin
+//        -> one LM-step launch (accept/reject, lambda, Cholesky solve of the next step),
+//      with no host round trip inside the loop (a lagged counter read lets the host stop
+//      launching once every tree has finished);
+//   5. fp64 audit for fp32 fits; D2H of the outputs.
+// Device buffers grow by byte capacity and never shrink (co_lib.cu:129-153); every call
+// re-seeds all per-tree state from c_init (co_lib.cu:284-305).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "../../include/cusr_co.h"
+#include "launch.h"
+#include "lm_kernels.cuh"
+#include "pack.h"
+
+namespace cusr {
+
+namespace {
+
+double g_last_setup_ms = -1.0, g_last_loop_ms = -1.0;
+
+struct DBuf {
+    void *ptr = nullptr;
+    size_t cap = 0;
+};
+
+struct Ctx {
+    int device = -1;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    DBuf code, desc, bin_trees, bin_tree_off, bin_item_off, items, n_items, counter;
+    DBuf xs_raw, xs, ym;
+    DBuf c, ctry, delta, cinit_f, lam, loss, loss_init, status, iters, pending, n_run;
+    DBuf partials, blk;
+    DBuf c64, l64, n_rev;
+    DBuf vals, jac;
+    int *h_nrun = nullptr;                  // pinned, one slot per iteration parity
+    std::vector<cudaEvent_t> events;        // timing events, reused across calls
+    cudaEvent_t ev_nrun[2] = {nullptr, nullptr};
+    bool step_attr_set[2] = {false, false};
+    CoStats stats{};
+};
+
+int grow(DBuf &b, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    if (bytes <= b.cap) return CO_OK;
+    if (b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.cap = 0;
+    cudaError_t e = cudaMalloc(&b.ptr, bytes);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "[cusr_b200] cudaMalloc %zu B failed: %s\n", bytes, cudaGetErrorString(e));
+        cudaGetLastError();
+        return e == cudaErrorMemoryAllocation ? CO_ERR_OOM : CO_ERR_CUDA;
+    }
+    b.cap = bytes;
+    return CO_OK;
+}
+
+void release(DBuf &b) {
+    if (b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.cap = 0;
+}
+
+#define CK(x)                                                                                \
+    do {                                                                                     \
+        cudaError_t _e = (x);                                                                \
+        if (_e != cudaSuccess) {                                                             \
+            fprintf(stderr, "[cusr_b200] CUDA error %s at %s:%d\n", cudaGetErrorString(_e),  \
+                    __FILE__, __LINE__);                                                     \
+            return CO_ERR_CUDA;                                                              \
+        }                                                                                    \
+    } while (0)
+#define GROW(buf, bytes)                    \
+    do {                                            \
+        int _r = grow(buf, (size_t)(bytes));        \
+        if (_r) return _r;                          \
+    } while (0)
+
+template <typename T> T *P(DBuf &b) { return reinterpret_cast<T *>(b.ptr); }
+
+cudaEvent_t event_at(Ctx *ctx, size_t i) {
+    while (ctx->events.size() <= i) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+        ctx->events.push_back(e);
+    }
+    return ctx->events[i];
+}
+
+double ms_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// Output sinks of one call (float for the reference ABI, double for the extended one).
+struct Outputs {
+    float *c_f = nullptr, *li_f = nullptr, *lf_f = nullptr;
+    double *c_d = nullptr, *li_d = nullptr, *lf_d = nullptr;
+    int32_t *status = nullptr, *iters = nullptr;
+};
+
+struct Problem {
+    const PopHeader *h;
+    const int32_t *nt;
+    const float *nv;
+    const int32_t *ci;
+    const TreeMeta *metas;
+    const float *c_init, *xs, *ym;
+};
+
+int check_args(const Problem &pr) {
+    const PopHeader *h = pr.h;
+    if (h->M_prob < 0 || h->N < 0 || h->n_vars < 0 || h->total_c < 0 || h->total_nodes < 0)
+        return CO_ERR_NULLARG;
+    // reference bounds on the header fields (co_lib.cu:211-212)
+    if (h->K_max > CO_MAX_K) return CO_ERR_BOUNDS;
+    if (h->max_stack > CO_MAX_STACK) return CO_ERR_BOUNDS;
+    if (h->n_vars > CO_MAX_VARS) return CO_ERR_BOUNDS;
+    // sum checks before any device work (co_lib.cu:214-220)
+    int64_t ks = 0, ns = 0;
+    for (int m = 0; m < h->M_prob; ++m) {
+        ks += pr.metas[m].K;
+        ns += pr.metas[m].n_nodes;
+    }
+    if (ks != (int64_t)h->total_c) return CO_ERR_SUM_C;
+    if (ns != (int64_t)h->total_nodes) return CO_ERR_SUM_NODES;
+    return CO_OK;
+}
+
+// Evaluate the pending trees of every bin at constants `cdev` (one fused launch per bin).
+template <typename T>
+int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cdev, T *partials,
+                const Problem &pr, int64_t ldx, bool grad, T *vals = nullptr, T *jac = nullptr,
+                int jac_kmax = 0) {
+    const int n_bins = (int)sc.bins.size();
+    {
+        ItemsParams ip;
+        ip.desc = P<TreeDesc>(ctx->desc);
+        ip.bin_trees = P<int32_t>(ctx->bin_trees);
+        ip.bin_tree_off = P<int64_t>(ctx->bin_tree_off);
+        ip.bin_item_off = P<int64_t>(ctx->bin_item_off);
+        ip.pending = P<int32_t>(ctx->pending);
+        ip.items = P<int2>(ctx->items);
+        ip.n_items = P<int>(ctx->n_items);
+        ip.counter = P<int>(ctx->counter);
+        build_items_kernel<<<n_bins, ITEMS_THREADS, 0, ctx->stream>>>(ip);
+        CK(cudaGetLastError());
+        ctx->stats.kernel_launches++;
+    }
+    for (int b = 0; b < n_bins; ++b) {
+        const Bin &bin = sc.bins[(size_t)b];
+        EvalParams<T> p;
+        p.code = P<uint32_t>(ctx->code);
+        p.desc = P<TreeDesc>(ctx->desc);
+        p.items = P<int2>(ctx->items) + bin.item_off;
+        p.n_items = P<int>(ctx->n_items) + b;
+        p.counter = P<int>(ctx->counter) + b;
+        p.c = cdev;
+        p.xs = P<float>(ctx->xs);
+        p.ym = P<float>(ctx->ym);
+        p.partials = partials;
+        p.ldx = ldx;
+        p.N = pr.h->N;
+        p.chunk = sc.chunk;
+        p.n_vars = pr.h->n_vars;
+        p.code_cap = bin.max_instr;
+        p.spill_cap = std::max(bin.max_spill, 1);
+        p.tape_cap = grad ? std::max(bin.max_tape, 1) : 1;
+        p.vals = vals;
+        p.jac = jac;
+        p.jac_kmax = jac_kmax;
+        const int kc = grad ? bin.kc : 4;
+        const size_t smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap);
+        if (smem > 227 * 1024) return CO_ERR_BOUNDS;
+        int occ = Launch<T>::occ(kc, grad, smem);
+        if (occ < 1) occ = 1;
+        int64_t grid = (int64_t)occ * ctx->sm_count;
+        if (grid > bin.max_items) grid = std::max<int64_t>(1, bin.max_items);
+        CK(Launch<T>::eval(kc, grad, p, (int)grid, smem, ctx->stream));
+        ctx->stats.eval_launches++;
+        ctx->stats.kernel_launches++;
+    }
+    (void)pk;
+    return CO_OK;
+}
+
+// Host + device state of one prepared problem (compiled programs, schedule, inputs on the
+// device). Shared by the fit and the evaluation entry points.
+struct Prep {
+    PackResult pk;
+    Schedule sc;
+    int64_t ldx = 0, y_rows = 0;
+    bool y_shared = false;
+};
+
+template <typename T>
+int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
+    const PopHeader *h = pr.h;
+    const int M = h->M_prob, N = h->N, n_vars = h->n_vars;
+    const int64_t total_c = h->total_c;
+    const bool fp64 = sizeof(T) == 8;
+    CoStats &st = ctx->stats;
+
+    // ---- compile + schedule (host) ----
+    int rc = compile_population(h, pr.nt, pr.nv, pr.ci, pr.metas, &pp.pk);
+    if (rc != CO_OK) return rc;
+    // shared targets: an explicit single row, or every row equal to row 0
+    bool y_shared = y_shared_in;
+    if (!y_shared && N > 0 && M > 0) {
+        y_shared = true;
+        const size_t rb = (size_t)N * sizeof(float);
+        for (int m = 1; m < M && y_shared; ++m)
+            if (std::memcmp(pr.ym, pr.ym + (size_t)m * N, rb) != 0) y_shared = false;
+    }
+    pp.y_shared = y_shared;
+    st.y_shared = y_shared ? 1 : 0;
+    const int round = EVAL_THREADS * EVAL_V;
+    Schedule &sc = pp.sc;
+    build_schedule(pp.pk, pr.metas, M, N, y_shared, fp64, round, ctx->sm_count * 3, &sc);
+    st.n_bins = (int)sc.bins.size();
+    pp.ldx = ((int64_t)N + round - 1) / round * round;
+    pp.y_rows = y_shared ? 1 : M;
+    const int64_t ldx = pp.ldx, y_rows = pp.y_rows;
+
+    // ---- device buffers (grow-only) ----
+    CK(cudaSetDevice(ctx->device));
+    GROW(ctx->code, pp.pk.code.size() * sizeof(uint32_t));
+    GROW(ctx->desc, (size_t)M * sizeof(TreeDesc));
+    GROW(ctx->bin_trees, (size_t)M * sizeof(int32_t));
+    GROW(ctx->bin_tree_off, (sc.bins.size() + 1) * sizeof(int64_t));
+    GROW(ctx->bin_item_off, sc.bins.size() * sizeof(int64_t));
+    GROW(ctx->items, (size_t)sc.total_items * sizeof(int2));
+    GROW(ctx->n_items, sc.bins.size() * sizeof(int));
+    GROW(ctx->counter, sc.bins.size() * sizeof(int));
+    GROW(ctx->xs_raw, (size_t)N * n_vars * sizeof(float));
+    GROW(ctx->xs, (size_t)n_vars * ldx * sizeof(float));
+    GROW(ctx->ym, (size_t)y_rows * ldx * sizeof(float));
+    GROW(ctx->c, total_c * sizeof(T));
+    GROW(ctx->ctry, total_c * sizeof(T));
+    GROW(ctx->delta, total_c * sizeof(T));
+    GROW(ctx->cinit_f, total_c * sizeof(float));
+    GROW(ctx->lam, (size_t)M * sizeof(T));
+    GROW(ctx->loss, (size_t)M * sizeof(T));
+    GROW(ctx->loss_init, (size_t)M * sizeof(T));
+    GROW(ctx->status, (size_t)M * sizeof(int32_t));
+    GROW(ctx->iters, (size_t)M * sizeof(int32_t));
+    GROW(ctx->pending, (size_t)M * sizeof(int32_t));
+    GROW(ctx->n_run, 2 * sizeof(int));
+    GROW(ctx->partials, (size_t)sc.partial_elems * sizeof(T));
+    GROW(ctx->blk, (size_t)sc.block_elems * sizeof(T));
+
+    // ---- H2D ----
+    cudaStream_t s = ctx->stream;
+    std::vector<int32_t> bin_trees;
+    std::vector<int64_t> bin_tree_off, bin_item_off;
+    bin_trees.reserve((size_t)M);
+    for (const Bin &b : sc.bins) {
+        bin_tree_off.push_back((int64_t)bin_trees.size());
+        bin_item_off.push_back(b.item_off);
+        bin_trees.insert(bin_trees.end(), b.trees.begin(), b.trees.end());
+    }
+    bin_tree_off.push_back((int64_t)bin_trees.size());
+    if (!pp.pk.code.empty())
+        CK(cudaMemcpyAsync(ctx->code.ptr, pp.pk.code.data(), pp.pk.code.size() * sizeof(uint32_t),
+                           cudaMemcpyHostToDevice, s));
+    if (M > 0) {
+        CK(cudaMemcpyAsync(ctx->desc.ptr, sc.desc.data(), (size_t)M * sizeof(TreeDesc),
+                           cudaMemcpyHostToDevice, s));
+        CK(cudaMemcpyAsync(ctx->bin_trees.ptr, bin_trees.data(),
+                           bin_trees.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    }
+    CK(cudaMemcpyAsync(ctx->bin_tree_off.ptr, bin_tree_off.data(),
+                       bin_tree_off.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    if (!bin_item_off.empty())
+        CK(cudaMemcpyAsync(ctx->bin_item_off.ptr, bin_item_off.data(),
+                           bin_item_off.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    if ((size_t)N * n_vars > 0) {
+        CK(cudaMemcpyAsync(ctx->xs_raw.ptr, pr.xs, (size_t)N * n_vars * sizeof(float),
+                           cudaMemcpyHostToDevice, s));
+        transpose_x_kernel<<<std::max(1, std::min(4 * ctx->sm_count,
+                                                  (int)((n_vars * ldx + 255) / 256))),
+                             256, 0, s>>>(P<float>(ctx->xs_raw), N, n_vars, ldx, P<float>(ctx->xs));
+        CK(cudaGetLastError());
+        st.kernel_launches++;
+    }
+    CK(cudaMemsetAsync(ctx->ym.ptr, 0, (size_t)y_rows * ldx * sizeof(float), s));
+    if (N > 0 && y_rows > 0) {
+        CK(cudaMemcpy2DAsync(ctx->ym.ptr, (size_t)ldx * sizeof(float), pr.ym,
+                             (size_t)N * sizeof(float), (size_t)N * sizeof(float), (size_t)y_rows,
+                             cudaMemcpyHostToDevice, s));
+    }
+    if (total_c > 0)
+        CK(cudaMemcpyAsync(ctx->cinit_f.ptr, pr.c_init, total_c * sizeof(float),
+                           cudaMemcpyHostToDevice, s));
+    return CO_OK;
+}
+
+inline int grid_for(Ctx *ctx, int64_t n) {
+    return (int)std::max<int64_t>(1, std::min<int64_t>(4 * ctx->sm_count, (n + 255) / 256));
+}
+
+template <typename T>
+int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &out) {
+    auto t_entry = std::chrono::steady_clock::now();
+    const PopHeader *h = pr.h;
+    const int M = h->M_prob, N = h->N;
+    const int64_t total_c = h->total_c;
+    const bool fp64 = sizeof(T) == 8;
+    CoStats &st = ctx->stats;
+    st = CoStats{};
+    st.precision = fp64 ? CO_PREC_FP64 : CO_PREC_FP32;
+
+    Prep pp;
+    int rc = prepare<T>(ctx, pr, opt.y_shared != 0, pp);
+    if (rc != CO_OK) return rc;
+    if (M == 0) {
+        st.setup_ms = ms_since(t_entry);
+        g_last_setup_ms = st.setup_ms;
+        g_last_loop_ms = 0.0;
+        return CO_OK;
+    }
+    const PackResult &pk = pp.pk;
+    const Schedule &sc = pp.sc;
+    const int64_t ldx = pp.ldx;
+    cudaStream_t s = ctx->stream;
+    init_state_kernel<T><<<grid_for(ctx, std::max<int64_t>(total_c, M)), 256, 0, s>>>(
+        P<float>(ctx->cinit_f), total_c, P<T>(ctx->c), P<T>(ctx->ctry), M, (T)opt.lambda0,
+        P<T>(ctx->lam), P<int32_t>(ctx->status), P<int32_t>(ctx->iters),
+        P<int32_t>(ctx->pending));
+    CK(cudaGetLastError());
+    st.kernel_launches++;
+
+    // ---- step-kernel launch geometry ----
+    const size_t step_smem = (size_t)STEP_WARPS * STEP_WARP_D * sizeof(double);
+    if (!ctx->step_attr_set[fp64 ? 1 : 0]) {
+        CK(cudaFuncSetAttribute(lm_step_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)step_smem));
+        ctx->step_attr_set[fp64 ? 1 : 0] = true;
+    }
+    int step_occ = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&step_occ, lm_step_kernel<T>, STEP_THREADS,
+                                                     step_smem));
+    const int step_grid = std::max(1, std::min((M + STEP_WARPS - 1) / STEP_WARPS,
+                                               std::max(1, step_occ) * ctx->sm_count));
+
+    StepParams<T> sp;
+    sp.desc = P<TreeDesc>(ctx->desc);
+    sp.M = M;
+    sp.partials = P<T>(ctx->partials);
+    sp.blk = P<T>(ctx->blk);
+    sp.c = P<T>(ctx->c);
+    sp.ctry = P<T>(ctx->ctry);
+    sp.delta = P<T>(ctx->delta);
+    sp.lam = P<T>(ctx->lam);
+    sp.loss = P<T>(ctx->loss);
+    sp.loss_init = P<T>(ctx->loss_init);
+    sp.status = P<int32_t>(ctx->status);
+    sp.iters = P<int32_t>(ctx->iters);
+    sp.pending = P<int32_t>(ctx->pending);
+    sp.xtol = (T)opt.xtol;
+
+    const int max_iter = std::max(0, opt.max_iter);
+    size_t ev_i = 0;
+    auto rec = [&](void) -> cudaEvent_t {
+        cudaEvent_t e = event_at(ctx, ev_i++);
+        if (e) cudaEventRecord(e, s);
+        return e;
+    };
+    std::vector<std::pair<size_t, size_t>> eval_spans, step_spans;
+
+    // ---- initial pass at c_init + solve of iteration 0 ----
+    size_t e0 = ev_i; rec();
+    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), pr, ldx, true);
+    if (rc) return rc;
+    size_t e1 = ev_i; rec();
+    sp.n_running = P<int>(ctx->n_run);
+    sp.initial = 1;
+    sp.do_solve = max_iter > 0 ? 1 : 0;
+    CK(cudaMemsetAsync(sp.n_running, 0, sizeof(int), s));
+    lm_step_kernel<T><<<step_grid, STEP_THREADS, step_smem, s>>>(sp);
+    CK(cudaGetLastError());
+    st.kernel_launches++;
+    size_t e2 = ev_i; rec();
+    eval_spans.push_back({e0, e1});
+    step_spans.push_back({e1, e2});
+    CK(cudaStreamSynchronize(s));
+    st.setup_ms = ms_since(t_entry);
+    auto t_loop = std::chrono::steady_clock::now();
+
+    // ---- LM iterations ----
+    // At most two iterations are in flight: before launching iteration `it` the host waits
+    // for the running-tree count of step it-2 and stops once no tree is running.
+    int iters_run = 0;
+    for (int it = 0; it < max_iter; ++it) {
+        const int slot = it & 1;
+        if (opt.early_exit && it >= 2) {
+            CK(cudaEventSynchronize(ctx->ev_nrun[slot]));
+            if (ctx->h_nrun[slot] == 0) break;
+        }
+        iters_run++;
+        size_t a = ev_i; rec();
+        rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), pr, ldx, true);
+        if (rc) return rc;
+        size_t b = ev_i; rec();
+        sp.n_running = P<int>(ctx->n_run) + slot;
+        sp.initial = 0;
+        sp.do_solve = (it + 1 < max_iter) ? 1 : 0;
+        CK(cudaMemsetAsync(sp.n_running, 0, sizeof(int), s));
+        lm_step_kernel<T><<<step_grid, STEP_THREADS, step_smem, s>>>(sp);
+        CK(cudaGetLastError());
+        st.kernel_launches++;
+        size_t c = ev_i; rec();
+        eval_spans.push_back({a, b});
+        step_spans.push_back({b, c});
+        if (opt.early_exit) {
+            CK(cudaMemcpyAsync(ctx->h_nrun + slot, sp.n_running, sizeof(int),
+                               cudaMemcpyDeviceToHost, s));
+            CK(cudaEventRecord(ctx->ev_nrun[slot], s));
+        }
+    }
+    CK(cudaStreamSynchronize(s));
+    st.loop_ms = ms_since(t_loop);
+    st.iters_run = iters_run;
+    auto t_fin = std::chrono::steady_clock::now();
+
+    // ---- fp64 audit of fp32 fits (lm_core.cuh:299-351; fp64 fits accept in fp64 already) ----
+    const bool audit = !fp64 && opt.fp64_audit != 0 && total_c > 0;
+    if (audit) {
+        GROW(ctx->c64, total_c * sizeof(double));
+        GROW(ctx->l64, 2 * (size_t)M * sizeof(double));
+        GROW(ctx->n_rev, sizeof(int));
+        // per-item partials are not needed any more: reuse the buffer for fp64 sums
+        GROW(ctx->partials, (size_t)sc.partial_elems * sizeof(double));
+        double *c64 = P<double>(ctx->c64), *l64 = P<double>(ctx->l64);
+        const int g1 = grid_for(ctx, std::max<int64_t>(total_c, M));
+        const float *srcs[2] = {reinterpret_cast<const float *>(ctx->c.ptr), P<float>(ctx->cinit_f)};
+        for (int pass = 0; pass < 2; ++pass) {
+            audit_prepare_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, srcs[pass], total_c,
+                                                    c64, P<int32_t>(ctx->pending));
+            CK(cudaGetLastError());
+            rc = launch_pass<double>(ctx, sc, pk, c64, P<double>(ctx->partials), pr, ldx, false);
+            if (rc) return rc;
+            audit_loss_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M,
+                                                  P<double>(ctx->partials), l64 + pass * M);
+            CK(cudaGetLastError());
+            st.kernel_launches += 2;
+        }
+        CK(cudaMemsetAsync(ctx->n_rev.ptr, 0, sizeof(int), s));
+        audit_apply_kernel<T><<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, l64, l64 + M,
+                                                 P<float>(ctx->cinit_f), P<T>(ctx->c),
+                                                 P<T>(ctx->loss), P<int32_t>(ctx->status),
+                                                 P<int>(ctx->n_rev));
+        CK(cudaGetLastError());
+        st.kernel_launches++;
+    }
+
+    // ---- D2H ----
+    std::vector<T> hc((size_t)total_c), hli((size_t)M), hlf((size_t)M);
+    std::vector<int32_t> hst((size_t)M), hit((size_t)M);
+    if (total_c > 0)
+        CK(cudaMemcpyAsync(hc.data(), ctx->c.ptr, total_c * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hli.data(), ctx->loss_init.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hlf.data(), ctx->loss.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hst.data(), ctx->status.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hit.data(), ctx->iters.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    int n_rev = 0;
+    if (audit)
+        CK(cudaMemcpyAsync(&n_rev, ctx->n_rev.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    st.n_reverted = n_rev;
+
+    for (int64_t i = 0; i < total_c; ++i) {
+        if (out.c_f) out.c_f[i] = (float)hc[(size_t)i];
+        if (out.c_d) out.c_d[i] = (double)hc[(size_t)i];
+    }
+    for (int m = 0; m < M; ++m) {
+        const int32_t s_ = hst[(size_t)m];
+        out.status[m] = (s_ == ST_RUNNING) ? STATUS_MAXITER : s_;
+        if (out.li_f) out.li_f[m] = (float)hli[(size_t)m];
+        if (out.lf_f) out.lf_f[m] = (float)hlf[(size_t)m];
+        if (out.li_d) out.li_d[m] = (double)hli[(size_t)m];
+        if (out.lf_d) out.lf_d[m] = (double)hlf[(size_t)m];
+        if (out.iters) out.iters[m] = hit[(size_t)m];
+    }
+    // node / sample evaluation counts: one initial evaluation plus each evaluated trial
+    int64_t node_evals = 0, sample_evals = 0;
+    for (int m = 0; m < M; ++m) {
+        const int64_t evals = 1 + (int64_t)hit[(size_t)m];
+        node_evals += evals * pr.metas[m].n_nodes * (int64_t)N;
+        sample_evals += evals * (int64_t)N;
+    }
+    st.node_evals = node_evals;
+    st.sample_evals = sample_evals;
+
+    // device-time split from the recorded events
+    double eval_ms = 0.0, step_ms = 0.0;
+    for (auto &sp_ : eval_spans) {
+        float x = 0.f;
+        if (cudaEventElapsedTime(&x, ctx->events[sp_.first], ctx->events[sp_.second]) == cudaSuccess)
+            eval_ms += x;
+    }
+    for (auto &sp_ : step_spans) {
+        float x = 0.f;
+        if (cudaEventElapsedTime(&x, ctx->events[sp_.first], ctx->events[sp_.second]) == cudaSuccess)
+            step_ms += x;
+    }
+    st.eval_ms = eval_ms;
+    st.step_ms = step_ms;
+    st.finish_ms = ms_since(t_fin);
+    g_last_setup_ms = st.setup_ms;
+    g_last_loop_ms = st.loop_ms;
+    return CO_OK;
+}
+
+// Evaluate every tree at given constants: values, Jacobian, normal-equation blocks.
+template <typename T>
+int run_eval(Ctx *ctx, const Problem &pr, bool y_shared, const double *c, double *vals_out,
+             double *jac_out, double *blocks_out) {
+    const PopHeader *h = pr.h;
+    const int M = h->M_prob, N = h->N;
+    const int64_t total_c = h->total_c;
+    ctx->stats = CoStats{};
+    ctx->stats.precision = sizeof(T) == 8 ? CO_PREC_FP64 : CO_PREC_FP32;
+    Prep pp;
+    int rc = prepare<T>(ctx, pr, y_shared, pp);
+    if (rc != CO_OK) return rc;
+    if (M == 0) return CO_OK;
+    if (jac_out && pp.pk.max_K > h->K_max) return CO_ERR_NULLARG;
+    cudaStream_t s = ctx->stream;
+    GROW(ctx->c64, total_c * sizeof(double));
+    if (total_c > 0)
+        CK(cudaMemcpyAsync(ctx->c64.ptr, c, total_c * sizeof(double), cudaMemcpyHostToDevice, s));
+    load_point_kernel<T><<<grid_for(ctx, std::max<int64_t>(total_c, M)), 256, 0, s>>>(
+        P<double>(ctx->c64), total_c, P<T>(ctx->ctry), M, P<int32_t>(ctx->pending));
+    CK(cudaGetLastError());
+    T *dv = nullptr, *dj = nullptr;
+    const int kmax = std::max(h->K_max, 1);
+    if (vals_out) {
+        GROW(ctx->vals, (size_t)M * N * sizeof(T));
+        dv = P<T>(ctx->vals);
+    }
+    if (jac_out) {
+        GROW(ctx->jac, (size_t)M * kmax * N * sizeof(T));
+        dj = P<T>(ctx->jac);
+        CK(cudaMemsetAsync(dj, 0, (size_t)M * kmax * N * sizeof(T), s));
+    }
+    rc = launch_pass<T>(ctx, pp.sc, pp.pk, P<T>(ctx->ctry), P<T>(ctx->partials), pr, pp.ldx, true,
+                        dv, dj, kmax);
+    if (rc) return rc;
+    sum_blocks_kernel<T><<<grid_for(ctx, M), 256, 0, s>>>(P<TreeDesc>(ctx->desc), M,
+                                                           P<T>(ctx->partials), P<T>(ctx->blk));
+    CK(cudaGetLastError());
+    std::vector<T> hv, hj, hb;
+    if (vals_out) {
+        hv.resize((size_t)M * N);
+        CK(cudaMemcpyAsync(hv.data(), dv, hv.size() * sizeof(T), cudaMemcpyDeviceToHost, s));
+    }
+    if (jac_out) {
+        hj.resize((size_t)M * kmax * N);
+        CK(cudaMemcpyAsync(hj.data(), dj, hj.size() * sizeof(T), cudaMemcpyDeviceToHost, s));
+    }
+    if (blocks_out) {
+        hb.resize((size_t)pp.sc.block_elems);
+        CK(cudaMemcpyAsync(hb.data(), ctx->blk.ptr, hb.size() * sizeof(T), cudaMemcpyDeviceToHost, s));
+    }
+    CK(cudaStreamSynchronize(s));
+    for (size_t i = 0; i < hv.size(); ++i) vals_out[i] = (double)hv[i];
+    if (jac_out) {
+        // reference d_J layout [M][K_max][N] (cusr/kernel/ad_interp.cuh:240-244)
+        for (size_t i = 0; i < hj.size(); ++i) jac_out[i] = (double)hj[i];
+    }
+    for (size_t i = 0; i < hb.size(); ++i) blocks_out[i] = (double)hb[i];
+    return CO_OK;
+}
+
+}  // namespace
+}  // namespace cusr
+
+using namespace cusr;
+
+extern "C" {
+
+void co_default_options(CoOptions *opt) {
+    if (!opt) return;
+    std::memset(opt, 0, sizeof(*opt));
+    opt->struct_size = (int32_t)sizeof(CoOptions);
+    opt->precision = CO_PREC_FP32;
+    opt->max_iter = 50;
+    opt->y_shared = 0;
+    opt->lambda0 = 1e-3;
+    opt->xtol = 1e-6;
+    opt->fp64_audit = -1;
+    opt->early_exit = 1;
+}
+
+int co_init(int device_id, void **handle_out) {
+    if (!handle_out) return CO_ERR_NULLARG;
+    *handle_out = nullptr;
+    cudaError_t e = cudaSetDevice(device_id);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "[cusr_b200] cudaSetDevice(%d): %s\n", device_id, cudaGetErrorString(e));
+        return CO_ERR_CUDA;
+    }
+    e = cudaFree(0);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "[cusr_b200] context init: %s\n", cudaGetErrorString(e));
+        return CO_ERR_CUDA;
+    }
+    Ctx *ctx = new (std::nothrow) Ctx();
+    if (!ctx) return CO_ERR_OOM;
+    ctx->device = device_id;
+    if (cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device_id) !=
+            cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMallocHost(&ctx->h_nrun, 2 * sizeof(int)) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_nrun[0], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_nrun[1], cudaEventDisableTiming) != cudaSuccess ||
+        eval_prepare_f32() != cudaSuccess || eval_prepare_f64() != cudaSuccess) {
+        fprintf(stderr, "[cusr_b200] device %d setup failed\n", device_id);
+        co_teardown(ctx);
+        return CO_ERR_CUDA;
+    }
+    *handle_out = ctx;
+    return CO_OK;
+}
+
+static int optimize_common(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+                           const int32_t *ci, const TreeMeta *metas, const float *c_init,
+                           const float *xs, const float *ym, const CoOptions &opt,
+                           const Outputs &out) {
+    Ctx *ctx = (Ctx *)handle;
+    Problem pr{h, nt, nv, ci, metas, c_init, xs, ym};
+    int rc = check_args(pr);
+    if (rc != CO_OK) return rc;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    if (opt.precision == CO_PREC_FP64) return run_fit<double>(ctx, pr, opt, out);
+    return run_fit<float>(ctx, pr, opt, out);
+}
+
+int co_optimize(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+                const int32_t *ci, const TreeMeta *metas, const float *c_init, const float *xs,
+                const float *ym, int max_iter, float *c_final_out, int32_t *status_out,
+                float *loss_init_out, float *loss_final_out) {
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym || !c_final_out ||
+        !status_out)
+        return CO_ERR_NULLARG;
+    CoOptions opt;
+    co_default_options(&opt);
+    opt.max_iter = max_iter;
+    Outputs out;
+    out.c_f = c_final_out;
+    out.status = status_out;
+    out.li_f = loss_init_out;
+    out.lf_f = loss_final_out;
+    return optimize_common(handle, h, nt, nv, ci, metas, c_init, xs, ym, opt, out);
+}
+
+int co_optimize_ex(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+                   const int32_t *ci, const TreeMeta *metas, const float *c_init, const float *xs,
+                   const float *ym, const CoOptions *opt_in, double *c_final_out,
+                   int32_t *status_out, double *loss_init_out, double *loss_final_out,
+                   int32_t *iters_out) {
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym || !c_final_out ||
+        !status_out)
+        return CO_ERR_NULLARG;
+    CoOptions opt;
+    co_default_options(&opt);
+    if (opt_in) {
+        if (opt_in->struct_size < (int32_t)offsetof(CoOptions, reserved)) return CO_ERR_NULLARG;
+        opt = *opt_in;
+    }
+    if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
+    if (opt.y_shared) {
+        // a single row: check the explicit layout, then run as shared
+    }
+    Outputs out;
+    out.c_d = c_final_out;
+    out.status = status_out;
+    out.li_d = loss_init_out;
+    out.lf_d = loss_final_out;
+    out.iters = iters_out;
+    return optimize_common(handle, h, nt, nv, ci, metas, c_init, xs, ym, opt, out);
+}
+
+int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+                const int32_t *ci, const TreeMeta *metas, const double *c, const float *xs,
+                const float *ym, int precision, int y_shared, double *vals_out,
+                double *jac_out, double *blocks_out) {
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c || !xs || !ym) return CO_ERR_NULLARG;
+    if (precision != CO_PREC_FP32 && precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    Problem pr{h, nt, nv, ci, metas, nullptr, xs, ym};
+    int rc = check_args(pr);
+    if (rc != CO_OK) return rc;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    std::vector<float> c_f((size_t)std::max(h->total_c, 0));
+    for (size_t i = 0; i < c_f.size(); ++i) c_f[i] = (float)c[i];
+    pr.c_init = c_f.data();
+    if (precision == CO_PREC_FP64)
+        return run_eval<double>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
+    return run_eval<float>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
+}
+
+int co_last_split(double *setup_ms_out, double *loop_ms_out) {
+    if (setup_ms_out) *setup_ms_out = g_last_setup_ms;
+    if (loop_ms_out) *loop_ms_out = g_last_loop_ms;
+    return 0;
+}
+
+int co_get_stats(void *handle, CoStats *out) {
+    if (!handle || !out) return CO_ERR_NULLARG;
+    *out = ((Ctx *)handle)->stats;
+    return CO_OK;
+}
+
+void co_teardown(void *handle) {
+    if (!handle) return;
+    Ctx *ctx = (Ctx *)handle;
+    cudaSetDevice(ctx->device);
+    DBuf *bufs[] = {&ctx->code, &ctx->desc, &ctx->bin_trees, &ctx->bin_tree_off,
+                    &ctx->bin_item_off, &ctx->items, &ctx->n_items, &ctx->counter,
+                    &ctx->xs_raw, &ctx->xs, &ctx->ym, &ctx->c, &ctx->ctry, &ctx->delta,
+                    &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
+                    &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->partials, &ctx->blk,
+                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac};
+    for (DBuf *b : bufs) release(*b);
+    for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->ev_nrun)
+        if (e) cudaEventDestroy(e);
+    if (ctx->h_nrun) cudaFreeHost(ctx->h_nrun);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+const char *co_strerror(int code) {
+    switch (code) {
+        case CO_OK: return "ok";
+        case CO_ERR_BOUNDS: return "K_max > 32 or max_stack > 64, or a tree beyond an engine limit";
+        case CO_ERR_CUDA: return "CUDA error";
+        case CO_ERR_SUM_C: return "sum(metas.K) != header.total_c";
+        case CO_ERR_SUM_NODES: return "sum(metas.n_nodes) != header.total_nodes";
+        case CO_ERR_NULLARG: return "null pointer / bad argument";
+        case CO_ERR_OOM: return "out of memory";
+        case CO_ERR_BADTREE: return "malformed tree bytecode";
+        default: return "unknown code";
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,338 @@
+// lm_kernels.cuh — per-tree LM bookkeeping on the device: accept / reject / lambda /
+// convergence of the evaluated trial, the damped Cholesky solve of the next step, the work
+// list of the next evaluation, and the fp64 audit.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "program.h"
+#include "eval_kernel.cuh"
+
+namespace cusr {
+
+// internal per-tree status: RUNNING while iterating, else the final STATUS_* code
+constexpr int32_t ST_RUNNING = -1;
+
+template <typename T>
+struct StepParams {
+    const TreeDesc *desc;
+    int M;
+    const T *partials;       // per-item sums of the last evaluation
+    T *blk;                  // normal-equation block at the accepted point, q_off
+    T *c;                    // accepted constants
+    T *ctry;                 // trial constants (evaluated point)
+    T *delta;                // last solved step
+    T *lam;                  // Marquardt damping
+    T *loss;                 // accepted 0.5*sum r^2
+    T *loss_init;
+    int32_t *status;
+    int32_t *iters;
+    int32_t *pending;        // 1: the tree's trial was evaluated by the last pass
+    int *n_running;          // trees still running after this step (early exit)
+    int initial;             // the evaluated point is c_init
+    int do_solve;            // solve a new step for every running tree
+    T xtol;
+};
+
+constexpr int STEP_THREADS = 256;
+constexpr int STEP_WARPS = STEP_THREADS / 32;
+// per-warp shared memory (doubles): sums [561 T] + A[32*32] + b[32]
+constexpr int STEP_SUMS_D = 576;
+constexpr int STEP_WARP_D = STEP_SUMS_D + CO_MAX_K * CO_MAX_K + CO_MAX_K;
+
+// One warp per tree. Mirrors the reference LM iteration (co_lib.cu:343-483 with the AD
+// ordering of :438-455, batch_lm_revad.cu:396-500):
+//   finalize the evaluated trial: non-finite loss -> FAIL_NAN; loss_try <= loss -> accept
+//   (c, loss, JtJ, Jtr move to the trial), then |delta| < xtol(|c_try| + xtol) -> CONVERGED,
+//   else lambda = max(0.1 lambda, 1e-12); otherwise reject, lambda *= 10, > 1e12 -> FAIL_NAN;
+//   solve: A = JtJ with diag *= (1 + lambda) (batch_lm_ad.cu:152-159), Cholesky in fp64
+//   (the reference's SOLVE_FP64 form), s <= 0 -> this iteration is a rejected step,
+//   lambda *= 10, > 1e12 -> FAIL_CHOLESKY; else c_try = c + delta is queued for evaluation.
+// The J/JtJ/Jtr of an accepted trial were built by the same pass that computed its loss, so
+// an accept needs no re-evaluation and a reject re-solves from the stored block.
+template <typename T>
+__global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<T> p) {
+    extern __shared__ double step_sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    T *sums = reinterpret_cast<T *>(step_sm + warp * STEP_WARP_D);
+    double *A = step_sm + warp * STEP_WARP_D + STEP_SUMS_D;
+    double *bv = A + CO_MAX_K * CO_MAX_K;
+    for (int m = blockIdx.x * STEP_WARPS + warp; m < p.M; m += gridDim.x * STEP_WARPS) {
+        int st = p.status[m];
+        if (st != ST_RUNNING) continue;
+        const TreeDesc d = p.desc[m];
+        const int K = d.K, P = nblock_size(K);
+        const int pend = p.pending[m];
+        if (pend) {
+            for (int e = lane; e < P; e += 32) {
+                const T *src = p.partials + d.p_off + e;
+                T s = T(0);
+                for (int ch = 0; ch < d.n_chunks; ++ch) s += src[(int64_t)ch * P];
+                sums[e] = s;
+            }
+        }
+        __syncwarp();
+        int accept = 0;
+        if (lane == 0) {
+            T lam = p.lam[m];
+            if (pend) {
+                p.pending[m] = 0;
+                const T ltry = T(0.5) * sums[P - 1];
+                if (p.initial) {
+                    p.loss_init[m] = ltry;
+                    p.loss[m] = ltry;
+                    accept = 1;
+                    if (K == 0) st = STATUS_K0_SKIP;
+                    else if (!Mth<T>::finite(ltry)) st = STATUS_FAIL_NAN;
+                } else {
+                    p.iters[m] += 1;
+                    if (!Mth<T>::finite(ltry)) {
+                        st = STATUS_FAIL_NAN;
+                    } else {
+                        T dn2 = T(0), cn2 = T(0);
+                        for (int k = 0; k < K; ++k) {
+                            const T dk = p.delta[d.c_off + k], ck = p.ctry[d.c_off + k];
+                            dn2 += dk * dk;
+                            cn2 += ck * ck;
+                        }
+                        const T dn = Mth<T>::sqrt(dn2), cn = Mth<T>::sqrt(cn2);
+                        if (ltry <= p.loss[m]) {
+                            accept = 1;
+                            p.loss[m] = ltry;
+                            for (int k = 0; k < K; ++k) p.c[d.c_off + k] = p.ctry[d.c_off + k];
+                            if (dn < p.xtol * (cn + p.xtol)) {
+                                st = STATUS_CONVERGED;
+                            } else {
+                                lam *= T(0.1);
+                                if (lam < T(1e-12)) lam = T(1e-12);
+                            }
+                        } else {
+                            lam *= T(10);
+                            if (lam > T(1e12)) st = STATUS_FAIL_NAN;
+                        }
+                    }
+                }
+            }
+            p.lam[m] = lam;
+        }
+        accept = __shfl_sync(0xffffffffu, accept, 0);
+        st = __shfl_sync(0xffffffffu, st, 0);
+        if (accept)
+            for (int e = lane; e < P; e += 32) p.blk[d.q_off + e] = sums[e];
+        __syncwarp();
+        if (lane == 0) {
+            if (st == ST_RUNNING && p.do_solve) {
+                T lam = p.lam[m];
+                const T *b = p.blk + d.q_off;
+                const int tri = K * (K + 1) / 2;
+                const double fac = (double)(T(1) + lam);
+                for (int i = 0; i < K; ++i) {
+                    bv[i] = -(double)b[tri + i];
+                    for (int l = 0; l <= i; ++l) {
+                        const double v = (double)b[i * (i + 1) / 2 + l];
+                        A[i * K + l] = v;
+                        A[l * K + i] = v;
+                    }
+                    A[i * K + i] *= fac;
+                }
+                bool ok = true;
+                for (int j = 0; j < K && ok; ++j) {
+                    double s = A[j * K + j];
+                    for (int k = 0; k < j; ++k) s -= A[j * K + k] * A[j * K + k];
+                    if (s <= 0.0) { ok = false; break; }
+                    A[j * K + j] = sqrt(s);
+                    for (int i = j + 1; i < K; ++i) {
+                        double t = A[i * K + j];
+                        for (int k = 0; k < j; ++k) t -= A[i * K + k] * A[j * K + k];
+                        A[i * K + j] = t / A[j * K + j];
+                    }
+                }
+                if (!ok) {
+                    p.iters[m] += 1;
+                    lam *= T(10);
+                    if (lam > T(1e12)) st = STATUS_FAIL_CHOLESKY;
+                    p.lam[m] = lam;
+                } else {
+                    for (int i = 0; i < K; ++i) {
+                        double s = bv[i];
+                        for (int k = 0; k < i; ++k) s -= A[i * K + k] * bv[k];
+                        bv[i] = s / A[i * K + i];
+                    }
+                    for (int i = K - 1; i >= 0; --i) {
+                        double s = bv[i];
+                        for (int k = i + 1; k < K; ++k) s -= A[k * K + i] * bv[k];
+                        bv[i] = s / A[i * K + i];
+                    }
+                    for (int k = 0; k < K; ++k) {
+                        const T dk = (T)bv[k];
+                        p.delta[d.c_off + k] = dk;
+                        p.ctry[d.c_off + k] = p.c[d.c_off + k] + dk;
+                    }
+                    p.pending[m] = 1;
+                }
+            }
+            p.status[m] = st;
+            if (st == ST_RUNNING) atomicAdd(p.n_running, 1);
+        }
+        __syncwarp();
+    }
+}
+
+// Work list of one bin: every chunk of every pending tree, bin order (most expensive
+// first). One block per bin; also resets the bin's work counter.
+struct ItemsParams {
+    const TreeDesc *desc;
+    const int32_t *bin_trees;      // concatenated per-bin tree lists
+    const int64_t *bin_tree_off;   // [n_bins + 1]
+    const int64_t *bin_item_off;   // [n_bins]
+    const int32_t *pending;
+    int2 *items;
+    int *n_items;                  // [n_bins]
+    int *counter;                  // [n_bins]
+};
+
+constexpr int ITEMS_THREADS = 1024;
+
+__global__ void __launch_bounds__(ITEMS_THREADS) build_items_kernel(const ItemsParams p) {
+    __shared__ int warp_tot[ITEMS_THREADS / 32];
+    __shared__ int s_run;
+    const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t t0 = p.bin_tree_off[b], t1 = p.bin_tree_off[b + 1];
+    int2 *items = p.items + p.bin_item_off[b];
+    if (tid == 0) s_run = 0;
+    __syncthreads();
+    for (int64_t base = t0; base < t1; base += ITEMS_THREADS) {
+        const int64_t ti = base + tid;
+        int tree = -1, cnt = 0;
+        if (ti < t1) {
+            tree = p.bin_trees[ti];
+            cnt = p.pending[tree] ? p.desc[tree].n_chunks : 0;
+        }
+        // block exclusive scan of cnt
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) warp_tot[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_tot[lane];
+            int inc = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += u;
+            }
+            warp_tot[lane] = inc - v;   // exclusive warp offsets
+        }
+        __syncthreads();
+        const int off = s_run + warp_tot[warp] + incl - cnt;
+        for (int c = 0; c < cnt; ++c) items[off + c] = make_int2(tree, c);
+        __syncthreads();
+        if (tid == ITEMS_THREADS - 1) s_run = off + cnt;
+        __syncthreads();
+    }
+    if (tid == 0) {
+        p.n_items[b] = s_run;
+        p.counter[b] = 0;
+    }
+}
+
+// SoA transpose of the inputs: xs [N][n_vars] (pop.bin) -> [n_vars][ldx], zero padded.
+__global__ void transpose_x_kernel(const float *__restrict__ xs, int64_t N, int n_vars,
+                                   int64_t ldx, float *__restrict__ out) {
+    const int64_t total = (int64_t)n_vars * ldx;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t v = e / ldx, i = e - v * ldx;
+        out[e] = (i < N) ? xs[i * n_vars + v] : 0.0f;
+    }
+}
+
+// Initial state of every tree: c = c_init, lambda0, RUNNING, initial evaluation pending.
+template <typename T>
+__global__ void init_state_kernel(const float *__restrict__ c_init, int64_t total_c, T *c,
+                                  T *ctry, int M, T lam0, T *lam, int32_t *status,
+                                  int32_t *iters, int32_t *pending) {
+    const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_c; i += gs) {
+        c[i] = (T)c_init[i];
+        ctry[i] = (T)c_init[i];
+    }
+    for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += gs) {
+        lam[m] = lam0;
+        status[m] = ST_RUNNING;
+        iters[m] = 0;
+        pending[m] = 1;
+    }
+}
+
+// Evaluation entry: constants of the evaluated point (fp64 from the caller), every tree pending.
+template <typename T>
+__global__ void load_point_kernel(const double *__restrict__ c64, int64_t total_c, T *c, int M,
+                                  int32_t *pending) {
+    const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_c; i += gs)
+        c[i] = (T)c64[i];
+    for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += gs)
+        pending[m] = 1;
+}
+
+// Per-tree normal-equation block = sum of its chunk partials in chunk order.
+template <typename T>
+__global__ void sum_blocks_kernel(const TreeDesc *desc, int M, const T *partials, T *blk) {
+    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+        const TreeDesc d = desc[m];
+        const int P = nblock_size(d.K);
+        for (int e = 0; e < P; ++e) {
+            T s = T(0);
+            for (int ch = 0; ch < d.n_chunks; ++ch) s += partials[d.p_off + (int64_t)ch * P + e];
+            blk[d.q_off + e] = (e == P - 1) ? T(0.5) * s : s;
+        }
+    }
+}
+
+// ---- fp64 honesty audit (lm_core.cuh:299-351) -------------------------------------------
+// Trees whose fp64 loss at the delivered constants is non-finite or worse than at c_init
+// are reverted to c_init, a CONVERGED status becomes MAXITER, and the reported final loss
+// becomes the fp64 loss at c_init.
+__global__ void audit_prepare_kernel(const TreeDesc *desc, int M, const float *c_now,
+                                     int64_t total_c, double *c64, int32_t *pending) {
+    const int64_t gs = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_c; i += gs)
+        c64[i] = (double)c_now[i];
+    for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += gs)
+        pending[m] = desc[m].K > 0 ? 1 : 0;
+}
+
+__global__ void audit_loss_kernel(const TreeDesc *desc, int M, const double *partials,
+                                  double *loss64) {
+    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+        const TreeDesc d = desc[m];
+        if (d.K == 0) { loss64[m] = 0.0; continue; }
+        const int P = nblock_size(d.K);
+        double s = 0.0;
+        for (int ch = 0; ch < d.n_chunks; ++ch) s += partials[d.p_off + (int64_t)ch * P + P - 1];
+        loss64[m] = 0.5 * s;
+    }
+}
+
+template <typename T>
+__global__ void audit_apply_kernel(const TreeDesc *desc, int M, const double *lfinal,
+                                   const double *linit, const float *c_init, T *c, T *loss,
+                                   int32_t *status, int *n_reverted) {
+    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+        const TreeDesc d = desc[m];
+        if (d.K == 0) continue;
+        const double lf = lfinal[m], li = linit[m];
+        if (!isfinite(lf) || (isfinite(li) && lf > li)) {
+            for (int k = 0; k < d.K; ++k) c[d.c_off + k] = (T)c_init[d.c_off + k];
+            if (status[m] == STATUS_CONVERGED) status[m] = ST_RUNNING;   // reported as MAXITER
+            loss[m] = (T)li;
+            atomicAdd(n_reverted, 1);
+        }
+    }
+}
+
+}  // namespace cusr

@@ -1,0 +1,148 @@
+// ops.h — value and local partial derivatives of every operator, shared by the device
+// interpreter and the host-side program checker so both compute the same thing.
+//
+// Value semantics follow the reference's CUDA interpreter and numpy oracle
+// (cusr/kernel/lm_core.cuh:58-106, cusr/benchmark/interp.py:32-49); derivative rules follow
+// its reverse-mode interpreter (cusr/kernel/revad_interp.cuh:86-131):
+//   SIN d=cos a, COS d=-sin a, TAN d=1+r^2, SINH d=cosh a, COSH d=sinh a, TANH d=1-r^2,
+//   LOG d=1/a, EXP d=r, INV d=-r^2, NEG d=-1, ABS d=sign0(a), SQRT d=1/(2r);
+//   ADD (1,1), SUB (1,-1), MUL (b,a), DIV (1/b, -o/b), POW (b*a^(b-1), o*log a),
+//   MAX/MIN select (ties to the left operand), comparisons (0,0).
+// The LOOSE_* operators of the numpy oracle (log|a|, sqrt|a|, |a|^b, 1/a, a/b) are
+// implemented natively (the reference CUDA kernel maps them to 0); their derivatives are
+// those of the same formulas. Unknown operator ids evaluate to 0 with zero derivative,
+// as in the reference kernel. MAX/MIN propagate NaN like numpy's maximum/minimum.
+#pragma once
+#include <math.h>
+#include "program.h"
+
+#define CUSR_HD __host__ __device__ __forceinline__
+
+namespace cusr {
+
+template <typename T> struct Mth;
+template <> struct Mth<float> {
+    static CUSR_HD float sin(float a) { return ::sinf(a); }
+    static CUSR_HD float cos(float a) { return ::cosf(a); }
+    static CUSR_HD void sincos(float a, float *s, float *c) {
+#ifdef __CUDA_ARCH__
+        ::sincosf(a, s, c);
+#else
+        *s = ::sinf(a); *c = ::cosf(a);
+#endif
+    }
+    static CUSR_HD float tan(float a) { return ::tanf(a); }
+    static CUSR_HD float sinh(float a) { return ::sinhf(a); }
+    static CUSR_HD float cosh(float a) { return ::coshf(a); }
+    static CUSR_HD float tanh(float a) { return ::tanhf(a); }
+    static CUSR_HD float log(float a) { return ::logf(a); }
+    static CUSR_HD float exp(float a) { return ::expf(a); }
+    static CUSR_HD float sqrt(float a) { return ::sqrtf(a); }
+    static CUSR_HD float pow(float a, float b) { return ::powf(a, b); }
+    static CUSR_HD float fabs(float a) { return ::fabsf(a); }
+    static CUSR_HD float copysign(float a, float b) { return ::copysignf(a, b); }
+    static CUSR_HD bool finite(float a) { return isfinite(a); }
+};
+template <> struct Mth<double> {
+    static CUSR_HD double sin(double a) { return ::sin(a); }
+    static CUSR_HD double cos(double a) { return ::cos(a); }
+    static CUSR_HD void sincos(double a, double *s, double *c) {
+#ifdef __CUDA_ARCH__
+        ::sincos(a, s, c);
+#else
+        *s = ::sin(a); *c = ::cos(a);
+#endif
+    }
+    static CUSR_HD double tan(double a) { return ::tan(a); }
+    static CUSR_HD double sinh(double a) { return ::sinh(a); }
+    static CUSR_HD double cosh(double a) { return ::cosh(a); }
+    static CUSR_HD double tanh(double a) { return ::tanh(a); }
+    static CUSR_HD double log(double a) { return ::log(a); }
+    static CUSR_HD double exp(double a) { return ::exp(a); }
+    static CUSR_HD double sqrt(double a) { return ::sqrt(a); }
+    static CUSR_HD double pow(double a, double b) { return ::pow(a, b); }
+    static CUSR_HD double fabs(double a) { return ::fabs(a); }
+    static CUSR_HD double copysign(double a, double b) { return ::copysign(a, b); }
+    static CUSR_HD bool finite(double a) { return isfinite(a); }
+};
+
+template <typename T> CUSR_HD T sign0(T a) {
+    return a > T(0) ? T(1) : (a < T(0) ? T(-1) : T(0));
+}
+
+// reverse-mode edge product with exact-zero annihilation (revad_interp.cuh:45-47): a zero
+// adjoint or a zero local partial contributes 0, never 0*inf = NaN.
+template <typename T> CUSR_HD T safe_mul(T a, T b) {
+    return (a == T(0) || b == T(0)) ? T(0) : a * b;
+}
+
+// Unary operator: r = f(a), d = f'(a).
+template <typename T> CUSR_HD void unary_op(uint32_t op, T a, T &r, T &d) {
+    using M = Mth<T>;
+    switch (op) {
+        case OP_SIN: { T s, c; M::sincos(a, &s, &c); r = s; d = c; break; }
+        case OP_COS: { T s, c; M::sincos(a, &s, &c); r = c; d = -s; break; }
+        case OP_TAN: r = M::tan(a); d = T(1) + r * r; break;
+        case OP_SINH: r = M::sinh(a); d = M::cosh(a); break;
+        case OP_COSH: r = M::cosh(a); d = M::sinh(a); break;
+        case OP_TANH: r = M::tanh(a); d = T(1) - r * r; break;
+        case OP_LOG: r = M::log(a); d = T(1) / a; break;
+        case OP_LOGABS: r = M::log(M::fabs(a)); d = T(1) / a; break;
+        case OP_EXP: r = M::exp(a); d = r; break;
+        case OP_INV: r = T(1) / a; d = -r * r; break;
+        case OP_NEG: r = -a; d = T(-1); break;
+        case OP_ABS: r = M::fabs(a); d = sign0(a); break;
+        case OP_SQRT: r = M::sqrt(a); d = T(1) / (T(2) * r); break;
+        case OP_SQRTABS: r = M::sqrt(M::fabs(a)); d = M::copysign(T(1) / (T(2) * r), a); break;
+        default: r = T(0); d = T(0); break;
+    }
+}
+
+// Binary operator: o = a OP b (a = left operand), da = do/da, db = do/db.
+template <typename T> CUSR_HD void binary_op(uint32_t op, T a, T b, T &o, T &da, T &db) {
+    using M = Mth<T>;
+    switch (op) {
+        case OP_ADD: o = a + b; da = T(1); db = T(1); break;
+        case OP_SUB: o = a - b; da = T(1); db = T(-1); break;
+        case OP_MUL: o = a * b; da = b; db = a; break;
+        case OP_DIV: o = a / b; da = T(1) / b; db = -o / b; break;
+        case OP_POW: o = M::pow(a, b); da = b * M::pow(a, b - T(1)); db = o * M::log(a); break;
+        case OP_POWABS: {
+            T aa = M::fabs(a);
+            o = M::pow(aa, b);
+            da = b * M::pow(aa, b - T(1)) * sign0(a);
+            db = o * M::log(aa);
+            break;
+        }
+        case OP_MAX:
+            o = (a != a || b != b) ? a + b : (a >= b ? a : b);
+            da = (a >= b) ? T(1) : T(0); db = T(1) - da; break;
+        case OP_MIN:
+            o = (a != a || b != b) ? a + b : (a <= b ? a : b);
+            da = (a <= b) ? T(1) : T(0); db = T(1) - da; break;
+        case OP_LT: o = (a < b) ? T(1) : T(0); da = T(0); db = T(0); break;
+        case OP_GT: o = (a > b) ? T(1) : T(0); da = T(0); db = T(0); break;
+        case OP_LE: o = (a <= b) ? T(1) : T(0); da = T(0); db = T(0); break;
+        case OP_GE: o = (a >= b) ? T(1) : T(0); da = T(0); db = T(0); break;
+        default: o = T(0); da = T(0); db = T(0); break;
+    }
+}
+
+// Tape slots an instruction writes in the forward sweep (read back in the reverse sweep).
+//   unary                      : d            (NEG, UZERO: none)
+//   MUL  VAR / CONST / POP     : - / [ds] / [dt, ds]   (dt of VAR/CONST is the operand)
+//   DIV, POW, POWABS           : [dt] (+ [ds] for CONST / POP)
+//   MAX, MIN                   : [dt]   (ds = 1 - dt)
+//   ADD, SUB, comparisons, zero: none
+CUSR_HD int tape_slots(uint32_t op, uint32_t mode) {
+    if (op == OP_LOAD) return 0;
+    if (op < OP_ADD) return (op == OP_NEG || op == OP_UZERO) ? 0 : 1;
+    switch (op) {
+        case OP_MUL: return mode == M_VAR ? 0 : (mode == M_CONST ? 1 : 2);
+        case OP_DIV: case OP_POW: case OP_POWABS: return mode == M_VAR ? 1 : 2;
+        case OP_MAX: case OP_MIN: return 1;
+        default: return 0;
+    }
+}
+
+}  // namespace cusr

@@ -1,0 +1,373 @@
+// pack.cpp — validate pop.bin trees, compile them to register-stack programs, and build the
+// cost-binned evaluation schedule.
+#include "pack.h"
+#include "ops.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace cusr {
+
+namespace {
+
+struct Node {
+    int32_t type;     // NodeType
+    int32_t op;       // OP_* for functions
+    int32_t idx;      // var index / const rank for leaves
+    int32_t left = -1, right = -1;
+    int32_t need = 1; // Sethi–Ullman register need
+};
+
+uint32_t map_unary(int fid) {
+    switch (fid) {
+        case F_SIN: return OP_SIN;   case F_COS: return OP_COS;   case F_TAN: return OP_TAN;
+        case F_SINH: return OP_SINH; case F_COSH: return OP_COSH; case F_TANH: return OP_TANH;
+        case F_LOG: return OP_LOG;   case F_LOOSE_LOG: return OP_LOGABS;
+        case F_EXP: return OP_EXP;   case F_INV: return OP_INV;   case F_LOOSE_INV: return OP_INV;
+        case F_NEG: return OP_NEG;   case F_ABS: return OP_ABS;
+        case F_SQRT: return OP_SQRT; case F_LOOSE_SQRT: return OP_SQRTABS;
+        default: return OP_UZERO;    // unknown id: value 0 (lm_core.cuh:82)
+    }
+}
+
+uint32_t map_binary(int fid) {
+    switch (fid) {
+        case F_ADD: return OP_ADD; case F_SUB: return OP_SUB; case F_MUL: return OP_MUL;
+        case F_DIV: return OP_DIV; case F_LOOSE_DIV: return OP_DIV;
+        case F_POW: return OP_POW; case F_LOOSE_POW: return OP_POWABS;
+        case F_MAX: return OP_MAX; case F_MIN: return OP_MIN;
+        case F_LT: return OP_LT;   case F_GT: return OP_GT;
+        case F_LE: return OP_LE;   case F_GE: return OP_GE;
+        default: return OP_BZERO;  // unknown id: value 0 (lm_core.cuh:100)
+    }
+}
+
+struct Gen {
+    const std::vector<Node> &nodes;
+    std::vector<uint32_t> &code;
+    int dep = 0, max_dep = 0, tape = 0;
+    bool overflow = false;
+
+    bool is_leaf(int i) const { return nodes[i].type == NT_VAR || nodes[i].type == NT_CONST; }
+    uint32_t leaf_mode(int i) const { return nodes[i].type == NT_VAR ? M_VAR : M_CONST; }
+
+    uint32_t alloc_tape(uint32_t op, uint32_t mode) {
+        int n = tape_slots(op, mode);
+        int ts = tape;
+        tape += n;
+        if (tape > PROG_MAX_TAPE) overflow = true;
+        return (uint32_t)(n ? ts : 0);
+    }
+
+    void emit_leaf(int i, bool live) {
+        uint32_t sd = 0;
+        if (live) {
+            sd = (uint32_t)dep++;
+            max_dep = std::max(max_dep, dep);
+            if (dep > PROG_MAX_SPILL) overflow = true;
+        }
+        code.push_back(enc(OP_LOAD, leaf_mode(i), 0, live ? 1u : 0u, (uint32_t)nodes[i].idx, sd, 0));
+    }
+
+    // Emit code leaving node i's value in TOS. `live`: TOS holds a value that must survive.
+    void gen(int i, bool live) {
+        const Node &n = nodes[i];
+        if (is_leaf(i)) { emit_leaf(i, live); return; }
+        if (n.type == NT_UFUNC) {
+            gen(n.left, live);
+            uint32_t op = (uint32_t)n.op;
+            uint32_t ts = alloc_tape(op, M_NONE);
+            code.push_back(enc(op, M_NONE, 0, 0, 0, 0, ts));
+            return;
+        }
+        const int L = n.left, R = n.right;
+        const uint32_t op = (uint32_t)n.op;
+        if (is_leaf(R)) {                       // TOS = value(L) OP leaf
+            gen(L, live);
+            uint32_t mode = leaf_mode(R);
+            uint32_t ts = alloc_tape(op, mode);
+            code.push_back(enc(op, mode, 0, 0, (uint32_t)nodes[R].idx, 0, ts));
+            return;
+        }
+        if (is_leaf(L)) {                       // TOS = leaf OP value(R)
+            gen(R, live);
+            uint32_t mode = leaf_mode(L);
+            uint32_t ts = alloc_tape(op, mode);
+            code.push_back(enc(op, mode, 1, 0, (uint32_t)nodes[L].idx, 0, ts));
+            return;
+        }
+        // both children are subtrees: the one with the larger need goes first and is spilled
+        const bool left_first = nodes[L].need >= nodes[R].need;
+        const int first = left_first ? L : R, second = left_first ? R : L;
+        gen(first, live);
+        gen(second, true);
+        --dep;
+        uint32_t ts = alloc_tape(op, M_POP);
+        code.push_back(enc(op, M_POP, left_first ? 1u : 0u, 0, 0, (uint32_t)dep, ts));
+    }
+};
+
+}  // namespace
+
+int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, int K,
+                 int n_vars, std::vector<uint32_t> &code, CompiledTree &ct) {
+    if (n <= 0) return CO_ERR_BADTREE;
+    if (n > CO_MAX_NODES) return CO_ERR_BOUNDS;
+    std::vector<Node> nodes((size_t)n);
+    std::vector<int32_t> st;
+    st.reserve((size_t)n);
+    std::vector<int32_t> seen((size_t)std::max(K, 1), 0);
+    bool unique = true;
+    // Right-to-left scan: the same visiting order as the reference interpreter
+    // (lm_core.cuh:63), building the child links of each function node.
+    for (int i = n - 1; i >= 0; --i) {
+        Node &nd = nodes[(size_t)i];
+        nd.type = nt[i];
+        switch (nt[i]) {
+            case NT_VAR: {
+                int v = (int)nv[i];
+                if (!(nv[i] >= 0.0f) || v < 0 || v >= n_vars || v > CO_MAX_VARS) return CO_ERR_BADTREE;
+                nd.idx = v; nd.need = 1;
+                st.push_back(i);
+                break;
+            }
+            case NT_CONST: {
+                int k = ci[i];
+                if (k < 0 || k >= K) return CO_ERR_BADTREE;
+                nd.idx = k; nd.need = 1;
+                if (seen[(size_t)k]++) unique = false;
+                st.push_back(i);
+                break;
+            }
+            case NT_UFUNC: {
+                if (st.empty()) return CO_ERR_BADTREE;
+                nd.left = st.back(); st.pop_back();
+                nd.op = (int32_t)map_unary((int)nv[i]);
+                nd.need = nodes[(size_t)nd.left].need;
+                st.push_back(i);
+                break;
+            }
+            case NT_BFUNC: {
+                if (st.size() < 2) return CO_ERR_BADTREE;
+                nd.left = st.back(); st.pop_back();    // first child in prefix order = left
+                nd.right = st.back(); st.pop_back();
+                nd.op = (int32_t)map_binary((int)nv[i]);
+                const Node &l = nodes[(size_t)nd.left], &r = nodes[(size_t)nd.right];
+                const bool lleaf = l.type == NT_VAR || l.type == NT_CONST;
+                const bool rleaf = r.type == NT_VAR || r.type == NT_CONST;
+                if (rleaf) nd.need = l.need;
+                else if (lleaf) nd.need = r.need;
+                else nd.need = (l.need == r.need) ? l.need + 1 : std::max(l.need, r.need);
+                st.push_back(i);
+                break;
+            }
+            default:
+                return CO_ERR_BADTREE;
+        }
+    }
+    if (st.size() != 1 || st[0] != 0) return CO_ERR_BADTREE;
+    for (int k = 0; k < K; ++k)
+        if (seen[(size_t)k] != 1) unique = false;
+
+    ct.code_off = (int32_t)code.size();
+    Gen g{nodes, code};
+    g.gen(0, false);
+    if (g.overflow) { code.resize((size_t)ct.code_off); return CO_ERR_BOUNDS; }
+    ct.n_instr = (int32_t)code.size() - ct.code_off;
+    ct.n_nodes = n;
+    ct.K = K;
+    ct.n_spill = g.max_dep;
+    ct.n_tape = g.tape;
+    ct.unique_const = unique;
+    return CO_OK;
+}
+
+int compile_population(const PopHeader *h, const int32_t *nt, const float *nv,
+                       const int32_t *ci, const TreeMeta *metas, PackResult *out) {
+    out->code.clear();
+    out->trees.assign((size_t)h->M_prob, CompiledTree{});
+    out->code.reserve((size_t)h->total_nodes);
+    out->bad_tree = -1;
+    for (int m = 0; m < h->M_prob; ++m) {
+        const TreeMeta &tm = metas[m];
+        if (tm.K < 0 || tm.K > CO_MAX_K) return CO_ERR_BOUNDS;
+        if (tm.n_nodes <= 0 || tm.node_offset < 0 ||
+            (int64_t)tm.node_offset + tm.n_nodes > (int64_t)h->total_nodes ||
+            tm.c_offset < 0 || (int64_t)tm.c_offset + tm.K > (int64_t)h->total_c) {
+            out->bad_tree = m;
+            return CO_ERR_BADTREE;
+        }
+        CompiledTree &ct = out->trees[(size_t)m];
+        int rc = compile_tree(nt + tm.node_offset, nv + tm.node_offset, ci + tm.node_offset,
+                              tm.n_nodes, tm.K, h->n_vars, out->code, ct);
+        if (rc != CO_OK) { out->bad_tree = m; return rc; }
+        out->max_instr = std::max(out->max_instr, ct.n_instr);
+        out->max_spill = std::max(out->max_spill, ct.n_spill);
+        out->max_tape = std::max(out->max_tape, ct.n_tape);
+        out->max_K = std::max(out->max_K, ct.K);
+    }
+    return CO_OK;
+}
+
+int kc_class(int K, bool fp64) {
+    if (fp64) {
+        if (K <= 4) return 4;
+        if (K <= 8) return 8;
+        return 32;
+    }
+    if (K <= 4) return 4;
+    if (K <= 8) return 8;
+    if (K <= 12) return 12;
+    if (K <= 16) return 16;
+    return 32;
+}
+
+void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
+                    bool y_shared, bool fp64, int round, int resident, Schedule *out) {
+    out->bins.clear();
+    out->desc.assign((size_t)M, TreeDesc{});
+    out->round = round;
+    const int64_t rounds_per_tree = (N + round - 1) / round;
+    const int64_t total_rounds = rounds_per_tree * (int64_t)M;
+    int64_t per_item = total_rounds / std::max<int64_t>(1, 8 * (int64_t)resident);
+    per_item = std::min<int64_t>(16, std::max<int64_t>(1, per_item));
+    out->chunk = (int32_t)(per_item * round);
+    const int n_chunks = (int)((N + out->chunk - 1) / out->chunk);
+    const int64_t ldy = ((int64_t)N + round - 1) / round * round;
+
+    const int classes[] = {4, 8, 12, 16, 32};
+    std::vector<int> bin_of_class(33, -1);
+    std::vector<double> cost((size_t)M);
+    int64_t p_off = 0, q_off = 0;
+    for (int m = 0; m < M; ++m) {
+        const CompiledTree &ct = pk.trees[(size_t)m];
+        TreeDesc &d = out->desc[(size_t)m];
+        d.code_off = ct.code_off;
+        d.n_instr = ct.n_instr;
+        d.K = ct.K;
+        d.c_off = metas[m].c_offset;
+        d.y_off = y_shared ? 0 : (int64_t)m * ldy;
+        d.p_off = p_off;
+        d.q_off = q_off;
+        d.n_chunks = n_chunks;
+        d.n_spill = (uint16_t)ct.n_spill;
+        d.n_tape = (uint8_t)ct.n_tape;
+        d.flags = ct.unique_const ? TD_UNIQUE_CONST : 0;
+        const int P = nblock_size(ct.K);
+        p_off += (int64_t)n_chunks * P;
+        q_off += P;
+        // forward + reverse sweep per instruction, plus the normal-equation update
+        cost[(size_t)m] = (double)N * (2.0 * ct.n_instr + 0.5 * ct.K * (ct.K + 1) * 0.25);
+        const int kc = kc_class(ct.K, fp64);
+        if (bin_of_class[(size_t)kc] < 0) {
+            bin_of_class[(size_t)kc] = (int)out->bins.size();
+            out->bins.push_back(Bin{});
+            out->bins.back().kc = kc;
+        }
+        Bin &b = out->bins[(size_t)bin_of_class[(size_t)kc]];
+        b.trees.push_back(m);
+        b.max_instr = std::max(b.max_instr, ct.n_instr);
+        b.max_spill = std::max(b.max_spill, ct.n_spill);
+        b.max_tape = std::max(b.max_tape, ct.n_tape);
+        b.max_items += n_chunks;
+        b.cost += cost[(size_t)m];
+    }
+    (void)classes;
+    // bins in ascending class order; trees inside a bin most expensive first (LPT order)
+    std::sort(out->bins.begin(), out->bins.end(),
+              [](const Bin &a, const Bin &b) { return a.kc < b.kc; });
+    int64_t item_off = 0, tree_off = 0;
+    for (Bin &b : out->bins) {
+        std::stable_sort(b.trees.begin(), b.trees.end(), [&](int32_t x, int32_t y) {
+            return cost[(size_t)x] > cost[(size_t)y];
+        });
+        b.item_off = item_off;
+        b.tree_off = tree_off;
+        item_off += b.max_items;
+        tree_off += (int64_t)b.trees.size();
+    }
+    out->partial_elems = p_off;
+    out->block_elems = q_off;
+    out->total_items = item_off;
+}
+
+double host_eval_program(const uint32_t *code, int n_instr, const double *x, const double *c,
+                         int K, double *grad) {
+    double spill[PROG_MAX_SPILL + 1];
+    double tape[PROG_MAX_TAPE + 2];
+    double tos = 0.0;
+    for (int pc = 0; pc < n_instr; ++pc) {
+        const uint32_t w = code[pc];
+        const uint32_t op = w_op(w), mode = w_mode(w), idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+        if (op == OP_LOAD) {
+            if (w_push(w)) spill[sd] = tos;
+            tos = (mode == M_VAR) ? x[idx] : c[idx];
+        } else if (op < OP_ADD) {
+            double r, d;
+            unary_op<double>(op, tos, r, d);
+            if (tape_slots(op, M_NONE)) tape[ts] = d;
+            tos = r;
+        } else {
+            const double s = (mode == M_VAR) ? x[idx] : (mode == M_CONST ? c[idx] : spill[sd]);
+            const bool sw = w_swap(w);
+            double o, da, db;
+            binary_op<double>(op, sw ? s : tos, sw ? tos : s, o, da, db);
+            const double dt = sw ? db : da, ds = sw ? da : db;
+            switch (op) {
+                case OP_MUL:
+                    if (mode == M_CONST) tape[ts] = ds;
+                    else if (mode == M_POP) { tape[ts] = dt; tape[ts + 1] = ds; }
+                    break;
+                case OP_DIV: case OP_POW: case OP_POWABS:
+                    tape[ts] = dt;
+                    if (mode != M_VAR) tape[ts + 1] = ds;
+                    break;
+                case OP_MAX: case OP_MIN: tape[ts] = dt; break;
+                default: break;
+            }
+            tos = o;
+        }
+    }
+    const double value = tos;
+    if (!grad) return value;
+    for (int k = 0; k < K; ++k) grad[k] = 0.0;
+    double adj = 1.0;
+    for (int pc = n_instr - 1; pc >= 0; --pc) {
+        const uint32_t w = code[pc];
+        const uint32_t op = w_op(w), mode = w_mode(w), idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+        if (op == OP_LOAD) {
+            if (mode == M_CONST) grad[idx] += adj;
+            if (w_push(w)) adj = spill[sd];
+            continue;
+        }
+        if (op < OP_ADD) {
+            if (op == OP_NEG) adj = -adj;
+            else if (op == OP_UZERO) adj = 0.0;
+            else adj = safe_mul(adj, tape[ts]);
+            continue;
+        }
+        const bool sw = w_swap(w);
+        double dt, ds;
+        switch (op) {
+            case OP_ADD: dt = 1.0; ds = 1.0; break;
+            case OP_SUB: dt = sw ? -1.0 : 1.0; ds = -dt; break;
+            case OP_MUL:
+                if (mode == M_VAR) { dt = x[idx]; ds = 0.0; }
+                else if (mode == M_CONST) { dt = c[idx]; ds = tape[ts]; }
+                else { dt = tape[ts]; ds = tape[ts + 1]; }
+                break;
+            case OP_DIV: case OP_POW: case OP_POWABS:
+                dt = tape[ts]; ds = (mode == M_VAR) ? 0.0 : tape[ts + 1]; break;
+            case OP_MAX: case OP_MIN: dt = tape[ts]; ds = 1.0 - dt; break;
+            default: dt = 0.0; ds = 0.0; break;
+        }
+        const double as = safe_mul(adj, ds);
+        adj = safe_mul(adj, dt);
+        if (mode == M_POP) spill[sd] = as;
+        else if (mode == M_CONST) grad[idx] += as;
+    }
+    return value;
+}
+
+}  // namespace cusr

@@ -1,0 +1,185 @@
+/* cusr_co.h — C ABI of the cusr-b200 batched Levenberg–Marquardt constant-fitting engine.
+ *
+ * One shared library, libcusr_b200.so (also installed under the names the CuSR loader
+ * expects, libcusr_co_ad.so / libcusr_co_fd.so), exports:
+ *
+ *   - the four entry points of the reference in-process drop-in, with identical
+ *     signatures, argument meaning and return codes, so the reference's ctypes loader
+ *     binds this library unchanged:
+ *         co_init        replaces cusr/kernel/co_lib.h:45   (co_lib.cu:165-183)
+ *         co_optimize    replaces cusr/kernel/co_lib.h:56-63 (co_lib.cu:188-521)
+ *         co_last_split  replaces cusr/kernel/co_lib.h:70    (co_lib.cu:531-541)
+ *         co_teardown    replaces cusr/kernel/co_lib.h:73    (co_lib.cu:549-568)
+ *   - co_optimize_ex / co_get_stats: the extended entry (precision, shared targets,
+ *     damping / tolerance knobs, fp64 outputs, per-tree iteration counts, timings).
+ *
+ * pop.bin structures (PopHeader 64 B, TreeMeta 16 B) keep the byte layout of
+ * cusr/kernel/pop_format.h:32-51 because the file format and the ABI carry them.
+ *
+ * All pointers are HOST pointers, borrowed for the duration of the call; outputs are
+ * caller-allocated. Calls are synchronous. A handle is bound to one device and is not
+ * re-entrant (one call at a time per handle). No entry point ever exits the process.
+ */
+#ifndef CUSR_CO_H
+#define CUSR_CO_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define POP_MAGIC   0x4D4C344D   /* 'M' '4' 'L' 'M' little-endian */
+#define POP_VERSION 1
+
+/* 64-byte population header (pop_format.h:32-43). */
+typedef struct PopHeader {
+    int32_t magic;
+    int32_t version;
+    int32_t M_prob;        /* number of trees                              */
+    int32_t total_nodes;   /* sum of n_nodes                               */
+    int32_t total_c;       /* sum of K                                     */
+    int32_t N;             /* samples                                      */
+    int32_t n_vars;        /* input variables                              */
+    int32_t K_max;         /* max K over trees                             */
+    int32_t max_stack;     /* max evaluation-stack depth                   */
+    int32_t reserved[7];
+} PopHeader;
+
+/* 16-byte per-tree record (pop_format.h:45-51). */
+typedef struct TreeMeta {
+    int32_t node_offset;
+    int32_t n_nodes;
+    int32_t c_offset;
+    int32_t K;
+} TreeMeta;
+
+/* Return codes (co_lib.h:35-41, plus -6 for malformed bytecode). */
+#define CO_OK              0
+#define CO_ERR_BOUNDS      2   /* K_max > 32, max_stack > 64, or beyond an engine limit */
+#define CO_ERR_CUDA       -1   /* a CUDA runtime call failed                            */
+#define CO_ERR_SUM_C      -2   /* sum(K) != header.total_c                              */
+#define CO_ERR_SUM_NODES  -3   /* sum(n_nodes) != header.total_nodes                    */
+#define CO_ERR_NULLARG    -4   /* null pointer / bad argument                           */
+#define CO_ERR_OOM        -5   /* device or host allocation failed                      */
+#define CO_ERR_BADTREE    -6   /* malformed tree: unknown node type, stack underflow,
+                                  var index >= n_vars, const rank outside [0,K)          */
+
+/* Per-tree status written to status_out (lm_core.cuh:46-56). */
+#define STATUS_CONVERGED      0
+#define STATUS_MAXITER        1
+#define STATUS_FAIL_NAN       2
+#define STATUS_K0_SKIP        3
+#define STATUS_FAIL_CHOLESKY  4
+
+/* Engine limits (the reference's are K<=32, stack<=64, nodes<=128). */
+#define CO_MAX_K        32
+#define CO_MAX_STACK    64    /* header.max_stack bound, as in the reference          */
+#define CO_MAX_NODES    1023  /* per tree                                              */
+#define CO_MAX_VARS     255
+
+/* ---- reference-compatible entry points ------------------------------------------ */
+
+/* Bind device `device_id`, create its primary context once, return an opaque handle.
+ * 0 OK; CO_ERR_NULLARG if handle_out is NULL; CO_ERR_CUDA if the device is unusable. */
+int  co_init(int device_id, void **handle_out);
+
+/* One batched LM fit (fp32 arithmetic, like the reference AD variant) of the population
+ * described by `header` and the arrays that follow (pop.bin layout). `ym` is [M_prob][N];
+ * rows that are all identical are detected and kept once on the device.
+ * Outputs: c_final_out[total_c], status_out[M_prob], loss_init_out[M_prob] and
+ * loss_final_out[M_prob] (both 0.5*sum(r^2); either may be NULL).
+ * Every call starts from c_init (no state carries over between calls). */
+int  co_optimize(void *handle, const PopHeader *header,
+                 const int32_t *nt, const float *nv, const int32_t *ci,
+                 const TreeMeta *metas,
+                 const float *c_init, const float *xs, const float *ym,
+                 int max_iter,
+                 float *c_final_out, int32_t *status_out,
+                 float *loss_init_out, float *loss_final_out);
+
+/* Setup / loop wall-clock split (ms) of the last co_optimize* call in this process.
+ * Always returns 0 and fills both (the engine always times its phases). */
+int  co_last_split(double *setup_ms_out, double *loop_ms_out);
+
+/* Free every device and host buffer of the handle. Safe on NULL. */
+void co_teardown(void *handle);
+
+/* ---- extended entry ---------------------------------------------------------------- */
+
+#define CO_PREC_FP32 0
+#define CO_PREC_FP64 1
+
+typedef struct CoOptions {
+    int32_t struct_size;    /* sizeof(CoOptions); lets the struct grow compatibly      */
+    int32_t precision;      /* CO_PREC_FP32 (default) or CO_PREC_FP64                  */
+    int32_t max_iter;       /* LM iterations (reference default 50)                    */
+    int32_t y_shared;       /* 1: ym points at ONE row of N targets shared by all trees;
+                               0: ym is [M_prob][N] (identical rows are still detected) */
+    double  lambda0;        /* initial Marquardt damping (reference 1e-3)              */
+    double  xtol;           /* step test |d| < xtol(|c_try| + xtol) (reference 1e-6)    */
+    int32_t fp64_audit;     /* -1 auto (on for fp32, off for fp64), 0 off, 1 on        */
+    int32_t early_exit;     /* 1 (default): stop launching once every tree is finished */
+    int32_t reserved[8];
+} CoOptions;
+
+/* Fill `opt` with the reference defaults (fp32, 50 iterations, lambda0 1e-3, xtol 1e-6,
+ * audit auto, early exit on). */
+void co_default_options(CoOptions *opt);
+
+/* Extended fit. Same inputs as co_optimize (ym may be a single shared row, see
+ * CoOptions.y_shared); outputs are fp64 so fp64 fits lose nothing. iters_out[M_prob]
+ * (may be NULL) receives the LM iterations each tree consumed. */
+int  co_optimize_ex(void *handle, const PopHeader *header,
+                    const int32_t *nt, const float *nv, const int32_t *ci,
+                    const TreeMeta *metas,
+                    const float *c_init, const float *xs, const float *ym,
+                    const CoOptions *opt,
+                    double *c_final_out, int32_t *status_out,
+                    double *loss_init_out, double *loss_final_out,
+                    int32_t *iters_out);
+
+typedef struct CoStats {
+    double  setup_ms;       /* entry .. first LM iteration (pack, H2D, initial pass)   */
+    double  loop_ms;        /* LM iterations                                            */
+    double  finish_ms;      /* audit + D2H                                              */
+    double  eval_ms;        /* device time of the fused evaluation kernels (events)     */
+    double  step_ms;        /* device time of the per-tree LM step kernels (events)     */
+    int64_t node_evals;     /* sum_m n_nodes(m) * N * (1 + evaluated trials of m)       */
+    int64_t sample_evals;   /* sum_m N * (1 + evaluated trials of m)                    */
+    int64_t eval_launches;  /* fused evaluation kernel launches                         */
+    int64_t kernel_launches;/* all kernel launches of the call                          */
+    int32_t iters_run;      /* LM iterations launched                                   */
+    int32_t n_bins;         /* scheduler bins used                                      */
+    int32_t y_shared;       /* 1 if targets were kept as one shared row                 */
+    int32_t precision;      /* CO_PREC_* of the call                                    */
+    int32_t n_reverted;     /* trees reverted to c_init by the fp64 audit               */
+    int32_t reserved[7];
+} CoStats;
+
+/* Statistics of the last co_optimize* call on `handle`. */
+int  co_get_stats(void *handle, CoStats *out);
+
+/* Evaluate every tree at the constants c[total_c] (fp64 in; computed in `precision`) and
+ * return any of (NULL skips an output):
+ *   vals_out   [M_prob][N]        tree value at each sample
+ *   jac_out    [M_prob][K_max][N] df/dc_k at each sample (the reference d_J layout,
+ *                                 cusr/kernel/ad_interp.cuh:240-244; rows k >= K stay 0)
+ *   blocks_out per tree in tree order, (K+1)(K+2)/2 values: JtJ lower triangle packed
+ *              row-major, Jtr, 0.5*sum r^2 (r = f - y)
+ * This is the same fused device pass the fit runs every iteration (no counterpart entry in
+ * the reference, whose eval_kernel_batched / *_jacobian_kernel are internal). */
+int  co_evaluate(void *handle, const PopHeader *header,
+                 const int32_t *nt, const float *nv, const int32_t *ci,
+                 const TreeMeta *metas, const double *c, const float *xs, const float *ym,
+                 int precision, int y_shared,
+                 double *vals_out, double *jac_out, double *blocks_out);
+
+/* Human-readable message for a return code (static storage). */
+const char *co_strerror(int code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUSR_CO_H */
