@@ -84,8 +84,8 @@ class CoStats(ctypes.Structure):
     _fields_ = [
         ("setup_ms", ctypes.c_double), ("loop_ms", ctypes.c_double),
         ("finish_ms", ctypes.c_double), ("eval_ms", ctypes.c_double),
-        ("step_ms", ctypes.c_double),
-        ("node_evals", ctypes.c_int64), ("sample_evals", ctypes.c_int64),
+        ("step_ms", ctypes.c_double), ("device_ms", ctypes.c_double),
+        ("flops", ctypes.c_double), ("node_evals", ctypes.c_int64), ("sample_evals", ctypes.c_int64),
         ("eval_launches", ctypes.c_int64), ("kernel_launches", ctypes.c_int64),
         ("iters_run", ctypes.c_int32), ("n_bins", ctypes.c_int32),
         ("y_shared", ctypes.c_int32), ("precision", ctypes.c_int32),
@@ -118,6 +118,13 @@ SIGNATURES = {
                         ctypes.POINTER(CoOptions), _F64, _I32, _F64, _F64, _I32], ctypes.c_int),
     "co_get_stats": ([ctypes.c_void_p, ctypes.POINTER(CoStats)], ctypes.c_int),
     "co_strerror": ([ctypes.c_int], ctypes.c_char_p),
+    "co_probe_peak": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_double),
+                       ctypes.POINTER(ctypes.c_double)], ctypes.c_int),
+    "co_load": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
+                 ctypes.POINTER(TreeMeta), _F32, _F32, _F32, ctypes.POINTER(CoOptions)],
+                ctypes.c_int),
+    "co_fit_loaded": ([ctypes.c_void_p, ctypes.POINTER(CoOptions), _F64, _I32, _F64, _F64, _I32],
+                      ctypes.c_int),
     "co_evaluate": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
                      ctypes.POINTER(TreeMeta), _F64, _F32, _F32, ctypes.c_int, ctypes.c_int,
                      _F64, _F64, _F64], ctypes.c_int),
@@ -250,15 +257,7 @@ class InProcessCO:
             y_shared = np.asarray(pop["ym"]).ndim == 1
         hdr = build_header(pop)
         args, keep = self._inputs(pop, y_shared=bool(y_shared))
-        opt = CoOptions()
-        self._lib.co_default_options(ctypes.byref(opt))
-        opt.precision = CO_PREC_FP64 if precision == "fp64" else CO_PREC_FP32
-        opt.max_iter = int(max_iter)
-        opt.y_shared = 1 if y_shared else 0
-        opt.lambda0 = float(lambda0)
-        opt.xtol = float(xtol)
-        opt.fp64_audit = int(fp64_audit)
-        opt.early_exit = 1 if early_exit else 0
+        opt = self._options(max_iter, precision, y_shared, lambda0, xtol, fp64_audit, early_exit)
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)
@@ -272,6 +271,51 @@ class InProcessCO:
         del keep
         if rc != CO_OK:
             raise COError(rc, "co_optimize_ex")
+        return {"c_final": c_final, "status": status, "loss_init": loss_init,
+                "loss_final": loss_final, "iters": iters}
+
+    def _options(self, max_iter=50, precision="fp32", y_shared=False, lambda0=1e-3, xtol=1e-6,
+                 fp64_audit=-1, early_exit=True) -> CoOptions:
+        opt = CoOptions()
+        self._lib.co_default_options(ctypes.byref(opt))
+        opt.precision = CO_PREC_FP64 if precision == "fp64" else CO_PREC_FP32
+        opt.max_iter = int(max_iter)
+        opt.y_shared = 1 if y_shared else 0
+        opt.lambda0 = float(lambda0)
+        opt.xtol = float(xtol)
+        opt.fp64_audit = int(fp64_audit)
+        opt.early_exit = 1 if early_exit else 0
+        return opt
+
+    def load(self, pop: dict, precision: str = "fp32", y_shared: bool | None = None) -> None:
+        """Upload a population once (co_load); fit it with fit_loaded() any number of times."""
+        if y_shared is None:
+            y_shared = np.asarray(pop["ym"]).ndim == 1
+        hdr = build_header(pop)
+        args, keep = self._inputs(pop, y_shared=bool(y_shared))
+        opt = self._options(precision=precision, y_shared=y_shared)
+        rc = self._lib.co_load(self._handle, ctypes.byref(hdr), *args, ctypes.byref(opt))
+        del keep
+        if rc != CO_OK:
+            raise COError(rc, "co_load")
+        self._loaded = (int(pop["M"]), int(pop["total_c"]), precision)
+
+    def fit_loaded(self, max_iter: int = 50, lambda0: float = 1e-3, xtol: float = 1e-6,
+                   fp64_audit: int = -1, early_exit: bool = True) -> dict:
+        """LM fit of the resident population from its c_init (inputs already in HBM)."""
+        M, total_c, precision = self._loaded
+        opt = self._options(max_iter, precision, False, lambda0, xtol, fp64_audit, early_exit)
+        c_final = np.zeros(total_c, np.float64)
+        status = np.zeros(M, np.int32)
+        loss_init = np.zeros(M, np.float64)
+        loss_final = np.zeros(M, np.float64)
+        iters = np.zeros(M, np.int32)
+        rc = self._lib.co_fit_loaded(
+            self._handle, ctypes.byref(opt), c_final.ctypes.data_as(_F64),
+            status.ctypes.data_as(_I32), loss_init.ctypes.data_as(_F64),
+            loss_final.ctypes.data_as(_F64), iters.ctypes.data_as(_I32))
+        if rc != CO_OK:
+            raise COError(rc, "co_fit_loaded")
         return {"c_final": c_final, "status": status, "loss_init": loss_init,
                 "loss_final": loss_final, "iters": iters}
 
@@ -317,6 +361,14 @@ class InProcessCO:
                 o += n
             out["blocks"] = parts
         return out
+
+    def probe_peak(self) -> tuple[float, float]:
+        """Measured (fp32, fp64) FMA peak of the device in TFLOP/s."""
+        a, b = ctypes.c_double(), ctypes.c_double()
+        rc = self._lib.co_probe_peak(self._handle, ctypes.byref(a), ctypes.byref(b))
+        if rc != CO_OK:
+            raise COError(rc, "co_probe_peak")
+        return a.value, b.value
 
     def stats(self) -> dict:
         st = CoStats()

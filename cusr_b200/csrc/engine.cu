@@ -41,13 +41,22 @@ struct DBuf {
     size_t cap = 0;
 };
 
+// Host + device state of one prepared problem (compiled programs, schedule, inputs on the
+// device). Shared by the fit and the evaluation entry points.
+struct Prep {
+    PackResult pk;
+    Schedule sc;
+    int64_t ldx = 0, y_rows = 0;
+    bool y_shared = false;
+};
+
 struct Ctx {
     int device = -1;
     int sm_count = 0;
     cudaStream_t stream = nullptr;
     DBuf code, desc, bin_trees, bin_tree_off, bin_item_off, items, n_items, counter;
     DBuf xs_raw, xs, ym;
-    DBuf c, ctry, delta, cinit_f, lam, loss, loss_init, status, iters, pending, n_run;
+    DBuf c, ctry, delta, cinit_f, lam, loss, loss_init, status, iters, pending, n_run, n_eval;
     DBuf partials, blk;
     DBuf c64, l64, n_rev;
     DBuf vals, jac;
@@ -55,6 +64,14 @@ struct Ctx {
     std::vector<cudaEvent_t> events;        // timing events, reused across calls
     cudaEvent_t ev_nrun[2] = {nullptr, nullptr};
     bool step_attr_set[2] = {false, false};
+    int smem_optin = 0;
+    cudaEvent_t ev_fit[2] = {nullptr, nullptr};
+    // resident problem (co_load / co_fit_loaded and every fit)
+    Prep prep;
+    PopHeader hdr{};
+    std::vector<int32_t> n_nodes, n_ops;
+    int prep_prec = -1;
+    bool loaded = false;
     CoStats stats{};
 };
 
@@ -148,7 +165,7 @@ int check_args(const Problem &pr) {
 // Evaluate the pending trees of every bin at constants `cdev` (one fused launch per bin).
 template <typename T>
 int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cdev, T *partials,
-                const Problem &pr, int64_t ldx, bool grad, T *vals = nullptr, T *jac = nullptr,
+                const PopHeader &hd, int64_t ldx, bool grad, T *vals = nullptr, T *jac = nullptr,
                 int jac_kmax = 0) {
     const int n_bins = (int)sc.bins.size();
     {
@@ -178,9 +195,9 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         p.ym = P<float>(ctx->ym);
         p.partials = partials;
         p.ldx = ldx;
-        p.N = pr.h->N;
+        p.N = hd.N;
         p.chunk = sc.chunk;
-        p.n_vars = pr.h->n_vars;
+        p.n_vars = hd.n_vars;
         p.code_cap = bin.max_instr;
         p.spill_cap = std::max(bin.max_spill, 1);
         p.tape_cap = grad ? std::max(bin.max_tape, 1) : 1;
@@ -189,7 +206,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         p.jac_kmax = jac_kmax;
         const int kc = grad ? bin.kc : 4;
         const size_t smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap);
-        if (smem > 227 * 1024) return CO_ERR_BOUNDS;
+        if (smem + 64 > (size_t)ctx->smem_optin) return CO_ERR_BOUNDS;
         int occ = Launch<T>::occ(kc, grad, smem);
         if (occ < 1) occ = 1;
         int64_t grid = (int64_t)occ * ctx->sm_count;
@@ -201,15 +218,6 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
     (void)pk;
     return CO_OK;
 }
-
-// Host + device state of one prepared problem (compiled programs, schedule, inputs on the
-// device). Shared by the fit and the evaluation entry points.
-struct Prep {
-    PackResult pk;
-    Schedule sc;
-    int64_t ldx = 0, y_rows = 0;
-    bool y_shared = false;
-};
 
 template <typename T>
 int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
@@ -263,6 +271,7 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     GROW(ctx->status, (size_t)M * sizeof(int32_t));
     GROW(ctx->iters, (size_t)M * sizeof(int32_t));
     GROW(ctx->pending, (size_t)M * sizeof(int32_t));
+    GROW(ctx->n_eval, (size_t)M * sizeof(int32_t));
     GROW(ctx->n_run, 2 * sizeof(int));
     GROW(ctx->partials, (size_t)sc.partial_elems * sizeof(T));
     GROW(ctx->blk, (size_t)sc.block_elems * sizeof(T));
@@ -317,34 +326,64 @@ inline int grid_for(Ctx *ctx, int64_t n) {
     return (int)std::max<int64_t>(1, std::min<int64_t>(4 * ctx->sm_count, (n + 255) / 256));
 }
 
+// Compile, schedule and upload a problem; it stays resident in the context until the next
+// load (inputs in HBM across fits).
 template <typename T>
-int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &out) {
-    auto t_entry = std::chrono::steady_clock::now();
-    const PopHeader *h = pr.h;
+int load(Ctx *ctx, const Problem &pr, bool y_shared) {
+    ctx->loaded = false;
+    ctx->stats = CoStats{};
+    ctx->stats.precision = sizeof(T) == 8 ? CO_PREC_FP64 : CO_PREC_FP32;
+    int rc = prepare<T>(ctx, pr, y_shared, ctx->prep);
+    if (rc != CO_OK) return rc;
+    ctx->hdr = *pr.h;
+    ctx->n_nodes.resize((size_t)pr.h->M_prob);
+    ctx->n_ops.resize((size_t)pr.h->M_prob);
+    for (int m = 0; m < pr.h->M_prob; ++m) {
+        const TreeMeta &tm = pr.metas[m];
+        ctx->n_nodes[(size_t)m] = tm.n_nodes;
+        int ops = 0;
+        for (int i = 0; i < tm.n_nodes; ++i) {
+            const int t = pr.nt[tm.node_offset + i];
+            ops += (t == NT_UFUNC || t == NT_BFUNC) ? 1 : 0;
+        }
+        ctx->n_ops[(size_t)m] = ops;
+    }
+    ctx->prep_prec = ctx->stats.precision;
+    ctx->loaded = true;
+    return CO_OK;
+}
+
+// One LM fit of the loaded problem, from its c_init.
+template <typename T>
+int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
+               std::chrono::steady_clock::time_point t_entry) {
+    const PopHeader *h = &ctx->hdr;
     const int M = h->M_prob, N = h->N;
     const int64_t total_c = h->total_c;
     const bool fp64 = sizeof(T) == 8;
     CoStats &st = ctx->stats;
+    const int keep_bins = st.n_bins, keep_ys = st.y_shared;
     st = CoStats{};
+    st.n_bins = keep_bins;
+    st.y_shared = keep_ys;
     st.precision = fp64 ? CO_PREC_FP64 : CO_PREC_FP32;
-
-    Prep pp;
-    int rc = prepare<T>(ctx, pr, opt.y_shared != 0, pp);
-    if (rc != CO_OK) return rc;
     if (M == 0) {
         st.setup_ms = ms_since(t_entry);
         g_last_setup_ms = st.setup_ms;
         g_last_loop_ms = 0.0;
         return CO_OK;
     }
+    int rc = CO_OK;
+    const Prep &pp = ctx->prep;
     const PackResult &pk = pp.pk;
     const Schedule &sc = pp.sc;
     const int64_t ldx = pp.ldx;
     cudaStream_t s = ctx->stream;
+    CK(cudaEventRecord(ctx->ev_fit[0], s));
     init_state_kernel<T><<<grid_for(ctx, std::max<int64_t>(total_c, M)), 256, 0, s>>>(
         P<float>(ctx->cinit_f), total_c, P<T>(ctx->c), P<T>(ctx->ctry), M, (T)opt.lambda0,
         P<T>(ctx->lam), P<int32_t>(ctx->status), P<int32_t>(ctx->iters),
-        P<int32_t>(ctx->pending));
+        P<int32_t>(ctx->pending), P<int32_t>(ctx->n_eval));
     CK(cudaGetLastError());
     st.kernel_launches++;
 
@@ -375,6 +414,7 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
     sp.status = P<int32_t>(ctx->status);
     sp.iters = P<int32_t>(ctx->iters);
     sp.pending = P<int32_t>(ctx->pending);
+    sp.n_eval = P<int32_t>(ctx->n_eval);
     sp.xtol = (T)opt.xtol;
 
     const int max_iter = std::max(0, opt.max_iter);
@@ -388,7 +428,7 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
 
     // ---- initial pass at c_init + solve of iteration 0 ----
     size_t e0 = ev_i; rec();
-    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), pr, ldx, true);
+    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true);
     if (rc) return rc;
     size_t e1 = ev_i; rec();
     sp.n_running = P<int>(ctx->n_run);
@@ -417,7 +457,7 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
         }
         iters_run++;
         size_t a = ev_i; rec();
-        rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), pr, ldx, true);
+        rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true);
         if (rc) return rc;
         size_t b = ev_i; rec();
         sp.n_running = P<int>(ctx->n_run) + slot;
@@ -456,7 +496,7 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
             audit_prepare_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, srcs[pass], total_c,
                                                     c64, P<int32_t>(ctx->pending));
             CK(cudaGetLastError());
-            rc = launch_pass<double>(ctx, sc, pk, c64, P<double>(ctx->partials), pr, ldx, false);
+            rc = launch_pass<double>(ctx, sc, pk, c64, P<double>(ctx->partials), *h, ldx, false);
             if (rc) return rc;
             audit_loss_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M,
                                                   P<double>(ctx->partials), l64 + pass * M);
@@ -474,17 +514,24 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
 
     // ---- D2H ----
     std::vector<T> hc((size_t)total_c), hli((size_t)M), hlf((size_t)M);
-    std::vector<int32_t> hst((size_t)M), hit((size_t)M);
+    std::vector<int32_t> hst((size_t)M), hit((size_t)M), hne((size_t)M);
     if (total_c > 0)
         CK(cudaMemcpyAsync(hc.data(), ctx->c.ptr, total_c * sizeof(T), cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(hli.data(), ctx->loss_init.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(hlf.data(), ctx->loss.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(hst.data(), ctx->status.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(hit.data(), ctx->iters.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hne.data(), ctx->n_eval.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     int n_rev = 0;
     if (audit)
         CK(cudaMemcpyAsync(&n_rev, ctx->n_rev.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaEventRecord(ctx->ev_fit[1], s));
     CK(cudaStreamSynchronize(s));
+    {
+        float dms = 0.f;
+        if (cudaEventElapsedTime(&dms, ctx->ev_fit[0], ctx->ev_fit[1]) == cudaSuccess)
+            st.device_ms = dms;
+    }
     st.n_reverted = n_rev;
 
     for (int64_t i = 0; i < total_c; ++i) {
@@ -500,13 +547,18 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
         if (out.lf_d) out.lf_d[m] = (double)hlf[(size_t)m];
         if (out.iters) out.iters[m] = hit[(size_t)m];
     }
-    // node / sample evaluation counts: one initial evaluation plus each evaluated trial
+    // evaluation counts: initial pass + every evaluated trial, per tree
     int64_t node_evals = 0, sample_evals = 0;
+    double flops = 0.0;
     for (int m = 0; m < M; ++m) {
-        const int64_t evals = 1 + (int64_t)hit[(size_t)m];
-        node_evals += evals * pr.metas[m].n_nodes * (int64_t)N;
+        const int64_t evals = hne[(size_t)m];
+        const int K = (int)(h->M_prob ? pk.trees[(size_t)m].K : 0);
+        node_evals += evals * ctx->n_nodes[(size_t)m] * (int64_t)N;
         sample_evals += evals * (int64_t)N;
+        // value + adjoint per operator node, plus the normal-equation update
+        flops += (double)evals * N * (2.0 * ctx->n_ops[(size_t)m] + 2.0 * nblock_size(K));
     }
+    st.flops = flops;
     st.node_evals = node_evals;
     st.sample_evals = sample_evals;
 
@@ -530,6 +582,14 @@ int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &ou
     return CO_OK;
 }
 
+template <typename T>
+int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &out) {
+    auto t_entry = std::chrono::steady_clock::now();
+    int rc = load<T>(ctx, pr, opt.y_shared != 0);
+    if (rc != CO_OK) return rc;
+    return fit_loaded<T>(ctx, opt, out, t_entry);
+}
+
 // Evaluate every tree at given constants: values, Jacobian, normal-equation blocks.
 template <typename T>
 int run_eval(Ctx *ctx, const Problem &pr, bool y_shared, const double *c, double *vals_out,
@@ -540,6 +600,7 @@ int run_eval(Ctx *ctx, const Problem &pr, bool y_shared, const double *c, double
     ctx->stats = CoStats{};
     ctx->stats.precision = sizeof(T) == 8 ? CO_PREC_FP64 : CO_PREC_FP32;
     Prep pp;
+    ctx->loaded = false;   // the evaluation reuses the resident buffers
     int rc = prepare<T>(ctx, pr, y_shared, pp);
     if (rc != CO_OK) return rc;
     if (M == 0) return CO_OK;
@@ -562,8 +623,8 @@ int run_eval(Ctx *ctx, const Problem &pr, bool y_shared, const double *c, double
         dj = P<T>(ctx->jac);
         CK(cudaMemsetAsync(dj, 0, (size_t)M * kmax * N * sizeof(T), s));
     }
-    rc = launch_pass<T>(ctx, pp.sc, pp.pk, P<T>(ctx->ctry), P<T>(ctx->partials), pr, pp.ldx, true,
-                        dv, dj, kmax);
+    rc = launch_pass<T>(ctx, pp.sc, pp.pk, P<T>(ctx->ctry), P<T>(ctx->partials), *pr.h, pp.ldx,
+                        true, dv, dj, kmax);
     if (rc) return rc;
     sum_blocks_kernel<T><<<grid_for(ctx, M), 256, 0, s>>>(P<TreeDesc>(ctx->desc), M,
                                                            P<T>(ctx->partials), P<T>(ctx->blk));
@@ -627,17 +688,30 @@ int co_init(int device_id, void **handle_out) {
     Ctx *ctx = new (std::nothrow) Ctx();
     if (!ctx) return CO_ERR_OOM;
     ctx->device = device_id;
-    if (cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device_id) !=
-            cudaSuccess ||
-        cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMallocHost(&ctx->h_nrun, 2 * sizeof(int)) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ctx->ev_nrun[0], cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ctx->ev_nrun[1], cudaEventDisableTiming) != cudaSuccess ||
-        eval_prepare_f32() != cudaSuccess || eval_prepare_f64() != cudaSuccess) {
-        fprintf(stderr, "[cusr_b200] device %d setup failed\n", device_id);
-        co_teardown(ctx);
-        return CO_ERR_CUDA;
+    struct Step { const char *what; cudaError_t e; };
+    int optin = 0;
+    Step steps[] = {
+        {"sm count", cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device_id)},
+        {"smem opt-in", cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device_id)},
+        {"stream", cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking)},
+        {"pinned counter", cudaMallocHost(&ctx->h_nrun, 2 * sizeof(int))},
+        {"event 0", cudaEventCreateWithFlags(&ctx->ev_nrun[0], cudaEventDisableTiming)},
+        {"event 1", cudaEventCreateWithFlags(&ctx->ev_nrun[1], cudaEventDisableTiming)},
+        {"fit event 0", cudaEventCreate(&ctx->ev_fit[0])},
+        {"fit event 1", cudaEventCreate(&ctx->ev_fit[1])},
+        {"fp32 kernels", eval_prepare_f32()},
+        {"fp64 kernels", eval_prepare_f64()},
+    };
+    for (const Step &st : steps) {
+        if (st.e != cudaSuccess) {
+            fprintf(stderr, "[cusr_b200] device %d setup (%s): %s\n", device_id, st.what,
+                    cudaGetErrorString(st.e));
+            cudaGetLastError();
+            co_teardown(ctx);
+            return CO_ERR_CUDA;
+        }
     }
+    ctx->smem_optin = optin;
     *handle_out = ctx;
     return CO_OK;
 }
@@ -720,6 +794,81 @@ int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float
     return run_eval<float>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
 }
 
+int co_load(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+            const int32_t *ci, const TreeMeta *metas, const float *c_init, const float *xs,
+            const float *ym, const CoOptions *opt_in) {
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym)
+        return CO_ERR_NULLARG;
+    CoOptions opt;
+    co_default_options(&opt);
+    if (opt_in) opt = *opt_in;
+    if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    Problem pr{h, nt, nv, ci, metas, c_init, xs, ym};
+    int rc = check_args(pr);
+    if (rc != CO_OK) return rc;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    rc = opt.precision == CO_PREC_FP64 ? load<double>(ctx, pr, opt.y_shared != 0)
+                                       : load<float>(ctx, pr, opt.y_shared != 0);
+    if (rc == CO_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess) return CO_ERR_CUDA;
+    return rc;
+}
+
+int co_fit_loaded(void *handle, const CoOptions *opt_in, double *c_final_out,
+                  int32_t *status_out, double *loss_init_out, double *loss_final_out,
+                  int32_t *iters_out) {
+    if (!handle || !c_final_out || !status_out) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    CoOptions opt;
+    co_default_options(&opt);
+    if (opt_in) opt = *opt_in;
+    if (!ctx->loaded || opt.precision != ctx->prep_prec) return CO_ERR_NULLARG;
+    if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    Outputs out;
+    out.c_d = c_final_out;
+    out.status = status_out;
+    out.li_d = loss_init_out;
+    out.lf_d = loss_final_out;
+    out.iters = iters_out;
+    auto t0 = std::chrono::steady_clock::now();
+    return opt.precision == CO_PREC_FP64 ? fit_loaded<double>(ctx, opt, out, t0)
+                                         : fit_loaded<float>(ctx, opt, out, t0);
+}
+
+int co_probe_peak(void *handle, double *fp32_tflops, double *fp64_tflops) {
+    if (!handle) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    GROW(ctx->c64, 64);
+    cudaStream_t s = ctx->stream;
+    const int blocks = ctx->sm_count * 8, threads = 256, iters = 8192;
+    const double fmas = (double)blocks * threads * iters * 16;
+    cudaEvent_t e0 = event_at(ctx, 0), e1 = event_at(ctx, 1);
+    for (int prec = 0; prec < 2; ++prec) {
+        double best = 0.0;
+        for (int rep = 0; rep < 3; ++rep) {
+            CK(cudaEventRecord(e0, s));
+            if (prec == 0)
+                fma_probe_kernel<float><<<blocks, threads, 0, s>>>(P<float>(ctx->c64), iters,
+                                                                  0.999f, 0.001f);
+            else
+                fma_probe_kernel<double><<<blocks, threads, 0, s>>>(P<double>(ctx->c64), iters / 4,
+                                                                   0.999, 0.001);
+            CK(cudaGetLastError());
+            CK(cudaEventRecord(e1, s));
+            CK(cudaEventSynchronize(e1));
+            float ms = 0.f;
+            CK(cudaEventElapsedTime(&ms, e0, e1));
+            const double tf = 2.0 * fmas / (prec == 0 ? 1.0 : 4.0) / (ms * 1e-3) / 1e12;
+            best = std::max(best, tf);
+        }
+        if (prec == 0 && fp32_tflops) *fp32_tflops = best;
+        if (prec == 1 && fp64_tflops) *fp64_tflops = best;
+    }
+    return CO_OK;
+}
+
 int co_last_split(double *setup_ms_out, double *loop_ms_out) {
     if (setup_ms_out) *setup_ms_out = g_last_setup_ms;
     if (loop_ms_out) *loop_ms_out = g_last_loop_ms;
@@ -740,11 +889,13 @@ void co_teardown(void *handle) {
                     &ctx->bin_item_off, &ctx->items, &ctx->n_items, &ctx->counter,
                     &ctx->xs_raw, &ctx->xs, &ctx->ym, &ctx->c, &ctx->ctry, &ctx->delta,
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
-                    &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->partials, &ctx->blk,
+                    &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
                     &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac};
     for (DBuf *b : bufs) release(*b);
     for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->ev_nrun)
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->ev_fit)
         if (e) cudaEventDestroy(e);
     if (ctx->h_nrun) cudaFreeHost(ctx->h_nrun);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);

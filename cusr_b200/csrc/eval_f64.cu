@@ -5,7 +5,6 @@
 namespace cusr {
 
 namespace {
-constexpr int kMaxDynSmem = 227 * 1024;
 
 template <int KC, bool G>
 cudaError_t one(const EvalParams<double> &p, int grid, size_t smem, cudaStream_t s) {
@@ -19,9 +18,18 @@ template <int KC, bool G> int occ(size_t smem) {
         return 0;
     return n;
 }
+// dynamic shared memory limit = the device's opt-in maximum minus the kernel's static part
 template <int KC, bool G> cudaError_t prep() {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess)
+        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<double, EVAL_V, KC, G>);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(lm_eval_kernel<double, EVAL_V, KC, G>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                optin - (int)fa.sharedSizeBytes);
 }
 }  // namespace
 

@@ -27,6 +27,7 @@ struct StepParams {
     int32_t *status;
     int32_t *iters;
     int32_t *pending;        // 1: the tree's trial was evaluated by the last pass
+    int32_t *n_eval;         // evaluations consumed per tree (initial pass + trials)
     int *n_running;          // trees still running after this step (early exit)
     int initial;             // the evaluated point is c_init
     int do_solve;            // solve a new step for every running tree
@@ -76,6 +77,7 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
             T lam = p.lam[m];
             if (pend) {
                 p.pending[m] = 0;
+                p.n_eval[m] += 1;
                 const T ltry = T(0.5) * sums[P - 1];
                 if (p.initial) {
                     p.loss_init[m] = ltry;
@@ -254,7 +256,7 @@ __global__ void transpose_x_kernel(const float *__restrict__ xs, int64_t N, int 
 template <typename T>
 __global__ void init_state_kernel(const float *__restrict__ c_init, int64_t total_c, T *c,
                                   T *ctry, int M, T lam0, T *lam, int32_t *status,
-                                  int32_t *iters, int32_t *pending) {
+                                  int32_t *iters, int32_t *pending, int32_t *n_eval) {
     const int64_t gs = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_c; i += gs) {
         c[i] = (T)c_init[i];
@@ -265,6 +267,7 @@ __global__ void init_state_kernel(const float *__restrict__ c_init, int64_t tota
         status[m] = ST_RUNNING;
         iters[m] = 0;
         pending[m] = 1;
+        n_eval[m] = 0;
     }
 }
 
@@ -291,6 +294,22 @@ __global__ void sum_blocks_kernel(const TreeDesc *desc, int M, const T *partials
             blk[d.q_off + e] = (e == P - 1) ? T(0.5) * s : s;
         }
     }
+}
+
+// Peak-throughput probes: independent FMA chains per thread (no memory traffic in the loop).
+template <typename T>
+__global__ void fma_probe_kernel(T *out, int iters, T b, T c) {
+    T a[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = (T)(threadIdx.x + i);
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a[i] = a[i] * b + c;
+    }
+    T s = T(0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) s += a[i];
+    if (s == T(-1.2345)) out[0] = s;   // keeps the chains alive
 }
 
 // ---- fp64 honesty audit (lm_core.cuh:299-351) -------------------------------------------

@@ -145,6 +145,10 @@ typedef struct CoStats {
     double  finish_ms;      /* audit + D2H                                              */
     double  eval_ms;        /* device time of the fused evaluation kernels (events)     */
     double  step_ms;        /* device time of the per-tree LM step kernels (events)     */
+    double  device_ms;      /* device time of the whole fit: init .. last D2H (events)  */
+    double  flops;          /* algorithmic FP work: per evaluated (tree, sample) 2 flops per
+                               operator node (value + adjoint) + 2 per normal-equation
+                               entry ((K+1)(K+2)/2)                                      */
     int64_t node_evals;     /* sum_m n_nodes(m) * N * (1 + evaluated trials of m)       */
     int64_t sample_evals;   /* sum_m N * (1 + evaluated trials of m)                    */
     int64_t eval_launches;  /* fused evaluation kernel launches                         */
@@ -157,7 +161,23 @@ typedef struct CoStats {
     int32_t reserved[7];
 } CoStats;
 
-/* Statistics of the last co_optimize* call on `handle`. */
+/* Resident problem: co_load compiles, schedules and uploads a population (programs,
+ * inputs, targets, c_init) into the handle's device buffers in the given precision;
+ * co_fit_loaded then runs a complete LM fit from the loaded c_init with every input
+ * already in HBM, as often as needed (the next co_load / co_optimize* / co_evaluate call
+ * replaces the resident problem). opt->precision must match the loaded precision;
+ * opt->y_shared applies to co_load. Outputs as co_optimize_ex. */
+int  co_load(void *handle, const PopHeader *header,
+             const int32_t *nt, const float *nv, const int32_t *ci,
+             const TreeMeta *metas,
+             const float *c_init, const float *xs, const float *ym,
+             const CoOptions *opt);
+int  co_fit_loaded(void *handle, const CoOptions *opt,
+                   double *c_final_out, int32_t *status_out,
+                   double *loss_init_out, double *loss_final_out,
+                   int32_t *iters_out);
+
+/* Statistics of the last co_optimize* / co_fit_loaded call on `handle`. */
 int  co_get_stats(void *handle, CoStats *out);
 
 /* Evaluate every tree at the constants c[total_c] (fp64 in; computed in `precision`) and
@@ -174,6 +194,10 @@ int  co_evaluate(void *handle, const PopHeader *header,
                  const TreeMeta *metas, const double *c, const float *xs, const float *ym,
                  int precision, int y_shared,
                  double *vals_out, double *jac_out, double *blocks_out);
+
+/* Measured FMA throughput of the bound device (independent FMA chains, no memory traffic):
+ * the FP32 / FP64 non-tensor peak the engine's roofline is reported against. */
+int  co_probe_peak(void *handle, double *fp32_tflops, double *fp64_tflops);
 
 /* Human-readable message for a return code (static storage). */
 const char *co_strerror(int code);

@@ -54,32 +54,58 @@ def _payloads(pop: dict, trees):
         yield (int(m), nt, nv, ci, pop["xs"], y, pop["c_init"][c_off:c_off + K])
 
 
-def fit_pop(pop: dict, nproc: int | None = None, trees=None) -> dict:
-    """Fit the trees `trees` (default all) of a pop; returns fp64 c_final over the whole pop
-    (unfitted trees keep c_init), status / nfev per tree, wall seconds and cores used."""
-    M = int(pop["M"])
-    trees = np.arange(M) if trees is None else np.asarray(trees)
-    c_final = np.asarray(pop["c_init"], np.float64).copy()
-    status = np.full(M, 3, np.int32)
-    nfev = np.zeros(M, np.int32)
-    payloads = list(_payloads(pop, trees))
-    for p in payloads:
-        status[p[0]] = 2
-    nproc = int(nproc or os.cpu_count() or 1)
-    t0 = time.perf_counter()
-    if nproc <= 1 or len(payloads) <= 1:
-        results = map(fit_one, payloads)
-        for m, c, s, nf in results:
+class Pool:
+    """Persistent spawn pool of scipy workers (one process per core), so repeated timed fits
+    do not pay process start-up (the reference keeps its pool alive the same way,
+    backends.py:31-50)."""
+
+    def __init__(self, nproc: int | None = None):
+        self.nproc = int(nproc or os.cpu_count() or 1)
+        self._pool = mp.get_context("spawn").Pool(processes=self.nproc) if self.nproc > 1 else None
+
+    def warm(self) -> None:
+        if self._pool is not None:
+            self._pool.map(_noop, range(self.nproc), chunksize=1)
+
+    def fit_pop(self, pop: dict, trees=None) -> dict:
+        M = int(pop["M"])
+        trees = np.arange(M) if trees is None else np.asarray(trees)
+        c_final = np.asarray(pop["c_init"], np.float64).copy()
+        status = np.full(M, 3, np.int32)
+        nfev = np.zeros(M, np.int32)
+        payloads = list(_payloads(pop, trees))
+        for p in payloads:
+            status[p[0]] = 2
+        t0 = time.perf_counter()
+        it = (self._pool.imap_unordered(fit_one, payloads, chunksize=1)
+              if self._pool is not None and len(payloads) > 1 else map(fit_one, payloads))
+        for m, c, s, nf in it:
             c_off, K = int(pop["metas"][m][2]), int(pop["metas"][m][3])
             c_final[c_off:c_off + K] = c
             status[m], nfev[m] = s, nf
-    else:
-        ctx = mp.get_context("spawn")
-        with ctx.Pool(processes=nproc) as pool:
-            for m, c, s, nf in pool.imap_unordered(fit_one, payloads, chunksize=4):
-                c_off, K = int(pop["metas"][m][2]), int(pop["metas"][m][3])
-                c_final[c_off:c_off + K] = c
-                status[m], nfev[m] = s, nf
-    wall = time.perf_counter() - t0
-    return dict(c_final=c_final, status=status, nfev=nfev, wall=wall, cores=nproc,
-                n_fitted=len(payloads))
+        wall = time.perf_counter() - t0
+        return dict(c_final=c_final, status=status, nfev=nfev, wall=wall, cores=self.nproc,
+                    n_fitted=len(payloads))
+
+    def close(self) -> None:
+        if self._pool is not None:
+            self._pool.terminate()
+            self._pool = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False
+
+
+def _noop(x):
+    return x
+
+
+def fit_pop(pop: dict, nproc: int | None = None, trees=None) -> dict:
+    """Fit the trees `trees` (default all) of a pop; returns fp64 c_final over the whole pop
+    (unfitted trees keep c_init), status / nfev per tree, wall seconds and cores used."""
+    with Pool(nproc) as pool:
+        return pool.fit_pop(pop, trees)
