@@ -218,3 +218,49 @@ def intermediate_scale(nt, nv, ci, xs, c) -> np.ndarray:
             scale = np.fmax(scale, np.abs(v))
             st.append(v)
     return scale
+
+
+def error_scale(nt, nv, ci, xs, c) -> np.ndarray:
+    """First-order rounding-error scale of evaluating the tree at each sample:
+    S = sum over operator nodes n of |d f / d v_n| * |v_n| (fp64, absolute partials).
+    A finite-precision evaluation with unit roundoff u differs from the exact value by about
+    u * S (times a small constant for library transcendentals), however the value itself
+    compares to S; S >> |f| flags an ill-conditioned sample (cancellation, cos(exp(big)))."""
+    xs = np.asarray(xs, np.float64)
+    c = np.asarray(c, np.float64)
+    N = xs.shape[0]
+    n = len(nt)
+    vals: list = [None] * n
+    d1: list = [None] * n
+    d2: list = [None] * n
+    st: list = []
+    with np.errstate(all="ignore"):
+        for i in range(n - 1, -1, -1):
+            t = int(nt[i])
+            if t == NTYPE_VAR:
+                v = xs[:, int(nv[i])]
+            elif t == NTYPE_CONST:
+                v = np.full(N, c[int(ci[i])])
+            elif t == NTYPE_UFUNC:
+                v, d = unary(int(nv[i]), st.pop())
+                d1[i] = np.abs(d)
+            else:
+                l = st.pop()
+                r = st.pop()
+                v, dl, dr = binary(int(nv[i]), l, r)
+                d1[i], d2[i] = np.abs(dl), np.abs(dr)
+            vals[i] = v
+            st.append(v)
+        S = np.zeros(N)
+        adj_st = [np.ones(N)]
+        for i in range(n):
+            t = int(nt[i])
+            adj = adj_st.pop()
+            if t == NTYPE_UFUNC:
+                S = S + np.nan_to_num(adj * np.abs(vals[i]), nan=np.inf)
+                adj_st.append(adj * d1[i])
+            elif t == NTYPE_BFUNC:
+                S = S + np.nan_to_num(adj * np.abs(vals[i]), nan=np.inf)
+                adj_st.append(adj * d2[i])
+                adj_st.append(adj * d1[i])
+    return S

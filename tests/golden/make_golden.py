@@ -1,0 +1,144 @@
+"""Generate the golden fixtures under tests/golden/ from the reference checkout.
+
+Run in a container where the reference (TensorConv/CuSR) is importable:
+
+    CUSR_REFERENCE=<reference checkout> python tests/golden/make_golden.py
+
+Everything written here comes from the reference's own code and files:
+  fixtures.npz / fixtures.json   the reference's known-answer populations
+                                 (cusr/kernel/tests/pop_fixture*.bin) and their truth JSONs
+  pop1000.npz                    data/fixtures/pop.bin (M=1000, N=1000, shared y stored once),
+                                 the reference AD kernel's A100 outputs for it
+                                 (cusr/kernel/tests/golden/ad/pop1000/*.bin), the reference
+                                 fp64 loss of both (cusr/benchmark/interp.loss_pop), and the
+                                 reference scipy fits (cusr.benchmark.backends.ScipyPop)
+  interp_vectors.npz             reference interpreter values (interp.eval_tree_arrays, fp64)
+                                 on PR1-config trees from cusr_b200.synth and on pop1000
+  pr1_scipy.npz                  reference ScipyPop fits of the PR1 configuration (seed 0)
+  jac_sample.npz                 the reference's reverse-AD Jacobian samples
+                                 (experiments/revad_v5/jac_sample_fixed.jsonl)
+The tests read only these files; the reference is not needed at test time.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+REF = Path(os.environ.get("CUSR_REFERENCE", "/root/reference"))
+
+
+def _pop_arrays(prefix: str, pop: dict) -> dict:
+    out = {}
+    for k in ("nt", "nv", "ci", "metas", "c_init", "xs", "ym"):
+        out[f"{prefix}/{k}"] = np.asarray(pop[k])
+    for k in ("M", "total_nodes", "total_c", "N", "n_vars", "K_max", "max_stack"):
+        out[f"{prefix}/{k}"] = np.asarray(int(pop[k]))
+    return out
+
+
+def main() -> None:
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(ROOT))
+    from cusr.benchmark import backends, interp, popio  # reference code
+
+    from cusr_b200 import synth
+
+    kt = REF / "cusr" / "kernel" / "tests"
+    # ---- known-answer fixtures ----
+    arrays, truths = {}, {}
+    names = ["pop_fixture", "pop_fixture_op", "pop_fixture_stress", "pop_fixture_scale_1e-6",
+             "pop_fixture_scale_1e-3", "pop_fixture_scale_1e0", "pop_fixture_scale_1e3",
+             "pop_fixture_scale_1e6"]
+    for name in names:
+        pop = popio.load_pop_bin(kt / f"{name}.bin")
+        arrays.update(_pop_arrays(name, pop))
+        # reference fp64 loss at c_init
+        arrays[f"{name}/loss_init64"] = interp.loss_pop(pop, pop["c_init"].astype(np.float64))
+    for tj in ("pop_fixture_truth.json", "pop_fixture_op_truth.json",
+               "pop_fixture_stress_truth.json", "pop_fixture_scale_truth.json"):
+        truths[tj] = json.loads((kt / tj).read_text())
+    np.savez_compressed(HERE / "fixtures.npz", **arrays)
+    (HERE / "fixtures.json").write_text(json.dumps(truths, indent=1))
+
+    # ---- pop1000 + reference kernel goldens + reference scipy fits ----
+    pop = popio.load_pop_bin(REF / "data" / "fixtures" / "pop.bin")
+    assert np.all(pop["ym"] == pop["ym"][0])
+    gd = kt / "golden" / "ad" / "pop1000"
+    g_c = np.fromfile(gd / "c_final.bin", np.float32)
+    g_st = np.fromfile(gd / "status.bin", np.int32)
+    g_li = np.fromfile(gd / "loss_init.bin", np.float32)
+    g_lf = np.fromfile(gd / "loss_final.bin", np.float32)
+    sc = backends.ScipyPop(nproc=os.cpu_count()).fit_pop(pop)
+    arr = _pop_arrays("pop", pop)
+    arr["pop/ym"] = pop["ym"][0].copy()            # shared row
+    arr.update({
+        "refkernel/c_final": g_c, "refkernel/status": g_st,
+        "refkernel/loss_init": g_li, "refkernel/loss_final": g_lf,
+        "refkernel/loss64": interp.loss_pop(pop, g_c.astype(np.float64)),
+        "init/loss64": interp.loss_pop(pop, pop["c_init"].astype(np.float64)),
+        "scipy/c_final": sc.c_final, "scipy/status": sc.status, "scipy/nfev": sc.n_iter,
+        "scipy/loss64": interp.loss_pop(pop, sc.c_final),
+    })
+    np.savez_compressed(HERE / "pop1000.npz", **arr)
+
+    # ---- interpreter vectors ----
+    pr1 = synth.make_config("pr1", M=64, N=200, seed=0)
+    vals = np.stack([interp.eval_pop_tree(_as_ref(pr1), m,
+                                          pr1["c_init"][pr1["metas"][m][2]:
+                                                        pr1["metas"][m][2] + pr1["metas"][m][3]])
+                     for m in range(pr1["M"])])
+    p1000 = {k: pop[k] for k in pop}
+    v1000 = np.stack([interp.eval_pop_tree(p1000, m,
+                                           pop["c_init"][pop["metas"][m][2]:
+                                                         pop["metas"][m][2] + pop["metas"][m][3]])
+                      for m in range(64)])
+    iv = _pop_arrays("pr1", pr1)
+    iv["pr1/values"] = vals
+    iv["pop1000/values"] = v1000
+    np.savez_compressed(HERE / "interp_vectors.npz", **iv)
+
+    # ---- PR1 configuration: reference scipy fits ----
+    pr1 = synth.make_config("pr1", seed=0)
+    ref_pop = _as_ref(pr1)
+    sc = backends.ScipyPop(nproc=os.cpu_count()).fit_pop(ref_pop)
+    arr = _pop_arrays("pop", pr1)
+    arr.update({"scipy/c_final": sc.c_final, "scipy/status": sc.status,
+                "scipy/nfev": sc.n_iter, "scipy/loss64": interp.loss_pop(ref_pop, sc.c_final),
+                "init/loss64": interp.loss_pop(ref_pop, pr1["c_init"].astype(np.float64))})
+    np.savez_compressed(HERE / "pr1_scipy.npz", **arr)
+
+    # ---- reference reverse-AD Jacobian samples ----
+    rows = [json.loads(l) for l in
+            (REF / "experiments" / "revad_v5" / "jac_sample_fixed.jsonl").read_text().splitlines()
+            if l.strip()]
+    js = {"n": np.asarray(len(rows))}
+    for i, r in enumerate(rows):
+        js[f"{i}/nt"] = np.asarray(r["nt"], np.int32)
+        js[f"{i}/nv"] = np.asarray(r["nv"], np.float32)
+        js[f"{i}/ci"] = np.asarray(r["ci"], np.int32)
+        js[f"{i}/c"] = np.asarray(r["c"], np.float32)
+        js[f"{i}/n_vars"] = np.asarray(int(r["n_vars"]))
+        js[f"{i}/x"] = np.asarray([p["x"] for p in r["pts"]], np.float32)
+        js[f"{i}/rev"] = np.asarray([p["rev"] for p in r["pts"]], np.float64)
+        js[f"{i}/fwd"] = np.asarray([p["fwd"] for p in r["pts"]], np.float64)
+    np.savez_compressed(HERE / "jac_sample.npz", **js)
+    print("golden fixtures written to", HERE)
+
+
+def _as_ref(pop: dict) -> dict:
+    """The reference loader's pop layout: ym is [M, N] (a shared row is replicated)."""
+    out = dict(pop)
+    ym = np.asarray(pop["ym"], np.float32)
+    if ym.ndim == 1:
+        out["ym"] = np.ascontiguousarray(np.broadcast_to(ym, (int(pop["M"]), int(pop["N"]))))
+    return out
+
+
+if __name__ == "__main__":
+    main()

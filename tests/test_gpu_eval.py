@@ -1,0 +1,205 @@
+"""Device interpreter parity (the fused pass, through the C ABI co_evaluate): values,
+reverse-mode Jacobians and normal-equation blocks against the CPU oracle, the reference's
+interpreter vectors and its reverse-AD Jacobian samples.
+
+Tolerances (written per test): fp64 1e-12 relative, fp32 1e-5 relative, each widened by
+64 * unit roundoff * S where S = sum |df/dv_n| |v_n| over the tree's operator nodes (the
+first-order rounding-error scale; it only matters for ill-conditioned samples such as
+cos(exp(34)), where 1-ulp differences in library transcendentals are amplified)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _helpers import GOLDEN, conditioned_close, load_npz_pop, make_tree, pop1000
+from cusr_b200 import InProcessCO, popio, synth
+from oracle import interp
+
+pytestmark = pytest.mark.gpu
+
+U64, U32 = 2.0 ** -53, 2.0 ** -24
+
+
+@pytest.fixture(scope="module")
+def co():
+    c = InProcessCO(device_id=0)
+    yield c
+    c.teardown()
+
+
+def _check_values(co, pop, precision, rel, unit, min_strict=0.97):
+    out = co.evaluate(pop, precision=precision, values=True)
+    vals = out["values"]
+    strict = total = 0
+    for m in range(int(pop["M"])):
+        nt, nv, ci, _y, K = interp.tree_view(pop, m)
+        off = int(pop["metas"][m][2])
+        c = np.asarray(pop["c_init"][off:off + K], np.float64)
+        if precision == "fp32":
+            c = c.astype(np.float32).astype(np.float64)
+        y = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c)
+        S = interp.error_scale(nt, nv, ci, pop["xs"], c)
+        big = interp.intermediate_scale(nt, nv, ci, pop["xs"], c) > 1e37
+        ok = conditioned_close(vals[m], y, S, rel, unit) | (big if precision == "fp32" else False)
+        assert ok.all(), (m, np.flatnonzero(~ok)[:5], vals[m][~ok][:5], y[~ok][:5])
+        fin = np.isfinite(y)
+        with np.errstate(all="ignore"):
+            strict += int(np.sum(np.abs(vals[m][fin] - y[fin]) <= rel * np.abs(y[fin]) + 1e-300))
+        total += int(fin.sum())
+    # the plain relative bound holds on nearly every sample (the rest are ill-conditioned)
+    assert strict / max(total, 1) >= min_strict
+
+
+def test_values_fp64_match_oracle(co):
+    _check_values(co, synth.make_config("pr1", M=96, N=300, seed=0), "fp64", 1e-12, U64)
+
+
+def test_values_fp32_match_oracle(co):
+    _check_values(co, synth.make_config("pr1", M=96, N=300, seed=0), "fp32", 1e-5, U32)
+
+
+def test_values_mid_config_both_precisions(co):
+    pop = synth.make_config("mid", M=64, N=700, seed=4)
+    _check_values(co, pop, "fp64", 1e-12, U64)
+    _check_values(co, pop, "fp32", 1e-5, U32, min_strict=0.95)
+
+
+def test_values_match_reference_interp_vectors(co):
+    z = np.load(GOLDEN / "interp_vectors.npz")
+    pop = load_npz_pop(z, "pr1")
+    vals = co.evaluate(pop, precision="fp64", values=True)["values"]
+    for m in range(pop["M"]):
+        nt, nv, ci, _y, K = interp.tree_view(pop, m)
+        off = int(pop["metas"][m][2])
+        S = interp.error_scale(nt, nv, ci, pop["xs"], pop["c_init"][off:off + K])
+        assert conditioned_close(vals[m], z["pr1/values"][m], S, 1e-12, U64).all(), m
+
+
+def _check_jacobian(co, pop, precision, tol):
+    out = co.evaluate(pop, precision=precision, values=False, jacobian=True)
+    J_dev = out["jacobian"]
+    for m in range(int(pop["M"])):
+        nt, nv, ci, _y, K = interp.tree_view(pop, m)
+        if K == 0:
+            continue
+        off = int(pop["metas"][m][2])
+        c = np.asarray(pop["c_init"][off:off + K], np.float64)
+        if precision == "fp32":
+            c = c.astype(np.float32).astype(np.float64)
+        y, J = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c)
+        S = interp.error_scale(nt, nv, ci, pop["xs"], c)
+        well = np.isfinite(y) & (S <= 1e2 * np.maximum(np.abs(y), 1e-3)) & np.all(np.isfinite(J), 1)
+        if precision == "fp32":
+            well &= interp.intermediate_scale(nt, nv, ci, pop["xs"], c) < 1e15
+        Jd = J_dev[m, :K].T
+        for k in range(K):
+            col = J[well, k]
+            if col.size == 0:
+                continue
+            scale = max(float(np.max(np.abs(col))), 1e-30)
+            err = float(np.max(np.abs(Jd[well, k] - col)))
+            assert err <= tol * scale, (m, k, err, scale)
+
+
+def test_jacobian_fp64_matches_oracle(co):
+    _check_jacobian(co, synth.make_config("pr1", M=64, N=256, seed=2), "fp64", 1e-10)
+
+
+def test_jacobian_fp32_matches_oracle(co):
+    _check_jacobian(co, synth.make_config("pr1", M=64, N=256, seed=2), "fp32", 1e-4)
+
+
+def test_jacobian_matches_reference_revad_samples(co):
+    """The reference's own reverse-AD gradients (fp32, experiments/revad_v5 samples)."""
+    z = np.load(GOLDEN / "jac_sample.npz")
+    trees, ys = [], []
+    n = int(z["n"])
+    for i in range(n):
+        trees.append((z[f"{i}/nt"], z[f"{i}/nv"], z[f"{i}/ci"], z[f"{i}/c"]))
+    # each sample tree carries its own points: evaluate tree by tree
+    for i in range(n):
+        x = z[f"{i}/x"]
+        pop = popio.build_pop([trees[i]], x, np.zeros((1, x.shape[0]), np.float32))
+        J = co.evaluate(pop, precision="fp32", values=False, jacobian=True)["jacobian"][0]
+        rev = z[f"{i}/rev"]
+        K = rev.shape[1]
+        Jd = J[:K].T
+        ok = np.isfinite(rev)
+        assert np.all(np.isfinite(Jd[ok])), i
+        scale = np.maximum(np.abs(rev[ok]), 1.0)
+        assert np.all(np.abs(Jd[ok] - rev[ok]) <= 2e-4 * scale), i
+
+
+def _ref_blocks(pop, m, c):
+    nt, nv, ci, y, K = interp.tree_view(pop, m)
+    f, J = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c)
+    r = f - np.asarray(y, np.float64)
+    tri = np.concatenate([J[:, i] @ J[:, :i + 1] for i in range(K)]) if K else np.zeros(0)
+    mag = np.concatenate([np.abs(J[:, i]) @ np.abs(J[:, :i + 1]) for i in range(K)]) if K else np.zeros(0)
+    jtr = J.T @ r
+    jtr_mag = np.abs(J).T @ np.abs(r)
+    return np.concatenate([tri, jtr, [0.5 * r @ r]]), np.concatenate([mag, jtr_mag, [0.5 * r @ r]])
+
+
+def _check_blocks(co, pop, precision, tol):
+    blocks = co.evaluate(pop, precision=precision, values=False, blocks=True)["blocks"]
+    n = 0
+    for m in range(int(pop["M"])):
+        off, K = int(pop["metas"][m][2]), int(pop["metas"][m][3])
+        c = np.asarray(pop["c_init"][off:off + K], np.float64)
+        if precision == "fp32":
+            c = c.astype(np.float32).astype(np.float64)
+        ref, mag = _ref_blocks(pop, m, c)
+        if not np.all(np.isfinite(ref)):
+            continue
+        nt, nv, ci, _y, _ = interp.tree_view(pop, m)
+        S = interp.error_scale(nt, nv, ci, pop["xs"], c)
+        f = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c)
+        if np.max(S / np.maximum(np.abs(f), 1e-3)) > 1e2:
+            continue   # ill-conditioned tree: checked by the value tests
+        assert np.all(np.abs(blocks[m] - ref) <= tol * mag + 1e-300), m
+        n += 1
+    assert n > 0
+
+
+def test_blocks_fp64_match_oracle(co):
+    _check_blocks(co, synth.make_config("pr1", M=64, N=1000, seed=6), "fp64", 1e-10)
+
+
+def test_blocks_fp32_match_oracle(co):
+    _check_blocks(co, synth.make_config("pr1", M=64, N=1000, seed=6), "fp32", 2e-4)
+
+
+def test_blocks_large_k_path(co):
+    """K in 17..32 uses the cooperative (per-warp Gram) accumulation."""
+    pop = synth.make_config("long", M=24, N=600, seed=3)
+    assert pop["K_max"] > 16
+    _check_blocks(co, pop, "fp64", 1e-10)
+    _check_blocks(co, pop, "fp32", 2e-4)
+
+
+def test_blocks_per_tree_targets(co):
+    pop = synth.make_config("physics", M=32, N=900, seed=1)
+    _check_blocks(co, pop, "fp64", 1e-10)
+
+
+def test_blocks_pop1000_reference_population(co):
+    pop, _ = pop1000()
+    _check_blocks(co, popio.slice_pop(pop, 200), "fp64", 1e-10)
+
+
+def test_ragged_sample_counts(co):
+    """N not a multiple of the block round, N = 1, N smaller than a warp."""
+    for N in (1, 7, 33, 257, 513):
+        pop = synth.make_config("pr1", M=20, N=N, seed=N)
+        _check_values(co, pop, "fp64", 1e-12, U64, min_strict=0.9)
+        _check_blocks(co, pop, "fp64", 1e-10)
+
+
+def test_unknown_operator_is_zero(co):
+    nt, nv, ci = make_tree([("b", 1), ("u", 99), ("v", 0), ("b", 77), ("c",), ("v", 0)])
+    pop = popio.build_pop([(nt, nv, ci, [1.5])], np.array([[0.5], [2.0]], np.float32),
+                          np.zeros((1, 2), np.float32))
+    out = co.evaluate(pop, precision="fp64", values=True, jacobian=True)
+    np.testing.assert_array_equal(out["values"][0], [0.0, 0.0])
+    np.testing.assert_array_equal(out["jacobian"][0, 0], [0.0, 0.0])

@@ -1,0 +1,137 @@
+"""The CPU oracle, pinned against the reference's own outputs: interpreter values from the
+reference numpy interpreter, the reference reverse-AD Jacobian samples, the reference's host-
+compiled interpreters (oracle/_ref, when built), the reference fixtures' known answers, and the
+reference ScipyPop fits."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from _helpers import GOLDEN, fixture_pop, fixture_truth, load_npz_pop, pop1000
+from cusr_b200 import popio
+from oracle import interp, lm, ref_host, scipy_lm
+
+
+def test_interp_matches_reference_values():
+    z = np.load(GOLDEN / "interp_vectors.npz")
+    pop = load_npz_pop(z, "pr1")
+    for m in range(pop["M"]):
+        off, K = int(pop["metas"][m][2]), int(pop["metas"][m][3])
+        y = interp.eval_pop_tree(pop, m, pop["c_init"][off:off + K])
+        np.testing.assert_array_equal(y, z["pr1/values"][m])
+    p1000, _ = pop1000()
+    for m in range(64):
+        off, K = int(p1000["metas"][m][2]), int(p1000["metas"][m][3])
+        y = interp.eval_pop_tree(p1000, m, p1000["c_init"][off:off + K])
+        np.testing.assert_array_equal(y, z["pop1000/values"][m])
+
+
+def test_jacobian_matches_reference_revad_samples():
+    z = np.load(GOLDEN / "jac_sample.npz")
+    for i in range(int(z["n"])):
+        nt, nv, ci, c = z[f"{i}/nt"], z[f"{i}/nv"], z[f"{i}/ci"], z[f"{i}/c"]
+        x = z[f"{i}/x"]
+        _, J = interp.value_and_jacobian(nt, nv, ci, x, c.astype(np.float64))
+        rev = z[f"{i}/rev"]
+        ok = np.isfinite(rev) & np.isfinite(J)
+        scale = np.maximum(np.abs(rev), 1.0)
+        # reference samples are fp32 evaluations of the same rules
+        assert np.all(np.abs(J[ok] - rev[ok]) <= 2e-4 * scale[ok]), i
+        # where fp32 gives a finite gradient the fp64 restatement does too
+        assert not np.any(np.isfinite(rev) & ~np.isfinite(J))
+
+
+@pytest.mark.skipif(not ref_host.available(), reason="oracle/_ref not built")
+def test_interp_matches_reference_host_build():
+    ref = ref_host.RefHost()
+    pop, _ = pop1000()
+    from cusr_b200 import synth
+    pops = [popio.slice_pop(pop, 60), synth.make_config("pr1", M=60, N=16, seed=5)]
+    for p in pops:
+        for m in range(int(p["M"])):
+            nt, nv, ci, _y, K = interp.tree_view(p, m)
+            if any(int(v) in (21, 24, 28, 5, 7) for v in nv[nt >= 2]):
+                continue   # LOOSE ops are not part of the reference CUDA interpreter
+            off = int(p["metas"][m][2])
+            c = np.asarray(p["c_init"][off:off + K], np.float32)
+            y64, J64 = interp.value_and_jacobian(nt, nv, ci, p["xs"][:16], c.astype(np.float64))
+            S = interp.error_scale(nt, nv, ci, p["xs"][:16], c)
+            for i in range(16):
+                v, g = ref.value_and_grad(nt, nv, ci, p["xs"][i], c)
+                if not np.isfinite(y64[i]) or S[i] > 1e3 * max(abs(y64[i]), 1.0):
+                    continue
+                assert abs(v - y64[i]) <= 1e-5 * abs(y64[i]) + 64 * 2.0 ** -24 * S[i]
+                ok = np.isfinite(J64[i]) & np.isfinite(g)
+                sc = max(1.0, float(np.max(np.abs(J64[i][ok]), initial=0.0)))
+                assert np.all(np.abs(g[ok] - J64[i][ok]) <= 1e-3 * sc)
+
+
+def test_lm_oracle_known_answer_fixture():
+    pop = fixture_pop("pop_fixture")
+    truth = fixture_truth("pop_fixture_truth.json")
+    for dtype in (np.float64, np.float32):
+        res = lm.fit_pop(pop, max_iter=50, dtype=dtype)
+        for i, fx in enumerate(truth["fixtures"]):
+            c = res["c_final"][fx["c_offset"]:fx["c_offset"] + fx["K"]]
+            rel = np.linalg.norm(c - fx["c_true"]) / np.linalg.norm(fx["c_true"])
+            assert res["status"][i] == lm.CONVERGED and rel < 5e-3, (fx["name"], rel)
+
+
+def test_lm_oracle_stress_statuses():
+    pop = fixture_pop("pop_fixture_stress")
+    truth = fixture_truth("pop_fixture_stress_truth.json")
+    res = lm.fit_pop(pop, max_iter=50, dtype=np.float32)
+    assert [int(s) for s in res["status"]] == [f["expect_status"] for f in truth["fixtures"]]
+
+
+def test_lm_oracle_op_fixture():
+    pop = fixture_pop("pop_fixture_op")
+    truth = fixture_truth("pop_fixture_op_truth.json")
+    res = lm.fit_pop(pop, max_iter=50, dtype=np.float64)
+    for i, fx in enumerate(truth["fixtures"]):
+        c = res["c_final"][fx["c_offset"]:fx["c_offset"] + fx["K"]]
+        rel = np.linalg.norm(c - fx["c_true"]) / np.linalg.norm(fx["c_true"])
+        assert res["status"][i] == lm.CONVERGED and rel < 5e-3, fx["name"]
+
+
+def test_lm_oracle_scale_fixture_tier1():
+    truth = fixture_truth("pop_fixture_scale_truth.json")
+    for f in truth["files"]:
+        pop = fixture_pop(f["bin"][:-4])
+        res = lm.fit_pop(pop, max_iter=50, dtype=np.float64)
+        for i, fx in enumerate(f["fixtures"]):
+            if fx["tier"] != 1:
+                continue
+            c = res["c_final"][fx["c_offset"]:fx["c_offset"] + fx["K"]]
+            ct = np.asarray(fx["c_true"])
+            rel = float(np.max(np.abs(c - ct) / np.maximum(np.abs(ct), 1e-30)))
+            assert res["status"][i] == lm.CONVERGED and rel < 5e-3, (f["bin"], fx["name"], rel)
+
+
+def test_lm_oracle_never_worse_than_init_fp64():
+    pop, _ = pop1000()
+    sub = popio.slice_pop(pop, 80)
+    res = lm.fit_pop(sub, max_iter=50, dtype=np.float32)
+    lf = interp.loss_pop(sub, res["c_final"])
+    li = interp.loss_pop(sub, sub["c_init"].astype(np.float64))
+    fin = np.isfinite(li)
+    assert np.all(lf[fin] <= li[fin] * (1 + 1e-12) + 1e-300)
+
+
+def test_scipy_restatement_matches_reference_scipy_fits():
+    pop, g = pop1000()
+    idx = np.arange(0, 1000, 25)
+    res = scipy_lm.fit_pop(pop, nproc=1, trees=idx)
+    for m in idx:
+        off, K = int(pop["metas"][m][2]), int(pop["metas"][m][3])
+        np.testing.assert_allclose(res["c_final"][off:off + K], g["scipy/c_final"][off:off + K],
+                                   rtol=1e-9, atol=1e-12)
+        assert res["status"][m] == g["scipy/status"][m]
+
+
+def test_reference_kernel_golden_is_consistent():
+    # the A100 goldens of the reference AD kernel reproduce their fp64 loss in the oracle
+    pop, g = pop1000()
+    lf = interp.loss_pop(pop, g["refkernel/c_final"].astype(np.float64))
+    np.testing.assert_allclose(lf, g["refkernel/loss64"], rtol=1e-12)
+    assert np.bincount(g["refkernel/status"], minlength=5).sum() == 1000
