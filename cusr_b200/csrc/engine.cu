@@ -59,7 +59,7 @@ struct Ctx {
     DBuf c, ctry, delta, cinit_f, lam, loss, loss_init, status, iters, pending, n_run, n_eval;
     DBuf partials, blk;
     DBuf c64, l64, n_rev;
-    DBuf vals, jac;
+    DBuf vals, jac, tape_g;
     int *h_nrun = nullptr;                  // pinned, one slot per iteration parity
     std::vector<cudaEvent_t> events;        // timing events, reused across calls
     cudaEvent_t ev_nrun[2] = {nullptr, nullptr};
@@ -205,13 +205,24 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         p.jac = jac;
         p.jac_kmax = jac_kmax;
         const int kc = grad ? bin.kc : 4;
-        const size_t smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap);
+        // tape in shared memory unless that leaves room for fewer than two resident blocks
+        bool tg = false;
+        size_t smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, true);
+        if (grad && 2 * (smem + 1024) > (size_t)ctx->smem_optin) {
+            tg = true;
+            smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, false);
+        }
         if (smem + 64 > (size_t)ctx->smem_optin) return CO_ERR_BOUNDS;
-        int occ = Launch<T>::occ(kc, grad, smem);
+        int occ = Launch<T>::occ(kc, grad, tg, smem);
         if (occ < 1) occ = 1;
         int64_t grid = (int64_t)occ * ctx->sm_count;
         if (grid > bin.max_items) grid = std::max<int64_t>(1, bin.max_items);
-        CK(Launch<T>::eval(kc, grad, p, (int)grid, smem, ctx->stream));
+        p.tape_g = nullptr;
+        if (tg) {
+            GROW(ctx->tape_g, (size_t)grid * p.tape_cap * EVAL_THREADS * EVAL_V * sizeof(T));
+            p.tape_g = ctx->tape_g.ptr;
+        }
+        CK(Launch<T>::eval(kc, grad, tg, p, (int)grid, smem, ctx->stream));
         ctx->stats.eval_launches++;
         ctx->stats.kernel_launches++;
     }
@@ -890,7 +901,7 @@ void co_teardown(void *handle) {
                     &ctx->xs_raw, &ctx->xs, &ctx->ym, &ctx->c, &ctx->ctry, &ctx->delta,
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
                     &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
-                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac};
+                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac, &ctx->tape_g};
     for (DBuf *b : bufs) release(*b);
     for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->ev_nrun)

@@ -56,6 +56,7 @@ struct EvalParams {
     int code_cap;            // shared-memory words reserved for a program
     int spill_cap;           // spill slots reserved per thread
     int tape_cap;            // tape slots reserved per thread
+    void *tape_g;            // global tape (TG instantiations): [block][tape_cap][thread]
     T *vals;                 // optional: per-sample values, [tree][N]
     T *jac;                  // optional: per-sample gradients, [tree][jac_kmax][N]
     int jac_kmax;
@@ -70,13 +71,14 @@ struct EvalSmem {
     static constexpr int kGStride = EVAL_THREADS * V + (kBig ? 1 : 0);  // gradient row stride (T)
     static constexpr int kGRows = kBig ? KC + 1 : KC;                   // + residual row
     size_t code, cval, x, spill, tape, grad, red, total;
-    __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap) {
+    __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
+                                 bool tape_in_smem = true) {
         size_t o = 0;
         code = o;  o += align16((size_t)code_cap * 4);
         cval = o;  o += align16((size_t)CO_MAX_K * sizeof(T));
         x = o;     o += align16((size_t)n_vars * EVAL_THREADS * V * 4);
         spill = o; o += align16((size_t)spill_cap * EVAL_THREADS * V * sizeof(T));
-        tape = o;  o += align16((size_t)tape_cap * EVAL_THREADS * V * sizeof(T));
+        tape = o;  o += tape_in_smem ? align16((size_t)tape_cap * EVAL_THREADS * V * sizeof(T)) : 0;
         grad = o;  o += align16((size_t)kGRows * kGStride * sizeof(T));
         red = o;   o += align16((size_t)EVAL_WARPS * nblock_size(KC) * sizeof(T));
         total = o;
@@ -294,10 +296,11 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code_
 // The fused evaluation kernel.
 //   T     arithmetic type (float / double)
 //   V     samples per thread
+//   TG    reverse tape in global scratch instead of shared memory
 //   KC    constant-count class of the bin (trees with K <= KC)
 //   GRAD  false: value and sum r^2 only (K = 0 trees never need more; the fp64 audit)
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int KC, bool GRAD>
+template <typename T, int V, int KC, bool GRAD, bool TG>
 __global__ void __launch_bounds__(EVAL_THREADS)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, KC> L;
@@ -309,12 +312,17 @@ lm_eval_kernel(const EvalParams<T> p) {
 
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_item;
-    const L lay(p.code_cap, p.n_vars, p.spill_cap, p.tape_cap);
+    const L lay(p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, !TG);
     uint32_t *code_s = reinterpret_cast<uint32_t *>(smem + lay.code);
     T *c_s = reinterpret_cast<T *>(smem + lay.cval);
     VecF<V> *x_s = reinterpret_cast<VecF<V> *>(smem + lay.x);
     VecT<T, V> *spill_s = reinterpret_cast<VecT<T, V> *>(smem + lay.spill);
-    VecT<T, V> *tape_s = reinterpret_cast<VecT<T, V> *>(smem + lay.tape);
+    // reverse tape: private shared-memory columns, or (TG, trees whose tape would not fit
+    // beside a second resident block) this block's slab of a global scratch buffer, read
+    // back by the same thread and served from L1/L2
+    VecT<T, V> *tape_s =
+        TG ? reinterpret_cast<VecT<T, V> *>(p.tape_g) + (int64_t)blockIdx.x * p.tape_cap * EVAL_THREADS
+           : reinterpret_cast<VecT<T, V> *>(smem + lay.tape);
     T *g_s = reinterpret_cast<T *>(smem + lay.grad);
     T *red_s = reinterpret_cast<T *>(smem + lay.red);
 

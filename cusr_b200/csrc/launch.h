@@ -10,32 +10,33 @@ namespace cusr {
 constexpr int EVAL_V = 2;   // samples per thread (both precisions)
 
 // kc: constant-count class (4, 8, 12, 16, 32 for fp32; 4, 8, 32 for fp64).
-// grad = false launches the value-only variant (fp64 audit).
-cudaError_t eval_launch_f32(int kc, bool grad, const EvalParams<float> &p, int grid, size_t smem,
-                            cudaStream_t s);
-cudaError_t eval_launch_f64(int kc, bool grad, const EvalParams<double> &p, int grid, size_t smem,
-                            cudaStream_t s);
-size_t eval_smem_f32(int kc, int code_cap, int n_vars, int spill_cap, int tape_cap);
-size_t eval_smem_f64(int kc, int code_cap, int n_vars, int spill_cap, int tape_cap);
+// grad = false launches the value-only variant (fp64 audit); tg = reverse tape in global
+// scratch (EvalParams::tape_g) instead of shared memory.
+cudaError_t eval_launch_f32(int kc, bool grad, bool tg, const EvalParams<float> &p, int grid,
+                            size_t smem, cudaStream_t s);
+cudaError_t eval_launch_f64(int kc, bool grad, bool tg, const EvalParams<double> &p, int grid,
+                            size_t smem, cudaStream_t s);
+size_t eval_smem_f32(int kc, int code_cap, int n_vars, int spill_cap, int tape_cap, bool tape_in_smem);
+size_t eval_smem_f64(int kc, int code_cap, int n_vars, int spill_cap, int tape_cap, bool tape_in_smem);
 // resident blocks per SM of an instantiation at the given dynamic shared memory
-int eval_blocks_per_sm_f32(int kc, bool grad, size_t smem);
-int eval_blocks_per_sm_f64(int kc, bool grad, size_t smem);
+int eval_blocks_per_sm_f32(int kc, bool grad, bool tg, size_t smem);
+int eval_blocks_per_sm_f64(int kc, bool grad, bool tg, size_t smem);
 // raise the dynamic shared-memory limit of every instantiation (once per device)
 cudaError_t eval_prepare_f32();
 cudaError_t eval_prepare_f64();
 
 template <typename T> struct Launch;
 template <> struct Launch<float> {
-    static cudaError_t eval(int kc, bool g, const EvalParams<float> &p, int grid, size_t sm,
-                            cudaStream_t s) { return eval_launch_f32(kc, g, p, grid, sm, s); }
-    static size_t smem(int kc, int a, int b, int c, int d) { return eval_smem_f32(kc, a, b, c, d); }
-    static int occ(int kc, bool g, size_t sm) { return eval_blocks_per_sm_f32(kc, g, sm); }
+    static cudaError_t eval(int kc, bool g, bool tg, const EvalParams<float> &p, int grid, size_t sm,
+                            cudaStream_t s) { return eval_launch_f32(kc, g, tg, p, grid, sm, s); }
+    static size_t smem(int kc, int a, int b, int c, int d, bool ts) { return eval_smem_f32(kc, a, b, c, d, ts); }
+    static int occ(int kc, bool g, bool tg, size_t sm) { return eval_blocks_per_sm_f32(kc, g, tg, sm); }
 };
 template <> struct Launch<double> {
-    static cudaError_t eval(int kc, bool g, const EvalParams<double> &p, int grid, size_t sm,
-                            cudaStream_t s) { return eval_launch_f64(kc, g, p, grid, sm, s); }
-    static size_t smem(int kc, int a, int b, int c, int d) { return eval_smem_f64(kc, a, b, c, d); }
-    static int occ(int kc, bool g, size_t sm) { return eval_blocks_per_sm_f64(kc, g, sm); }
+    static cudaError_t eval(int kc, bool g, bool tg, const EvalParams<double> &p, int grid, size_t sm,
+                            cudaStream_t s) { return eval_launch_f64(kc, g, tg, p, grid, sm, s); }
+    static size_t smem(int kc, int a, int b, int c, int d, bool ts) { return eval_smem_f64(kc, a, b, c, d, ts); }
+    static int occ(int kc, bool g, bool tg, size_t sm) { return eval_blocks_per_sm_f64(kc, g, tg, sm); }
 };
 
 }  // namespace cusr

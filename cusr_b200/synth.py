@@ -184,7 +184,7 @@ def _grammar_pop(cfg, M: int, N: int, rng) -> dict:
             continue
         c_gt = rng.standard_normal(int((gt[0] == CONST).sum()))
         y = eval_tree(*gt, xs, c_gt)
-        if _ok(y) and np.std(y) > 1e-6:
+        if _ok(y) and (N < 2 or np.std(y) > 1e-6):
             break
     y = (y + cfg["noise"] * rng.standard_normal(N)).astype(np.float32)
     trees = []

@@ -264,3 +264,33 @@ def error_scale(nt, nv, ci, xs, c) -> np.ndarray:
                 adj_st.append(adj * d2[i])
                 adj_st.append(adj * d1[i])
     return S
+
+
+def intermediate_range(nt, nv, ci, xs, c):
+    """Per-sample (max |v|, min nonzero |v|) over every node value of the tree (fp64): tells
+    whether a narrower format can represent the evaluation at all (fp32 overflows above
+    ~3.4e38 and loses precision below ~1.2e-38)."""
+    xs = np.asarray(xs, np.float64)
+    c = np.asarray(c, np.float64)
+    N = xs.shape[0]
+    st: list = []
+    hi = np.zeros(N)
+    lo = np.full(N, np.inf)
+    with np.errstate(all="ignore"):
+        for i in range(len(nt) - 1, -1, -1):
+            t = int(nt[i])
+            if t == NTYPE_VAR:
+                v = xs[:, int(nv[i])]
+            elif t == NTYPE_CONST:
+                v = np.full(N, c[int(ci[i])])
+            elif t == NTYPE_UFUNC:
+                v, _ = unary(int(nv[i]), st.pop())
+            else:
+                l = st.pop()
+                r = st.pop()
+                v, _, _ = binary(int(nv[i]), l, r)
+            a = np.abs(v)
+            hi = np.fmax(hi, a)
+            lo = np.where((a > 0) & np.isfinite(a), np.fmin(lo, a), lo)
+            st.append(v)
+    return hi, lo
