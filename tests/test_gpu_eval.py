@@ -40,10 +40,13 @@ def _check_values(co, pop, precision, rel, unit, min_strict=0.97):
         y = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c)
         S = interp.error_scale(nt, nv, ci, pop["xs"], c)
         hi, lo = interp.intermediate_range(nt, nv, ci, pop["xs"], c)
-        outside = (hi > 1e37) | (lo < 1e-30)   # not representable in normal fp32
-        ok = conditioned_close(vals[m], y, S, rel, unit) | (outside if precision == "fp32" else False)
+        if precision == "fp32":
+            outside = (hi > 1e37) | (lo < 1e-30)   # not representable in normal fp32
+        else:
+            outside = np.zeros(y.shape, bool)
+        ok = conditioned_close(vals[m], y, S, rel, unit) | outside
         assert ok.all(), (m, np.flatnonzero(~ok)[:5], vals[m][~ok][:5], y[~ok][:5])
-        fin = np.isfinite(y) & ~(outside if precision == "fp32" else False)
+        fin = np.isfinite(y) & ~outside
         with np.errstate(all="ignore"):
             strict += int(np.sum(np.abs(vals[m][fin] - y[fin]) <= rel * np.abs(y[fin]) + 1e-300))
         total += int(fin.sum())
@@ -93,14 +96,27 @@ def _check_jacobian(co, pop, precision, tol):
         if precision == "fp32":
             hi, lo = interp.intermediate_range(nt, nv, ci, pop["xs"], c)
             well &= (hi < 1e15) & (lo > 1e-15)
+            # elements whose gradient an fp32 evaluation of the same rules (numpy) reproduces
+            # to 1e-4: elsewhere fp32 itself cannot resolve the gradient (e.g. sin(exp(.)))
+            _, J32 = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c.astype(np.float32),
+                                               dtype=np.float32)
+            J32 = J32.astype(np.float64)
+            with np.errstate(all="ignore"):
+                resolved = np.abs(J32 - J) <= 1e-4 * np.abs(J) + 1e-30
+        else:
+            resolved = np.ones(J.shape, bool)
         Jd = J_dev[m, :K].T
         for k in range(K):
-            col = J[well, k]
+            sel = well & resolved[:, k]
+            col = J[sel, k]
             if col.size == 0:
                 continue
             scale = max(float(np.max(np.abs(col))), 1e-30)
-            err = float(np.max(np.abs(Jd[well, k] - col)))
+            # normwise per column, and elementwise for the elements fp32 resolves
+            err = float(np.max(np.abs(Jd[sel, k] - col)))
             assert err <= tol * scale, (m, k, err, scale)
+            if precision == "fp32":
+                assert np.all(np.abs(Jd[sel, k] - col) <= 1e-2 * np.abs(col) + tol * scale), (m, k)
 
 
 def test_jacobian_fp64_matches_oracle(co):
@@ -135,17 +151,20 @@ def test_jacobian_matches_reference_revad_samples(co):
 
 
 def _ref_blocks(pop, m, c):
+    """Oracle block and a magnitude bound of each entry's rounding error: Gram entries by
+    sum |J_i||J_j|, Jtr and the loss by sum |J| (|f| + |y|) (r = f - y cancels near a fit)."""
     nt, nv, ci, y, K = interp.tree_view(pop, m)
     f, J = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c)
-    r = f - np.asarray(y, np.float64)
+    y = np.asarray(y, np.float64)
+    r = f - y
+    fy = np.abs(f) + np.abs(y)
     tri = np.concatenate([J[:, i] @ J[:, :i + 1] for i in range(K)]) if K else np.zeros(0)
     mag = np.concatenate([np.abs(J[:, i]) @ np.abs(J[:, :i + 1]) for i in range(K)]) if K else np.zeros(0)
-    jtr = J.T @ r
-    jtr_mag = np.abs(J).T @ np.abs(r)
-    return np.concatenate([tri, jtr, [0.5 * r @ r]]), np.concatenate([mag, jtr_mag, [0.5 * r @ r]])
+    return (np.concatenate([tri, J.T @ r, [0.5 * r @ r]]),
+            np.concatenate([mag, np.abs(J).T @ fy, [np.abs(r) @ fy]]))
 
 
-def _check_blocks(co, pop, precision, tol):
+def _check_blocks(co, pop, precision, tol, max_cond=None):
     blocks = co.evaluate(pop, precision=precision, values=False, blocks=True)["blocks"]
     n = 0
     for m in range(int(pop["M"])):
@@ -159,7 +178,8 @@ def _check_blocks(co, pop, precision, tol):
         nt, nv, ci, _y, _ = interp.tree_view(pop, m)
         S = interp.error_scale(nt, nv, ci, pop["xs"], c)
         f = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c)
-        if np.max(S / np.maximum(np.abs(f), 1e-3)) > 1e2:
+        cond = max_cond if max_cond is not None else (1e2 if precision == "fp32" else 1e5)
+        if np.max(S) / (np.sqrt(np.mean(f * f)) + 1e-3) > cond:
             continue   # ill-conditioned tree: checked by the value tests
         if precision == "fp32":
             hi, lo = interp.intermediate_range(nt, nv, ci, pop["xs"], c)
@@ -182,12 +202,46 @@ def test_blocks_fp32_match_oracle(co):
     _check_blocks(co, synth.make_config("pr1", M=64, N=1000, seed=6), "fp32", 2e-4)
 
 
+def _sum_of_terms_pop(M, K_lo, K_hi, N, seed):
+    """Well-conditioned trees with many constants: c0 + sum_k c_k * g_k(x), g in
+    {x_j, sin x_j, exp(-x_j^2)-like products}; K = 17..32 exercises the cooperative path."""
+    rng = np.random.default_rng(seed)
+    xs = rng.uniform(-1.5, 1.5, size=(N, 3)).astype(np.float32)
+    trees = []
+    for _ in range(M):
+        K = int(rng.integers(K_lo, K_hi + 1))
+        nodes = [("b", 1)] * (K - 1) + [("c",)]
+        for k in range(1, K):
+            v = int(rng.integers(3))
+            kind = int(rng.integers(3))
+            term = [("b", 3), ("c",)]
+            if kind == 0:
+                term += [("v", v)]
+            elif kind == 1:
+                term += [("u", 14), ("v", v)]
+            else:
+                term += [("b", 3), ("v", v), ("v", (v + 1) % 3)]
+            nodes += term
+        nt, nv, ci = make_tree(nodes)
+        trees.append((nt, nv, ci, rng.normal(0, 1, K).astype(np.float32)))
+    y = (np.sin(xs[:, 0]) + xs[:, 1] * xs[:, 2]).astype(np.float32)
+    return popio.build_pop(trees, xs, y)
+
+
 def test_blocks_large_k_path(co):
     """K in 17..32 uses the cooperative (per-warp Gram) accumulation."""
-    pop = synth.make_config("long", M=24, N=600, seed=3)
+    pop = _sum_of_terms_pop(40, 17, 32, 700, seed=3)
     assert pop["K_max"] > 16
     _check_blocks(co, pop, "fp64", 1e-10)
     _check_blocks(co, pop, "fp32", 2e-4)
+
+
+def test_blocks_long_trees_global_tape(co):
+    """63-255-node trees: the reverse tape lives in global scratch (too large for shared
+    memory next to a second resident block)."""
+    pop = synth.make_config("long", M=24, N=600, seed=3)
+    _check_blocks(co, pop, "fp64", 1e-9, max_cond=1e6)
+    _check_values(co, pop, "fp64", 1e-12, U64, min_strict=0.8)
 
 
 def test_blocks_per_tree_targets(co):
