@@ -27,7 +27,8 @@ ALIASES = ("libcusr_co_ad.so", "libcusr_co_fd.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-O3", f"-I{INCLUDE}"]
-SOURCES = ["eval_f32.cu", "eval_f64.cu", "engine.cu", "pack.cpp", "debug_api.cpp"]
+SOURCES = ["eval_f32.cu", "eval_f64.cu", "engine.cu", "pack.cpp", "debug_api.cpp",
+           "noalloc.cu"]
 
 
 def _nvcc() -> str:

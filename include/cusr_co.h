@@ -199,6 +199,32 @@ int  co_evaluate(void *handle, const PopHeader *header,
  * the FP32 / FP64 non-tensor peak the engine's roofline is reported against. */
 int  co_probe_peak(void *handle, double *fp32_tflops, double *fp64_tflops);
 
+/* Allocation-free evaluation (no counterpart in the reference). For callers that cannot
+ * allocate device memory — their GPU memory is owned by their own pool allocator, or they
+ * cannot afford the device-wide synchronisation of cudaMalloc/cudaFree inside their loop.
+ * Same fused pass as co_evaluate (fp32 normal-equation blocks only), but every scratch buffer
+ * (compiled programs, descriptors, work lists, counters, transposed inputs, the padded target
+ * row, per-chunk partial sums) lives in one fixed 32 MiB device array inside the library; the
+ * call makes no cudaMalloc / cudaFree or other allocating CUDA call.
+ *   header, nt, nv, ci, metas  HOST pointers (pop.bin layout; compiled on the host)
+ *   c_dev                      DEVICE float[total_c] constants
+ *   xs_dev                     DEVICE float[N][n_vars] inputs (pop.bin layout)
+ *   y_dev                      DEVICE float[N], one target row shared by every tree
+ *   blocks_dev                 DEVICE float output, per tree in tree order (K+1)(K+2)/2
+ *                              values: JtJ lower triangle, Jtr, 0.5*sum r^2
+ *   stream                     cudaStream_t (NULL = legacy default stream)
+ * Returns CO_ERR_BOUNDS when the population needs more than the fixed array or a tree's
+ * reverse tape does not fit in shared memory. The first call on a device resolves the array's
+ * device address (cudaGetSymbolAddress) and configures the kernels: make it before any stream
+ * capture. Every call shares the one array and overwrites it; calls are serialised inside the
+ * library and return after their work completes, because work of two calls overlapping on the
+ * GPU would race on it. The caller's current device is restored on return. */
+int  co_evaluate_noalloc(int device_id, const PopHeader *header,
+                         const int32_t *nt, const float *nv, const int32_t *ci,
+                         const TreeMeta *metas,
+                         const float *c_dev, const float *xs_dev, const float *y_dev,
+                         float *blocks_dev, void *stream);
+
 /* Human-readable message for a return code (static storage). */
 const char *co_strerror(int code);
 
