@@ -19,11 +19,12 @@ extern "C" int cusr_compile_tree(const int32_t *nt, const float *nv, const int32
     info_out[1] = ct.n_spill;
     info_out[2] = ct.n_tape;
     info_out[3] = ct.unique_const ? 1 : 0;
-    info_out[4] = 0;
+    info_out[4] = ct.n_bwd;
     return CO_OK;
 }
 
-extern "C" double cusr_eval_program(const uint32_t *code, int n_instr, const double *x,
-                                    const double *c, int K, double *grad) {
-    return cusr::host_eval_program(code, n_instr, x, c, K, grad);
+extern "C" double cusr_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd,
+                                    int n_bwd, const double *x, const double *c, int K,
+                                    double *grad) {
+    return cusr::host_eval_program(fwd, n_fwd, bwd, n_bwd, x, c, K, grad);
 }

@@ -8,13 +8,13 @@ namespace {
 
 template <int KC, bool G, bool TG>
 cudaError_t one(const EvalParams<CUSR_T> &p, int grid, size_t smem, cudaStream_t s) {
-    lm_eval_kernel<CUSR_T, EVAL_V, KC, G, TG><<<grid, EVAL_THREADS, smem, s>>>(p);
+    lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG><<<grid, EVAL_NT, smem, s>>>(p);
     return cudaGetLastError();
 }
 template <int KC, bool G, bool TG> int occ(size_t smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, KC, G, TG>,
-                                                      EVAL_THREADS, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG>,
+                                                      EVAL_NT, smem) != cudaSuccess)
         return 0;
     return n;
 }
@@ -25,9 +25,9 @@ template <int KC, bool G, bool TG> cudaError_t prep() {
     if (e == cudaSuccess)
         e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa;
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<CUSR_T, EVAL_V, KC, G, TG>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG>);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(lm_eval_kernel<CUSR_T, EVAL_V, KC, G, TG>,
+    return cudaFuncSetAttribute(lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 optin - (int)fa.sharedSizeBytes);
 }
@@ -46,7 +46,7 @@ cudaError_t CUSR_FN(eval_launch)(int kc, bool grad, bool tg, const EvalParams<CU
 size_t CUSR_FN(eval_smem)(int kc, int code_cap, int n_vars, int spill_cap, int tape_cap,
                           bool tape_in_smem) {
 #define X(KC) \
-    if (kc == KC) return EvalSmem<CUSR_T, EVAL_V, KC>(code_cap, n_vars, spill_cap, tape_cap, tape_in_smem).total;
+    if (kc == KC) return EvalSmem<CUSR_T, EVAL_V, EVAL_NT, KC>(code_cap, n_vars, spill_cap, tape_cap, tape_in_smem).total;
     CUSR_KCS(X)
 #undef X
     return 0;

@@ -12,11 +12,12 @@
 // (d_J[M*K_max*N], co_lib.cu:233, 351, 388); here J rows never leave the SM.
 //
 // Execution model (B200 / sm_100a):
-//   * persistent blocks of 128 threads pull work items from an atomic counter; items of a
+//   * persistent blocks of NT threads pull work items from an atomic counter; items of a
 //     bin are ordered most-expensive-tree first (LPT);
 //   * every thread evaluates V consecutive samples at once (instruction decode is amortised
 //     over V samples and the V chains give independent instructions);
-//   * the tree program (warp-uniform) and the constants sit in shared memory; each thread's
+//   * the forward and reverse programs (program.h; warp-uniform, every opcode specialised so
+//     each case is straight-line code) and the constants sit in shared memory; each thread's
 //     spill stack, reverse tape, gradient rows and input row are private shared-memory
 //     columns laid out [slot][thread] (conflict-free, no block barriers inside an item);
 //   * the normal-equation sums for K <= 16 live in registers (KC = constant-count class,
@@ -31,9 +32,6 @@
 #include "ops.h"
 
 namespace cusr {
-
-constexpr int EVAL_THREADS = 128;
-constexpr int EVAL_WARPS = EVAL_THREADS / 32;
 
 template <typename T, int V> struct alignas(sizeof(T) * V) VecT { T v[V]; };
 template <int V> struct alignas(4 * V) VecF { float v[V]; };
@@ -51,9 +49,9 @@ struct EvalParams {
     T *partials;             // per-item sums, slot TreeDesc::p_off + chunk * nblock_size(K)
     int64_t ldx;
     int N;
-    int chunk;               // samples per item (multiple of EVAL_THREADS * V)
+    int chunk;               // samples per item (multiple of NT * V)
     int n_vars;
-    int code_cap;            // shared-memory words reserved for a program
+    int code_cap;            // shared-memory words reserved for the two programs of a tree
     int spill_cap;           // spill slots reserved per thread
     int tape_cap;            // tape slots reserved per thread
     void *tape_g;            // global tape (TG instantiations): [block][tape_cap][thread]
@@ -65,22 +63,22 @@ struct EvalParams {
 __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
 // Shared-memory layout of one block; the host sizes the launch with the same function.
-template <typename T, int V, int KC>
+template <typename T, int V, int NT, int KC>
 struct EvalSmem {
     static constexpr bool kBig = KC > 16;
-    static constexpr int kGStride = EVAL_THREADS * V + (kBig ? 1 : 0);  // gradient row stride (T)
-    static constexpr int kGRows = kBig ? KC + 1 : KC;                   // + residual row
+    static constexpr int kGStride = NT * V + (kBig ? 1 : 0);   // gradient row stride (T)
+    static constexpr int kGRows = kBig ? KC + 1 : KC;         // + residual row
     size_t code, cval, x, spill, tape, grad, red, total;
     __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
                                  bool tape_in_smem = true) {
         size_t o = 0;
         code = o;  o += align16((size_t)code_cap * 4);
         cval = o;  o += align16((size_t)CO_MAX_K * sizeof(T));
-        x = o;     o += align16((size_t)n_vars * EVAL_THREADS * V * 4);
-        spill = o; o += align16((size_t)spill_cap * EVAL_THREADS * V * sizeof(T));
-        tape = o;  o += tape_in_smem ? align16((size_t)tape_cap * EVAL_THREADS * V * sizeof(T)) : 0;
+        x = o;     o += align16((size_t)n_vars * NT * V * 4);
+        spill = o; o += align16((size_t)spill_cap * NT * V * sizeof(T));
+        tape = o;  o += tape_in_smem ? align16((size_t)tape_cap * NT * V * sizeof(T)) : 0;
         grad = o;  o += align16((size_t)kGRows * kGStride * sizeof(T));
-        red = o;   o += align16((size_t)EVAL_WARPS * nblock_size(KC) * sizeof(T));
+        red = o;   o += align16((size_t)(NT / 32) * nblock_size(KC) * sizeof(T));
         total = o;
     }
 };
@@ -94,112 +92,125 @@ __device__ __forceinline__ T warp_sum(T v) {
     return v;
 }
 
+template <typename T, int V>
+__device__ __forceinline__ VecT<T, V> pack(const T (&a)[V]) {
+    VecT<T, V> r;
+    CUSR_FOR_V r.v[j] = a[j];
+    return r;
+}
+
 // ---------------------------------------------------------------------------------------
-// Forward sweep: value of the program at V samples; records the reverse tape when GRAD.
+// Forward sweep. xt / sp / tp point at this thread's column (x_s + tid, ...); slot k of a
+// column is element k * NT.
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, bool GRAD>
-__device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code_s, int n_instr,
-                                              const T *__restrict__ c_s,
-                                              const VecF<V> *__restrict__ x_s,
-                                              VecT<T, V> *__restrict__ spill_s,
-                                              VecT<T, V> *__restrict__ tape_s, int tid,
-                                              T (&tos)[V]) {
-    typedef VecT<T, V> VT;
-    for (int pc = 0; pc < n_instr; ++pc) {
-        const uint32_t w = code_s[pc];
-        const uint32_t op = w_op(w), mode = w_mode(w);
-        if (op == OP_LOAD) {
-            if (w_push(w)) {
-                VT t; CUSR_FOR_V t.v[j] = tos[j];
-                spill_s[w_sd(w) * EVAL_THREADS + tid] = t;
+template <typename T, int V, int NT, bool GRAD, uint32_t OP, uint32_t MODE, bool SW>
+__device__ __forceinline__ void fwd_bin(uint32_t w, const T *__restrict__ c_s,
+                                        const VecF<V> *__restrict__ xt,
+                                        const VecT<T, V> *__restrict__ sp,
+                                        VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
+    T s[V];
+    if constexpr (MODE == M_VAR) {
+        const VecF<V> xv = xt[w_idx(w) * NT];
+        CUSR_FOR_V s[j] = (T)xv.v[j];
+    } else if constexpr (MODE == M_CONST) {
+        const T cv = c_s[w_idx(w)];
+        CUSR_FOR_V s[j] = cv;
+    } else {
+        const VecT<T, V> t = sp[w_sd(w) * NT];
+        CUSR_FOR_V s[j] = t.v[j];
+    }
+    T o[V], dt[V], ds[V];
+    CUSR_FOR_V {
+        T da, db;
+        binary_op<T>(OP, SW ? s[j] : tos[j], SW ? tos[j] : s[j], o[j], da, db);
+        dt[j] = SW ? db : da;
+        ds[j] = SW ? da : db;
+    }
+    if constexpr (GRAD) {
+        const int ts = (int)w_ts(w);
+        if constexpr (OP == OP_MUL) {
+            if constexpr (MODE == M_CONST) {
+                tp[ts * NT] = pack<T, V>(ds);
+            } else if constexpr (MODE == M_POP) {
+                tp[ts * NT] = pack<T, V>(dt);
+                tp[(ts + 1) * NT] = pack<T, V>(ds);
             }
-            if (mode == M_VAR) {
-                const VecF<V> xv = x_s[w_idx(w) * EVAL_THREADS + tid];
+        } else if constexpr (OP == OP_DIV || OP == OP_POW || OP == OP_POWABS) {
+            tp[ts * NT] = pack<T, V>(dt);
+            if constexpr (MODE != M_VAR) tp[(ts + 1) * NT] = pack<T, V>(ds);
+        } else if constexpr (OP == OP_MAX || OP == OP_MIN) {
+            tp[ts * NT] = pack<T, V>(dt);
+        }
+    }
+    CUSR_FOR_V tos[j] = o[j];
+}
+
+template <typename T, int V, int NT, bool GRAD, uint32_t OP>
+__device__ __forceinline__ void fwd_un(uint32_t w, VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
+    T d[V];
+    CUSR_FOR_V {
+        T r;
+        unary_op<T>(OP, tos[j], r, d[j]);
+        tos[j] = r;
+    }
+    if constexpr (GRAD && OP != OP_NEG && OP != OP_UZERO) tp[w_ts(w) * NT] = pack<T, V>(d);
+}
+
+template <typename T, int V, int NT, bool GRAD>
+__device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code, int n,
+                                              const T *__restrict__ c_s,
+                                              const VecF<V> *__restrict__ xt,
+                                              VecT<T, V> *__restrict__ sp,
+                                              VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
+    for (int pc = 0; pc < n; ++pc) {
+        const uint32_t w = code[pc];
+        switch (w_code(w)) {
+            case XOP_PUSH_VAR:
+                sp[w_sd(w) * NT] = pack<T, V>(tos);
+                [[fallthrough]];
+            case XOP_LOAD_VAR: {
+                const VecF<V> xv = xt[w_idx(w) * NT];
                 CUSR_FOR_V tos[j] = (T)xv.v[j];
-            } else {
+                break;
+            }
+            case XOP_PUSH_CONST:
+                sp[w_sd(w) * NT] = pack<T, V>(tos);
+                [[fallthrough]];
+            case XOP_LOAD_CONST: {
                 const T cv = c_s[w_idx(w)];
                 CUSR_FOR_V tos[j] = cv;
+                break;
             }
-            continue;
-        }
-        if (op < OP_ADD) {
-            T r[V], d[V];
-            switch (op) {
-#define CUSR_UN(OPC) case OPC: CUSR_FOR_V unary_op<T>(OPC, tos[j], r[j], d[j]); break;
-                CUSR_UN(OP_SIN) CUSR_UN(OP_COS) CUSR_UN(OP_TAN) CUSR_UN(OP_SINH)
-                CUSR_UN(OP_COSH) CUSR_UN(OP_TANH) CUSR_UN(OP_LOG) CUSR_UN(OP_LOGABS)
-                CUSR_UN(OP_EXP) CUSR_UN(OP_INV) CUSR_UN(OP_NEG) CUSR_UN(OP_ABS)
-                CUSR_UN(OP_SQRT) CUSR_UN(OP_SQRTABS)
+#define CUSR_UN(OPC) case xop_un(OPC): fwd_un<T, V, NT, GRAD, OPC>(w, tp, tos); break;
+            CUSR_UN(OP_SIN) CUSR_UN(OP_COS) CUSR_UN(OP_TAN) CUSR_UN(OP_SINH)
+            CUSR_UN(OP_COSH) CUSR_UN(OP_TANH) CUSR_UN(OP_LOG) CUSR_UN(OP_LOGABS)
+            CUSR_UN(OP_EXP) CUSR_UN(OP_INV) CUSR_UN(OP_NEG) CUSR_UN(OP_ABS)
+            CUSR_UN(OP_SQRT) CUSR_UN(OP_SQRTABS) CUSR_UN(OP_UZERO)
 #undef CUSR_UN
-                default: CUSR_FOR_V { r[j] = T(0); d[j] = T(0); } break;
-            }
-            if (GRAD && op != OP_NEG && op != OP_UZERO) {
-                VT t; CUSR_FOR_V t.v[j] = d[j];
-                tape_s[w_ts(w) * EVAL_THREADS + tid] = t;
-            }
-            CUSR_FOR_V tos[j] = r[j];
-            continue;
-        }
-        // binary: fetch the source operand
-        T s[V];
-        if (mode == M_VAR) {
-            const VecF<V> xv = x_s[w_idx(w) * EVAL_THREADS + tid];
-            CUSR_FOR_V s[j] = (T)xv.v[j];
-        } else if (mode == M_CONST) {
-            const T cv = c_s[w_idx(w)];
-            CUSR_FOR_V s[j] = cv;
-        } else {
-            const VT t = spill_s[w_sd(w) * EVAL_THREADS + tid];
-            CUSR_FOR_V s[j] = t.v[j];
-        }
-        const bool sw = w_swap(w);
-        T o[V], dt[V], ds[V];
-        switch (op) {
-#define CUSR_BIN(OPC)                                                                    \
-    case OPC:                                                                            \
-        CUSR_FOR_V {                                                                     \
-            T da, db;                                                                    \
-            binary_op<T>(OPC, sw ? s[j] : tos[j], sw ? tos[j] : s[j], o[j], da, db);     \
-            dt[j] = sw ? db : da; ds[j] = sw ? da : db;                                  \
-        }                                                                                \
+#define CUSR_B(OPC, MODE, SW)                                                          \
+    case xop_bin(OPC, MODE, SW):                                                       \
+        fwd_bin<T, V, NT, GRAD, OPC, MODE, SW>(w, c_s, xt, sp, tp, tos);               \
         break;
-            CUSR_BIN(OP_ADD) CUSR_BIN(OP_SUB) CUSR_BIN(OP_MUL) CUSR_BIN(OP_DIV)
-            CUSR_BIN(OP_POW) CUSR_BIN(OP_POWABS) CUSR_BIN(OP_MAX) CUSR_BIN(OP_MIN)
-            CUSR_BIN(OP_LT) CUSR_BIN(OP_GT) CUSR_BIN(OP_LE) CUSR_BIN(OP_GE)
-#undef CUSR_BIN
-            default: CUSR_FOR_V { o[j] = T(0); dt[j] = T(0); ds[j] = T(0); } break;
+// operand order matters: every (mode, order); commutative ones are emitted unswapped
+#define CUSR_B6(OPC) CUSR_B(OPC, M_VAR, 0) CUSR_B(OPC, M_VAR, 1) CUSR_B(OPC, M_CONST, 0) \
+                     CUSR_B(OPC, M_CONST, 1) CUSR_B(OPC, M_POP, 0) CUSR_B(OPC, M_POP, 1)
+#define CUSR_B3(OPC) CUSR_B(OPC, M_VAR, 0) CUSR_B(OPC, M_CONST, 0) CUSR_B(OPC, M_POP, 0)
+            CUSR_B3(OP_ADD) CUSR_B6(OP_SUB) CUSR_B3(OP_MUL) CUSR_B6(OP_DIV)
+            CUSR_B6(OP_POW) CUSR_B6(OP_POWABS) CUSR_B6(OP_MAX) CUSR_B6(OP_MIN)
+            CUSR_B3(OP_LT) CUSR_B3(OP_GT) CUSR_B3(OP_LE) CUSR_B3(OP_GE) CUSR_B3(OP_BZERO)
+#undef CUSR_B3
+#undef CUSR_B6
+#undef CUSR_B
+            default: break;
         }
-        if (GRAD) {
-            const int ts = (int)w_ts(w);
-            VT a, b;
-            CUSR_FOR_V { a.v[j] = dt[j]; b.v[j] = ds[j]; }
-            switch (op) {
-                case OP_MUL:
-                    if (mode == M_CONST) tape_s[ts * EVAL_THREADS + tid] = b;
-                    else if (mode == M_POP) {
-                        tape_s[ts * EVAL_THREADS + tid] = a;
-                        tape_s[(ts + 1) * EVAL_THREADS + tid] = b;
-                    }
-                    break;
-                case OP_DIV: case OP_POW: case OP_POWABS:
-                    tape_s[ts * EVAL_THREADS + tid] = a;
-                    if (mode != M_VAR) tape_s[(ts + 1) * EVAL_THREADS + tid] = b;
-                    break;
-                case OP_MAX: case OP_MIN:
-                    tape_s[ts * EVAL_THREADS + tid] = a;
-                    break;
-                default: break;
-            }
-        }
-        CUSR_FOR_V tos[j] = o[j];
     }
 }
 
 // gradient row access: [k][thread*V + j], rows padded in the cooperative (big-K) layout
 template <typename T, int V, int GSTRIDE>
-__device__ __forceinline__ void grad_put(T *__restrict__ g_s, int k, int tid, const T (&a)[V],
+__device__ __forceinline__ void grad_put(T *__restrict__ gt, int k, const T (&a)[V],
                                          bool unique) {
-    T *row = g_s + k * GSTRIDE + tid * V;
+    T *row = gt + k * GSTRIDE;
     if (unique) {
         CUSR_FOR_V row[j] = a[j];
     } else {
@@ -208,87 +219,116 @@ __device__ __forceinline__ void grad_put(T *__restrict__ g_s, int k, int tid, co
 }
 
 // ---------------------------------------------------------------------------------------
-// Reverse sweep: adjoints from the root to the leaves; grad row k receives df/dc_k.
+// Reverse sweep over the reverse program: adjoints from the root to the leaves; gradient
+// row k receives df/dc_k (gt = g_s + tid * V).
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int GSTRIDE>
-__device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code_s, int n_instr,
+template <typename T, int V, int NT, int GSTRIDE>
+__device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code, int n,
                                               const T *__restrict__ c_s,
-                                              const VecF<V> *__restrict__ x_s,
-                                              VecT<T, V> *__restrict__ spill_s,
-                                              const VecT<T, V> *__restrict__ tape_s,
-                                              T *__restrict__ g_s, int tid, bool unique) {
+                                              const VecF<V> *__restrict__ xt,
+                                              VecT<T, V> *__restrict__ sp,
+                                              const VecT<T, V> *__restrict__ tp,
+                                              T *__restrict__ gt, bool unique) {
     typedef VecT<T, V> VT;
     T adj[V];
     CUSR_FOR_V adj[j] = T(1);
-    for (int pc = n_instr - 1; pc >= 0; --pc) {
-        const uint32_t w = code_s[pc];
-        const uint32_t op = w_op(w), mode = w_mode(w);
-        if (op == OP_LOAD) {
-            if (mode == M_CONST) grad_put<T, V, GSTRIDE>(g_s, (int)w_idx(w), tid, adj, unique);
-            if (w_push(w)) {
-                const VT t = spill_s[w_sd(w) * EVAL_THREADS + tid];
+    for (int pc = 0; pc < n; ++pc) {
+        const uint32_t w = code[pc];
+        switch (w_code(w)) {
+            case B_GRAD:
+                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
+                break;
+            case B_GRAD_RESTORE: {
+                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
+                const VT t = sp[w_sd(w) * NT];
                 CUSR_FOR_V adj[j] = t.v[j];
+                break;
             }
-            continue;
-        }
-        if (op < OP_ADD) {
-            if (op == OP_NEG) {
+            case B_RESTORE: {
+                const VT t = sp[w_sd(w) * NT];
+                CUSR_FOR_V adj[j] = t.v[j];
+                break;
+            }
+            case B_GRAD_NEG: {
+                T a[V];
+                CUSR_FOR_V a[j] = -adj[j];
+                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                break;
+            }
+            case B_SPILL:
+                sp[w_sd(w) * NT] = pack<T, V>(adj);
+                break;
+            case B_SPILL_NEG: {
+                T a[V];
+                CUSR_FOR_V a[j] = -adj[j];
+                sp[w_sd(w) * NT] = pack<T, V>(a);
+                break;
+            }
+            case B_NEG:
                 CUSR_FOR_V adj[j] = -adj[j];
-            } else if (op == OP_UZERO) {
+                break;
+            case B_GRAD_THEN_NEG:
+                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
+                CUSR_FOR_V adj[j] = -adj[j];
+                break;
+            case B_SPILL_THEN_NEG:
+                sp[w_sd(w) * NT] = pack<T, V>(adj);
+                CUSR_FOR_V adj[j] = -adj[j];
+                break;
+            case B_SCALE_X: {
+                const VecF<V> xv = xt[w_idx(w) * NT];
+                CUSR_FOR_V adj[j] = safe_mul(adj[j], (T)xv.v[j]);
+                break;
+            }
+            case B_SCALE_T0: {
+                const VT t0 = tp[w_ts(w) * NT];
+                CUSR_FOR_V adj[j] = safe_mul(adj[j], t0.v[j]);
+                break;
+            }
+            case B_MULC: {
+                const VT t0 = tp[w_ts(w) * NT];
+                const T cv = c_s[w_idx(w)];
+                T a[V];
+                CUSR_FOR_V { a[j] = safe_mul(adj[j], t0.v[j]); adj[j] = safe_mul(adj[j], cv); }
+                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                break;
+            }
+            case B_GRAD_T1_T0:
+            case B_SPILL_T1_T0: {
+                const int ts = (int)w_ts(w);
+                const VT t0 = tp[ts * NT], t1 = tp[(ts + 1) * NT];
+                T a[V];
+                CUSR_FOR_V { a[j] = safe_mul(adj[j], t1.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
+                if (w_code(w) == B_GRAD_T1_T0) grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                else sp[w_sd(w) * NT] = pack<T, V>(a);
+                break;
+            }
+            case B_GRAD_1MT0_T0:
+            case B_SPILL_1MT0_T0: {
+                const VT t0 = tp[w_ts(w) * NT];
+                T a[V];
+                CUSR_FOR_V { a[j] = safe_mul(adj[j], T(1) - t0.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
+                if (w_code(w) == B_GRAD_1MT0_T0) grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                else sp[w_sd(w) * NT] = pack<T, V>(a);
+                break;
+            }
+            case B_ZERO:
                 CUSR_FOR_V adj[j] = T(0);
-            } else {
-                const VT d = tape_s[w_ts(w) * EVAL_THREADS + tid];
-                CUSR_FOR_V adj[j] = safe_mul(adj[j], d.v[j]);
-            }
-            continue;
-        }
-        const bool sw = w_swap(w);
-        const int ts = (int)w_ts(w);
-        T dt[V], ds[V];
-        switch (op) {
-            case OP_ADD: CUSR_FOR_V { dt[j] = T(1); ds[j] = T(1); } break;
-            case OP_SUB: CUSR_FOR_V { dt[j] = sw ? T(-1) : T(1); ds[j] = -dt[j]; } break;
-            case OP_MUL:
-                if (mode == M_VAR) {
-                    const VecF<V> xv = x_s[w_idx(w) * EVAL_THREADS + tid];
-                    CUSR_FOR_V { dt[j] = (T)xv.v[j]; ds[j] = T(0); }
-                } else if (mode == M_CONST) {
-                    const T cv = c_s[w_idx(w)];
-                    const VT b = tape_s[ts * EVAL_THREADS + tid];
-                    CUSR_FOR_V { dt[j] = cv; ds[j] = b.v[j]; }
-                } else {
-                    const VT a = tape_s[ts * EVAL_THREADS + tid];
-                    const VT b = tape_s[(ts + 1) * EVAL_THREADS + tid];
-                    CUSR_FOR_V { dt[j] = a.v[j]; ds[j] = b.v[j]; }
-                }
                 break;
-            case OP_DIV: case OP_POW: case OP_POWABS: {
-                const VT a = tape_s[ts * EVAL_THREADS + tid];
-                CUSR_FOR_V { dt[j] = a.v[j]; ds[j] = T(0); }
-                if (mode != M_VAR) {
-                    const VT b = tape_s[(ts + 1) * EVAL_THREADS + tid];
-                    CUSR_FOR_V ds[j] = b.v[j];
-                }
+            case B_GRAD_ZERO: {
+                T a[V];
+                CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
+                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
                 break;
             }
-            case OP_MAX: case OP_MIN: {
-                const VT a = tape_s[ts * EVAL_THREADS + tid];
-                CUSR_FOR_V { dt[j] = a.v[j]; ds[j] = T(1) - a.v[j]; }
+            case B_SPILL_ZERO: {
+                T a[V];
+                CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
+                sp[w_sd(w) * NT] = pack<T, V>(a);
                 break;
             }
-            default: CUSR_FOR_V { dt[j] = T(0); ds[j] = T(0); } break;
+            default: break;
         }
-        if (mode != M_VAR) {
-            T as[V];
-            CUSR_FOR_V as[j] = safe_mul(adj[j], ds[j]);
-            if (mode == M_POP) {
-                VT t; CUSR_FOR_V t.v[j] = as[j];
-                spill_s[w_sd(w) * EVAL_THREADS + tid] = t;
-            } else {
-                grad_put<T, V, GSTRIDE>(g_s, (int)w_idx(w), tid, as, unique);
-            }
-        }
-        CUSR_FOR_V adj[j] = safe_mul(adj[j], dt[j]);
     }
 }
 
@@ -296,17 +336,19 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code_
 // The fused evaluation kernel.
 //   T     arithmetic type (float / double)
 //   V     samples per thread
-//   TG    reverse tape in global scratch instead of shared memory
+//   NT    threads per block
 //   KC    constant-count class of the bin (trees with K <= KC)
 //   GRAD  false: value and sum r^2 only (K = 0 trees never need more; the fp64 audit)
+//   TG    reverse tape in global scratch instead of shared memory
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int KC, bool GRAD, bool TG>
-__global__ void __launch_bounds__(EVAL_THREADS)
+template <typename T, int V, int NT, int KC, bool GRAD, bool TG>
+__global__ void __launch_bounds__(NT)
 lm_eval_kernel(const EvalParams<T> p) {
-    typedef EvalSmem<T, V, KC> L;
+    typedef EvalSmem<T, V, NT, KC> L;
     constexpr bool kBig = L::kBig;
     constexpr int GS = L::kGStride;
-    constexpr int ROUND = EVAL_THREADS * V;
+    constexpr int ROUND = NT * V;
+    constexpr int NW = NT / 32;
     constexpr int NTRI = KC * (KC + 1) / 2;
     constexpr int NACC = kBig ? (nblock_size(32) + 31) / 32 : 1;  // entries per lane (big-K)
 
@@ -321,13 +363,17 @@ lm_eval_kernel(const EvalParams<T> p) {
     // beside a second resident block) this block's slab of a global scratch buffer, read
     // back by the same thread and served from L1/L2
     VecT<T, V> *tape_s =
-        TG ? reinterpret_cast<VecT<T, V> *>(p.tape_g) + (int64_t)blockIdx.x * p.tape_cap * EVAL_THREADS
+        TG ? reinterpret_cast<VecT<T, V> *>(p.tape_g) + (int64_t)blockIdx.x * p.tape_cap * NT
            : reinterpret_cast<VecT<T, V> *>(smem + lay.tape);
     T *g_s = reinterpret_cast<T *>(smem + lay.grad);
     T *red_s = reinterpret_cast<T *>(smem + lay.red);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n_items = *p.n_items;
+    VecF<V> *xt = x_s + tid;
+    VecT<T, V> *spt = spill_s + tid;
+    VecT<T, V> *tpt = tape_s + tid;
+    T *gt = g_s + tid * V;
 
     for (;;) {
         if (tid == 0) s_item = atomicAdd(p.counter, 1);
@@ -339,9 +385,11 @@ lm_eval_kernel(const EvalParams<T> p) {
         const int K = d.K;
         const bool unique = (d.flags & TD_UNIQUE_CONST) != 0;
         const bool grad = GRAD && K > 0;
-        for (int i = tid; i < d.n_instr; i += EVAL_THREADS) code_s[i] = p.code[d.code_off + i];
-        for (int i = tid; i < K; i += EVAL_THREADS) c_s[i] = p.c[d.c_off + i];
+        const int n_code = d.n_instr + d.n_bwd;   // the reverse program follows the forward one
+        for (int i = tid; i < n_code; i += NT) code_s[i] = p.code[d.code_off + i];
+        for (int i = tid; i < K; i += NT) c_s[i] = p.c[d.c_off + i];
         __syncthreads();
+        const uint32_t *bcode_s = code_s + d.n_instr;
 
         // accumulators (register path) / lane-owned Gram entries (big-K path)
         T acc[kBig ? 1 : (NTRI > 0 ? NTRI : 1)];
@@ -375,12 +423,11 @@ lm_eval_kernel(const EvalParams<T> p) {
         for (int64_t base = s0; base < s_end; base += ROUND) {
             const int64_t si = base + (int64_t)tid * V;
             for (int v = 0; v < p.n_vars; ++v)
-                x_s[v * EVAL_THREADS + tid] =
-                    *reinterpret_cast<const VecF<V> *>(p.xs + (int64_t)v * p.ldx + si);
+                xt[v * NT] = *reinterpret_cast<const VecF<V> *>(p.xs + (int64_t)v * p.ldx + si);
             const VecF<V> yv = *reinterpret_cast<const VecF<V> *>(yrow + si);
 
             T f[V];
-            forward_sweep<T, V, GRAD>(code_s, d.n_instr, c_s, x_s, spill_s, tape_s, tid, f);
+            forward_sweep<T, V, NT, GRAD>(code_s, d.n_instr, c_s, xt, spt, tpt, f);
             T r[V];
             bool valid[V];
             CUSR_FOR_V {
@@ -394,16 +441,14 @@ lm_eval_kernel(const EvalParams<T> p) {
             if (grad) {
                 if (!unique) {
                     for (int k = 0; k < K; ++k) {
-                        CUSR_FOR_V g_s[k * GS + tid * V + j] = T(0);
+                        CUSR_FOR_V gt[k * GS + j] = T(0);
                     }
                 }
-                reverse_sweep<T, V, GS>(code_s, d.n_instr, c_s, x_s, spill_s, tape_s, g_s, tid,
-                                        unique);
+                reverse_sweep<T, V, NT, GS>(bcode_s, d.n_bwd, c_s, xt, spt, tpt, gt, unique);
                 if (p.jac) {
                     T *jrow = p.jac + (int64_t)wi.x * p.jac_kmax * p.N;
                     for (int k = 0; k < K; ++k) {
-                        CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] =
-                            g_s[k * GS + tid * V + j];
+                        CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = gt[k * GS + j];
                     }
                 }
                 if constexpr (!kBig) {
@@ -411,7 +456,7 @@ lm_eval_kernel(const EvalParams<T> p) {
                         T g[KC];
 #pragma unroll
                         for (int k = 0; k < KC; ++k)
-                            if (k < K) g[k] = valid[j] ? g_s[k * GS + tid * V + j] : T(0);
+                            if (k < K) g[k] = valid[j] ? gt[k * GS + j] : T(0);
 #pragma unroll
                         for (int i = 0; i < KC; ++i) {
                             if (i < K) {
@@ -424,9 +469,9 @@ lm_eval_kernel(const EvalParams<T> p) {
                 } else {
                     // stage the residual as row K, zero invalid samples' gradients
                     CUSR_FOR_V {
-                        g_s[K * GS + tid * V + j] = r[j];
+                        gt[K * GS + j] = r[j];
                         if (!valid[j])
-                            for (int k = 0; k < K; ++k) g_s[k * GS + tid * V + j] = T(0);
+                            for (int k = 0; k < K; ++k) gt[k * GS + j] = T(0);
                     }
                     __syncwarp();
                     const int sbase = warp * 32 * V;
@@ -452,7 +497,7 @@ lm_eval_kernel(const EvalParams<T> p) {
             if (tid == 0) {
                 T s = T(0);
 #pragma unroll
-                for (int w = 0; w < EVAL_WARPS; ++w) s += red_s[w];
+                for (int w = 0; w < NW; ++w) s += red_s[w];
                 dst[nblock_size(K) - 1] = s;
             }
         } else if constexpr (!kBig) {
@@ -478,10 +523,10 @@ lm_eval_kernel(const EvalParams<T> p) {
             lsum = warp_sum(lsum);
             if (lane == 0) rw[tri + K] = lsum;
             __syncthreads();
-            for (int e = tid; e < P; e += EVAL_THREADS) {
+            for (int e = tid; e < P; e += NT) {
                 T s = T(0);
 #pragma unroll
-                for (int w = 0; w < EVAL_WARPS; ++w) s += red_s[w * nblock_size(KC) + e];
+                for (int w = 0; w < NW; ++w) s += red_s[w * nblock_size(KC) + e];
                 dst[e] = s;
             }
         } else {
@@ -490,10 +535,10 @@ lm_eval_kernel(const EvalParams<T> p) {
             for (int u = 0; u < NACC; ++u)
                 if (boff_i[u] >= 0) rw[lane + 32 * u] = bacc[u];
             __syncthreads();
-            for (int e = tid; e < P; e += EVAL_THREADS) {
+            for (int e = tid; e < P; e += NT) {
                 T s = T(0);
 #pragma unroll
-                for (int w = 0; w < EVAL_WARPS; ++w) s += red_s[w * nblock_size(KC) + e];
+                for (int w = 0; w < NW; ++w) s += red_s[w * nblock_size(KC) + e];
                 dst[e] = s;
             }
         }

@@ -7,7 +7,9 @@
 
 namespace cusr {
 
-constexpr int EVAL_V = 2;   // samples per thread (both precisions)
+constexpr int EVAL_V = 2;        // samples per thread (both precisions)
+constexpr int EVAL_NT = 128;     // threads per block
+constexpr int EVAL_THREADS = EVAL_NT;
 
 // kc: constant-count class (4, 8, 12, 16, 32 for fp32; 4, 8, 32 for fp64).
 // grad = false launches the value-only variant (fp64 audit); tg = reverse tape in global

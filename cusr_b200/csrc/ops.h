@@ -41,6 +41,14 @@ template <> struct Mth<float> {
     static CUSR_HD float pow(float a, float b) { return ::powf(a, b); }
     static CUSR_HD float fabs(float a) { return ::fabsf(a); }
     static CUSR_HD float copysign(float a, float b) { return ::copysignf(a, b); }
+    // correctly rounded reciprocal: the same value as 1.0f / a, without a general division
+    static CUSR_HD float rcp(float a) {
+#ifdef __CUDA_ARCH__
+        return __frcp_rn(a);
+#else
+        return 1.0f / a;
+#endif
+    }
     static CUSR_HD bool finite(float a) { return isfinite(a); }
 };
 template <> struct Mth<double> {
@@ -63,6 +71,13 @@ template <> struct Mth<double> {
     static CUSR_HD double pow(double a, double b) { return ::pow(a, b); }
     static CUSR_HD double fabs(double a) { return ::fabs(a); }
     static CUSR_HD double copysign(double a, double b) { return ::copysign(a, b); }
+    static CUSR_HD double rcp(double a) {
+#ifdef __CUDA_ARCH__
+        return __drcp_rn(a);
+#else
+        return 1.0 / a;
+#endif
+    }
     static CUSR_HD bool finite(double a) { return isfinite(a); }
 };
 
@@ -86,14 +101,14 @@ template <typename T> CUSR_HD void unary_op(uint32_t op, T a, T &r, T &d) {
         case OP_SINH: r = M::sinh(a); d = M::cosh(a); break;
         case OP_COSH: r = M::cosh(a); d = M::sinh(a); break;
         case OP_TANH: r = M::tanh(a); d = T(1) - r * r; break;
-        case OP_LOG: r = M::log(a); d = T(1) / a; break;
-        case OP_LOGABS: r = M::log(M::fabs(a)); d = T(1) / a; break;
+        case OP_LOG: r = M::log(a); d = M::rcp(a); break;
+        case OP_LOGABS: r = M::log(M::fabs(a)); d = M::rcp(a); break;
         case OP_EXP: r = M::exp(a); d = r; break;
-        case OP_INV: r = T(1) / a; d = -r * r; break;
+        case OP_INV: r = M::rcp(a); d = -r * r; break;
         case OP_NEG: r = -a; d = T(-1); break;
         case OP_ABS: r = M::fabs(a); d = sign0(a); break;
-        case OP_SQRT: r = M::sqrt(a); d = T(1) / (T(2) * r); break;
-        case OP_SQRTABS: r = M::sqrt(M::fabs(a)); d = M::copysign(T(1) / (T(2) * r), a); break;
+        case OP_SQRT: r = M::sqrt(a); d = M::rcp(T(2) * r); break;
+        case OP_SQRTABS: r = M::sqrt(M::fabs(a)); d = M::copysign(M::rcp(T(2) * r), a); break;
         default: r = T(0); d = T(0); break;
     }
 }
@@ -105,7 +120,7 @@ template <typename T> CUSR_HD void binary_op(uint32_t op, T a, T b, T &o, T &da,
         case OP_ADD: o = a + b; da = T(1); db = T(1); break;
         case OP_SUB: o = a - b; da = T(1); db = T(-1); break;
         case OP_MUL: o = a * b; da = b; db = a; break;
-        case OP_DIV: o = a / b; da = T(1) / b; db = -o / b; break;
+        case OP_DIV: o = a / b; da = M::rcp(b); db = -o * da; break;
         case OP_POW: o = M::pow(a, b); da = b * M::pow(a, b - T(1)); db = o * M::log(a); break;
         case OP_POWABS: {
             T aa = M::fabs(a);

@@ -9,6 +9,17 @@
 
 namespace cusr {
 
+// Decode a forward opcode back to (op, mode, swap).
+void decode_xop(uint32_t xop, uint32_t &op, uint32_t &mode, uint32_t &swap) {
+    if (xop < 8) { op = OP_LOAD; mode = (xop & 1) ? M_CONST : M_VAR; swap = 0; return; }
+    if (xop < 32) { op = OP_SIN + (xop - 8); mode = M_NONE; swap = 0; return; }
+    const uint32_t r = xop - 32;
+    op = OP_ADD + r / 6;
+    const uint32_t m = (r % 6) / 2;
+    mode = m == 0 ? M_VAR : (m == 1 ? M_CONST : M_POP);
+    swap = r & 1;
+}
+
 namespace {
 
 struct Node {
@@ -67,7 +78,22 @@ struct Gen {
             max_dep = std::max(max_dep, dep);
             if (dep > PROG_MAX_SPILL) overflow = true;
         }
-        code.push_back(enc(OP_LOAD, leaf_mode(i), 0, live ? 1u : 0u, (uint32_t)nodes[i].idx, sd, 0));
+        const bool var = nodes[i].type == NT_VAR;
+        const uint32_t xop = live ? (var ? XOP_PUSH_VAR : XOP_PUSH_CONST)
+                                  : (var ? XOP_LOAD_VAR : XOP_LOAD_CONST);
+        code.push_back(enc(xop, (uint32_t)nodes[i].idx, sd, 0));
+    }
+
+    // binary instruction with canonical operand order: commutative operators never swap, a
+    // swapped comparison becomes the mirrored comparison
+    void emit_bin(uint32_t op, uint32_t mode, uint32_t swap, uint32_t idx, uint32_t sd) {
+        if (swap && (op == OP_ADD || op == OP_MUL || op == OP_BZERO)) swap = 0;
+        if (swap && (op == OP_LT || op == OP_GT || op == OP_LE || op == OP_GE)) {
+            op = op == OP_LT ? OP_GT : op == OP_GT ? OP_LT : op == OP_LE ? OP_GE : OP_LE;
+            swap = 0;
+        }
+        const uint32_t ts = alloc_tape(op, mode);
+        code.push_back(enc(xop_bin(op, mode, swap), idx, sd, ts));
     }
 
     // Emit code leaving node i's value in TOS. `live`: TOS holds a value that must survive.
@@ -76,25 +102,21 @@ struct Gen {
         if (is_leaf(i)) { emit_leaf(i, live); return; }
         if (n.type == NT_UFUNC) {
             gen(n.left, live);
-            uint32_t op = (uint32_t)n.op;
-            uint32_t ts = alloc_tape(op, M_NONE);
-            code.push_back(enc(op, M_NONE, 0, 0, 0, 0, ts));
+            const uint32_t op = (uint32_t)n.op;
+            const uint32_t ts = alloc_tape(op, M_NONE);
+            code.push_back(enc(xop_un(op), 0, 0, ts));
             return;
         }
         const int L = n.left, R = n.right;
         const uint32_t op = (uint32_t)n.op;
         if (is_leaf(R)) {                       // TOS = value(L) OP leaf
             gen(L, live);
-            uint32_t mode = leaf_mode(R);
-            uint32_t ts = alloc_tape(op, mode);
-            code.push_back(enc(op, mode, 0, 0, (uint32_t)nodes[R].idx, 0, ts));
+            emit_bin(op, leaf_mode(R), 0, (uint32_t)nodes[R].idx, 0);
             return;
         }
         if (is_leaf(L)) {                       // TOS = leaf OP value(R)
             gen(R, live);
-            uint32_t mode = leaf_mode(L);
-            uint32_t ts = alloc_tape(op, mode);
-            code.push_back(enc(op, mode, 1, 0, (uint32_t)nodes[L].idx, 0, ts));
+            emit_bin(op, leaf_mode(L), 1, (uint32_t)nodes[L].idx, 0);
             return;
         }
         // both children are subtrees: the one with the larger need goes first and is spilled
@@ -103,10 +125,47 @@ struct Gen {
         gen(first, live);
         gen(second, true);
         --dep;
-        uint32_t ts = alloc_tape(op, M_POP);
-        code.push_back(enc(op, M_POP, left_first ? 1u : 0u, 0, 0, (uint32_t)dep, ts));
+        emit_bin(op, M_POP, left_first ? 1u : 0u, 0, (uint32_t)dep);
     }
 };
+
+// Reverse program: forward instructions in reverse order, each mapped to its adjoint update;
+// instructions without reverse work are dropped.
+void emit_reverse(const uint32_t *fwd, int n, std::vector<uint32_t> &out) {
+    for (int pc = n - 1; pc >= 0; --pc) {
+        const uint32_t w = fwd[pc];
+        const uint32_t xop = w_code(w), idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+        uint32_t op, mode, swap;
+        decode_xop(xop, op, mode, swap);
+        int b = -1;
+        if (op == OP_LOAD) {
+            if (xop == XOP_LOAD_CONST) b = B_GRAD;
+            else if (xop == XOP_PUSH_CONST) b = B_GRAD_RESTORE;
+            else if (xop == XOP_PUSH_VAR) b = B_RESTORE;
+        } else if (op < OP_ADD) {
+            if (op == OP_NEG) b = B_NEG;
+            else if (op == OP_UZERO) b = B_ZERO;
+            else b = B_SCALE_T0;
+        } else {
+            const bool V = mode == M_VAR, C = mode == M_CONST;
+            switch (op) {
+                case OP_ADD: b = V ? -1 : (C ? B_GRAD : B_SPILL); break;
+                case OP_SUB:
+                    if (!swap) b = V ? -1 : (C ? B_GRAD_NEG : B_SPILL_NEG);
+                    else b = V ? B_NEG : (C ? B_GRAD_THEN_NEG : B_SPILL_THEN_NEG);
+                    break;
+                case OP_MUL: b = V ? B_SCALE_X : (C ? B_MULC : B_SPILL_T1_T0); break;
+                case OP_DIV: case OP_POW: case OP_POWABS:
+                    b = V ? B_SCALE_T0 : (C ? B_GRAD_T1_T0 : B_SPILL_T1_T0); break;
+                case OP_MAX: case OP_MIN:
+                    b = V ? B_SCALE_T0 : (C ? B_GRAD_1MT0_T0 : B_SPILL_1MT0_T0); break;
+                default:   // comparisons, unknown operator: zero partials
+                    b = V ? B_ZERO : (C ? B_GRAD_ZERO : B_SPILL_ZERO); break;
+            }
+        }
+        if (b >= 0) out.push_back(enc((uint32_t)b, idx, sd, ts));
+    }
+}
 
 }  // namespace
 
@@ -175,6 +234,13 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
     g.gen(0, false);
     if (g.overflow) { code.resize((size_t)ct.code_off); return CO_ERR_BOUNDS; }
     ct.n_instr = (int32_t)code.size() - ct.code_off;
+    ct.bcode_off = (int32_t)code.size();
+    {
+        std::vector<uint32_t> rev;
+        emit_reverse(code.data() + ct.code_off, ct.n_instr, rev);
+        code.insert(code.end(), rev.begin(), rev.end());
+    }
+    ct.n_bwd = (int32_t)code.size() - ct.bcode_off;
     ct.n_nodes = n;
     ct.K = K;
     ct.n_spill = g.max_dep;
@@ -202,7 +268,7 @@ int compile_population(const PopHeader *h, const int32_t *nt, const float *nv,
         int rc = compile_tree(nt + tm.node_offset, nv + tm.node_offset, ci + tm.node_offset,
                               tm.n_nodes, tm.K, h->n_vars, out->code, ct);
         if (rc != CO_OK) { out->bad_tree = m; return rc; }
-        out->max_instr = std::max(out->max_instr, ct.n_instr);
+        out->max_instr = std::max(out->max_instr, ct.n_instr + ct.n_bwd);
         out->max_spill = std::max(out->max_spill, ct.n_spill);
         out->max_tape = std::max(out->max_tape, ct.n_tape);
         out->max_K = std::max(out->max_K, ct.K);
@@ -245,6 +311,8 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         TreeDesc &d = out->desc[(size_t)m];
         d.code_off = ct.code_off;
         d.n_instr = ct.n_instr;
+        d.bcode_off = ct.bcode_off;
+        d.n_bwd = ct.n_bwd;
         d.K = ct.K;
         d.c_off = metas[m].c_offset;
         d.y_off = y_shared ? 0 : (int64_t)m * ldy;
@@ -267,7 +335,7 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         }
         Bin &b = out->bins[(size_t)bin_of_class[(size_t)kc]];
         b.trees.push_back(m);
-        b.max_instr = std::max(b.max_instr, ct.n_instr);
+        b.max_instr = std::max(b.max_instr, ct.n_instr + ct.n_bwd);
         b.max_spill = std::max(b.max_spill, ct.n_spill);
         b.max_tape = std::max(b.max_tape, ct.n_tape);
         b.max_items += n_chunks;
@@ -292,16 +360,18 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
     out->total_items = item_off;
 }
 
-double host_eval_program(const uint32_t *code, int n_instr, const double *x, const double *c,
-                         int K, double *grad) {
+double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, int n_bwd,
+                         const double *x, const double *c, int K, double *grad) {
     double spill[PROG_MAX_SPILL + 1];
     double tape[PROG_MAX_TAPE + 2];
     double tos = 0.0;
-    for (int pc = 0; pc < n_instr; ++pc) {
-        const uint32_t w = code[pc];
-        const uint32_t op = w_op(w), mode = w_mode(w), idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+    for (int pc = 0; pc < n_fwd; ++pc) {
+        const uint32_t w = fwd[pc];
+        const uint32_t idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+        uint32_t op, mode, swap;
+        decode_xop(w_code(w), op, mode, swap);
         if (op == OP_LOAD) {
-            if (w_push(w)) spill[sd] = tos;
+            if (w_code(w) >= XOP_PUSH_VAR) spill[sd] = tos;
             tos = (mode == M_VAR) ? x[idx] : c[idx];
         } else if (op < OP_ADD) {
             double r, d;
@@ -310,10 +380,9 @@ double host_eval_program(const uint32_t *code, int n_instr, const double *x, con
             tos = r;
         } else {
             const double s = (mode == M_VAR) ? x[idx] : (mode == M_CONST ? c[idx] : spill[sd]);
-            const bool sw = w_swap(w);
             double o, da, db;
-            binary_op<double>(op, sw ? s : tos, sw ? tos : s, o, da, db);
-            const double dt = sw ? db : da, ds = sw ? da : db;
+            binary_op<double>(op, swap ? s : tos, swap ? tos : s, o, da, db);
+            const double dt = swap ? db : da, ds = swap ? da : db;
             switch (op) {
                 case OP_MUL:
                     if (mode == M_CONST) tape[ts] = ds;
@@ -333,39 +402,32 @@ double host_eval_program(const uint32_t *code, int n_instr, const double *x, con
     if (!grad) return value;
     for (int k = 0; k < K; ++k) grad[k] = 0.0;
     double adj = 1.0;
-    for (int pc = n_instr - 1; pc >= 0; --pc) {
-        const uint32_t w = code[pc];
-        const uint32_t op = w_op(w), mode = w_mode(w), idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
-        if (op == OP_LOAD) {
-            if (mode == M_CONST) grad[idx] += adj;
-            if (w_push(w)) adj = spill[sd];
-            continue;
+    for (int pc = 0; pc < n_bwd; ++pc) {
+        const uint32_t w = bwd[pc];
+        const uint32_t idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+        const double t0 = tape[ts], t1 = tape[ts + 1];
+        switch (w_code(w)) {
+            case B_GRAD: grad[idx] += adj; break;
+            case B_GRAD_RESTORE: grad[idx] += adj; adj = spill[sd]; break;
+            case B_RESTORE: adj = spill[sd]; break;
+            case B_GRAD_NEG: grad[idx] += -adj; break;
+            case B_SPILL: spill[sd] = adj; break;
+            case B_SPILL_NEG: spill[sd] = -adj; break;
+            case B_NEG: adj = -adj; break;
+            case B_GRAD_THEN_NEG: grad[idx] += adj; adj = -adj; break;
+            case B_SPILL_THEN_NEG: spill[sd] = adj; adj = -adj; break;
+            case B_SCALE_X: adj = safe_mul(adj, x[idx]); break;
+            case B_SCALE_T0: adj = safe_mul(adj, t0); break;
+            case B_MULC: grad[idx] += safe_mul(adj, t0); adj = safe_mul(adj, c[idx]); break;
+            case B_GRAD_T1_T0: grad[idx] += safe_mul(adj, t1); adj = safe_mul(adj, t0); break;
+            case B_SPILL_T1_T0: spill[sd] = safe_mul(adj, t1); adj = safe_mul(adj, t0); break;
+            case B_GRAD_1MT0_T0: grad[idx] += safe_mul(adj, 1.0 - t0); adj = safe_mul(adj, t0); break;
+            case B_SPILL_1MT0_T0: spill[sd] = safe_mul(adj, 1.0 - t0); adj = safe_mul(adj, t0); break;
+            case B_ZERO: adj = 0.0; break;
+            case B_GRAD_ZERO: adj = 0.0; break;
+            case B_SPILL_ZERO: spill[sd] = 0.0; adj = 0.0; break;
+            default: break;
         }
-        if (op < OP_ADD) {
-            if (op == OP_NEG) adj = -adj;
-            else if (op == OP_UZERO) adj = 0.0;
-            else adj = safe_mul(adj, tape[ts]);
-            continue;
-        }
-        const bool sw = w_swap(w);
-        double dt, ds;
-        switch (op) {
-            case OP_ADD: dt = 1.0; ds = 1.0; break;
-            case OP_SUB: dt = sw ? -1.0 : 1.0; ds = -dt; break;
-            case OP_MUL:
-                if (mode == M_VAR) { dt = x[idx]; ds = 0.0; }
-                else if (mode == M_CONST) { dt = c[idx]; ds = tape[ts]; }
-                else { dt = tape[ts]; ds = tape[ts + 1]; }
-                break;
-            case OP_DIV: case OP_POW: case OP_POWABS:
-                dt = tape[ts]; ds = (mode == M_VAR) ? 0.0 : tape[ts + 1]; break;
-            case OP_MAX: case OP_MIN: dt = tape[ts]; ds = 1.0 - dt; break;
-            default: dt = 0.0; ds = 0.0; break;
-        }
-        const double as = safe_mul(adj, ds);
-        adj = safe_mul(adj, dt);
-        if (mode == M_POP) spill[sd] = as;
-        else if (mode == M_CONST) grad[idx] += as;
     }
     return value;
 }

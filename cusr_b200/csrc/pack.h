@@ -11,7 +11,9 @@ namespace cusr {
 // One compiled tree.
 struct CompiledTree {
     int32_t code_off = 0;
-    int32_t n_instr = 0;
+    int32_t n_instr = 0;      // forward instructions
+    int32_t bcode_off = 0;
+    int32_t n_bwd = 0;        // reverse instructions
     int32_t n_nodes = 0;
     int32_t K = 0;
     int32_t n_spill = 0;
@@ -70,7 +72,8 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
 
 // Reference evaluation of a compiled program on the host (fp64), forward value plus the
 // reverse sweep into grad[0..K). Used by the CPU tests of the compiler.
-double host_eval_program(const uint32_t *code, int n_instr, const double *x, const double *c,
-                         int K, double *grad);
+double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, int n_bwd,
+                         const double *x, const double *c, int K, double *grad);
+void decode_xop(uint32_t xop, uint32_t &op, uint32_t &mode, uint32_t &swap);
 
 }  // namespace cusr

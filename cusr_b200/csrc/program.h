@@ -1,27 +1,28 @@
 // program.h — the compiled tree program executed by the device interpreter.
 //
 // The pop.bin bytecode (prefix order, one node per slot: nt/nv/ci, cusr/kernel/pop_format.h)
-// is compiled on the host, once per call, into a short register-stack program:
+// is compiled on the host, once per call, into two short register-stack programs:
 //
-//   * the value being built lives in a register ("TOS") of every thread;
-//   * VAR and CONST leaves that feed a binary operator are folded into that operator as its
-//     source operand (no push / pop);
-//   * the two subtrees of a binary node are evaluated in Sethi–Ullman order (the one that
-//     needs more stack first), so the spill stack in shared memory is as shallow as it can
-//     be; the order of evaluation does not change any value (every node still computes
-//     `left OP right` on the same operands, cusr/kernel/lm_core.cuh:85-101);
-//   * each instruction carries the shared-memory slot of its spill (sd) and of its reverse-
-//     mode tape entries (ts), so the forward and backward sweeps address the same words.
+//   forward  — evaluates the tree: the value being built lives in a register ("TOS") of every
+//              thread; VAR and CONST leaves that feed a binary operator are folded into it as
+//              its source operand; two non-leaf children are evaluated in Sethi–Ullman order
+//              (the one that needs more stack first) so the shared-memory spill stack is as
+//              shallow as it can be; the order of evaluation changes no value (every node
+//              still computes `left OP right` of the same operands,
+//              cusr/kernel/lm_core.cuh:85-101). Instructions that have a reverse-mode partial
+//              write it to their tape slots.
+//   reverse  — the adjoint sweep, in reverse order, with the instructions that have no reverse
+//              work left out (`+ x`, a leaf load that starts a chain) and every other one
+//              reduced to one of a few specialised adjoint updates.
 //
-// Instruction word (32 bits):
-//   [0,6)   op       OP_*
-//   [6,8)   mode     source operand: M_POP (spill stack slot sd), M_VAR (x[idx]),
-//                    M_CONST (c[idx]), M_NONE (unary)
-//   [8]     swap     1: the source operand is the LEFT operand (src OP tos)
-//   [9]     push     OP_LOAD only: spill the live TOS to slot sd before loading
-//   [10,18) idx      variable index or constant rank
-//   [18,24) sd       spill slot
-//   [24,32) ts       first tape slot of this instruction
+// Every opcode is specialised by operator, operand source and operand order, so the
+// interpreter's cases are straight-line code.
+//
+// Word (32 bits, both programs):
+//   [0,8)   opcode    forward: XOP (xop_*), reverse: BOP (B_*)
+//   [8,16)  idx       variable index or constant rank
+//   [16,24) sd        spill slot
+//   [24,32) ts        first tape slot
 #pragma once
 #include <stdint.h>
 
@@ -64,27 +65,57 @@ enum FuncId : int32_t {
     F_NEG = 25, F_ABS = 26, F_SQRT = 27, F_LOOSE_SQRT = 28
 };
 
-__host__ __device__ constexpr inline uint32_t enc(uint32_t op, uint32_t mode, uint32_t swap,
-                                                  uint32_t push, uint32_t idx, uint32_t sd,
+__host__ __device__ constexpr inline uint32_t enc(uint32_t code, uint32_t idx, uint32_t sd,
                                                   uint32_t ts) {
-    return (op & 63u) | ((mode & 3u) << 6) | ((swap & 1u) << 8) | ((push & 1u) << 9) |
-           ((idx & 255u) << 10) | ((sd & 63u) << 18) | ((ts & 255u) << 24);
+    return (code & 255u) | ((idx & 255u) << 8) | ((sd & 255u) << 16) | ((ts & 255u) << 24);
 }
-__host__ __device__ inline uint32_t w_op(uint32_t w)   { return w & 63u; }
-__host__ __device__ inline uint32_t w_mode(uint32_t w) { return (w >> 6) & 3u; }
-__host__ __device__ inline uint32_t w_swap(uint32_t w) { return (w >> 8) & 1u; }
-__host__ __device__ inline uint32_t w_push(uint32_t w) { return (w >> 9) & 1u; }
-__host__ __device__ inline uint32_t w_idx(uint32_t w)  { return (w >> 10) & 255u; }
-__host__ __device__ inline uint32_t w_sd(uint32_t w)   { return (w >> 18) & 63u; }
+__host__ __device__ inline uint32_t w_code(uint32_t w) { return w & 255u; }
+__host__ __device__ inline uint32_t w_idx(uint32_t w)  { return (w >> 8) & 255u; }
+__host__ __device__ inline uint32_t w_sd(uint32_t w)   { return (w >> 16) & 255u; }
 __host__ __device__ inline uint32_t w_ts(uint32_t w)   { return (w >> 24) & 255u; }
 
-constexpr int PROG_MAX_SPILL = 63;   // sd field
+// forward opcodes
+constexpr uint32_t XOP_LOAD_VAR = 0, XOP_LOAD_CONST = 1, XOP_PUSH_VAR = 2, XOP_PUSH_CONST = 3;
+// unary operator u (OP_SIN .. OP_UZERO)
+__host__ __device__ constexpr inline uint32_t xop_un(uint32_t op) { return 8u + (op - OP_SIN); }
+// binary operator (OP_ADD .. OP_BZERO) with source mode (M_VAR / M_CONST / M_POP) and order
+__host__ __device__ constexpr inline uint32_t xop_bin(uint32_t op, uint32_t mode, uint32_t swap) {
+    return 32u + (op - OP_ADD) * 6u + (mode == M_VAR ? 0u : (mode == M_CONST ? 2u : 4u)) + swap;
+}
+
+// reverse opcodes (t0 = tape[ts], t1 = tape[ts+1], safe = exact-zero annihilating product)
+enum BOp : uint32_t {
+    B_GRAD = 0,          // grad[idx] <- adj
+    B_GRAD_RESTORE,      // grad[idx] <- adj; adj <- spill[sd]
+    B_RESTORE,           // adj <- spill[sd]
+    B_GRAD_NEG,          // grad[idx] <- -adj
+    B_SPILL,             // spill[sd] <- adj
+    B_SPILL_NEG,         // spill[sd] <- -adj
+    B_NEG,               // adj <- -adj
+    B_GRAD_THEN_NEG,     // grad[idx] <- adj; adj <- -adj
+    B_SPILL_THEN_NEG,    // spill[sd] <- adj; adj <- -adj
+    B_SCALE_X,           // adj <- safe(adj, x[idx])
+    B_SCALE_T0,          // adj <- safe(adj, t0)
+    B_MULC,              // grad[idx] <- safe(adj, t0); adj <- safe(adj, c[idx])
+    B_GRAD_T1_T0,        // grad[idx] <- safe(adj, t1); adj <- safe(adj, t0)
+    B_SPILL_T1_T0,       // spill[sd] <- safe(adj, t1); adj <- safe(adj, t0)
+    B_GRAD_1MT0_T0,      // grad[idx] <- safe(adj, 1 - t0); adj <- safe(adj, t0)
+    B_SPILL_1MT0_T0,     // spill[sd] <- safe(adj, 1 - t0); adj <- safe(adj, t0)
+    B_ZERO,              // adj <- 0
+    B_GRAD_ZERO,         // grad[idx] <- 0; adj <- 0
+    B_SPILL_ZERO,        // spill[sd] <- 0; adj <- 0
+    B_COUNT
+};
+
+constexpr int PROG_MAX_SPILL = 63;   // spill slots
 constexpr int PROG_MAX_TAPE  = 255;  // ts field (+1 for two-slot entries)
 
-// Per-tree descriptor uploaded to the device (48 bytes).
+// Per-tree descriptor uploaded to the device (64 bytes).
 struct TreeDesc {
-    int32_t code_off;    // first instruction in the code array
-    int32_t n_instr;
+    int32_t code_off;    // first forward instruction in the code array
+    int32_t n_instr;     // forward instructions
+    int32_t bcode_off;   // first reverse instruction
+    int32_t n_bwd;       // reverse instructions
     int32_t K;           // constants of the tree
     int32_t c_off;       // offset of the tree's constants
     int64_t y_off;       // element offset of the tree's target row (0 when shared)
@@ -94,8 +125,9 @@ struct TreeDesc {
     uint16_t n_spill;    // spill slots used
     uint8_t  n_tape;     // tape slots used
     uint8_t  flags;      // TD_UNIQUE_CONST: every rank 0..K-1 occurs exactly once
+    int32_t pad[2];
 };
-static_assert(sizeof(TreeDesc) == 48, "TreeDesc layout");
+static_assert(sizeof(TreeDesc) == 64, "TreeDesc layout");
 constexpr uint8_t TD_UNIQUE_CONST = 1;
 
 // Sizes of the normal-equation block of a tree with K constants:

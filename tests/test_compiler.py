@@ -26,15 +26,17 @@ def compile_tree(nt, nv, ci, K, n_vars):
     rc = LIB.cusr_compile_tree(nt.ctypes.data_as(VP), nv.ctypes.data_as(VP), ci.ctypes.data_as(VP),
                                len(nt), int(K), int(n_vars), code.ctypes.data_as(VP), 2048,
                                info.ctypes.data_as(VP))
-    return rc, code[: info[0]].copy(), info
+    return rc, (code[: info[0]].copy(), code[info[0]: info[0] + info[4]].copy()), info
 
 
 def run_program(code, x, c, K):
+    fwd, bwd = code
     x = np.ascontiguousarray(x, np.float64)
     c = np.ascontiguousarray(c if len(c) else [0.0], np.float64)
     g = np.zeros(max(K, 1))
-    v = LIB.cusr_eval_program(code.ctypes.data_as(VP), len(code), x.ctypes.data_as(VP),
-                              c.ctypes.data_as(VP), int(K), g.ctypes.data_as(VP))
+    v = LIB.cusr_eval_program(fwd.ctypes.data_as(VP), len(fwd), bwd.ctypes.data_as(VP), len(bwd),
+                              x.ctypes.data_as(VP), c.ctypes.data_as(VP), int(K),
+                              g.ctypes.data_as(VP))
     return v, g[:K]
 
 
@@ -137,6 +139,15 @@ def test_deep_spill_stack():
         v, g = run_program(code, xs[i], c, K)
         np.testing.assert_allclose(v, y[i], rtol=1e-12)
         np.testing.assert_allclose(g, J[i], rtol=1e-10, atol=1e-12)
+
+
+def test_reverse_program_drops_no_op_instructions():
+    # c0 * x0 + x1: the "+ x1" has no reverse work
+    nt, nv, ci = make_tree([("b", 1), ("b", 3), ("c",), ("v", 0), ("v", 1)])
+    rc, (fwd, bwd), info = compile_tree(nt, nv, ci, 1, 2)
+    assert rc == 0 and len(bwd) < len(fwd)
+    v, g = run_program((fwd, bwd), np.array([2.0, 3.0]), np.array([0.5]), 1)
+    assert v == pytest.approx(4.0) and g[0] == pytest.approx(2.0)
 
 
 def test_repeated_constant_rank_accumulates():
