@@ -329,6 +329,14 @@ def run_profile_case(args) -> None:
     from cusr_b200 import InProcessCO, synth
 
     pop = synth.make_config(CONFIG, M=2048, seed=0)
+    metas = np.asarray(pop["metas"])
+    K = metas[:, 3]
+    bins = {}
+    for kc, lo, hi in ((4, 0, 4), (8, 5, 8), (12, 9, 12)):
+        sel = (K >= lo) & (K <= hi)
+        bins[str(kc)] = {"trees": int(sel.sum()), "nodes": int(metas[sel, 1].sum()),
+                         "tree_samples": int(sel.sum()) * int(pop["N"])}
+    print(json.dumps({"profile_bins": bins}), flush=True)
     co = InProcessCO(device_id=0)
     co.load(pop, precision="fp32", y_shared=True)
     res = co.fit_loaded(max_iter=args.profile_iters)

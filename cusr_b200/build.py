@@ -49,16 +49,21 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
+def build(force: bool = False, verbose: bool = False, defines: tuple = (), obj_dir: Path = None,
+          lib: Path = None) -> Path:
+    """Compile every source for sm_100a and link the library (incremental)."""
     nvcc = _nvcc()
-    OBJ.mkdir(exist_ok=True)
+    OBJ = obj_dir or globals()["OBJ"]
+    LIB = lib or globals()["LIB"]
+    OBJ.mkdir(parents=True, exist_ok=True)
+    flags = NVCC_FLAGS + [f"-D{d}" for d in defines]
     hdrs = _headers()
     jobs = []
     for src in SOURCES:
         s = CSRC / src
         o = OBJ / (s.stem + ".o")
         if force or _stale(o, [s, *hdrs, Path(__file__)]):
-            jobs.append([nvcc, *NVCC_FLAGS, "-c", str(s), "-o", str(o)])
+            jobs.append([nvcc, *flags, "-c", str(s), "-o", str(o)])
 
     def run(cmd):
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -72,6 +77,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objs = [OBJ / (Path(s).stem + ".o") for s in SOURCES]
     if force or jobs or _stale(LIB, objs):
         run([nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"])
+    if lib is not None:
+        return LIB
     for alias in ALIASES:
         a = HERE / alias
         if a.is_symlink() or a.exists():

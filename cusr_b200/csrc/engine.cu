@@ -54,12 +54,17 @@ struct Ctx {
     int device = -1;
     int sm_count = 0;
     cudaStream_t stream = nullptr;
+    // bins of one pass run on these streams concurrently, so one bin's tail overlaps the next
+    static constexpr int kBinStreams = 4;
+    cudaStream_t bin_streams[kBinStreams] = {};
+    cudaEvent_t ev_fork = nullptr, ev_join[kBinStreams] = {};
+    DBuf tape_gs[kBinStreams];
     DBuf code, desc, bin_trees, bin_tree_off, bin_item_off, items, n_items, counter;
     DBuf xs_raw, xs, ym;
     DBuf c, ctry, delta, cinit_f, lam, loss, loss_init, status, iters, pending, n_run, n_eval;
     DBuf partials, blk;
     DBuf c64, l64, n_rev;
-    DBuf vals, jac, tape_g;
+    DBuf vals, jac;
     int *h_nrun = nullptr;                  // pinned, one slot per iteration parity
     std::vector<cudaEvent_t> events;        // timing events, reused across calls
     cudaEvent_t ev_nrun[2] = {nullptr, nullptr};
@@ -182,7 +187,11 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         CK(cudaGetLastError());
         ctx->stats.kernel_launches++;
     }
+    const int n_streams = std::min(n_bins, (int)Ctx::kBinStreams);
+    CK(cudaEventRecord(ctx->ev_fork, ctx->stream));
+    for (int si = 0; si < n_streams; ++si) CK(cudaStreamWaitEvent(ctx->bin_streams[si], ctx->ev_fork, 0));
     for (int b = 0; b < n_bins; ++b) {
+        const int si = b % n_streams;
         const Bin &bin = sc.bins[(size_t)b];
         EvalParams<T> p;
         p.code = P<uint32_t>(ctx->code);
@@ -208,7 +217,11 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         // tape in shared memory unless that leaves room for fewer than two resident blocks
         bool tg = false;
         size_t smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, true);
+#ifdef CUSR_FORCE_GLOBAL_TAPE
+        if (grad) {
+#else
         if (grad && 2 * (smem + 1024) > (size_t)ctx->smem_optin) {
+#endif
             tg = true;
             smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, false);
         }
@@ -219,12 +232,17 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         if (grid > bin.max_items) grid = std::max<int64_t>(1, bin.max_items);
         p.tape_g = nullptr;
         if (tg) {
-            GROW(ctx->tape_g, (size_t)grid * p.tape_cap * EVAL_THREADS * EVAL_V * sizeof(T));
-            p.tape_g = ctx->tape_g.ptr;
+            // one global tape per stream: bins on different streams run concurrently
+            GROW(ctx->tape_gs[si], (size_t)grid * p.tape_cap * EVAL_THREADS * EVAL_V * sizeof(T));
+            p.tape_g = ctx->tape_gs[si].ptr;
         }
-        CK(Launch<T>::eval(kc, grad, tg, p, (int)grid, smem, ctx->stream));
+        CK(Launch<T>::eval(kc, grad, tg, p, (int)grid, smem, ctx->bin_streams[si]));
         ctx->stats.eval_launches++;
         ctx->stats.kernel_launches++;
+    }
+    for (int si = 0; si < n_streams; ++si) {
+        CK(cudaEventRecord(ctx->ev_join[si], ctx->bin_streams[si]));
+        CK(cudaStreamWaitEvent(ctx->stream, ctx->ev_join[si], 0));
     }
     (void)pk;
     return CO_OK;
@@ -708,6 +726,15 @@ int co_init(int device_id, void **handle_out) {
         {"pinned counter", cudaMallocHost(&ctx->h_nrun, 2 * sizeof(int))},
         {"event 0", cudaEventCreateWithFlags(&ctx->ev_nrun[0], cudaEventDisableTiming)},
         {"event 1", cudaEventCreateWithFlags(&ctx->ev_nrun[1], cudaEventDisableTiming)},
+        {"bin stream 0", cudaStreamCreateWithFlags(&ctx->bin_streams[0], cudaStreamNonBlocking)},
+        {"bin stream 1", cudaStreamCreateWithFlags(&ctx->bin_streams[1], cudaStreamNonBlocking)},
+        {"bin stream 2", cudaStreamCreateWithFlags(&ctx->bin_streams[2], cudaStreamNonBlocking)},
+        {"bin stream 3", cudaStreamCreateWithFlags(&ctx->bin_streams[3], cudaStreamNonBlocking)},
+        {"fork event", cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming)},
+        {"join event 0", cudaEventCreateWithFlags(&ctx->ev_join[0], cudaEventDisableTiming)},
+        {"join event 1", cudaEventCreateWithFlags(&ctx->ev_join[1], cudaEventDisableTiming)},
+        {"join event 2", cudaEventCreateWithFlags(&ctx->ev_join[2], cudaEventDisableTiming)},
+        {"join event 3", cudaEventCreateWithFlags(&ctx->ev_join[3], cudaEventDisableTiming)},
         {"fit event 0", cudaEventCreate(&ctx->ev_fit[0])},
         {"fit event 1", cudaEventCreate(&ctx->ev_fit[1])},
         {"fp32 kernels", eval_prepare_f32()},
@@ -901,7 +928,8 @@ void co_teardown(void *handle) {
                     &ctx->xs_raw, &ctx->xs, &ctx->ym, &ctx->c, &ctx->ctry, &ctx->delta,
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
                     &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
-                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac, &ctx->tape_g};
+                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac,
+                    &ctx->tape_gs[0], &ctx->tape_gs[1], &ctx->tape_gs[2], &ctx->tape_gs[3]};
     for (DBuf *b : bufs) release(*b);
     for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->ev_nrun)
@@ -909,6 +937,11 @@ void co_teardown(void *handle) {
     for (cudaEvent_t e : ctx->ev_fit)
         if (e) cudaEventDestroy(e);
     if (ctx->h_nrun) cudaFreeHost(ctx->h_nrun);
+    for (cudaStream_t bs : ctx->bin_streams)
+        if (bs) cudaStreamDestroy(bs);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    for (cudaEvent_t e : ctx->ev_join)
+        if (e) cudaEventDestroy(e);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }

@@ -72,7 +72,7 @@ struct EvalSmem {
     __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
                                  bool tape_in_smem = true) {
         size_t o = 0;
-        code = o;  o += align16((size_t)code_cap * 4);
+        code = o;  o += align16((size_t)(code_cap + 1) * 4);
         cval = o;  o += align16((size_t)CO_MAX_K * sizeof(T));
         x = o;     o += align16((size_t)n_vars * NT * V * 4);
         spill = o; o += align16((size_t)spill_cap * NT * V * sizeof(T));
@@ -162,8 +162,10 @@ __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code,
                                               const VecF<V> *__restrict__ xt,
                                               VecT<T, V> *__restrict__ sp,
                                               VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
+    uint32_t wn = code[0];
     for (int pc = 0; pc < n; ++pc) {
-        const uint32_t w = code[pc];
+        const uint32_t w = wn;
+        wn = code[pc + 1];   // next word in flight while this one executes (programs are padded)
         switch (w_code(w)) {
             case XOP_PUSH_VAR:
                 sp[w_sd(w) * NT] = pack<T, V>(tos);
@@ -232,8 +234,10 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
     typedef VecT<T, V> VT;
     T adj[V];
     CUSR_FOR_V adj[j] = T(1);
+    uint32_t wn = code[0];
     for (int pc = 0; pc < n; ++pc) {
-        const uint32_t w = code[pc];
+        const uint32_t w = wn;
+        wn = code[pc + 1];
         switch (w_code(w)) {
             case B_GRAD:
                 grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
@@ -387,6 +391,7 @@ lm_eval_kernel(const EvalParams<T> p) {
         const bool grad = GRAD && K > 0;
         const int n_code = d.n_instr + d.n_bwd;   // the reverse program follows the forward one
         for (int i = tid; i < n_code; i += NT) code_s[i] = p.code[d.code_off + i];
+        if (tid == 0) code_s[n_code] = 0u;   // prefetch pad after the reverse program
         for (int i = tid; i < K; i += NT) c_s[i] = p.c[d.c_off + i];
         __syncthreads();
         const uint32_t *bcode_s = code_s + d.n_instr;

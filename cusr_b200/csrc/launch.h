@@ -7,8 +7,14 @@
 
 namespace cusr {
 
-constexpr int EVAL_V = 2;        // samples per thread (both precisions)
-constexpr int EVAL_NT = 128;     // threads per block
+#ifndef CUSR_EVAL_V
+#define CUSR_EVAL_V 2
+#endif
+#ifndef CUSR_EVAL_NT
+#define CUSR_EVAL_NT 128
+#endif
+constexpr int EVAL_V = CUSR_EVAL_V;    // samples per thread (both precisions)
+constexpr int EVAL_NT = CUSR_EVAL_NT;  // threads per block
 constexpr int EVAL_THREADS = EVAL_NT;
 
 // kc: constant-count class (4, 8, 12, 16, 32 for fp32; 4, 8, 32 for fp64).

@@ -276,6 +276,18 @@ int compile_population(const PopHeader *h, const int32_t *nt, const float *nv,
     return CO_OK;
 }
 
+int tape_class(int n_tape) {
+#ifdef CUSR_NO_TAPE_CLASSES
+    (void)n_tape;
+    return 0;
+#else
+    static const int bounds[] = {8, 16, 24, 32, 48, 64, 96, 128, 192, 256};
+    int c = 0;
+    while (c < 9 && n_tape > bounds[c]) ++c;
+    return c;
+#endif
+}
+
 int kc_class(int K, bool fp64) {
     if (fp64) {
         if (K <= 4) return 4;
@@ -302,8 +314,9 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
     const int n_chunks = (int)((N + out->chunk - 1) / out->chunk);
     const int64_t ldy = ((int64_t)N + round - 1) / round * round;
 
-    const int classes[] = {4, 8, 12, 16, 32};
-    std::vector<int> bin_of_class(33, -1);
+    // bins: (constant-count class, tape class); a launch reserves shared memory for the
+    // largest tape of its bin, so trees of very different tape sizes are kept apart
+    std::vector<int> bin_of_class(33 * 16, -1);
     std::vector<double> cost((size_t)M);
     int64_t p_off = 0, q_off = 0;
     for (int m = 0; m < M; ++m) {
@@ -328,12 +341,15 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         // forward + reverse sweep per instruction, plus the normal-equation update
         cost[(size_t)m] = (double)N * (2.0 * ct.n_instr + 0.5 * ct.K * (ct.K + 1) * 0.25);
         const int kc = kc_class(ct.K, fp64);
-        if (bin_of_class[(size_t)kc] < 0) {
-            bin_of_class[(size_t)kc] = (int)out->bins.size();
+        const int tc = tape_class(ct.n_tape);
+        const size_t key = (size_t)kc * 16 + (size_t)tc;
+        if (bin_of_class[key] < 0) {
+            bin_of_class[key] = (int)out->bins.size();
             out->bins.push_back(Bin{});
             out->bins.back().kc = kc;
+            out->bins.back().tclass = tc;
         }
-        Bin &b = out->bins[(size_t)bin_of_class[(size_t)kc]];
+        Bin &b = out->bins[(size_t)bin_of_class[key]];
         b.trees.push_back(m);
         b.max_instr = std::max(b.max_instr, ct.n_instr + ct.n_bwd);
         b.max_spill = std::max(b.max_spill, ct.n_spill);
@@ -341,10 +357,10 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         b.max_items += n_chunks;
         b.cost += cost[(size_t)m];
     }
-    (void)classes;
     // bins in ascending class order; trees inside a bin most expensive first (LPT order)
-    std::sort(out->bins.begin(), out->bins.end(),
-              [](const Bin &a, const Bin &b) { return a.kc < b.kc; });
+    std::sort(out->bins.begin(), out->bins.end(), [](const Bin &a, const Bin &b) {
+        return a.kc != b.kc ? a.kc < b.kc : a.tclass < b.tclass;
+    });
     int64_t item_off = 0, tree_off = 0;
     for (Bin &b : out->bins) {
         std::stable_sort(b.trees.begin(), b.trees.end(), [&](int32_t x, int32_t y) {

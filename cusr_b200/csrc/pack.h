@@ -44,6 +44,7 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
 // the fused accumulation), each bin evaluated by one kernel instantiation.
 struct Bin {
     int kc = 0;                       // constant-count class (template parameter)
+    int tclass = 0;                   // tape-size class (shared-memory reservation)
     std::vector<int32_t> trees;       // tree ids, most expensive first
     int32_t max_instr = 0, max_spill = 0, max_tape = 0;
     int64_t max_items = 0;            // sum of chunks of the bin's trees
@@ -64,6 +65,8 @@ struct Schedule {
 
 // K classes for fp32 and fp64 arithmetic (largest class = cooperative accumulation).
 int kc_class(int K, bool fp64);
+// Tape-size classes (slot bounds 8, 16, 24, 32, 48, 64, 96, 128, 192, 256).
+int tape_class(int n_tape);
 
 // Build the schedule: bins, per-tree descriptors, chunking (round = samples per round of a
 // block, resident = concurrently resident blocks on the device).
