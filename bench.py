@@ -323,6 +323,42 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_config(args) -> None:
+    """One BASELINE configuration on one GPU (pr1, mid, physics, long, scale, sharded):
+    resident-input fits/s and node-evals/s, device-timed, with its CPU baseline sample."""
+    from cusr_b200 import InProcessCO, synth
+
+    name = args.config
+    pop = synth.make_config(name, M=args.M, N=args.N, seed=0)
+    precision, max_iter = pop["precision"], int(pop["max_iter"])
+    shared = np.asarray(pop["ym"]).ndim == 1
+    co = InProcessCO(device_id=0)
+    co.load(pop, precision=precision, y_shared=shared)
+    for _ in range(args.warmup):
+        co.fit_loaded(max_iter=max_iter)
+    dev, nodes, launches, res = [], 0, 0, None
+    for _ in range(args.steps):
+        res = co.fit_loaded(max_iter=max_iter)
+        st = co.stats()
+        dev.append(st["device_ms"])
+        nodes += st["node_evals"]
+        launches += st["kernel_launches"]
+    total_ms = float(sum(dev))
+    M = int(pop["M"])
+    line = {"metric": f"LM fits/sec ({name}: M={M}, N={pop['N']}, {max_iter} iters, {precision})",
+            "value": M * args.steps / (total_ms / 1e3), "unit": "fits/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f64" if precision == "fp64" else "f32", "data": "synthetic",
+            "config": {"workload": name, "trees": M, "N": int(pop["N"]), "max_iter": max_iter,
+                       "y_shared": bool(shared)},
+            "node_evals_per_s": nodes / (total_ms / 1e3), "gpu_launches": launches,
+            "statuses": np.bincount(res["status"], minlength=5).tolist()}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(pop, target_s=10.0)
+    print(json.dumps(line), flush=True)
+
+
 def run_profile_case(args) -> None:
     """Small case of the same kernel for ncu captures: 2,048 trees of the metric
     configuration (same N, same tree distribution), a few LM iterations."""
@@ -358,7 +394,15 @@ def main() -> None:
     ap.add_argument("--profile-case", action="store_true",
                     help="run the small ncu case (2,048 trees) instead of the benchmark")
     ap.add_argument("--profile-iters", type=int, default=2)
+    ap.add_argument("--config", default=None,
+                    help="bench one BASELINE configuration instead of the headline metric: "
+                         "pr1, mid, physics, long, scale, sharded")
+    ap.add_argument("--M", type=int, default=None)
+    ap.add_argument("--N", type=int, default=None)
     args = ap.parse_args()
+    if args.config:
+        run_config(args)
+        return
     if args.profile_case:
         run_profile_case(args)
         return

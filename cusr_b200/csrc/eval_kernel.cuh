@@ -203,7 +203,10 @@ __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code,
 #undef CUSR_B3
 #undef CUSR_B6
 #undef CUSR_B
-            default: break;
+            default:
+                // every word was checked against this case set on the host
+                // (valid_forward_code / valid_reverse_code), so no bounds check is needed
+                __builtin_unreachable();
         }
     }
 }
@@ -331,7 +334,10 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
                 sp[w_sd(w) * NT] = pack<T, V>(a);
                 break;
             }
-            default: break;
+            default:
+                // every word was checked against this case set on the host
+                // (valid_forward_code / valid_reverse_code), so no bounds check is needed
+                __builtin_unreachable();
         }
     }
 }

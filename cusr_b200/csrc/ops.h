@@ -91,9 +91,24 @@ template <typename T> CUSR_HD T safe_mul(T a, T b) {
     return (a == T(0) || b == T(0)) ? T(0) : a * b;
 }
 
+template <typename T> CUSR_HD void unary_op(uint32_t op, T a, T &r, T &d);
+template <typename T> CUSR_HD void binary_op(uint32_t op, T a, T b, T &o, T &da, T &db);
+
+#if defined(__CUDA_ARCH__)
+// operators outside the common grammar run out of line, keeping the interpreter's hot code
+// small; both helpers are the same formulas as below
+template <typename T> __device__ __noinline__ void unary_rare(uint32_t op, T a, T &r, T &d);
+template <typename T> __device__ __noinline__ void binary_rare(uint32_t op, T a, T b, T &o, T &da, T &db);
+#define CUSR_IS_RARE_UN(op) ((op) == OP_TAN || (op) == OP_SINH || (op) == OP_COSH || (op) == OP_TANH)
+#define CUSR_IS_RARE_BIN(op) ((op) == OP_POW || (op) == OP_POWABS)
+#endif
+
 // Unary operator: r = f(a), d = f'(a).
 template <typename T> CUSR_HD void unary_op(uint32_t op, T a, T &r, T &d) {
     using M = Mth<T>;
+#if defined(__CUDA_ARCH__)
+    if (CUSR_IS_RARE_UN(op)) { unary_rare<T>(op, a, r, d); return; }
+#endif
     switch (op) {
         case OP_SIN: { T s, c; M::sincos(a, &s, &c); r = s; d = c; break; }
         case OP_COS: { T s, c; M::sincos(a, &s, &c); r = c; d = -s; break; }
@@ -116,6 +131,9 @@ template <typename T> CUSR_HD void unary_op(uint32_t op, T a, T &r, T &d) {
 // Binary operator: o = a OP b (a = left operand), da = do/da, db = do/db.
 template <typename T> CUSR_HD void binary_op(uint32_t op, T a, T b, T &o, T &da, T &db) {
     using M = Mth<T>;
+#if defined(__CUDA_ARCH__)
+    if (CUSR_IS_RARE_BIN(op)) { binary_rare<T>(op, a, b, o, da, db); return; }
+#endif
     switch (op) {
         case OP_ADD: o = a + b; da = T(1); db = T(1); break;
         case OP_SUB: o = a - b; da = T(1); db = T(-1); break;
@@ -142,6 +160,29 @@ template <typename T> CUSR_HD void binary_op(uint32_t op, T a, T b, T &o, T &da,
         default: o = T(0); da = T(0); db = T(0); break;
     }
 }
+
+#if defined(__CUDA_ARCH__)
+template <typename T> __device__ __noinline__ void unary_rare(uint32_t op, T a, T &r, T &d) {
+    using M = Mth<T>;
+    switch (op) {
+        case OP_TAN: r = M::tan(a); d = T(1) + r * r; break;
+        case OP_SINH: r = M::sinh(a); d = M::cosh(a); break;
+        case OP_COSH: r = M::cosh(a); d = M::sinh(a); break;
+        default: r = M::tanh(a); d = T(1) - r * r; break;
+    }
+}
+template <typename T> __device__ __noinline__ void binary_rare(uint32_t op, T a, T b, T &o, T &da, T &db) {
+    using M = Mth<T>;
+    if (op == OP_POW) {
+        o = M::pow(a, b); da = b * M::pow(a, b - T(1)); db = o * M::log(a);
+    } else {
+        T aa = M::fabs(a);
+        o = M::pow(aa, b);
+        da = b * M::pow(aa, b - T(1)) * sign0(a);
+        db = o * M::log(aa);
+    }
+}
+#endif
 
 // Tape slots an instruction writes in the forward sweep (read back in the reverse sweep).
 //   unary                      : d            (NEG, UZERO: none)

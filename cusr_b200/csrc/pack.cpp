@@ -241,6 +241,11 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
         code.insert(code.end(), rev.begin(), rev.end());
     }
     ct.n_bwd = (int32_t)code.size() - ct.bcode_off;
+    // the interpreter dispatches without a bounds check: every word must be a known opcode
+    for (int i = 0; i < ct.n_instr; ++i)
+        if (!valid_forward_code(w_code(code[(size_t)(ct.code_off + i)]))) return CO_ERR_BADTREE;
+    for (int i = 0; i < ct.n_bwd; ++i)
+        if (!valid_reverse_code(w_code(code[(size_t)(ct.bcode_off + i)]))) return CO_ERR_BADTREE;
     ct.n_nodes = n;
     ct.K = K;
     ct.n_spill = g.max_dep;

@@ -110,6 +110,18 @@ enum BOp : uint32_t {
 constexpr int PROG_MAX_SPILL = 63;   // spill slots
 constexpr int PROG_MAX_TAPE  = 255;  // ts field (+1 for two-slot entries)
 
+// The opcodes the device interpreter has a case for (its switch has no bounds check).
+__host__ __device__ inline bool valid_forward_code(uint32_t c) {
+    if (c <= XOP_PUSH_CONST) return true;
+    if (c >= xop_un(OP_SIN) && c <= xop_un(OP_UZERO)) return true;
+    if (c < 32u || c > xop_bin(OP_BZERO, M_POP, 1)) return false;
+    const uint32_t op = OP_ADD + (c - 32u) / 6u, swap = (c - 32u) & 1u;
+    const bool unordered = op == OP_ADD || op == OP_MUL || op == OP_LT || op == OP_GT ||
+                           op == OP_LE || op == OP_GE || op == OP_BZERO;
+    return !(unordered && swap);
+}
+__host__ __device__ inline bool valid_reverse_code(uint32_t c) { return c < B_COUNT; }
+
 // Per-tree descriptor uploaded to the device (64 bytes).
 struct TreeDesc {
     int32_t code_off;    // first forward instruction in the code array
