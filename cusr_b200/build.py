@@ -28,7 +28,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-O3", f"-I{INCLUDE}"]
 SOURCES = ["eval_f32.cu", "eval_f64.cu", "engine.cu", "pack.cpp", "debug_api.cpp",
-           "noalloc.cu"]
+           "noalloc.cu", "shard_comm.cpp"]
 
 
 def _nvcc() -> str:
@@ -76,7 +76,7 @@ def build(force: bool = False, verbose: bool = False, defines: tuple = (), obj_d
         list(ex.map(run, jobs))
     objs = [OBJ / (Path(s).stem + ".o") for s in SOURCES]
     if force or jobs or _stale(LIB, objs):
-        run([nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"])
+        run([nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart", "-ldl"])
     if lib is not None:
         return LIB
     for alias in ALIASES:

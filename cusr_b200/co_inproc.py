@@ -30,6 +30,7 @@ CO_ERR_SUM_NODES = -3
 CO_ERR_NULLARG = -4
 CO_ERR_OOM = -5
 CO_ERR_BADTREE = -6
+SHARD_ID_BYTES = 128
 
 CO_PREC_FP32 = 0
 CO_PREC_FP64 = 1
@@ -76,7 +77,7 @@ class CoOptions(ctypes.Structure):
         ("max_iter", ctypes.c_int32), ("y_shared", ctypes.c_int32),
         ("lambda0", ctypes.c_double), ("xtol", ctypes.c_double),
         ("fp64_audit", ctypes.c_int32), ("early_exit", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 8),
+        ("sample_sharded", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7),
     ]
 
 
@@ -128,6 +129,13 @@ SIGNATURES = {
     "co_evaluate": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
                      ctypes.POINTER(TreeMeta), _F64, _F32, _F32, ctypes.c_int, ctypes.c_int,
                      _F64, _F64, _F64], ctypes.c_int),
+    "co_shard_unique_id": ([ctypes.POINTER(ctypes.c_ubyte)], ctypes.c_int),
+    "co_shard_init": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte), ctypes.c_int,
+                       ctypes.c_int, ctypes.c_double], ctypes.c_int),
+    "co_optimize_sharded": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
+                             ctypes.POINTER(TreeMeta), _F32, _F32, _F32,
+                             ctypes.POINTER(CoOptions), _F64, _I32, _F64, _F64, _I32],
+                            ctypes.c_int),
 }
 
 
@@ -147,6 +155,17 @@ def load_library(lib_path: str | Path | None = None) -> ctypes.CDLL:
         fn.argtypes = argtypes
         fn.restype = restype
     return lib
+
+
+def shard_unique_id(lib_path: str | Path | None = None) -> bytes:
+    """A new 128-byte group id for the sample-sharded mode (co_shard_unique_id); create it
+    on one rank and give it to every rank's InProcessCO.shard_init."""
+    lib = load_library(lib_path)
+    buf = (ctypes.c_ubyte * SHARD_ID_BYTES)()
+    rc = lib.co_shard_unique_id(buf)
+    if rc != CO_OK:
+        raise COError(rc, "co_shard_unique_id")
+    return bytes(buf)
 
 
 def _c_ptr(arr, dtype):
@@ -250,6 +269,32 @@ class InProcessCO:
         """Extended fit: precision 'fp32' | 'fp64'; y_shared=True passes one target row
         (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a 1-D ym).
         Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters."""
+        return self._fit_ex("co_optimize_ex", pop, max_iter, precision, y_shared, lambda0,
+                            xtol, fp64_audit, early_exit)
+
+    def shard_init(self, unique_id: bytes, nranks: int, rank: int,
+                   timeout_s: float = 120.0) -> None:
+        """Join a sample-sharded group (co_shard_init). `unique_id` comes from
+        shard_unique_id() on one rank, shared with the others (e.g. a torch.distributed
+        broadcast). Every later wait of a sharded fit is bounded by `timeout_s`."""
+        if len(unique_id) != SHARD_ID_BYTES:
+            raise ValueError(f"unique id must be {SHARD_ID_BYTES} bytes")
+        buf = (ctypes.c_ubyte * SHARD_ID_BYTES).from_buffer_copy(unique_id)
+        rc = self._lib.co_shard_init(self._handle, buf, int(nranks), int(rank), float(timeout_s))
+        if rc != CO_OK:
+            raise COError(rc, "co_shard_init")
+
+    def optimize_sharded(self, pop: dict, max_iter: int = 50, precision: str = "fp32",
+                         y_shared: bool | None = None, lambda0: float = 1e-3,
+                         xtol: float = 1e-6, fp64_audit: int = -1, early_exit: bool = True):
+        """Sample-sharded fit (co_optimize_sharded): `pop` carries the whole population but
+        only this rank's slice of the samples (pop['N'], 'xs', 'ym'); the normal equations
+        are summed over the group every iteration, so every rank returns the same result."""
+        return self._fit_ex("co_optimize_sharded", pop, max_iter, precision, y_shared, lambda0,
+                            xtol, fp64_audit, early_exit)
+
+    def _fit_ex(self, entry, pop, max_iter, precision, y_shared, lambda0, xtol, fp64_audit,
+                early_exit):
         if self._torn:
             raise RuntimeError("InProcessCO used after teardown()")
         M, total_c = int(pop["M"]), int(pop["total_c"])
@@ -263,14 +308,14 @@ class InProcessCO:
         loss_init = np.zeros(M, np.float64)
         loss_final = np.zeros(M, np.float64)
         iters = np.zeros(M, np.int32)
-        rc = self._lib.co_optimize_ex(
+        rc = getattr(self._lib, entry)(
             self._handle, ctypes.byref(hdr), *args, ctypes.byref(opt),
             c_final.ctypes.data_as(_F64), status.ctypes.data_as(_I32),
             loss_init.ctypes.data_as(_F64), loss_final.ctypes.data_as(_F64),
             iters.ctypes.data_as(_I32))
         del keep
         if rc != CO_OK:
-            raise COError(rc, "co_optimize_ex")
+            raise COError(rc, entry)
         return {"c_final": c_final, "status": status, "loss_init": loss_init,
                 "loss_final": loss_final, "iters": iters}
 

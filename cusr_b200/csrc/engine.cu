@@ -29,6 +29,7 @@
 #include "launch.h"
 #include "lm_kernels.cuh"
 #include "pack.h"
+#include "shard_comm.h"
 
 namespace cusr {
 
@@ -77,6 +78,10 @@ struct Ctx {
     std::vector<int32_t> n_nodes, n_ops;
     int prep_prec = -1;
     bool loaded = false;
+    // sample-sharded mode
+    ShardComm shard;
+    DBuf red;
+    cudaEvent_t ev_sync = nullptr;
     CoStats stats{};
 };
 
@@ -355,6 +360,30 @@ inline int grid_for(Ctx *ctx, int64_t n) {
     return (int)std::max<int64_t>(1, std::min<int64_t>(4 * ctx->sm_count, (n + 255) / 256));
 }
 
+// Wait for all work queued on the context stream; in the sample-sharded mode the wait is
+// bounded by the group's deadline (a failed peer would otherwise stall the all-reduce).
+int sync_stream(Ctx *ctx, bool sharded) {
+    if (!sharded) {
+        CK(cudaStreamSynchronize(ctx->stream));
+        return CO_OK;
+    }
+    CK(cudaEventRecord(ctx->ev_sync, ctx->stream));
+    return shard_wait_event(ctx->shard, ctx->ev_sync);
+}
+
+// Sample-sharded mode: sum this rank's chunk partials per tree and all-reduce them.
+template <typename T>
+int shard_reduce_blocks(Ctx *ctx, int M, int64_t block_elems) {
+    GROW(ctx->red, (size_t)block_elems * sizeof(T));
+    reduce_chunks_kernel<T><<<grid_for(ctx, M), 256, 0, ctx->stream>>>(
+        P<TreeDesc>(ctx->desc), M, P<T>(ctx->partials), P<T>(ctx->red));
+    CK(cudaGetLastError());
+    ctx->stats.kernel_launches++;
+    return shard_allreduce(ctx->shard, ctx->red.ptr, (size_t)block_elems, sizeof(T) == 8,
+                           ctx->stream);
+}
+
+
 // Compile, schedule and upload a problem; it stays resident in the context until the next
 // load (inputs in HBM across fits).
 template <typename T>
@@ -408,6 +437,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     const Schedule &sc = pp.sc;
     const int64_t ldx = pp.ldx;
     cudaStream_t s = ctx->stream;
+    const bool sharded = opt.sample_sharded != 0;
+    if (sharded && !ctx->shard.comm) return CO_ERR_NULLARG;
     CK(cudaEventRecord(ctx->ev_fit[0], s));
     init_state_kernel<T><<<grid_for(ctx, std::max<int64_t>(total_c, M)), 256, 0, s>>>(
         P<float>(ctx->cinit_f), total_c, P<T>(ctx->c), P<T>(ctx->ctry), M, (T)opt.lambda0,
@@ -444,6 +475,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     sp.iters = P<int32_t>(ctx->iters);
     sp.pending = P<int32_t>(ctx->pending);
     sp.n_eval = P<int32_t>(ctx->n_eval);
+    sp.reduced = nullptr;
     sp.xtol = (T)opt.xtol;
 
     const int max_iter = std::max(0, opt.max_iter);
@@ -459,6 +491,11 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     size_t e0 = ev_i; rec();
     rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true);
     if (rc) return rc;
+    if (sharded) {
+        rc = shard_reduce_blocks<T>(ctx, M, sc.block_elems);
+        if (rc) return rc;
+        sp.reduced = P<T>(ctx->red);
+    }
     size_t e1 = ev_i; rec();
     sp.n_running = P<int>(ctx->n_run);
     sp.initial = 1;
@@ -470,7 +507,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     size_t e2 = ev_i; rec();
     eval_spans.push_back({e0, e1});
     step_spans.push_back({e1, e2});
-    CK(cudaStreamSynchronize(s));
+    rc = sync_stream(ctx, sharded);
+    if (rc) return rc;
     st.setup_ms = ms_since(t_entry);
     auto t_loop = std::chrono::steady_clock::now();
 
@@ -481,13 +519,22 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     for (int it = 0; it < max_iter; ++it) {
         const int slot = it & 1;
         if (opt.early_exit && it >= 2) {
-            CK(cudaEventSynchronize(ctx->ev_nrun[slot]));
+            if (sharded) {
+                rc = shard_wait_event(ctx->shard, ctx->ev_nrun[slot]);
+                if (rc) return rc;
+            } else {
+                CK(cudaEventSynchronize(ctx->ev_nrun[slot]));
+            }
             if (ctx->h_nrun[slot] == 0) break;
         }
         iters_run++;
         size_t a = ev_i; rec();
         rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true);
         if (rc) return rc;
+        if (sharded) {
+            rc = shard_reduce_blocks<T>(ctx, M, sc.block_elems);
+            if (rc) return rc;
+        }
         size_t b = ev_i; rec();
         sp.n_running = P<int>(ctx->n_run) + slot;
         sp.initial = 0;
@@ -505,7 +552,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
             CK(cudaEventRecord(ctx->ev_nrun[slot], s));
         }
     }
-    CK(cudaStreamSynchronize(s));
+    rc = sync_stream(ctx, sharded);
+    if (rc) return rc;
     st.loop_ms = ms_since(t_loop);
     st.iters_run = iters_run;
     auto t_fin = std::chrono::steady_clock::now();
@@ -532,6 +580,10 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
             CK(cudaGetLastError());
             st.kernel_launches += 2;
         }
+        if (sharded) {   // the fp64 losses over all samples: sum the ranks' halves
+            rc = shard_allreduce(ctx->shard, l64, 2 * (size_t)M, true, s);
+            if (rc) return rc;
+        }
         CK(cudaMemsetAsync(ctx->n_rev.ptr, 0, sizeof(int), s));
         audit_apply_kernel<T><<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, l64, l64 + M,
                                                  P<float>(ctx->cinit_f), P<T>(ctx->c),
@@ -555,7 +607,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     if (audit)
         CK(cudaMemcpyAsync(&n_rev, ctx->n_rev.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaEventRecord(ctx->ev_fit[1], s));
-    CK(cudaStreamSynchronize(s));
+    rc = sync_stream(ctx, sharded);
+    if (rc) return rc;
     {
         float dms = 0.f;
         if (cudaEventElapsedTime(&dms, ctx->ev_fit[0], ctx->ev_fit[1]) == cudaSuccess)
@@ -735,6 +788,7 @@ int co_init(int device_id, void **handle_out) {
         {"join event 1", cudaEventCreateWithFlags(&ctx->ev_join[1], cudaEventDisableTiming)},
         {"join event 2", cudaEventCreateWithFlags(&ctx->ev_join[2], cudaEventDisableTiming)},
         {"join event 3", cudaEventCreateWithFlags(&ctx->ev_join[3], cudaEventDisableTiming)},
+        {"sync event", cudaEventCreateWithFlags(&ctx->ev_sync, cudaEventDisableTiming)},
         {"fit event 0", cudaEventCreate(&ctx->ev_fit[0])},
         {"fit event 1", cudaEventCreate(&ctx->ev_fit[1])},
         {"fp32 kernels", eval_prepare_f32()},
@@ -801,9 +855,7 @@ int co_optimize_ex(void *handle, const PopHeader *h, const int32_t *nt, const fl
     }
     if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
-    if (opt.y_shared) {
-        // a single row: check the explicit layout, then run as shared
-    }
+    opt.sample_sharded = 0;
     Outputs out;
     out.c_d = c_final_out;
     out.status = status_out;
@@ -861,6 +913,7 @@ int co_fit_loaded(void *handle, const CoOptions *opt_in, double *c_final_out,
     co_default_options(&opt);
     if (opt_in) opt = *opt_in;
     if (!ctx->loaded || opt.precision != ctx->prep_prec) return CO_ERR_NULLARG;
+    opt.sample_sharded = 0;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
     Outputs out;
@@ -907,6 +960,47 @@ int co_probe_peak(void *handle, double *fp32_tflops, double *fp64_tflops) {
     return CO_OK;
 }
 
+int co_shard_unique_id(unsigned char id_out[128]) {
+    if (!id_out) return CO_ERR_NULLARG;
+    return shard_unique_id(id_out);
+}
+
+int co_shard_init(void *handle, const unsigned char id[128], int nranks, int rank,
+                  double timeout_s) {
+    if (!handle || !id) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    return shard_init(ctx->shard, id, nranks, rank, timeout_s);
+}
+
+int co_optimize_sharded(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+                        const int32_t *ci, const TreeMeta *metas, const float *c_init,
+                        const float *xs, const float *ym, const CoOptions *opt_in,
+                        double *c_final_out, int32_t *status_out, double *loss_init_out,
+                        double *loss_final_out, int32_t *iters_out) {
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym || !c_final_out ||
+        !status_out)
+        return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    if (!ctx->shard.comm) return CO_ERR_NULLARG;   // co_shard_init first
+    CoOptions opt;
+    co_default_options(&opt);
+    if (opt_in) {
+        if (opt_in->struct_size < (int32_t)offsetof(CoOptions, reserved)) return CO_ERR_NULLARG;
+        opt = *opt_in;
+    }
+    opt.sample_sharded = 1;
+    if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
+    Outputs out;
+    out.c_d = c_final_out;
+    out.status = status_out;
+    out.li_d = loss_init_out;
+    out.lf_d = loss_final_out;
+    out.iters = iters_out;
+    return optimize_common(handle, h, nt, nv, ci, metas, c_init, xs, ym, opt, out);
+}
+
 int co_last_split(double *setup_ms_out, double *loop_ms_out) {
     if (setup_ms_out) *setup_ms_out = g_last_setup_ms;
     if (loop_ms_out) *loop_ms_out = g_last_loop_ms;
@@ -928,7 +1022,7 @@ void co_teardown(void *handle) {
                     &ctx->xs_raw, &ctx->xs, &ctx->ym, &ctx->c, &ctx->ctry, &ctx->delta,
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
                     &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
-                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac,
+                    &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac, &ctx->red,
                     &ctx->tape_gs[0], &ctx->tape_gs[1], &ctx->tape_gs[2], &ctx->tape_gs[3]};
     for (DBuf *b : bufs) release(*b);
     for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
@@ -937,6 +1031,8 @@ void co_teardown(void *handle) {
     for (cudaEvent_t e : ctx->ev_fit)
         if (e) cudaEventDestroy(e);
     if (ctx->h_nrun) cudaFreeHost(ctx->h_nrun);
+    shard_destroy(ctx->shard);
+    if (ctx->ev_sync) cudaEventDestroy(ctx->ev_sync);
     for (cudaStream_t bs : ctx->bin_streams)
         if (bs) cudaStreamDestroy(bs);
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);

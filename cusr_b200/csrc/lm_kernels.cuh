@@ -28,6 +28,8 @@ struct StepParams {
     int32_t *iters;
     int32_t *pending;        // 1: the tree's trial was evaluated by the last pass
     int32_t *n_eval;         // evaluations consumed per tree (initial pass + trials)
+    const T *reduced;        // sample-sharded mode: per-tree sums all-reduced over ranks
+                             // (q_off layout, replaces the chunk partials), else null
     int *n_running;          // trees still running after this step (early exit)
     int initial;             // the evaluated point is c_init
     int do_solve;            // solve a new step for every running tree
@@ -64,11 +66,15 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
         const int K = d.K, P = nblock_size(K);
         const int pend = p.pending[m];
         if (pend) {
-            for (int e = lane; e < P; e += 32) {
-                const T *src = p.partials + d.p_off + e;
-                T s = T(0);
-                for (int ch = 0; ch < d.n_chunks; ++ch) s += src[(int64_t)ch * P];
-                sums[e] = s;
+            if (p.reduced) {
+                for (int e = lane; e < P; e += 32) sums[e] = p.reduced[d.q_off + e];
+            } else {
+                for (int e = lane; e < P; e += 32) {
+                    const T *src = p.partials + d.p_off + e;
+                    T s = T(0);
+                    for (int ch = 0; ch < d.n_chunks; ++ch) s += src[(int64_t)ch * P];
+                    sums[e] = s;
+                }
             }
         }
         __syncwarp();
@@ -280,6 +286,21 @@ __global__ void load_point_kernel(const double *__restrict__ c64, int64_t total_
         c[i] = (T)c64[i];
     for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += gs)
         pending[m] = 1;
+}
+
+// Sample-sharded mode: per-tree sums of this rank's chunk partials, in chunk order (raw sums,
+// the all-reduce input).
+template <typename T>
+__global__ void reduce_chunks_kernel(const TreeDesc *desc, int M, const T *partials, T *out) {
+    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+        const TreeDesc d = desc[m];
+        const int P = nblock_size(d.K);
+        for (int e = 0; e < P; ++e) {
+            T s = T(0);
+            for (int ch = 0; ch < d.n_chunks; ++ch) s += partials[d.p_off + (int64_t)ch * P + e];
+            out[d.q_off + e] = s;
+        }
+    }
 }
 
 // Per-tree normal-equation block = sum of its chunk partials in chunk order.

@@ -81,3 +81,24 @@ def gather_to_root(pop: dict, idx: np.ndarray, res: dict, group=None):
     if rank != 0:
         return None
     return merge(pop, gathered)
+
+
+def sample_range(N: int, rank: int, world: int) -> tuple[int, int]:
+    """[lo, hi) of the contiguous sample slice of `rank` (sizes differ by at most one)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a group of {world}")
+    base, extra = divmod(int(N), int(world))
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def sample_slice(pop: dict, rank: int, world: int) -> dict:
+    """The population with only `rank`'s slice of the samples, for the sample-sharded mode
+    (every rank keeps all trees and the same c_init; xs rows and ym columns are split)."""
+    lo, hi = sample_range(int(pop["N"]), rank, world)
+    out = dict(pop)
+    out["xs"] = np.ascontiguousarray(np.asarray(pop["xs"], np.float32)[lo:hi])
+    ym = np.asarray(pop["ym"], np.float32)
+    out["ym"] = np.ascontiguousarray(ym[lo:hi] if ym.ndim == 1 else ym[:, lo:hi])
+    out["N"] = hi - lo
+    return out

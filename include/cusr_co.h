@@ -120,7 +120,8 @@ typedef struct CoOptions {
     double  xtol;           /* step test |d| < xtol(|c_try| + xtol) (reference 1e-6)    */
     int32_t fp64_audit;     /* -1 auto (on for fp32, off for fp64), 0 off, 1 on        */
     int32_t early_exit;     /* 1 (default): stop launching once every tree is finished */
-    int32_t reserved[8];
+    int32_t sample_sharded; /* set by co_optimize_sharded (0 elsewhere)                 */
+    int32_t reserved[7];
 } CoOptions;
 
 /* Fill `opt` with the reference defaults (fp32, 50 iterations, lambda0 1e-3, xtol 1e-6,
@@ -176,6 +177,33 @@ int  co_fit_loaded(void *handle, const CoOptions *opt,
                    double *c_final_out, int32_t *status_out,
                    double *loss_init_out, double *loss_final_out,
                    int32_t *iters_out);
+
+/* ---- sample-sharded mode (one process per GPU, samples split across ranks) ----------- */
+
+/* A 128-byte id for a new group of ranks: created on one rank, shared with the others by any
+ * means (e.g. torch.distributed broadcast). Needs NCCL (loaded at run time). */
+int  co_shard_unique_id(unsigned char id_out[128]);
+
+/* Join the group as `rank` of `nranks` on the handle's device. Every later wait of a
+ * sharded fit is bounded by timeout_s: a peer that fails or never arrives makes the call
+ * return CO_ERR_CUDA (the communicator is aborted) instead of hanging. */
+int  co_shard_init(void *handle, const unsigned char id[128], int nranks, int rank,
+                   double timeout_s);
+
+/* Sample-sharded fit: every rank passes the WHOLE population (same trees, same c_init) but
+ * only its own slice of the samples (header->N = local sample count; xs / ym hold those
+ * samples). Per-tree JtJ / Jtr / 0.5*sum r^2 are all-reduced each iteration (and the fp64
+ * audit losses once), so all ranks take identical steps and return identical outputs, equal
+ * to one fit over all samples up to the order of the floating-point sums.
+ * (No counterpart in the reference, which has no multi-GPU path.) */
+int  co_optimize_sharded(void *handle, const PopHeader *header,
+                         const int32_t *nt, const float *nv, const int32_t *ci,
+                         const TreeMeta *metas,
+                         const float *c_init, const float *xs, const float *ym,
+                         const CoOptions *opt,
+                         double *c_final_out, int32_t *status_out,
+                         double *loss_init_out, double *loss_final_out,
+                         int32_t *iters_out);
 
 /* Statistics of the last co_optimize* / co_fit_loaded call on `handle`. */
 int  co_get_stats(void *handle, CoStats *out);

@@ -73,3 +73,64 @@ def test_gather_to_root_gloo_world2():
     parts = shard.lpt_partition(shard.tree_costs(pop), 2)
     for r, p in enumerate(parts):
         assert all(status[m] == r for m in p)
+
+
+def test_sample_range_partitions():
+    for N in (0, 1, 7, 10, 1001):
+        for world in (1, 2, 3, 8):
+            spans = [shard.sample_range(N, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == N
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            sizes = [hi - lo for lo, hi in spans]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def _normal_equations(pop):
+    """Per tree: (JtJ, Jtr, 0.5 sum r^2) at c_init, fp64, from the oracle."""
+    from oracle import interp
+
+    out = []
+    for m in range(int(pop["M"])):
+        nt, nv, ci, y, K = interp.tree_view(pop, m)
+        c_off = int(pop["metas"][m][2])
+        c = np.asarray(pop["c_init"][c_off:c_off + K], np.float64)
+        f, J = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c)
+        r = f - np.asarray(y, np.float64)
+        out.append(np.concatenate([(J.T @ J)[np.triu_indices(K)], J.T @ r, [0.5 * r @ r]]))
+    return np.concatenate(out)
+
+
+def _sample_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    pop = synth.make_config("pr1", M=24, N=301, seed=5)
+    local = torch.from_numpy(_normal_equations(shard.sample_slice(pop, rank, world)))
+    dist.all_reduce(local)          # the exchange step of the sample-sharded mode
+    if rank == 0:
+        q.put(local.numpy().tolist())
+    dist.destroy_process_group()
+
+
+def test_sample_sharded_normal_equations_gloo_world2():
+    """Summing the per-slice normal equations over the group reproduces the full-sample
+    ones: the decomposition the sample-sharded fit relies on."""
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = tmp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_sample_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    summed = np.asarray(q.get(timeout=120))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    full = _normal_equations(synth.make_config("pr1", M=24, N=301, seed=5))
+    finite = np.isfinite(full)
+    np.testing.assert_array_equal(np.isfinite(summed), finite)
+    np.testing.assert_allclose(summed[finite], full[finite], rtol=1e-10,
+                               atol=1e-10 * np.abs(full[finite]).max())
