@@ -359,6 +359,55 @@ def run_config(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
+    """The sample-sharded configuration (M=512 trees, N=10,000,000 samples, fp32, 30 iters)
+    on `world` GPUs: every rank loads all trees and its contiguous slice of the samples; the
+    engine all-reduces the per-tree normal equations over NCCL every iteration. Strong
+    scaling (the problem is fixed); time = max over ranks of the device-timed fit."""
+    from cusr_b200 import InProcessCO, co_inproc, shard, synth
+
+    pop = synth.make_config("sharded", M=args.M, N=args.N, seed=0)
+    precision, max_iter = pop["precision"], int(pop["max_iter"])
+    mine = shard.sample_slice(pop, rank, world) if world > 1 else pop
+    co = InProcessCO(device_id=local if world > 1 else 0)
+    if world > 1:
+        import torch.distributed as dist
+
+        box = [co_inproc.shard_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        co.shard_init(box[0], world, rank, timeout_s=120.0)
+    co.load(mine, precision=precision, y_shared=True)
+    sharded = world > 1
+    for _ in range(args.warmup):
+        co.fit_loaded(max_iter=max_iter, sample_sharded=sharded)
+    barrier(world)
+    dev, launches, nodes = [], 0, 0
+    for _ in range(args.steps):
+        co.fit_loaded(max_iter=max_iter, sample_sharded=sharded)
+        st = co.stats()
+        dev.append(st["device_ms"])
+        launches += st["kernel_launches"]
+        nodes += st["node_evals"]
+    barrier(world)
+    total_ms = max_over_ranks(float(sum(dev)), world)
+    nodes_all = sum_over_ranks(float(nodes), world)
+    if rank != 0:
+        return
+    M = int(pop["M"])
+    print(json.dumps({
+        "metric": f"LM fits/sec (sample-sharded: M={M}, N={pop['N']}, {max_iter} iters, "
+                  f"{precision})",
+        "value": M * args.steps / (total_ms / 1e3), "unit": "fits/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32" if precision == "fp32" else "f64", "data": "synthetic",
+        "config": {"workload": "sharded", "trees": M, "N": int(pop["N"]),
+                   "max_iter": max_iter, "parallelism": f"sample-sharded x{world} "
+                   "(NCCL all-reduce of JtJ/Jtr/loss per iteration)"},
+        "node_evals_per_s": nodes_all / (total_ms / 1e3), "gpu_launches": launches}),
+        flush=True)
+
+
 def run_profile_case(args) -> None:
     """Small case of the same kernel for ncu captures: 2,048 trees of the metric
     configuration (same N, same tree distribution), a few LM iterations."""
@@ -397,6 +446,8 @@ def main() -> None:
     ap.add_argument("--config", default=None,
                     help="bench one BASELINE configuration instead of the headline metric: "
                          "pr1, mid, physics, long, scale, sharded")
+    ap.add_argument("--sample-sharded", action="store_true",
+                    help="the sample-sharded configuration (M=512, N=10M) over all ranks")
     ap.add_argument("--M", type=int, default=None)
     ap.add_argument("--N", type=int, default=None)
     args = ap.parse_args()
@@ -408,7 +459,9 @@ def main() -> None:
         return
     world, rank, local = dist_setup()
     try:
-        if args.impl == "reference":
+        if args.sample_sharded:
+            run_sample_sharded(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, world, rank)
         else:
             run_ours(args, world, rank, local)

@@ -346,10 +346,14 @@ class InProcessCO:
         self._loaded = (int(pop["M"]), int(pop["total_c"]), precision)
 
     def fit_loaded(self, max_iter: int = 50, lambda0: float = 1e-3, xtol: float = 1e-6,
-                   fp64_audit: int = -1, early_exit: bool = True) -> dict:
-        """LM fit of the resident population from its c_init (inputs already in HBM)."""
+                   fp64_audit: int = -1, early_exit: bool = True,
+                   sample_sharded: bool = False) -> dict:
+        """LM fit of the resident population from its c_init (inputs already in HBM).
+        sample_sharded=True: the loaded samples are this rank's slice and the normal
+        equations are summed over the shard_init group each iteration."""
         M, total_c, precision = self._loaded
         opt = self._options(max_iter, precision, False, lambda0, xtol, fp64_audit, early_exit)
+        opt.sample_sharded = 1 if sample_sharded else 0
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)

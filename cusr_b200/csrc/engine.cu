@@ -913,7 +913,7 @@ int co_fit_loaded(void *handle, const CoOptions *opt_in, double *c_final_out,
     co_default_options(&opt);
     if (opt_in) opt = *opt_in;
     if (!ctx->loaded || opt.precision != ctx->prep_prec) return CO_ERR_NULLARG;
-    opt.sample_sharded = 0;
+    if (opt.sample_sharded && !ctx->shard.comm) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
     Outputs out;

@@ -120,7 +120,9 @@ typedef struct CoOptions {
     double  xtol;           /* step test |d| < xtol(|c_try| + xtol) (reference 1e-6)    */
     int32_t fp64_audit;     /* -1 auto (on for fp32, off for fp64), 0 off, 1 on        */
     int32_t early_exit;     /* 1 (default): stop launching once every tree is finished */
-    int32_t sample_sharded; /* set by co_optimize_sharded (0 elsewhere)                 */
+    int32_t sample_sharded; /* 1: all-reduce over the co_shard_init group (set by      */
+                            /* co_optimize_sharded; honoured by co_fit_loaded; ignored  */
+                            /* by co_optimize_ex)                                       */
     int32_t reserved[7];
 } CoOptions;
 
