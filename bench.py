@@ -256,6 +256,17 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
     clk = clocks.stop()
     barrier(world)
     total_ms = max_over_ranks(float(sum(dev_ms)), world)
+
+    # the same fits with the reference kernel's numerics (--use_fast_math instantiation)
+    for _ in range(args.warmup):
+        co.fit_loaded(max_iter=50, precision="fp32_fast")
+    barrier(world)
+    fast_ms = 0.0
+    for _ in range(args.steps):
+        co.fit_loaded(max_iter=50, precision="fp32_fast")
+        fast_ms += co.stats()["device_ms"]
+    barrier(world)
+    fast_ms = max_over_ranks(fast_ms, world)
     M_total = int(pop["M"])
     value = M_total * args.steps / (total_ms / 1e3)
     node_evals_total = sum_over_ranks(float(node_evals), world)
@@ -314,6 +325,11 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
         "e2e": {"value": e2e_value, "unit": "fits/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "entry": "co_optimize_ex (pinned host buffers)"},
         "roofline": roofline,
+        "fp32_fast": {"value": M_total * args.steps / (fast_ms / 1e3),
+                      "ms_per_step": fast_ms / args.steps,
+                      "note": "same fits, interpreter built with the reference kernel's "
+                              "--use_fast_math flags (CO_PREC_FP32_FAST); measured after the "
+                              "headline steps"},
         "gpu_launches": int(launches),
         "clocks": clk,
         "node_evals_per_s": roofline["node_evals_per_s"],
@@ -331,6 +347,8 @@ def run_config(args) -> None:
     name = args.config
     pop = synth.make_config(name, M=args.M, N=args.N, seed=0)
     precision, max_iter = pop["precision"], int(pop["max_iter"])
+    if args.fast_math and precision == "fp32":
+        precision = "fp32_fast"
     shared = np.asarray(pop["ym"]).ndim == 1
     co = InProcessCO(device_id=0)
     co.load(pop, precision=precision, y_shared=shared)
@@ -351,7 +369,7 @@ def run_config(args) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f64" if precision == "fp64" else "f32", "data": "synthetic",
             "config": {"workload": name, "trees": M, "N": int(pop["N"]), "max_iter": max_iter,
-                       "y_shared": bool(shared)},
+                       "y_shared": bool(shared), "precision": precision},
             "node_evals_per_s": nodes / (total_ms / 1e3), "gpu_launches": launches,
             "statuses": np.bincount(res["status"], minlength=5).tolist()}
     if not args.no_cpu_baseline:
@@ -446,6 +464,8 @@ def main() -> None:
     ap.add_argument("--config", default=None,
                     help="bench one BASELINE configuration instead of the headline metric: "
                          "pr1, mid, physics, long, scale, sharded")
+    ap.add_argument("--fast-math", action="store_true",
+                    help="--config: run fp32 configurations with CO_PREC_FP32_FAST")
     ap.add_argument("--sample-sharded", action="store_true",
                     help="the sample-sharded configuration (M=512, N=10M) over all ranks")
     ap.add_argument("--M", type=int, default=None)

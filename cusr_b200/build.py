@@ -27,8 +27,10 @@ ALIASES = ("libcusr_co_ad.so", "libcusr_co_fd.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-O3", f"-I{INCLUDE}"]
-SOURCES = ["eval_f32.cu", "eval_f64.cu", "engine.cu", "pack.cpp", "debug_api.cpp",
-           "noalloc.cu", "shard_comm.cpp"]
+SOURCES = ["eval_f32.cu", "eval_f32_fast.cu", "eval_f64.cu", "engine.cu", "pack.cpp",
+           "debug_api.cpp", "noalloc.cu", "shard_comm.cpp"]
+# the reference kernel's numerics (cusr/kernel/Makefile:9) for CoOptions.math = CO_MATH_FAST
+FILE_FLAGS = {"eval_f32_fast.cu": ["--use_fast_math"]}
 
 
 def _nvcc() -> str:
@@ -63,7 +65,7 @@ def build(force: bool = False, verbose: bool = False, defines: tuple = (), obj_d
         s = CSRC / src
         o = OBJ / (s.stem + ".o")
         if force or _stale(o, [s, *hdrs, Path(__file__)]):
-            jobs.append([nvcc, *flags, "-c", str(s), "-o", str(o)])
+            jobs.append([nvcc, *flags, *FILE_FLAGS.get(src, []), "-c", str(s), "-o", str(o)])
 
     def run(cmd):
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -34,6 +34,17 @@ SHARD_ID_BYTES = 128
 
 CO_PREC_FP32 = 0
 CO_PREC_FP64 = 1
+CO_PREC_FP32_FAST = 2
+# precision names: 'fp32' (IEEE fp32 functions), 'fp64', 'fp32_fast' (the reference kernel's
+# --use_fast_math numerics)
+PRECISIONS = {"fp32": CO_PREC_FP32, "fp64": CO_PREC_FP64, "fp32_fast": CO_PREC_FP32_FAST}
+
+
+def prec_code(precision: str) -> int:
+    try:
+        return PRECISIONS[precision]
+    except KeyError:
+        raise ValueError(f"precision must be one of {sorted(PRECISIONS)}") from None
 
 STATUS_CONVERGED, STATUS_MAXITER, STATUS_FAIL_NAN, STATUS_K0_SKIP, STATUS_FAIL_CHOLESKY = range(5)
 
@@ -323,7 +334,7 @@ class InProcessCO:
                  fp64_audit=-1, early_exit=True) -> CoOptions:
         opt = CoOptions()
         self._lib.co_default_options(ctypes.byref(opt))
-        opt.precision = CO_PREC_FP64 if precision == "fp64" else CO_PREC_FP32
+        opt.precision = prec_code(precision)
         opt.max_iter = int(max_iter)
         opt.y_shared = 1 if y_shared else 0
         opt.lambda0 = float(lambda0)
@@ -347,11 +358,13 @@ class InProcessCO:
 
     def fit_loaded(self, max_iter: int = 50, lambda0: float = 1e-3, xtol: float = 1e-6,
                    fp64_audit: int = -1, early_exit: bool = True,
-                   sample_sharded: bool = False) -> dict:
+                   sample_sharded: bool = False, precision: str | None = None) -> dict:
         """LM fit of the resident population from its c_init (inputs already in HBM).
         sample_sharded=True: the loaded samples are this rank's slice and the normal
-        equations are summed over the shard_init group each iteration."""
-        M, total_c, precision = self._loaded
+        equations are summed over the shard_init group each iteration. `precision` may switch
+        between 'fp32' and 'fp32_fast' on an fp32 load (default: the load's)."""
+        M, total_c, loaded_prec = self._loaded
+        precision = precision or loaded_prec
         opt = self._options(max_iter, precision, False, lambda0, xtol, fp64_audit, early_exit)
         opt.sample_sharded = 1 if sample_sharded else 0
         c_final = np.zeros(total_c, np.float64)
@@ -392,7 +405,7 @@ class InProcessCO:
 
         rc = self._lib.co_evaluate(
             self._handle, ctypes.byref(hdr), nt_p, nv_p, ci_p, metas_buf, p64(c), xs_p, ym_p,
-            CO_PREC_FP64 if precision == "fp64" else CO_PREC_FP32, 1 if y_shared else 0,
+            prec_code(precision), 1 if y_shared else 0,
             p64(vals), p64(jac), p64(blk))
         del keep
         if rc != CO_OK:

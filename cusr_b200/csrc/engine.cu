@@ -76,7 +76,8 @@ struct Ctx {
     Prep prep;
     PopHeader hdr{};
     std::vector<int32_t> n_nodes, n_ops;
-    int prep_prec = -1;
+    int prep_prec = -1;     // arithmetic type of the loaded problem (CO_PREC_FP32 / _FP64)
+    bool fast = false;      // fp32 launches use the fast-math instantiations (CO_PREC_FP32_FAST)
     bool loaded = false;
     // sample-sharded mode
     ShardComm shard;
@@ -231,7 +232,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
             smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, false);
         }
         if (smem + 64 > (size_t)ctx->smem_optin) return CO_ERR_BOUNDS;
-        int occ = Launch<T>::occ(kc, grad, tg, smem);
+        int occ = Launch<T>::occ(kc, grad, tg, ctx->fast, smem);
         if (occ < 1) occ = 1;
         int64_t grid = (int64_t)occ * ctx->sm_count;
         if (grid > bin.max_items) grid = std::max<int64_t>(1, bin.max_items);
@@ -241,7 +242,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
             GROW(ctx->tape_gs[si], (size_t)grid * p.tape_cap * EVAL_THREADS * EVAL_V * sizeof(T));
             p.tape_g = ctx->tape_gs[si].ptr;
         }
-        CK(Launch<T>::eval(kc, grad, tg, p, (int)grid, smem, ctx->bin_streams[si]));
+        CK(Launch<T>::eval(kc, grad, tg, ctx->fast, p, (int)grid, smem, ctx->bin_streams[si]));
         ctx->stats.eval_launches++;
         ctx->stats.kernel_launches++;
     }
@@ -424,7 +425,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     st = CoStats{};
     st.n_bins = keep_bins;
     st.y_shared = keep_ys;
-    st.precision = fp64 ? CO_PREC_FP64 : CO_PREC_FP32;
+    st.precision = fp64 ? CO_PREC_FP64 : (ctx->fast ? CO_PREC_FP32_FAST : CO_PREC_FP32);
     if (M == 0) {
         st.setup_ms = ms_since(t_entry);
         g_last_setup_ms = st.setup_ms;
@@ -792,6 +793,7 @@ int co_init(int device_id, void **handle_out) {
         {"fit event 0", cudaEventCreate(&ctx->ev_fit[0])},
         {"fit event 1", cudaEventCreate(&ctx->ev_fit[1])},
         {"fp32 kernels", eval_prepare_f32()},
+        {"fp32 fast-math kernels", eval_prepare_f32_fast()},
         {"fp64 kernels", eval_prepare_f64()},
     };
     for (const Step &st : steps) {
@@ -808,6 +810,10 @@ int co_init(int device_id, void **handle_out) {
     return CO_OK;
 }
 
+static bool valid_prec(int p) {
+    return p == CO_PREC_FP32 || p == CO_PREC_FP64 || p == CO_PREC_FP32_FAST;
+}
+
 static int optimize_common(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
                            const int32_t *ci, const TreeMeta *metas, const float *c_init,
                            const float *xs, const float *ym, const CoOptions &opt,
@@ -817,6 +823,7 @@ static int optimize_common(void *handle, const PopHeader *h, const int32_t *nt, 
     int rc = check_args(pr);
     if (rc != CO_OK) return rc;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    ctx->fast = opt.precision == CO_PREC_FP32_FAST;
     if (opt.precision == CO_PREC_FP64) return run_fit<double>(ctx, pr, opt, out);
     return run_fit<float>(ctx, pr, opt, out);
 }
@@ -853,7 +860,7 @@ int co_optimize_ex(void *handle, const PopHeader *h, const int32_t *nt, const fl
         if (opt_in->struct_size < (int32_t)offsetof(CoOptions, reserved)) return CO_ERR_NULLARG;
         opt = *opt_in;
     }
-    if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
     opt.sample_sharded = 0;
     Outputs out;
@@ -870,7 +877,7 @@ int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float
                 const float *ym, int precision, int y_shared, double *vals_out,
                 double *jac_out, double *blocks_out) {
     if (!handle || !h || !nt || !nv || !ci || !metas || !c || !xs || !ym) return CO_ERR_NULLARG;
-    if (precision != CO_PREC_FP32 && precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    if (!valid_prec(precision)) return CO_ERR_NULLARG;
     Ctx *ctx = (Ctx *)handle;
     Problem pr{h, nt, nv, ci, metas, nullptr, xs, ym};
     int rc = check_args(pr);
@@ -879,6 +886,7 @@ int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float
     std::vector<float> c_f((size_t)std::max(h->total_c, 0));
     for (size_t i = 0; i < c_f.size(); ++i) c_f[i] = (float)c[i];
     pr.c_init = c_f.data();
+    ctx->fast = precision == CO_PREC_FP32_FAST;
     if (precision == CO_PREC_FP64)
         return run_eval<double>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
     return run_eval<float>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
@@ -892,7 +900,7 @@ int co_load(void *handle, const PopHeader *h, const int32_t *nt, const float *nv
     CoOptions opt;
     co_default_options(&opt);
     if (opt_in) opt = *opt_in;
-    if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
     Ctx *ctx = (Ctx *)handle;
     Problem pr{h, nt, nv, ci, metas, c_init, xs, ym};
     int rc = check_args(pr);
@@ -912,7 +920,10 @@ int co_fit_loaded(void *handle, const CoOptions *opt_in, double *c_final_out,
     CoOptions opt;
     co_default_options(&opt);
     if (opt_in) opt = *opt_in;
-    if (!ctx->loaded || opt.precision != ctx->prep_prec) return CO_ERR_NULLARG;
+    if (!ctx->loaded || !valid_prec(opt.precision) ||
+        (opt.precision == CO_PREC_FP64) != (ctx->prep_prec == CO_PREC_FP64))
+        return CO_ERR_NULLARG;
+    ctx->fast = opt.precision == CO_PREC_FP32_FAST;
     if (opt.sample_sharded && !ctx->shard.comm) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
@@ -990,7 +1001,7 @@ int co_optimize_sharded(void *handle, const PopHeader *h, const int32_t *nt, con
         opt = *opt_in;
     }
     opt.sample_sharded = 1;
-    if (opt.precision != CO_PREC_FP32 && opt.precision != CO_PREC_FP64) return CO_ERR_NULLARG;
+    if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
     Outputs out;
     out.c_d = c_final_out;

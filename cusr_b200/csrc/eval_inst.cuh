@@ -1,19 +1,24 @@
 // eval_inst.cuh — host launchers for the instantiations of lm_eval_kernel<T, ...> of one
-// arithmetic type; included by eval_f32.cu / eval_f64.cu with CUSR_T and the list of
-// constant-count classes CUSR_KCS(X) defined.
+// arithmetic type; included by eval_f32.cu / eval_f32_fast.cu / eval_f64.cu with CUSR_T, the
+// launcher suffix CUSR_FN, the list of constant-count classes CUSR_KCS(X) and CUSR_FAST
+// (1 in the translation unit compiled with --use_fast_math) defined.
 #include "launch.h"
+
+#ifndef CUSR_FAST
+#define CUSR_FAST 0
+#endif
 
 namespace cusr {
 namespace {
 
 template <int KC, bool G, bool TG>
 cudaError_t one(const EvalParams<CUSR_T> &p, int grid, size_t smem, cudaStream_t s) {
-    lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG><<<grid, EVAL_NT, smem, s>>>(p);
+    lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)><<<grid, EVAL_NT, smem, s>>>(p);
     return cudaGetLastError();
 }
 template <int KC, bool G, bool TG> int occ(size_t smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)>,
                                                       EVAL_NT, smem) != cudaSuccess)
         return 0;
     return n;
@@ -25,9 +30,9 @@ template <int KC, bool G, bool TG> cudaError_t prep() {
     if (e == cudaSuccess)
         e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa;
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)>);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG>,
+    return cudaFuncSetAttribute(lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 optin - (int)fa.sharedSizeBytes);
 }

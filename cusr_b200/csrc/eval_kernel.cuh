@@ -350,8 +350,11 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
 //   KC    constant-count class of the bin (trees with K <= KC)
 //   GRAD  false: value and sum r^2 only (K = 0 trees never need more; the fp64 audit)
 //   TG    reverse tape in global scratch instead of shared memory
+//   FAST  instantiated in the translation unit built with the reference kernel's
+//         --use_fast_math flags (approximate transcendentals, division and square root,
+//         denormals flushed); the source is the same, only the name differs
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int NT, int KC, bool GRAD, bool TG>
+template <typename T, int V, int NT, int KC, bool GRAD, bool TG, bool FAST>
 __global__ void __launch_bounds__(NT)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;

@@ -41,9 +41,12 @@ template <> struct Mth<float> {
     static CUSR_HD float pow(float a, float b) { return ::powf(a, b); }
     static CUSR_HD float fabs(float a) { return ::fabsf(a); }
     static CUSR_HD float copysign(float a, float b) { return ::copysignf(a, b); }
-    // correctly rounded reciprocal: the same value as 1.0f / a, without a general division
+    // correctly rounded reciprocal: the same value as 1.0f / a, without a general division;
+    // under --use_fast_math the reference's 1.0f / a is the approximate division, kept here
     static CUSR_HD float rcp(float a) {
-#ifdef __CUDA_ARCH__
+#if defined(__CUDA_ARCH__) && defined(__USE_FAST_MATH__)
+        return 1.0f / a;
+#elif defined(__CUDA_ARCH__)
         return __frcp_rn(a);
 #else
         return 1.0f / a;

@@ -109,10 +109,15 @@ void co_teardown(void *handle);
 
 #define CO_PREC_FP32 0
 #define CO_PREC_FP64 1
+/* fp32 with the reference kernel's numerics: the interpreter is compiled with its
+ * --use_fast_math flags (hardware sin/cos/exp/log/pow approximations, approximate division and
+ * square root, denormals flushed), as cusr/kernel/Makefile:9 builds batch_lm_ad. The LM step
+ * and the fp64 audit are unchanged. */
+#define CO_PREC_FP32_FAST 2
 
 typedef struct CoOptions {
     int32_t struct_size;    /* sizeof(CoOptions); lets the struct grow compatibly      */
-    int32_t precision;      /* CO_PREC_FP32 (default) or CO_PREC_FP64                  */
+    int32_t precision;      /* CO_PREC_FP32 (default), CO_PREC_FP64, CO_PREC_FP32_FAST */
     int32_t max_iter;       /* LM iterations (reference default 50)                    */
     int32_t y_shared;       /* 1: ym points at ONE row of N targets shared by all trees;
                                0: ym is [M_prob][N] (identical rows are still detected) */

@@ -35,12 +35,12 @@ def _check_values(co, pop, precision, rel, unit, min_strict=0.97):
         nt, nv, ci, _y, K = interp.tree_view(pop, m)
         off = int(pop["metas"][m][2])
         c = np.asarray(pop["c_init"][off:off + K], np.float64)
-        if precision == "fp32":
+        if precision in ("fp32", "fp32_fast"):
             c = c.astype(np.float32).astype(np.float64)
         y = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c)
         S = interp.error_scale(nt, nv, ci, pop["xs"], c)
         hi, lo = interp.intermediate_range(nt, nv, ci, pop["xs"], c)
-        if precision == "fp32":
+        if precision in ("fp32", "fp32_fast"):
             outside = (hi > 1e37) | (lo < 1e-30)   # not representable in normal fp32
         else:
             outside = np.zeros(y.shape, bool)
@@ -60,6 +60,47 @@ def test_values_fp64_match_oracle(co):
 
 def test_values_fp32_match_oracle(co):
     _check_values(co, synth.make_config("pr1", M=96, N=300, seed=0), "fp32", 1e-5, U32)
+
+
+def test_values_fp32_fast_match_oracle(co):
+    """The reference kernel's numerics (--use_fast_math): hardware sin/cos/exp/log
+    approximations (absolute error about 2^-21.4 on the primary range, growing with |x|),
+    approximate division and square root, denormals flushed. Checked against the fp64 oracle
+    with the condition-scaled bound widened to those errors; nearly every sample still meets
+    a plain 1e-4 relative bound."""
+    for pop in (synth.make_config("pr1", M=96, N=300, seed=0),
+                synth.make_config("mid", M=64, N=700, seed=4)):
+        _check_values(co, pop, "fp32_fast", 1e-4, 2.0 ** -20, min_strict=0.85)
+        _report_fast_values(co, pop)
+
+
+def _report_fast_values(co, pop):
+    """Error statistics of the fast-math values against the fp64 oracle and the IEEE fp32
+    path (written next to the GPU run's other parity reports)."""
+    import json
+    import os
+
+    if not os.path.isdir("gpurun_out"):
+        return
+    fast = co.evaluate(pop, precision="fp32_fast", values=True)["values"]
+    ieee = co.evaluate(pop, precision="fp32", values=True)["values"]
+    rel_f, rel_i = [], []
+    for m in range(int(pop["M"])):
+        nt, nv, ci, _y, K = interp.tree_view(pop, m)
+        off = int(pop["metas"][m][2])
+        c = np.asarray(pop["c_init"][off:off + K], np.float32).astype(np.float64)
+        y = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c)
+        fin = np.isfinite(y) & (np.abs(y) > 1e-30)
+        with np.errstate(all="ignore"):
+            rel_f.append(np.abs(fast[m][fin] - y[fin]) / np.abs(y[fin]))
+            rel_i.append(np.abs(ieee[m][fin] - y[fin]) / np.abs(y[fin]))
+    rf, ri = np.concatenate(rel_f), np.concatenate(rel_i)
+    q = [0.5, 0.9, 0.99, 0.999]
+    with open(f"gpurun_out/fast_values_M{pop['M']}_N{pop['N']}.json", "w") as f:
+        json.dump({"fast_rel_quantiles": np.nanquantile(rf, q).tolist(),
+                   "ieee_rel_quantiles": np.nanquantile(ri, q).tolist(),
+                   "fast_within_1e-5": float(np.mean(rf <= 1e-5)),
+                   "ieee_within_1e-5": float(np.mean(ri <= 1e-5))}, f)
 
 
 def test_values_mid_config_both_precisions(co):
@@ -88,7 +129,7 @@ def _check_jacobian(co, pop, precision, tol):
             continue
         off = int(pop["metas"][m][2])
         c = np.asarray(pop["c_init"][off:off + K], np.float64)
-        if precision == "fp32":
+        if precision in ("fp32", "fp32_fast"):
             c = c.astype(np.float32).astype(np.float64)
         y, J = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c)
         S = interp.error_scale(nt, nv, ci, pop["xs"], c)
@@ -170,7 +211,7 @@ def _check_blocks(co, pop, precision, tol, max_cond=None):
     for m in range(int(pop["M"])):
         off, K = int(pop["metas"][m][2]), int(pop["metas"][m][3])
         c = np.asarray(pop["c_init"][off:off + K], np.float64)
-        if precision == "fp32":
+        if precision in ("fp32", "fp32_fast"):
             c = c.astype(np.float32).astype(np.float64)
         ref, mag = _ref_blocks(pop, m, c)
         if not np.all(np.isfinite(ref)):

@@ -153,6 +153,32 @@ def test_pop1000_vs_reference_kernel_golden(co):
     assert np.mean(as_good[elig]) >= 0.9
 
 
+def test_pop1000_fast_math_vs_reference_kernel_golden(co):
+    """CO_PREC_FP32_FAST reproduces the reference kernel's build numerics (--use_fast_math);
+    on its own fixture the fits are as good as its A100 goldens on most trees, never worse
+    than c_init (fp64 audit), and agree with its statuses about as often as the IEEE mode."""
+    pop, g = pop1000()
+    res = co.optimize_ex(pop, max_iter=50, precision="fp32_fast")
+    acc = co.optimize_ex(pop, max_iter=50, precision="fp32")
+    ours = interp.loss_pop(pop, res["c_final"])
+    theirs = g["refkernel/loss64"]
+    init = g["init/loss64"]
+    K = pop["metas"][:, 3]
+    elig = (K > 0) & np.isfinite(init)
+    not_worse_than_init = ours[elig] <= init[elig] * (1 + 1e-9) + 1e-12
+    as_good = ours <= theirs * (1 + 1e-3) + 1e-9
+    same_status = np.mean(res["status"] == g["refkernel/status"])
+    same_status_ieee = np.mean(acc["status"] == g["refkernel/status"])
+    _report("pop1000_fast_vs_refkernel", {
+        "as_good_as_refkernel": float(np.mean(as_good[elig])),
+        "status_agreement_fast": float(same_status),
+        "status_agreement_ieee": float(same_status_ieee),
+        "status_fast": np.bincount(res["status"], minlength=5).tolist(),
+        "status_refkernel": np.bincount(g["refkernel/status"], minlength=5).tolist()})
+    assert np.all(not_worse_than_init)
+    assert np.mean(as_good[elig]) >= 0.9
+
+
 def test_fp32_audit_invariant(co):
     """Delivered constants are never worse than c_init in fp64 (lm_core.cuh:299-351)."""
     pop = synth.make_config("mid", M=512, N=2000, seed=5)
