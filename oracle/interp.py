@@ -266,6 +266,81 @@ def error_scale(nt, nv, ci, xs, c) -> np.ndarray:
     return S
 
 
+FAST_MATH_UNIT = 2.0 ** -21.41
+
+
+def fast_math_error_scale(nt, nv, ci, xs, c) -> np.ndarray:
+    """Error scale A of an fp32 evaluation built with nvcc --use_fast_math (the reference
+    kernel's flags, cusr/kernel/Makefile:9): the result differs from the exact value by about
+    FAST_MATH_UNIT * A beyond the rounding covered by error_scale. Per operator node, |d f /
+    d v_n| times the published error of the intrinsic it maps to (CUDA C++ Programming Guide,
+    intrinsic functions): __sinf / __cosf absolute 2^-21.41 on [-pi, pi], growing with |a|
+    outside; __logf absolute 2^-21.41 on [0.5, 2], 3 ulp elsewhere; __expf (and the
+    hyperbolics built on it) 2 + 1.173 |a| ulp; __powf through exp2(b log2 a); approximate
+    division, reciprocal and square root 2 ulp."""
+    xs = np.asarray(xs, np.float64)
+    c = np.asarray(c, np.float64)
+    N = xs.shape[0]
+    n = len(nt)
+    vals: list = [None] * n
+    args: list = [None] * n
+    d1: list = [None] * n
+    d2: list = [None] * n
+    st: list = []
+    with np.errstate(all="ignore"):
+        for i in range(n - 1, -1, -1):
+            t = int(nt[i])
+            if t == NTYPE_VAR:
+                v = xs[:, int(nv[i])]
+            elif t == NTYPE_CONST:
+                v = np.full(N, c[int(ci[i])])
+            elif t == NTYPE_UFUNC:
+                a = st.pop()
+                v, d = unary(int(nv[i]), a)
+                args[i] = (a, None)
+                d1[i] = np.abs(d)
+            else:
+                l = st.pop()
+                r = st.pop()
+                v, dl, dr = binary(int(nv[i]), l, r)
+                args[i] = (l, r)
+                d1[i], d2[i] = np.abs(dl), np.abs(dr)
+            vals[i] = v
+            st.append(v)
+        A = np.zeros(N)
+        adj_st = [np.ones(N)]
+        for i in range(n):
+            t = int(nt[i])
+            if t not in (NTYPE_UFUNC, NTYPE_BFUNC):
+                adj_st.pop()
+                continue
+            adj = adj_st.pop()
+            f = int(nv[i])
+            v = np.abs(vals[i])
+            a = np.abs(args[i][0])
+            if t == NTYPE_UFUNC:
+                if f in (F.SIN, F.COS, F.TAN):
+                    e = np.fmax(1.0, a) * (1.0 + (v * v if f == F.TAN else 0.0))
+                elif f in (F.LOG, F.LOOSE_LOG):
+                    e = 1.0 + v
+                elif f in (F.EXP, F.SINH, F.COSH, F.TANH):
+                    e = v * (1.0 + a)
+                else:
+                    e = v
+                A = A + np.nan_to_num(adj * e, nan=np.inf)
+                adj_st.append(adj * d1[i])
+            else:
+                if f in (F.POW, F.LOOSE_POW):
+                    b = np.abs(args[i][1])
+                    e = v * (1.0 + np.abs(np.log(np.fmax(a, 1e-300))) * b)
+                else:
+                    e = v
+                A = A + np.nan_to_num(adj * e, nan=np.inf)
+                adj_st.append(adj * d2[i])
+                adj_st.append(adj * d1[i])
+    return A
+
+
 def intermediate_range(nt, nv, ci, xs, c):
     """Per-sample (max |v|, min nonzero |v|) over every node value of the tree (fp64): tells
     whether a narrower format can represent the evaluation at all (fp32 overflows above

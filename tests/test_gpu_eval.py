@@ -27,7 +27,7 @@ def co():
     c.teardown()
 
 
-def _check_values(co, pop, precision, rel, unit, min_strict=0.97):
+def _check_values(co, pop, precision, rel, unit, min_strict=0.97, fast_k=0.0):
     out = co.evaluate(pop, precision=precision, values=True)
     vals = out["values"]
     strict = total = 0
@@ -44,6 +44,9 @@ def _check_values(co, pop, precision, rel, unit, min_strict=0.97):
             outside = (hi > 1e37) | (lo < 1e-30)   # not representable in normal fp32
         else:
             outside = np.zeros(y.shape, bool)
+        if fast_k:
+            S = S + fast_k / (64.0 * unit) * interp.FAST_MATH_UNIT * interp.fast_math_error_scale(
+                nt, nv, ci, pop["xs"], c)
         ok = conditioned_close(vals[m], y, S, rel, unit) | outside
         assert ok.all(), (m, np.flatnonzero(~ok)[:5], vals[m][~ok][:5], y[~ok][:5])
         fin = np.isfinite(y) & ~outside
@@ -66,11 +69,12 @@ def test_values_fp32_fast_match_oracle(co):
     """The reference kernel's numerics (--use_fast_math): hardware sin/cos/exp/log
     approximations (absolute error about 2^-21.4 on the primary range, growing with |x|),
     approximate division and square root, denormals flushed. Checked against the fp64 oracle
-    with the condition-scaled bound widened to those errors; nearly every sample still meets
-    a plain 1e-4 relative bound."""
+    with the fp32 condition-scaled bound plus 8x the intrinsics' published error bounds
+    propagated through the tree (oracle fast_math_error_scale); most samples still meet a
+    plain 1e-4 relative bound."""
     for pop in (synth.make_config("pr1", M=96, N=300, seed=0),
                 synth.make_config("mid", M=64, N=700, seed=4)):
-        _check_values(co, pop, "fp32_fast", 1e-4, 2.0 ** -20, min_strict=0.85)
+        _check_values(co, pop, "fp32_fast", 1e-5, U32, min_strict=0.85, fast_k=8.0)
         _report_fast_values(co, pop)
 
 
