@@ -23,6 +23,11 @@ INCLUDE = HERE.parent / "include"
 OBJ = HERE / "_build"
 LIB = HERE / "libcusr_b200.so"
 ALIASES = ("libcusr_co_ad.so", "libcusr_co_fd.so")
+# command-line front end with the reference binary's interface, and the names the reference's
+# subprocess callers use for it
+CLI = HERE / "batch_lm_b200"
+CLI_SOURCE = "batch_lm_cli.cpp"
+CLI_ALIASES = ("batch_lm", "batch_lm_ad")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
@@ -78,16 +83,22 @@ def build(force: bool = False, verbose: bool = False, defines: tuple = (), obj_d
         list(ex.map(run, jobs))
     objs = [OBJ / (Path(s).stem + ".o") for s in SOURCES]
     if force or jobs or _stale(LIB, objs):
-        run([nvcc, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart", "-ldl"])
+        run([nvcc, *ARCH, "-shared", "-Xlinker", f"-soname={LIB.name}", "-o", str(LIB),
+             *map(str, objs), "-lcudart", "-ldl"])
     if lib is not None:
         return LIB
-    for alias in ALIASES:
-        a = HERE / alias
-        if a.is_symlink() or a.exists():
-            if a.is_symlink() and os.readlink(a) == LIB.name:
-                continue
-            a.unlink()
-        a.symlink_to(LIB.name)
+    cli_src = CSRC / CLI_SOURCE
+    if force or _stale(CLI, [cli_src, LIB, *hdrs]):
+        run(["g++", "-O2", "-std=c++17", f"-I{INCLUDE}", str(cli_src), "-o", str(CLI),
+             f"-L{HERE}", f"-l:{LIB.name}", "-Wl,-rpath,$ORIGIN"])
+    for names, target in ((ALIASES, LIB.name), (CLI_ALIASES, CLI.name)):
+        for alias in names:
+            a = HERE / alias
+            if a.is_symlink() or a.exists():
+                if a.is_symlink() and os.readlink(a) == target:
+                    continue
+                a.unlink()
+            a.symlink_to(target)
     return LIB
 
 
