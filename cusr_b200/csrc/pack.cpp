@@ -1,6 +1,8 @@
 // pack.cpp — validate pop.bin trees, compile them to register-stack programs, and build the
 // cost-binned evaluation schedule.
 #include "pack.h"
+
+#include <thread>
 #include "ops.h"
 
 #include <algorithm>
@@ -254,25 +256,91 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
     return CO_OK;
 }
 
-int compile_population(const PopHeader *h, const int32_t *nt, const float *nv,
-                       const int32_t *ci, const TreeMeta *metas, PackResult *out) {
-    out->code.clear();
-    out->trees.assign((size_t)h->M_prob, CompiledTree{});
-    out->code.reserve((size_t)h->total_nodes);
-    out->bad_tree = -1;
-    for (int m = 0; m < h->M_prob; ++m) {
+namespace {
+
+// Compile trees [m0, m1) into `code` (offsets relative to its start). On failure returns the
+// code and sets `bad` to the first failing tree.
+int compile_range(const PopHeader *h, const int32_t *nt, const float *nv, const int32_t *ci,
+                  const TreeMeta *metas, int m0, int m1, std::vector<uint32_t> &code,
+                  std::vector<CompiledTree> &trees, int &bad) {
+    for (int m = m0; m < m1; ++m) {
         const TreeMeta &tm = metas[m];
+        bad = m;
         if (tm.K < 0 || tm.K > CO_MAX_K) return CO_ERR_BOUNDS;
         if (tm.n_nodes <= 0 || tm.node_offset < 0 ||
             (int64_t)tm.node_offset + tm.n_nodes > (int64_t)h->total_nodes ||
-            tm.c_offset < 0 || (int64_t)tm.c_offset + tm.K > (int64_t)h->total_c) {
-            out->bad_tree = m;
+            tm.c_offset < 0 || (int64_t)tm.c_offset + tm.K > (int64_t)h->total_c)
             return CO_ERR_BADTREE;
-        }
-        CompiledTree &ct = out->trees[(size_t)m];
         int rc = compile_tree(nt + tm.node_offset, nv + tm.node_offset, ci + tm.node_offset,
-                              tm.n_nodes, tm.K, h->n_vars, out->code, ct);
-        if (rc != CO_OK) { out->bad_tree = m; return rc; }
+                              tm.n_nodes, tm.K, h->n_vars, code, trees[(size_t)m]);
+        if (rc != CO_OK) return rc;
+    }
+    bad = -1;
+    return CO_OK;
+}
+
+}  // namespace
+
+// Trees compile independently: large populations are split into contiguous ranges of about
+// equal node count, compiled on host threads and concatenated in tree order, so the
+// program layout (and every result) is the same as a serial compile.
+int compile_population(const PopHeader *h, const int32_t *nt, const float *nv,
+                       const int32_t *ci, const TreeMeta *metas, PackResult *out) {
+    const int M = h->M_prob;
+    out->code.clear();
+    out->trees.assign((size_t)M, CompiledTree{});
+    out->bad_tree = -1;
+    unsigned hw = std::thread::hardware_concurrency();
+    int n_parts = (int)std::min<unsigned>(hw ? hw : 1, 16);
+    if (M < 4096 || h->total_nodes < (1 << 16)) n_parts = 1;
+    // range boundaries by node count (metas are validated inside the ranges; a corrupt
+    // n_nodes only skews the split)
+    std::vector<int> bounds{0};
+    if (n_parts > 1) {
+        const double per = (double)std::max<int64_t>(h->total_nodes, 1) / n_parts;
+        double acc = 0.0;
+        for (int m = 0; m < M && (int)bounds.size() < n_parts; ++m) {
+            acc += (double)std::max(metas[m].n_nodes, 0);
+            if (acc >= per * (double)bounds.size()) bounds.push_back(m + 1);
+        }
+    }
+    if (bounds.back() != M) bounds.push_back(M);
+    const int P = (int)bounds.size() - 1;
+    std::vector<std::vector<uint32_t>> codes((size_t)P);
+    std::vector<int> rcs((size_t)P, CO_OK), bads((size_t)P, -1);
+    auto work = [&](int p) {
+        codes[(size_t)p].reserve((size_t)h->total_nodes / (size_t)P + 64);
+        rcs[(size_t)p] = compile_range(h, nt, nv, ci, metas, bounds[(size_t)p],
+                                       bounds[(size_t)p + 1], codes[(size_t)p], out->trees,
+                                       bads[(size_t)p]);
+    };
+    if (P == 1) {
+        work(0);
+    } else {
+        std::vector<std::thread> th;
+        th.reserve((size_t)P);
+        for (int p = 0; p < P; ++p) th.emplace_back(work, p);
+        for (std::thread &t : th) t.join();
+    }
+    for (int p = 0; p < P; ++p) {
+        if (rcs[(size_t)p] != CO_OK) {   // the lowest failing tree, as a serial compile
+            out->bad_tree = bads[(size_t)p];
+            return rcs[(size_t)p];
+        }
+    }
+    size_t total = 0;
+    for (const auto &c : codes) total += c.size();
+    out->code.reserve(total);
+    for (int p = 0; p < P; ++p) {
+        const int32_t base = (int32_t)out->code.size();
+        for (int m = bounds[(size_t)p]; m < bounds[(size_t)p + 1]; ++m) {
+            CompiledTree &ct = out->trees[(size_t)m];
+            ct.code_off += base;
+            ct.bcode_off += base;
+        }
+        out->code.insert(out->code.end(), codes[(size_t)p].begin(), codes[(size_t)p].end());
+    }
+    for (const CompiledTree &ct : out->trees) {
         out->max_instr = std::max(out->max_instr, ct.n_instr + ct.n_bwd);
         out->max_spill = std::max(out->max_spill, ct.n_spill);
         out->max_tape = std::max(out->max_tape, ct.n_tape);
