@@ -88,7 +88,8 @@ class CoOptions(ctypes.Structure):
         ("max_iter", ctypes.c_int32), ("y_shared", ctypes.c_int32),
         ("lambda0", ctypes.c_double), ("xtol", ctypes.c_double),
         ("fp64_audit", ctypes.c_int32), ("early_exit", ctypes.c_int32),
-        ("sample_sharded", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7),
+        ("sample_sharded", ctypes.c_int32), ("keep_inputs", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 6),
     ]
 
 
@@ -224,7 +225,7 @@ class InProcessCO:
 
     _build_header = staticmethod(build_header)
 
-    def _inputs(self, pop: dict, y_shared: bool = False):
+    def _inputs(self, pop: dict, y_shared: bool = False, keep_inputs: bool = False):
         M = int(pop["M"])
         keep = []
 
@@ -233,6 +234,10 @@ class InProcessCO:
             keep.append(a)
             return p
 
+        if keep_inputs:   # X / y stay resident on the device: no pointers passed
+            metas_buf = self._metas(pop, keep)
+            return (ptr("nt", np.int32), ptr("nv", np.float32), ptr("ci", np.int32), metas_buf,
+                    ptr("c_init", np.float32), None, None), keep
         ym = np.asarray(pop["ym"], np.float32)
         if y_shared:
             ym = ym.reshape(-1)[: int(pop["N"])]
@@ -241,13 +246,19 @@ class InProcessCO:
             ym = np.broadcast_to(ym, (M, int(pop["N"])))
         ym_p, ym_a = _c_ptr(ym, np.float32)
         keep.append(ym_a)
+        metas_buf = self._metas(pop, keep)
+        return (ptr("nt", np.int32), ptr("nv", np.float32), ptr("ci", np.int32), metas_buf,
+                ptr("c_init", np.float32), ptr("xs", np.float32), ym_p), keep
+
+    @staticmethod
+    def _metas(pop: dict, keep: list):
+        M = int(pop["M"])
         metas_np = np.ascontiguousarray(pop["metas"], dtype=np.int32).reshape(M, 4)
         metas_buf = (TreeMeta * max(M, 1))()
         if M:
             ctypes.memmove(metas_buf, metas_np.ctypes.data, M * 16)
         keep.append(metas_buf)
-        return (ptr("nt", np.int32), ptr("nv", np.float32), ptr("ci", np.int32), metas_buf,
-                ptr("c_init", np.float32), ptr("xs", np.float32), ym_p), keep
+        return metas_buf
 
     def optimize(self, pop: dict, max_iter: int = 50):
         """Reference-compatible fit (fp32). Returns {'c_final','status','loss_init',
@@ -276,12 +287,14 @@ class InProcessCO:
 
     def optimize_ex(self, pop: dict, max_iter: int = 50, precision: str = "fp32",
                     y_shared: bool | None = None, lambda0: float = 1e-3, xtol: float = 1e-6,
-                    fp64_audit: int = -1, early_exit: bool = True):
-        """Extended fit: precision 'fp32' | 'fp64'; y_shared=True passes one target row
-        (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a 1-D ym).
+                    fp64_audit: int = -1, early_exit: bool = True, keep_inputs: bool = False):
+        """Extended fit: precision 'fp32' | 'fp64' | 'fp32_fast'; y_shared=True passes one
+        target row (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a
+        1-D ym). keep_inputs=True reuses the X / shared y left on the device by the previous
+        call (pop needs no 'xs' / 'ym' then): the in-loop case of new trees on fixed data.
         Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters."""
         return self._fit_ex("co_optimize_ex", pop, max_iter, precision, y_shared, lambda0,
-                            xtol, fp64_audit, early_exit)
+                            xtol, fp64_audit, early_exit, keep_inputs)
 
     def shard_init(self, unique_id: bytes, nranks: int, rank: int,
                    timeout_s: float = 120.0) -> None:
@@ -297,23 +310,27 @@ class InProcessCO:
 
     def optimize_sharded(self, pop: dict, max_iter: int = 50, precision: str = "fp32",
                          y_shared: bool | None = None, lambda0: float = 1e-3,
-                         xtol: float = 1e-6, fp64_audit: int = -1, early_exit: bool = True):
+                         xtol: float = 1e-6, fp64_audit: int = -1, early_exit: bool = True,
+                         keep_inputs: bool = False):
         """Sample-sharded fit (co_optimize_sharded): `pop` carries the whole population but
         only this rank's slice of the samples (pop['N'], 'xs', 'ym'); the normal equations
         are summed over the group every iteration, so every rank returns the same result."""
         return self._fit_ex("co_optimize_sharded", pop, max_iter, precision, y_shared, lambda0,
-                            xtol, fp64_audit, early_exit)
+                            xtol, fp64_audit, early_exit, keep_inputs)
 
     def _fit_ex(self, entry, pop, max_iter, precision, y_shared, lambda0, xtol, fp64_audit,
-                early_exit):
+                early_exit, keep_inputs=False):
         if self._torn:
             raise RuntimeError("InProcessCO used after teardown()")
         M, total_c = int(pop["M"]), int(pop["total_c"])
-        if y_shared is None:
+        if keep_inputs:
+            y_shared = True
+        elif y_shared is None:
             y_shared = np.asarray(pop["ym"]).ndim == 1
         hdr = build_header(pop)
-        args, keep = self._inputs(pop, y_shared=bool(y_shared))
+        args, keep = self._inputs(pop, y_shared=bool(y_shared), keep_inputs=keep_inputs)
         opt = self._options(max_iter, precision, y_shared, lambda0, xtol, fp64_audit, early_exit)
+        opt.keep_inputs = 1 if keep_inputs else 0
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)

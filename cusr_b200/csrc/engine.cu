@@ -78,6 +78,9 @@ struct Ctx {
     std::vector<int32_t> n_nodes, n_ops;
     int prep_prec = -1;     // arithmetic type of the loaded problem (CO_PREC_FP32 / _FP64)
     bool fast = false;      // fp32 launches use the fast-math instantiations (CO_PREC_FP32_FAST)
+    // the inputs resident in xs / ym (for CoOptions.keep_inputs)
+    bool in_valid = false, in_shared = false;
+    int in_N = -1, in_nvars = -1;
     bool loaded = false;
     // sample-sharded mode
     ShardComm shard;
@@ -152,6 +155,7 @@ struct Problem {
     const int32_t *ci;
     const TreeMeta *metas;
     const float *c_init, *xs, *ym;
+    bool keep_inputs = false;   // X / shared y resident from the previous upload
 };
 
 int check_args(const Problem &pr) {
@@ -265,8 +269,11 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     // ---- compile + schedule (host) ----
     int rc = compile_population(h, pr.nt, pr.nv, pr.ci, pr.metas, &pp.pk);
     if (rc != CO_OK) return rc;
+    if (pr.keep_inputs &&
+        !(ctx->in_valid && ctx->in_shared && ctx->in_N == N && ctx->in_nvars == n_vars))
+        return CO_ERR_NULLARG;
     // shared targets: an explicit single row, or every row equal to row 0
-    bool y_shared = y_shared_in;
+    bool y_shared = y_shared_in || pr.keep_inputs;
     if (!y_shared && N > 0 && M > 0) {
         y_shared = true;
         const size_t rb = (size_t)N * sizeof(float);
@@ -336,6 +343,10 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     if (!bin_item_off.empty())
         CK(cudaMemcpyAsync(ctx->bin_item_off.ptr, bin_item_off.data(),
                            bin_item_off.size() * sizeof(int64_t), cudaMemcpyHostToDevice, s));
+    if (pr.keep_inputs) {
+        // X and the shared row are already in xs / ym, in this layout (same N, n_vars)
+    } else {
+    ctx->in_valid = false;
     if ((size_t)N * n_vars > 0) {
         CK(cudaMemcpyAsync(ctx->xs_raw.ptr, pr.xs, (size_t)N * n_vars * sizeof(float),
                            cudaMemcpyHostToDevice, s));
@@ -350,6 +361,11 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
         CK(cudaMemcpy2DAsync(ctx->ym.ptr, (size_t)ldx * sizeof(float), pr.ym,
                              (size_t)N * sizeof(float), (size_t)N * sizeof(float), (size_t)y_rows,
                              cudaMemcpyHostToDevice, s));
+    }
+    ctx->in_valid = true;
+    ctx->in_shared = y_shared;
+    ctx->in_N = N;
+    ctx->in_nvars = n_vars;
     }
     if (total_c > 0)
         CK(cudaMemcpyAsync(ctx->cinit_f.ptr, pr.c_init, total_c * sizeof(float),
@@ -755,6 +771,25 @@ void co_default_options(CoOptions *opt) {
     opt->early_exit = 1;
 }
 
+// Caller options over the defaults: the first struct_size bytes of the caller's struct are
+// taken (at least the fields up to early_exit, the original layout), later fields keep their
+// defaults, so callers built against an older, shorter CoOptions keep working.
+static bool read_options(const CoOptions *in, CoOptions *out) {
+    co_default_options(out);
+    if (!in) return true;
+    const int32_t min_size = (int32_t)offsetof(CoOptions, sample_sharded);
+    if (in->struct_size < min_size) return false;
+    const size_t n = std::min<size_t>((size_t)in->struct_size, sizeof(CoOptions));
+    std::memcpy(out, in, n);
+    out->struct_size = (int32_t)sizeof(CoOptions);
+    return true;
+}
+
+static bool has_inputs(const float *xs, const float *ym, const CoOptions *opt_in) {
+    return (xs && ym) || (opt_in && opt_in->struct_size >= (int32_t)offsetof(CoOptions, reserved) &&
+                          opt_in->keep_inputs);
+}
+
 int co_init(int device_id, void **handle_out) {
     if (!handle_out) return CO_ERR_NULLARG;
     *handle_out = nullptr;
@@ -820,6 +855,7 @@ static int optimize_common(void *handle, const PopHeader *h, const int32_t *nt, 
                            const Outputs &out) {
     Ctx *ctx = (Ctx *)handle;
     Problem pr{h, nt, nv, ci, metas, c_init, xs, ym};
+    pr.keep_inputs = opt.keep_inputs != 0;
     int rc = check_args(pr);
     if (rc != CO_OK) return rc;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
@@ -851,15 +887,11 @@ int co_optimize_ex(void *handle, const PopHeader *h, const int32_t *nt, const fl
                    const float *ym, const CoOptions *opt_in, double *c_final_out,
                    int32_t *status_out, double *loss_init_out, double *loss_final_out,
                    int32_t *iters_out) {
-    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym || !c_final_out ||
-        !status_out)
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init ||
+        !has_inputs(xs, ym, opt_in) || !c_final_out || !status_out)
         return CO_ERR_NULLARG;
     CoOptions opt;
-    co_default_options(&opt);
-    if (opt_in) {
-        if (opt_in->struct_size < (int32_t)offsetof(CoOptions, reserved)) return CO_ERR_NULLARG;
-        opt = *opt_in;
-    }
+    if (!read_options(opt_in, &opt)) return CO_ERR_NULLARG;
     if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
     opt.sample_sharded = 0;
@@ -895,14 +927,14 @@ int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float
 int co_load(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
             const int32_t *ci, const TreeMeta *metas, const float *c_init, const float *xs,
             const float *ym, const CoOptions *opt_in) {
-    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym)
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !has_inputs(xs, ym, opt_in))
         return CO_ERR_NULLARG;
     CoOptions opt;
-    co_default_options(&opt);
-    if (opt_in) opt = *opt_in;
+    if (!read_options(opt_in, &opt)) return CO_ERR_NULLARG;
     if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
     Ctx *ctx = (Ctx *)handle;
     Problem pr{h, nt, nv, ci, metas, c_init, xs, ym};
+    pr.keep_inputs = opt.keep_inputs != 0;
     int rc = check_args(pr);
     if (rc != CO_OK) return rc;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
@@ -918,8 +950,7 @@ int co_fit_loaded(void *handle, const CoOptions *opt_in, double *c_final_out,
     if (!handle || !c_final_out || !status_out) return CO_ERR_NULLARG;
     Ctx *ctx = (Ctx *)handle;
     CoOptions opt;
-    co_default_options(&opt);
-    if (opt_in) opt = *opt_in;
+    if (!read_options(opt_in, &opt)) return CO_ERR_NULLARG;
     if (!ctx->loaded || !valid_prec(opt.precision) ||
         (opt.precision == CO_PREC_FP64) != (ctx->prep_prec == CO_PREC_FP64))
         return CO_ERR_NULLARG;
@@ -989,17 +1020,13 @@ int co_optimize_sharded(void *handle, const PopHeader *h, const int32_t *nt, con
                         const float *xs, const float *ym, const CoOptions *opt_in,
                         double *c_final_out, int32_t *status_out, double *loss_init_out,
                         double *loss_final_out, int32_t *iters_out) {
-    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init || !xs || !ym || !c_final_out ||
-        !status_out)
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c_init ||
+        !has_inputs(xs, ym, opt_in) || !c_final_out || !status_out)
         return CO_ERR_NULLARG;
     Ctx *ctx = (Ctx *)handle;
     if (!ctx->shard.comm) return CO_ERR_NULLARG;   // co_shard_init first
     CoOptions opt;
-    co_default_options(&opt);
-    if (opt_in) {
-        if (opt_in->struct_size < (int32_t)offsetof(CoOptions, reserved)) return CO_ERR_NULLARG;
-        opt = *opt_in;
-    }
+    if (!read_options(opt_in, &opt)) return CO_ERR_NULLARG;
     opt.sample_sharded = 1;
     if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
     if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;

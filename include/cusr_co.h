@@ -128,7 +128,13 @@ typedef struct CoOptions {
     int32_t sample_sharded; /* 1: all-reduce over the co_shard_init group (set by      */
                             /* co_optimize_sharded; honoured by co_fit_loaded; ignored  */
                             /* by co_optimize_ex)                                       */
-    int32_t reserved[7];
+    int32_t keep_inputs;    /* 1: reuse the inputs X and the SHARED target row resident  */
+                            /* from the previous call on this handle (same N, n_vars);   */
+                            /* xs / ym are not read and may be NULL. In-loop callers     */
+                            /* (new trees and c_init every generation, fixed data) skip  */
+                            /* the re-upload. CO_ERR_NULLARG if nothing compatible is    */
+                            /* resident. (co_optimize_ex, co_optimize_sharded, co_load)  */
+    int32_t reserved[6];
 } CoOptions;
 
 /* Fill `opt` with the reference defaults (fp32, 50 iterations, lambda0 1e-3, xtol 1e-6,
