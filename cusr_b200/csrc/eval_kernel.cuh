@@ -334,6 +334,11 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
                 sp[w_sd(w) * NT] = pack<T, V>(a);
                 break;
             }
+            case B_SCALE_1MT0: {
+                const VT t0 = tp[w_ts(w) * NT];
+                CUSR_FOR_V adj[j] = safe_mul(adj[j], T(1) - t0.v[j]);
+                break;
+            }
             default:
                 // every word was checked against this case set on the host
                 // (valid_forward_code / valid_reverse_code), so no bounds check is needed

@@ -56,21 +56,37 @@ uint32_t map_binary(int fid) {
     }
 }
 
+// Code generation. Forward: each node's value is left in TOS (register), leaves feeding a
+// binary operator are folded into it, two subtree children run in Sethi–Ullman order with
+// the first one spilled. Reverse: generated from the same tree walk, so it addresses the
+// forward program's spill and tape slots.
+//
+// Activity: a node is active when its subtree holds a constant. Only active nodes have
+// adjoint work (the derivative of f with respect to the constants never flows through a
+// constant-free subtree), so the reverse program skips inactive subtrees entirely, and the
+// tape partials of inactive nodes are not kept: their forward stores go to two dump slots
+// (0, 1) instead of slots of their own. Values are unchanged; the gradient is the same
+// sum of the same products, minus the terms that are structurally zero.
 struct Gen {
     const std::vector<Node> &nodes;
+    const std::vector<char> &act;
     std::vector<uint32_t> &code;
+    std::vector<uint32_t> word;   // per node: its forward instruction (leaf: PUSH / LOAD)
+    std::vector<int32_t> first;   // per two-subtree node: the child evaluated (and spilled) first
     int dep = 0, max_dep = 0, tape = 0;
     bool overflow = false;
 
     bool is_leaf(int i) const { return nodes[i].type == NT_VAR || nodes[i].type == NT_CONST; }
     uint32_t leaf_mode(int i) const { return nodes[i].type == NT_VAR ? M_VAR : M_CONST; }
 
-    uint32_t alloc_tape(uint32_t op, uint32_t mode) {
+    uint32_t alloc_tape(uint32_t op, uint32_t mode, bool keep) {
         int n = tape_slots(op, mode);
+        if (!n) return 0;
+        if (!keep) return 0;           // dump slots 0..1
         int ts = tape;
         tape += n;
         if (tape > PROG_MAX_TAPE) overflow = true;
-        return (uint32_t)(n ? ts : 0);
+        return (uint32_t)ts;
     }
 
     void emit_leaf(int i, bool live) {
@@ -83,19 +99,21 @@ struct Gen {
         const bool var = nodes[i].type == NT_VAR;
         const uint32_t xop = live ? (var ? XOP_PUSH_VAR : XOP_PUSH_CONST)
                                   : (var ? XOP_LOAD_VAR : XOP_LOAD_CONST);
-        code.push_back(enc(xop, (uint32_t)nodes[i].idx, sd, 0));
+        word[(size_t)i] = enc(xop, (uint32_t)nodes[i].idx, sd, 0);
+        code.push_back(word[(size_t)i]);
     }
 
     // binary instruction with canonical operand order: commutative operators never swap, a
     // swapped comparison becomes the mirrored comparison
-    void emit_bin(uint32_t op, uint32_t mode, uint32_t swap, uint32_t idx, uint32_t sd) {
+    void emit_bin(int i, uint32_t op, uint32_t mode, uint32_t swap, uint32_t idx, uint32_t sd) {
         if (swap && (op == OP_ADD || op == OP_MUL || op == OP_BZERO)) swap = 0;
         if (swap && (op == OP_LT || op == OP_GT || op == OP_LE || op == OP_GE)) {
             op = op == OP_LT ? OP_GT : op == OP_GT ? OP_LT : op == OP_LE ? OP_GE : OP_LE;
             swap = 0;
         }
-        const uint32_t ts = alloc_tape(op, mode);
-        code.push_back(enc(xop_bin(op, mode, swap), idx, sd, ts));
+        const uint32_t ts = alloc_tape(op, mode, act[(size_t)i] != 0);
+        word[(size_t)i] = enc(xop_bin(op, mode, swap), idx, sd, ts);
+        code.push_back(word[(size_t)i]);
     }
 
     // Emit code leaving node i's value in TOS. `live`: TOS holds a value that must survive.
@@ -105,69 +123,131 @@ struct Gen {
         if (n.type == NT_UFUNC) {
             gen(n.left, live);
             const uint32_t op = (uint32_t)n.op;
-            const uint32_t ts = alloc_tape(op, M_NONE);
-            code.push_back(enc(xop_un(op), 0, 0, ts));
+            const uint32_t ts = alloc_tape(op, M_NONE, act[(size_t)i] != 0);
+            word[(size_t)i] = enc(xop_un(op), 0, 0, ts);
+            code.push_back(word[(size_t)i]);
             return;
         }
         const int L = n.left, R = n.right;
         const uint32_t op = (uint32_t)n.op;
         if (is_leaf(R)) {                       // TOS = value(L) OP leaf
             gen(L, live);
-            emit_bin(op, leaf_mode(R), 0, (uint32_t)nodes[R].idx, 0);
+            emit_bin(i, op, leaf_mode(R), 0, (uint32_t)nodes[R].idx, 0);
             return;
         }
         if (is_leaf(L)) {                       // TOS = leaf OP value(R)
             gen(R, live);
-            emit_bin(op, leaf_mode(L), 1, (uint32_t)nodes[L].idx, 0);
+            emit_bin(i, op, leaf_mode(L), 1, (uint32_t)nodes[L].idx, 0);
             return;
         }
         // both children are subtrees: the one with the larger need goes first and is spilled
         const bool left_first = nodes[L].need >= nodes[R].need;
-        const int first = left_first ? L : R, second = left_first ? R : L;
-        gen(first, live);
+        const int f = left_first ? L : R, second = left_first ? R : L;
+        first[(size_t)i] = f;
+        gen(f, live);
         gen(second, true);
         --dep;
-        emit_bin(op, M_POP, left_first ? 1u : 0u, 0, (uint32_t)dep);
+        emit_bin(i, op, M_POP, left_first ? 1u : 0u, 0, (uint32_t)dep);
+    }
+
+    // ---- reverse program ----
+    std::vector<uint32_t> *rev = nullptr;
+    void put(uint32_t b, uint32_t idx, uint32_t sd, uint32_t ts) { rev->push_back(enc(b, idx, sd, ts)); }
+
+    // Reverse of node i's subtree with its adjoint in `adj`. `restore`: the forward code of
+    // this subtree began with a PUSH whose spill slot `rsd` holds the adjoint of an active
+    // sibling evaluated earlier; that adjoint is reloaded once this subtree is done.
+    void rgen(int i, bool restore, uint32_t rsd) {
+        const Node &n = nodes[(size_t)i];
+        if (n.type == NT_CONST) {
+            if (restore) put(B_GRAD_RESTORE, (uint32_t)n.idx, rsd, 0);
+            else put(B_GRAD, (uint32_t)n.idx, 0, 0);
+            return;
+        }
+        if (!act[(size_t)i]) {                  // VAR leaf or constant-free subtree
+            if (restore) put(B_RESTORE, 0, rsd, 0);
+            return;
+        }
+        const uint32_t w = word[(size_t)i];
+        uint32_t op, mode, swap;
+        decode_xop(w_code(w), op, mode, swap);
+        const uint32_t idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
+        if (n.type == NT_UFUNC) {
+            put(op == OP_NEG ? B_NEG : (op == OP_UZERO ? B_ZERO : B_SCALE_T0), 0, 0, ts);
+            rgen(n.left, restore, rsd);
+            return;
+        }
+        const bool V = mode == M_VAR, C = mode == M_CONST;
+        if (V || C) {
+            // TOS = the subtree child t, source = the folded leaf (active iff a constant)
+            const int t = is_leaf(n.right) ? n.left : n.right;
+            const bool at = act[(size_t)t] != 0;
+            int b = -1;
+            switch (op) {
+                case OP_ADD: b = V ? -1 : B_GRAD; break;
+                case OP_SUB:
+                    if (!swap) b = V ? -1 : B_GRAD_NEG;
+                    else b = V ? B_NEG : (at ? B_GRAD_THEN_NEG : B_GRAD);
+                    break;
+                case OP_MUL: b = V ? B_SCALE_X : B_MULC; break;
+                case OP_DIV: case OP_POW: case OP_POWABS: b = V ? B_SCALE_T0 : B_GRAD_T1_T0; break;
+                case OP_MAX: case OP_MIN: b = V ? B_SCALE_T0 : B_GRAD_1MT0_T0; break;
+                default: b = V ? B_ZERO : B_GRAD_ZERO; break;
+            }
+            if (C && !at) {
+                // only the constant needs its partial; the TOS subtree is inactive
+                if (b == B_GRAD && restore) { put(B_GRAD_RESTORE, idx, rsd, 0); return; }
+                put((uint32_t)b, idx, 0, ts);
+                if (restore) put(B_RESTORE, 0, rsd, 0);
+                return;
+            }
+            if (b >= 0) put((uint32_t)b, idx, 0, ts);
+            rgen(t, restore, rsd);
+            return;
+        }
+        // M_POP: TOS = the second-evaluated child, the spill slot sd = the first
+        const int fc = first[(size_t)i], second = fc == n.left ? n.right : n.left;
+        const bool af = act[(size_t)fc] != 0, as = act[(size_t)second] != 0;
+        // partials: dt (TOS) at ts, ds (spilled operand) at ts + 1 (MAX / MIN: ds = 1 - dt)
+        if (af && as) {
+            int b;
+            switch (op) {
+                case OP_ADD: b = B_SPILL; break;
+                case OP_SUB: b = swap ? B_SPILL_THEN_NEG : B_SPILL_NEG; break;
+                case OP_MUL: case OP_DIV: case OP_POW: case OP_POWABS: b = B_SPILL_T1_T0; break;
+                case OP_MAX: case OP_MIN: b = B_SPILL_1MT0_T0; break;
+                default: b = B_SPILL_ZERO; break;
+            }
+            put((uint32_t)b, 0, sd, ts);
+            rgen(second, true, sd);
+            rgen(fc, restore, rsd);
+        } else if (as) {                        // adjoint to the TOS operand only
+            int b;
+            switch (op) {
+                case OP_ADD: b = -1; break;
+                case OP_SUB: b = swap ? B_NEG : -1; break;
+                case OP_MUL: case OP_DIV: case OP_POW: case OP_POWABS:
+                case OP_MAX: case OP_MIN: b = B_SCALE_T0; break;
+                default: b = B_ZERO; break;
+            }
+            if (b >= 0) put((uint32_t)b, 0, 0, ts);
+            rgen(second, false, 0);
+            if (restore) put(B_RESTORE, 0, rsd, 0);
+        } else {                                // adjoint to the spilled operand only
+            int b;
+            uint32_t t = ts;
+            switch (op) {
+                case OP_ADD: b = -1; break;
+                case OP_SUB: b = swap ? -1 : B_NEG; break;
+                case OP_MUL: case OP_DIV: case OP_POW: case OP_POWABS: b = B_SCALE_T0; t = ts + 1; break;
+                case OP_MAX: case OP_MIN: b = B_SCALE_1MT0; break;
+                default: b = B_ZERO; break;
+            }
+            if (b >= 0) put((uint32_t)b, 0, 0, t);
+            rgen(fc, restore, rsd);
+        }
     }
 };
-
-// Reverse program: forward instructions in reverse order, each mapped to its adjoint update;
-// instructions without reverse work are dropped.
-void emit_reverse(const uint32_t *fwd, int n, std::vector<uint32_t> &out) {
-    for (int pc = n - 1; pc >= 0; --pc) {
-        const uint32_t w = fwd[pc];
-        const uint32_t xop = w_code(w), idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
-        uint32_t op, mode, swap;
-        decode_xop(xop, op, mode, swap);
-        int b = -1;
-        if (op == OP_LOAD) {
-            if (xop == XOP_LOAD_CONST) b = B_GRAD;
-            else if (xop == XOP_PUSH_CONST) b = B_GRAD_RESTORE;
-            else if (xop == XOP_PUSH_VAR) b = B_RESTORE;
-        } else if (op < OP_ADD) {
-            if (op == OP_NEG) b = B_NEG;
-            else if (op == OP_UZERO) b = B_ZERO;
-            else b = B_SCALE_T0;
-        } else {
-            const bool V = mode == M_VAR, C = mode == M_CONST;
-            switch (op) {
-                case OP_ADD: b = V ? -1 : (C ? B_GRAD : B_SPILL); break;
-                case OP_SUB:
-                    if (!swap) b = V ? -1 : (C ? B_GRAD_NEG : B_SPILL_NEG);
-                    else b = V ? B_NEG : (C ? B_GRAD_THEN_NEG : B_SPILL_THEN_NEG);
-                    break;
-                case OP_MUL: b = V ? B_SCALE_X : (C ? B_MULC : B_SPILL_T1_T0); break;
-                case OP_DIV: case OP_POW: case OP_POWABS:
-                    b = V ? B_SCALE_T0 : (C ? B_GRAD_T1_T0 : B_SPILL_T1_T0); break;
-                case OP_MAX: case OP_MIN:
-                    b = V ? B_SCALE_T0 : (C ? B_GRAD_1MT0_T0 : B_SPILL_1MT0_T0); break;
-                default:   // comparisons, unknown operator: zero partials
-                    b = V ? B_ZERO : (C ? B_GRAD_ZERO : B_SPILL_ZERO); break;
-            }
-        }
-        if (b >= 0) out.push_back(enc((uint32_t)b, idx, sd, ts));
-    }
-}
 
 }  // namespace
 
@@ -179,6 +259,7 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
     std::vector<int32_t> st;
     st.reserve((size_t)n);
     std::vector<int32_t> seen((size_t)std::max(K, 1), 0);
+    std::vector<char> act((size_t)n, 0);   // subtree holds a constant (children first)
     bool unique = true;
     // Right-to-left scan: the same visiting order as the reference interpreter
     // (lm_core.cuh:63), building the child links of each function node.
@@ -198,6 +279,7 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
                 if (k < 0 || k >= K) return CO_ERR_BADTREE;
                 nd.idx = k; nd.need = 1;
                 if (seen[(size_t)k]++) unique = false;
+                act[(size_t)i] = 1;
                 st.push_back(i);
                 break;
             }
@@ -206,6 +288,7 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
                 nd.left = st.back(); st.pop_back();
                 nd.op = (int32_t)map_unary((int)nv[i]);
                 nd.need = nodes[(size_t)nd.left].need;
+                act[(size_t)i] = act[(size_t)nd.left];
                 st.push_back(i);
                 break;
             }
@@ -214,6 +297,7 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
                 nd.left = st.back(); st.pop_back();    // first child in prefix order = left
                 nd.right = st.back(); st.pop_back();
                 nd.op = (int32_t)map_binary((int)nv[i]);
+                act[(size_t)i] = (char)(act[(size_t)nd.left] | act[(size_t)nd.right]);
                 const Node &l = nodes[(size_t)nd.left], &r = nodes[(size_t)nd.right];
                 const bool lleaf = l.type == NT_VAR || l.type == NT_CONST;
                 const bool rleaf = r.type == NT_VAR || r.type == NT_CONST;
@@ -232,14 +316,32 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
         if (seen[(size_t)k] != 1) unique = false;
 
     ct.code_off = (int32_t)code.size();
-    Gen g{nodes, code};
+    // dump slots for the partials of inactive nodes (only when some inactive node has any)
+    bool dump = false;
+    for (int i = 0; i < n && !dump; ++i) {
+        const Node &nd = nodes[(size_t)i];
+        if (act[(size_t)i] || (nd.type != NT_UFUNC && nd.type != NT_BFUNC)) continue;
+        uint32_t mode = M_NONE;
+        if (nd.type == NT_BFUNC) {
+            const Node &r = nodes[(size_t)nd.right], &l = nodes[(size_t)nd.left];
+            if (r.type == NT_VAR || r.type == NT_CONST) mode = r.type == NT_VAR ? M_VAR : M_CONST;
+            else if (l.type == NT_VAR || l.type == NT_CONST) mode = l.type == NT_VAR ? M_VAR : M_CONST;
+            else mode = M_POP;
+        }
+        dump = tape_slots((uint32_t)nd.op, mode) > 0;
+    }
+    Gen g{nodes, act, code};
+    g.word.assign((size_t)n, 0u);
+    g.first.assign((size_t)n, -1);
+    g.tape = dump ? 2 : 0;
     g.gen(0, false);
     if (g.overflow) { code.resize((size_t)ct.code_off); return CO_ERR_BOUNDS; }
     ct.n_instr = (int32_t)code.size() - ct.code_off;
     ct.bcode_off = (int32_t)code.size();
     {
         std::vector<uint32_t> rev;
-        emit_reverse(code.data() + ct.code_off, ct.n_instr, rev);
+        g.rev = &rev;
+        g.rgen(0, false, 0);
         code.insert(code.end(), rev.begin(), rev.end());
     }
     ct.n_bwd = (int32_t)code.size() - ct.bcode_off;
@@ -515,6 +617,7 @@ double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, in
             case B_ZERO: adj = 0.0; break;
             case B_GRAD_ZERO: adj = 0.0; break;
             case B_SPILL_ZERO: spill[sd] = 0.0; adj = 0.0; break;
+            case B_SCALE_1MT0: adj = safe_mul(adj, 1.0 - t0); break;
             default: break;
         }
     }

@@ -104,6 +104,7 @@ enum BOp : uint32_t {
     B_ZERO,              // adj <- 0
     B_GRAD_ZERO,         // grad[idx] <- 0; adj <- 0
     B_SPILL_ZERO,        // spill[sd] <- 0; adj <- 0
+    B_SCALE_1MT0,        // adj <- safe(adj, 1 - t0)
     B_COUNT
 };
 
