@@ -184,10 +184,10 @@ __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code,
                 break;
             }
 #define CUSR_UN(OPC) case xop_un(OPC): fwd_un<T, V, NT, GRAD, OPC>(w, tp, tos); break;
-            CUSR_UN(OP_SIN) CUSR_UN(OP_COS) CUSR_UN(OP_TAN) CUSR_UN(OP_SINH)
-            CUSR_UN(OP_COSH) CUSR_UN(OP_TANH) CUSR_UN(OP_LOG) CUSR_UN(OP_LOGABS)
-            CUSR_UN(OP_EXP) CUSR_UN(OP_INV) CUSR_UN(OP_NEG) CUSR_UN(OP_ABS)
-            CUSR_UN(OP_SQRT) CUSR_UN(OP_SQRTABS) CUSR_UN(OP_UZERO)
+            CUSR_UN(OP_SIN) CUSR_UN(OP_COS) CUSR_UN(OP_LOG) CUSR_UN(OP_LOGABS)
+            CUSR_UN(OP_SQRT) CUSR_UN(OP_SQRTABS)
+            CUSR_UN(OP_TAN) CUSR_UN(OP_SINH) CUSR_UN(OP_COSH) CUSR_UN(OP_TANH)
+            CUSR_UN(OP_EXP) CUSR_UN(OP_INV) CUSR_UN(OP_NEG) CUSR_UN(OP_ABS) CUSR_UN(OP_UZERO)
 #undef CUSR_UN
 #define CUSR_B(OPC, MODE, SW)                                                          \
     case xop_bin(OPC, MODE, SW):                                                       \
@@ -332,6 +332,11 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
                 T a[V];
                 CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
                 sp[w_sd(w) * NT] = pack<T, V>(a);
+                break;
+            }
+            case B_SCALE2_T: {
+                const VT t0 = tp[w_ts(w) * NT], t1 = tp[w_idx(w) * NT];
+                CUSR_FOR_V adj[j] = safe_mul(safe_mul(adj[j], t0.v[j]), t1.v[j]);
                 break;
             }
             case B_SCALE_1MT0: {

@@ -173,7 +173,15 @@ struct Gen {
         decode_xop(w_code(w), op, mode, swap);
         const uint32_t idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
         if (n.type == NT_UFUNC) {
-            put(op == OP_NEG ? B_NEG : (op == OP_UZERO ? B_ZERO : B_SCALE_T0), 0, 0, ts);
+            const uint32_t b = op == OP_NEG ? B_NEG : (op == OP_UZERO ? B_ZERO : B_SCALE_T0);
+            // two chained scaling unary nodes: one instruction
+            const Node &c = nodes[(size_t)n.left];
+            if (b == B_SCALE_T0 && c.type == NT_UFUNC && c.op != OP_NEG && c.op != OP_UZERO) {
+                put(B_SCALE2_T, w_ts(word[(size_t)n.left]), 0, ts);
+                rgen(c.left, restore, rsd);
+                return;
+            }
+            put(b, 0, 0, ts);
             rgen(n.left, restore, rsd);
             return;
         }
@@ -618,6 +626,7 @@ double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, in
             case B_GRAD_ZERO: adj = 0.0; break;
             case B_SPILL_ZERO: spill[sd] = 0.0; adj = 0.0; break;
             case B_SCALE_1MT0: adj = safe_mul(adj, 1.0 - t0); break;
+            case B_SCALE2_T: adj = safe_mul(safe_mul(adj, t0), tape[w_idx(w)]); break;
             default: break;
         }
     }

@@ -105,6 +105,7 @@ enum BOp : uint32_t {
     B_GRAD_ZERO,         // grad[idx] <- 0; adj <- 0
     B_SPILL_ZERO,        // spill[sd] <- 0; adj <- 0
     B_SCALE_1MT0,        // adj <- safe(adj, 1 - t0)
+    B_SCALE2_T,          // adj <- safe(safe(adj, t0), tape[idx])   (two chained unary nodes)
     B_COUNT
 };
 
