@@ -78,6 +78,7 @@ struct Ctx {
     std::vector<int32_t> n_nodes, n_ops;
     int prep_prec = -1;     // arithmetic type of the loaded problem (CO_PREC_FP32 / _FP64)
     bool fast = false;      // fp32 launches use the fast-math instantiations (CO_PREC_FP32_FAST)
+    int wide_mode = -1;     // block width per bin: -1 by occupancy, 0 narrow, 1 wide
     // the inputs resident in xs / ym (for CoOptions.keep_inputs)
     bool in_valid = false, in_shared = false;
     int in_N = -1, in_nvars = -1;
@@ -224,29 +225,54 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         p.jac = jac;
         p.jac_kmax = jac_kmax;
         const int kc = grad ? bin.kc : 4;
-        // tape in shared memory unless that leaves room for fewer than two resident blocks
-        bool tg = false;
-        size_t smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, true);
+        // Block width: the narrow (EVAL_NT) or the wide (EVAL_NT_WIDE) instantiation, whichever
+        // keeps more warps resident (registers and shared memory both counted); a bin whose
+        // items do not fill the narrow slots takes the wide blocks, which finish an item in
+        // about half the time.
+        struct Shape { bool tg; size_t smem; int occ; };
+        auto shape = [&](bool w) -> Shape {
+            Shape sh{false, Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, true, w), 0};
 #ifdef CUSR_FORCE_GLOBAL_TAPE
-        if (grad) {
+            if (grad) {
 #else
-        if (grad && 2 * (smem + 1024) > (size_t)ctx->smem_optin) {
+            // tape in shared memory unless that leaves room for fewer than two resident blocks
+            if (grad && 2 * (sh.smem + 1024) > (size_t)ctx->smem_optin) {
 #endif
-            tg = true;
-            smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, false);
+                sh.tg = true;
+                sh.smem = Launch<T>::smem(kc, p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, false, w);
+            }
+            sh.occ = sh.smem + 64 > (size_t)ctx->smem_optin
+                         ? 0 : Launch<T>::occ(kc, grad, sh.tg, ctx->fast, w, sh.smem);
+            return sh;
+        };
+        const Shape nrw = shape(false);
+        bool wide = false;
+        Shape sh = nrw;
+        if (grad && ctx->wide_mode != 0) {
+            const Shape wd = shape(true);
+            const int64_t warps_n = (int64_t)nrw.occ * EVAL_NT / 32, warps_w = (int64_t)wd.occ * EVAL_NT_WIDE / 32;
+            if (wd.occ > 0 &&
+                (ctx->wide_mode == 1 || warps_w >= warps_n ||
+                 bin.max_items < (int64_t)nrw.occ * ctx->sm_count)) {
+                wide = true;
+                sh = wd;
+            }
         }
-        if (smem + 64 > (size_t)ctx->smem_optin) return CO_ERR_BOUNDS;
-        int occ = Launch<T>::occ(kc, grad, tg, ctx->fast, smem);
+        if (sh.occ < 1 && sh.smem + 64 > (size_t)ctx->smem_optin) return CO_ERR_BOUNDS;
+        const int nt = wide ? EVAL_NT_WIDE : EVAL_NT;
+        const bool tg = sh.tg;
+        const size_t smem = sh.smem;
+        int occ = sh.occ;
         if (occ < 1) occ = 1;
         int64_t grid = (int64_t)occ * ctx->sm_count;
         if (grid > bin.max_items) grid = std::max<int64_t>(1, bin.max_items);
         p.tape_g = nullptr;
         if (tg) {
             // one global tape per stream: bins on different streams run concurrently
-            GROW(ctx->tape_gs[si], (size_t)grid * p.tape_cap * EVAL_THREADS * EVAL_V * sizeof(T));
+            GROW(ctx->tape_gs[si], (size_t)grid * p.tape_cap * nt * EVAL_V * sizeof(T));
             p.tape_g = ctx->tape_gs[si].ptr;
         }
-        CK(Launch<T>::eval(kc, grad, tg, ctx->fast, p, (int)grid, smem, ctx->bin_streams[si]));
+        CK(Launch<T>::eval(kc, grad, tg, ctx->fast, wide, p, (int)grid, smem, ctx->bin_streams[si]));
         ctx->stats.eval_launches++;
         ctx->stats.kernel_launches++;
     }
@@ -282,7 +308,7 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     }
     pp.y_shared = y_shared;
     st.y_shared = y_shared ? 1 : 0;
-    const int round = EVAL_THREADS * EVAL_V;
+    const int round = EVAL_ROUND;
     Schedule &sc = pp.sc;
     build_schedule(pp.pk, pr.metas, M, N, y_shared, fp64, round, ctx->sm_count * 3, &sc);
     st.n_bins = (int)sc.bins.size();
@@ -840,6 +866,8 @@ int co_init(int device_id, void **handle_out) {
             return CO_ERR_CUDA;
         }
     }
+    // CUSR_EVAL_WIDE=0 / 1 pins the evaluation block width (measurements); unset: per bin
+    if (const char *e = std::getenv("CUSR_EVAL_WIDE")) ctx->wide_mode = std::atoi(e) ? 1 : 0;
     ctx->smem_optin = optin;
     *handle_out = ctx;
     return CO_OK;

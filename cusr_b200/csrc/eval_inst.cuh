@@ -11,56 +11,68 @@
 namespace cusr {
 namespace {
 
-template <int KC, bool G, bool TG>
+template <int KC, bool G, bool TG, int NT = EVAL_NT>
 cudaError_t one(const EvalParams<CUSR_T> &p, int grid, size_t smem, cudaStream_t s) {
-    lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)><<<grid, EVAL_NT, smem, s>>>(p);
+    lm_eval_kernel<CUSR_T, EVAL_V, NT, KC, G, TG, (CUSR_FAST != 0)><<<grid, NT, smem, s>>>(p);
     return cudaGetLastError();
 }
-template <int KC, bool G, bool TG> int occ(size_t smem) {
+template <int KC, bool G, bool TG, int NT = EVAL_NT> int occ(size_t smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)>,
-                                                      EVAL_NT, smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, NT, KC, G, TG, (CUSR_FAST != 0)>,
+                                                      NT, smem) != cudaSuccess)
         return 0;
     return n;
 }
 // dynamic shared memory limit = the device's opt-in maximum minus the kernel's static part
-template <int KC, bool G, bool TG> cudaError_t prep() {
+template <int KC, bool G, bool TG, int NT = EVAL_NT> cudaError_t prep() {
     int dev = 0, optin = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess)
         e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa;
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_eval_kernel<CUSR_T, EVAL_V, NT, KC, G, TG, (CUSR_FAST != 0)>);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(lm_eval_kernel<CUSR_T, EVAL_V, EVAL_NT, KC, G, TG, (CUSR_FAST != 0)>,
+    return cudaFuncSetAttribute(lm_eval_kernel<CUSR_T, EVAL_V, NT, KC, G, TG, (CUSR_FAST != 0)>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 optin - (int)fa.sharedSizeBytes);
 }
 }  // namespace
 
-cudaError_t CUSR_FN(eval_launch)(int kc, bool grad, bool tg, const EvalParams<CUSR_T> &p, int grid,
-                                 size_t smem, cudaStream_t s) {
+cudaError_t CUSR_FN(eval_launch)(int kc, bool grad, bool tg, bool wide, const EvalParams<CUSR_T> &p,
+                                 int grid, size_t smem, cudaStream_t s) {
     if (!grad) return one<4, false, false>(p, grid, smem, s);
-#define X(KC) \
-    if (kc == KC) return tg ? one<KC, true, true>(p, grid, smem, s) : one<KC, true, false>(p, grid, smem, s);
+#define X(KC)                                                                                  \
+    if (kc == KC) {                                                                            \
+        if (wide) return tg ? one<KC, true, true, EVAL_NT_WIDE>(p, grid, smem, s)              \
+                            : one<KC, true, false, EVAL_NT_WIDE>(p, grid, smem, s);            \
+        return tg ? one<KC, true, true>(p, grid, smem, s) : one<KC, true, false>(p, grid, smem, s); \
+    }
     CUSR_KCS(X)
 #undef X
     return cudaErrorInvalidValue;
 }
 
 size_t CUSR_FN(eval_smem)(int kc, int code_cap, int n_vars, int spill_cap, int tape_cap,
-                          bool tape_in_smem) {
-#define X(KC) \
-    if (kc == KC) return EvalSmem<CUSR_T, EVAL_V, EVAL_NT, KC>(code_cap, n_vars, spill_cap, tape_cap, tape_in_smem).total;
+                          bool tape_in_smem, bool wide) {
+#define X(KC)                                                                                     \
+    if (kc == KC)                                                                                 \
+        return wide ? EvalSmem<CUSR_T, EVAL_V, EVAL_NT_WIDE, KC>(code_cap, n_vars, spill_cap,     \
+                                                                 tape_cap, tape_in_smem).total    \
+                    : EvalSmem<CUSR_T, EVAL_V, EVAL_NT, KC>(code_cap, n_vars, spill_cap, tape_cap, \
+                                                            tape_in_smem).total;
     CUSR_KCS(X)
 #undef X
     return 0;
 }
 
-int CUSR_FN(eval_blocks_per_sm)(int kc, bool grad, bool tg, size_t smem) {
+int CUSR_FN(eval_blocks_per_sm)(int kc, bool grad, bool tg, bool wide, size_t smem) {
     if (!grad) return occ<4, false, false>(smem);
-#define X(KC) \
-    if (kc == KC) return tg ? occ<KC, true, true>(smem) : occ<KC, true, false>(smem);
+#define X(KC)                                                                        \
+    if (kc == KC) {                                                                  \
+        if (wide) return tg ? occ<KC, true, true, EVAL_NT_WIDE>(smem)                \
+                            : occ<KC, true, false, EVAL_NT_WIDE>(smem);              \
+        return tg ? occ<KC, true, true>(smem) : occ<KC, true, false>(smem);          \
+    }
     CUSR_KCS(X)
 #undef X
     return 0;
@@ -69,9 +81,11 @@ int CUSR_FN(eval_blocks_per_sm)(int kc, bool grad, bool tg, size_t smem) {
 cudaError_t CUSR_FN(eval_prepare)() {
     cudaError_t e = prep<4, false, false>();
     if (e != cudaSuccess) return e;
-#define X(KC)                                                      \
-    if ((e = prep<KC, true, false>()) != cudaSuccess) return e;     \
-    if ((e = prep<KC, true, true>()) != cudaSuccess) return e;
+#define X(KC)                                                                       \
+    if ((e = prep<KC, true, false>()) != cudaSuccess) return e;                      \
+    if ((e = prep<KC, true, true>()) != cudaSuccess) return e;                       \
+    if ((e = prep<KC, true, false, EVAL_NT_WIDE>()) != cudaSuccess) return e;        \
+    if ((e = prep<KC, true, true, EVAL_NT_WIDE>()) != cudaSuccess) return e;
     CUSR_KCS(X)
 #undef X
     return cudaSuccess;

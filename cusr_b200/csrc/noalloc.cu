@@ -108,7 +108,7 @@ int evaluate_noalloc(int dev, const PopHeader *h, const int32_t *nt, const float
     PackResult pk;
     rc = compile_population(h, nt, nv, ci, metas, &pk);
     if (rc != CO_OK) return rc;
-    const int round = EVAL_THREADS * EVAL_V;
+    const int round = EVAL_ROUND;
     Schedule sc;
     build_schedule(pk, metas, M, N, /*y_shared=*/true, /*fp64=*/false, round, ds->sm_count * 3,
                    &sc);
@@ -146,9 +146,9 @@ int evaluate_noalloc(int dev, const PopHeader *h, const int32_t *nt, const float
     for (int b = 0; b < n_bins; ++b) {
         const Bin &bin = sc.bins[(size_t)b];
         smem[(size_t)b] = eval_smem_f32(bin.kc, bin.max_instr, n_vars, std::max(bin.max_spill, 1),
-                                       std::max(bin.max_tape, 1), true);
+                                       std::max(bin.max_tape, 1), true, false);
         if (2 * (smem[(size_t)b] + 1024) > (size_t)ds->smem_optin) return CO_ERR_BOUNDS;
-        int occ = std::max(1, eval_blocks_per_sm_f32(bin.kc, true, false, smem[(size_t)b]));
+        int occ = std::max(1, eval_blocks_per_sm_f32(bin.kc, true, false, false, smem[(size_t)b]));
         grid[(size_t)b] = (int)std::min<int64_t>((int64_t)occ * ds->sm_count,
                                                  std::max<int64_t>(1, bin.max_items));
     }
@@ -208,7 +208,7 @@ int evaluate_noalloc(int dev, const PopHeader *h, const int32_t *nt, const float
         p.vals = nullptr;
         p.jac = nullptr;
         p.jac_kmax = 0;
-        NA_CK(eval_launch_f32(bin.kc, true, false, p, grid[(size_t)b], smem[(size_t)b], stream));
+        NA_CK(eval_launch_f32(bin.kc, true, false, false, p, grid[(size_t)b], smem[(size_t)b], stream));
     }
     na_sum_blocks<<<std::max(1, std::min(4 * ds->sm_count, (M + 255) / 256)), 256, 0, stream>>>(
         dDesc, M, dPart, blocks_dev);

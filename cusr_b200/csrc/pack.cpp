@@ -492,7 +492,8 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
     const int64_t rounds_per_tree = (N + round - 1) / round;
     const int64_t total_rounds = rounds_per_tree * (int64_t)M;
     int64_t per_item = total_rounds / std::max<int64_t>(1, 8 * (int64_t)resident);
-    per_item = std::min<int64_t>(16, std::max<int64_t>(1, per_item));
+    // at most 4,096 samples per item
+    per_item = std::min<int64_t>(std::max(1, 4096 / round), std::max<int64_t>(1, per_item));
     out->chunk = (int32_t)(per_item * round);
     const int n_chunks = (int)((N + out->chunk - 1) / out->chunk);
     const int64_t ldy = ((int64_t)N + round - 1) / round * round;
