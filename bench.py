@@ -427,11 +427,11 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
 
 
 def run_profile_case(args) -> None:
-    """Small case of the same kernel for ncu captures: 2,048 trees of the metric
-    configuration (same N, same tree distribution), a few LM iterations."""
+    """Small case of the same kernel for ncu captures: --profile-trees trees (default 8,192)
+    of the metric configuration (same N, same tree distribution), a few LM iterations."""
     from cusr_b200 import InProcessCO, synth
 
-    pop = synth.make_config(CONFIG, M=2048, seed=0)
+    pop = synth.make_config(CONFIG, M=args.profile_trees, seed=0)
     metas = np.asarray(pop["metas"])
     K = metas[:, 3]
     bins = {}
@@ -459,8 +459,9 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", action="store_true",
-                    help="run the small ncu case (2,048 trees) instead of the benchmark")
+                    help="run the small ncu case (--profile-trees trees) instead of the benchmark")
     ap.add_argument("--profile-iters", type=int, default=2)
+    ap.add_argument("--profile-trees", type=int, default=8192)
     ap.add_argument("--config", default=None,
                     help="bench one BASELINE configuration instead of the headline metric: "
                          "pr1, mid, physics, long, scale, sharded")
