@@ -151,12 +151,13 @@ def pinned_copy(pop: dict) -> dict:
     return out
 
 
-def traffic_from_profile():
-    """DRAM bytes per launch of the evaluation kernel from the committed ncu summary."""
+def profile_value(key: str):
+    """A number recorded in the committed ncu summary of the evaluation kernel
+    (profiles/lm_eval_kernel_metric.md, lines `key: value`)."""
     if not PROFILE_SUMMARY.exists():
         return None
     for line in PROFILE_SUMMARY.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        if line.strip().startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
@@ -305,7 +306,12 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
         "frac": (achieved / fp32_peak) if achieved and fp32_peak else None,
         "peak_source": "measured FP32 FMA probe (co_probe_peak, same run); MEASURED_PEAKS.json "
                        "holds only HBM and bf16 tensor peaks",
-        "traffic": traffic_from_profile(),
+        "traffic": profile_value("traffic_bytes_per_launch"),
+        "traffic_note": "dram read+write bytes of one evaluation launch (ncu, committed "
+                        "profile summary); inputs and partial sums are L2-resident",
+        "issue": {"bound": "issue", "achieved_pct": profile_value("issue_active_pct"),
+                  "note": "issue slots busy on the evaluation kernel (ncu): the interpreter is "
+                          "bound by instruction issue latency, not FMA or HBM throughput"},
         "avg_launch_ms": avg_launch_ms,
         "flops_def": "per evaluated (tree, sample): 2 per operator node (value + adjoint) + "
                      "2 per normal-equation entry (K+1)(K+2)/2",
