@@ -141,6 +141,9 @@ SIGNATURES = {
     "co_evaluate": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
                      ctypes.POINTER(TreeMeta), _F64, _F32, _F32, ctypes.c_int, ctypes.c_int,
                      _F64, _F64, _F64], ctypes.c_int),
+    "co_jacobian_fd": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
+                        ctypes.POINTER(TreeMeta), _F64, _F32, _F32, ctypes.c_int, ctypes.c_int,
+                        ctypes.c_double, _F64], ctypes.c_int),
     "co_shard_unique_id": ([ctypes.POINTER(ctypes.c_ubyte)], ctypes.c_int),
     "co_shard_init": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte), ctypes.c_int,
                        ctypes.c_int, ctypes.c_double], ctypes.c_int),
@@ -440,6 +443,27 @@ class InProcessCO:
                 o += n
             out["blocks"] = parts
         return out
+
+    def jacobian_fd(self, pop: dict, c=None, precision: str = "fp32", eps: float = 0.0):
+        """Finite-difference Jacobian [M, K_max, N] on the device (co_jacobian_fd; the
+        reference FD variant's forward difference, eps <= 0: 1e-3 fp32 / 1e-7 fp64)."""
+        if self._torn:
+            raise RuntimeError("InProcessCO used after teardown()")
+        M, N, K_max = int(pop["M"]), int(pop["N"]), int(pop["K_max"])
+        y_shared = np.asarray(pop["ym"]).ndim == 1
+        hdr = build_header(pop)
+        args, keep = self._inputs(pop, y_shared=y_shared)
+        nt_p, nv_p, ci_p, metas_buf, _c0, xs_p, ym_p = args
+        c = np.ascontiguousarray(pop["c_init"] if c is None else c, np.float64)
+        jac = np.zeros((M, max(K_max, 1), N), np.float64)
+        rc = self._lib.co_jacobian_fd(
+            self._handle, ctypes.byref(hdr), nt_p, nv_p, ci_p, metas_buf,
+            c.ctypes.data_as(_F64), xs_p, ym_p, prec_code(precision), 1 if y_shared else 0,
+            float(eps), jac.ctypes.data_as(_F64))
+        del keep
+        if rc != CO_OK:
+            raise COError(rc, "co_jacobian_fd")
+        return jac
 
     def probe_peak(self) -> tuple[float, float]:
         """Measured (fp32, fp64) FMA peak of the device in TFLOP/s."""

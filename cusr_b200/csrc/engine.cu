@@ -777,6 +777,58 @@ int run_eval(Ctx *ctx, const Problem &pr, bool y_shared, const double *c, double
     return CO_OK;
 }
 
+// Finite-difference Jacobian of every tree at constants c: one value pass at c and one per
+// constant column with that column stepped (fd_perturb_kernel), J in the reference d_J
+// layout [M][K_max][N]. An independent on-device check of the reverse-mode Jacobian.
+template <typename T>
+int run_jac_fd(Ctx *ctx, const Problem &pr, bool y_shared, const double *c, double eps,
+               double *jac_out) {
+    const PopHeader *h = pr.h;
+    const int M = h->M_prob, N = h->N;
+    const int64_t total_c = h->total_c;
+    ctx->stats = CoStats{};
+    ctx->stats.precision = sizeof(T) == 8 ? CO_PREC_FP64 : CO_PREC_FP32;
+    Prep pp;
+    ctx->loaded = false;
+    int rc = prepare<T>(ctx, pr, y_shared, pp);
+    if (rc != CO_OK) return rc;
+    if (M == 0) return CO_OK;
+    if (pp.pk.max_K > h->K_max) return CO_ERR_NULLARG;
+    cudaStream_t s = ctx->stream;
+    const int kmax = std::max(h->K_max, 1);
+    GROW(ctx->c64, total_c * sizeof(double));
+    GROW(ctx->vals, 2 * (size_t)M * N * sizeof(T));
+    GROW(ctx->jac, (size_t)M * kmax * N * sizeof(T));
+    if (total_c > 0)
+        CK(cudaMemcpyAsync(ctx->c64.ptr, c, total_c * sizeof(double), cudaMemcpyHostToDevice, s));
+    load_point_kernel<T><<<grid_for(ctx, std::max<int64_t>(total_c, M)), 256, 0, s>>>(
+        P<double>(ctx->c64), total_c, P<T>(ctx->ctry), M, P<int32_t>(ctx->pending));
+    CK(cudaGetLastError());
+    T *v0 = P<T>(ctx->vals), *vk = v0 + (size_t)M * N, *dj = P<T>(ctx->jac);
+    CK(cudaMemsetAsync(dj, 0, (size_t)M * kmax * N * sizeof(T), s));
+    rc = launch_pass<T>(ctx, pp.sc, pp.pk, P<T>(ctx->ctry), P<T>(ctx->partials), *pr.h, pp.ldx,
+                        false, v0);
+    if (rc) return rc;
+    const int g = grid_for(ctx, (int64_t)M * N);
+    for (int k = 0; k < pp.pk.max_K; ++k) {
+        fd_perturb_kernel<T><<<grid_for(ctx, M), 256, 0, s>>>(
+            P<TreeDesc>(ctx->desc), M, P<T>(ctx->ctry), k, (T)eps, P<T>(ctx->c), P<T>(ctx->lam),
+            P<int32_t>(ctx->pending));
+        CK(cudaGetLastError());
+        rc = launch_pass<T>(ctx, pp.sc, pp.pk, P<T>(ctx->c), P<T>(ctx->partials), *pr.h, pp.ldx,
+                            false, vk);
+        if (rc) return rc;
+        fd_column_kernel<T><<<g, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, N, k, kmax, vk, v0,
+                                               P<T>(ctx->lam), dj);
+        CK(cudaGetLastError());
+    }
+    std::vector<T> hj((size_t)M * kmax * N);
+    CK(cudaMemcpyAsync(hj.data(), dj, hj.size() * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    for (size_t i = 0; i < hj.size(); ++i) jac_out[i] = (double)hj[i];
+    return CO_OK;
+}
+
 }  // namespace
 }  // namespace cusr
 
@@ -950,6 +1002,26 @@ int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float
     if (precision == CO_PREC_FP64)
         return run_eval<double>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
     return run_eval<float>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
+}
+
+int co_jacobian_fd(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
+                   const int32_t *ci, const TreeMeta *metas, const double *c, const float *xs,
+                   const float *ym, int precision, int y_shared, double eps, double *jac_out) {
+    if (!handle || !h || !nt || !nv || !ci || !metas || !c || !xs || !ym || !jac_out)
+        return CO_ERR_NULLARG;
+    if (!valid_prec(precision)) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    Problem pr{h, nt, nv, ci, metas, nullptr, xs, ym};
+    int rc = check_args(pr);
+    if (rc != CO_OK) return rc;
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    std::vector<float> c_f((size_t)std::max(h->total_c, 0));
+    for (size_t i = 0; i < c_f.size(); ++i) c_f[i] = (float)c[i];
+    pr.c_init = c_f.data();
+    ctx->fast = precision == CO_PREC_FP32_FAST;
+    if (precision == CO_PREC_FP64)
+        return run_jac_fd<double>(ctx, pr, y_shared != 0, c, eps > 0 ? eps : 1e-7, jac_out);
+    return run_jac_fd<float>(ctx, pr, y_shared != 0, c, eps > 0 ? eps : 1e-3, jac_out);
 }
 
 int co_load(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,

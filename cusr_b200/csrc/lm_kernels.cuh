@@ -288,6 +288,45 @@ __global__ void load_point_kernel(const double *__restrict__ c64, int64_t total_
         pending[m] = 1;
 }
 
+// Finite-difference Jacobian, column k (the reference FD variant, batch_lm_ad.cu:95-132):
+// every tree with K > k gets c_k + h with h = eps * |c_k| (eps when c_k == 0), the step taken
+// as the representable difference (c_k + h) - c_k (eps again if that is 0); the other
+// constants stay. Trees with K <= k are not evaluated (pending = 0).
+template <typename T>
+__global__ void fd_perturb_kernel(const TreeDesc *desc, int M, const T *c, int k, T eps,
+                                  T *c_out, T *h_out, int32_t *pending) {
+    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+        const TreeDesc d = desc[m];
+        for (int t = 0; t < d.K; ++t) c_out[d.c_off + t] = c[d.c_off + t];
+        T h = T(0);
+        if (k < d.K) {
+            const T saved = c[d.c_off + k];
+            h = eps * (saved < T(0) ? -saved : saved);
+            if (h == T(0)) h = eps;
+            const T cp = saved + h;
+            h = cp - saved;
+            if (h == T(0)) h = eps;
+            c_out[d.c_off + k] = cp;
+        }
+        h_out[m] = h;
+        pending[m] = k < d.K ? 1 : 0;
+    }
+}
+
+// J[m][k][i] = (f_k(x_i) - f(x_i)) / h_m for the trees with K > k (IEEE division).
+template <typename T>
+__global__ void fd_column_kernel(const TreeDesc *desc, int M, int N, int k, int kmax,
+                                 const T *vals_k, const T *vals_0, const T *h, T *jac) {
+    const int64_t total = (int64_t)M * N;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int m = (int)(e / N);
+        if (k >= desc[m].K) continue;
+        const int64_t i = e - (int64_t)m * N;
+        jac[((int64_t)m * kmax + k) * N + i] = (vals_k[e] - vals_0[e]) / h[m];
+    }
+}
+
 // Sample-sharded mode: per-tree sums of this rank's chunk partials, in chunk order (raw sums,
 // the all-reduce input).
 template <typename T>

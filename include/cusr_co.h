@@ -218,6 +218,18 @@ int  co_optimize_sharded(void *handle, const PopHeader *header,
                          double *loss_init_out, double *loss_final_out,
                          int32_t *iters_out);
 
+/* Finite-difference Jacobian (the reference FD variant's forward difference,
+ * batch_lm_ad.cu:95-132): for each constant column k, h = eps*|c_k| (eps when c_k == 0),
+ * taken as the representable step (c_k + h) - c_k, and J[m][k][i] = (f(c + h e_k; x_i) -
+ * f(c; x_i)) / h, evaluated on the device by value passes of the same interpreter. jac_out is
+ * [M_prob][K_max][N] fp64 (rows k >= K are 0). eps <= 0 selects 1e-3 (fp32, the reference's
+ * eps_rel) or 1e-7 (fp64). An independent check of the reverse-mode Jacobian. */
+int  co_jacobian_fd(void *handle, const PopHeader *header,
+                    const int32_t *nt, const float *nv, const int32_t *ci,
+                    const TreeMeta *metas, const double *c,
+                    const float *xs, const float *ym, int precision, int y_shared,
+                    double eps, double *jac_out);
+
 /* Statistics of the last co_optimize* / co_fit_loaded call on `handle`. */
 int  co_get_stats(void *handle, CoStats *out);
 

@@ -314,3 +314,37 @@ def test_unknown_operator_is_zero(co):
     out = co.evaluate(pop, precision="fp64", values=True, jacobian=True)
     np.testing.assert_array_equal(out["values"][0], [0.0, 0.0])
     np.testing.assert_array_equal(out["jacobian"][0, 0], [0.0, 0.0])
+
+
+def _fd_check(co, pop, precision, eps, rtol, min_frac):
+    """The on-device finite-difference Jacobian (co_jacobian_fd) against the reverse-mode one
+    (co_evaluate): two independent derivative paths of the same interpreter agree to the FD
+    truncation error on well-scaled samples."""
+    jr = co.evaluate(pop, precision=precision, values=False, jacobian=True)["jacobian"]
+    jf = co.jacobian_fd(pop, precision=precision, eps=eps)
+    Ks = np.asarray(pop["metas"])[:, 3]
+    ok = tot = 0
+    for m in range(int(pop["M"])):
+        K = int(Ks[m])
+        if K == 0:
+            assert not np.any(jf[m])
+            continue
+        a, b = jf[m, :K], jr[m, :K]
+        fin = np.isfinite(a) & np.isfinite(b)
+        scale = np.maximum(np.abs(b), np.abs(b[fin]).max(initial=0) * 1e-3 + 1e-12)
+        with np.errstate(all="ignore"):
+            good = np.abs(a - b) <= rtol * scale
+        ok += int(np.sum(good & fin))
+        tot += int(fin.sum())
+        assert not np.any(jf[m, K:]), m      # rows k >= K are never written
+    assert ok / max(tot, 1) >= min_frac, ok / max(tot, 1)
+
+
+def test_fd_jacobian_fp64_matches_reverse(co):
+    _fd_check(co, synth.make_config("pr1", M=64, N=200, seed=3), "fp64", 1e-7, 1e-5, 0.97)
+
+
+def test_fd_jacobian_fp32_reference_step(co):
+    """fp32 with the reference's eps_rel = 1e-3 (batch_lm.cu:207): first-order truncation, so
+    a loose tolerance; the point is the same column layout and step rule."""
+    _fd_check(co, synth.make_config("pr1", M=64, N=200, seed=4), "fp32", 0.0, 2e-2, 0.9)
