@@ -266,6 +266,31 @@ def error_scale(nt, nv, ci, xs, c) -> np.ndarray:
     return S
 
 
+def fd_jacobian(nt, nv, ci, xs, c, eps: float, dtype=np.float64) -> np.ndarray:
+    """Forward-difference Jacobian (N, K) of the reference FD variant
+    (cusr/kernel/batch_lm_ad.cu:95-132): h = eps*|c_k| (eps when c_k == 0), taken as the
+    representable step (c_k + h) - c_k (eps again if that is 0), J[:, k] = (f(c + h e_k) -
+    f(c)) / h, all in `dtype`."""
+    c = np.asarray(c, dtype).ravel()
+    T = np.dtype(dtype).type
+    f0 = eval_tree_arrays(nt, nv, ci, xs, c, dtype=dtype)
+    J = np.zeros((f0.shape[0], c.size), dtype)
+    with np.errstate(all="ignore"):
+        for k in range(c.size):
+            saved = c[k]
+            h = T(eps) * abs(saved)
+            if h == 0:
+                h = T(eps)
+            cp = saved + h
+            h = cp - saved
+            if h == 0:
+                h = T(eps)
+            ck = c.copy()
+            ck[k] = cp
+            J[:, k] = (eval_tree_arrays(nt, nv, ci, xs, ck, dtype=dtype) - f0) / h
+    return J
+
+
 FAST_MATH_UNIT = 2.0 ** -21.41
 
 

@@ -344,6 +344,33 @@ def test_fd_jacobian_fp64_matches_reverse(co):
     _fd_check(co, synth.make_config("pr1", M=64, N=200, seed=3), "fp64", 1e-7, 1e-5, 0.97)
 
 
+def test_fd_jacobian_fp64_matches_oracle_fd(co):
+    """Same formula on the CPU (oracle.interp.fd_jacobian): the device FD columns agree to the
+    conditioning of the difference quotient (an error e in f becomes 2e/h in J)."""
+    pop = synth.make_config("pr1", M=48, N=150, seed=5)
+    jf = co.jacobian_fd(pop, precision="fp64", eps=1e-6)
+    strict = total = 0
+    for m in range(int(pop["M"])):
+        nt, nv, ci, _y, K = interp.tree_view(pop, m)
+        if K == 0:
+            continue
+        off = int(pop["metas"][m][2])
+        c = np.asarray(pop["c_init"][off:off + K], np.float64)
+        ref = interp.fd_jacobian(nt, nv, ci, pop["xs"], c, 1e-6)
+        S = interp.error_scale(nt, nv, ci, pop["xs"], c)
+        h = np.maximum(np.abs(c) * 1e-6, 1e-300)
+        for k in range(K):
+            got = jf[m, k]
+            tol = 1e-6 * np.abs(ref[:, k]) + 64 * U64 * 2 * (S + 1e-300) / h[k]
+            both = np.isfinite(got) & np.isfinite(ref[:, k])
+            with np.errstate(all="ignore"):
+                ok = np.abs(got - ref[:, k]) <= tol
+            assert np.all(ok[both]), (m, k)
+            strict += int(np.sum(np.abs(got - ref[:, k])[both] <= 1e-6 * np.abs(ref[both, k]) + 1e-300))
+            total += int(both.sum())
+    assert strict / max(total, 1) >= 0.9
+
+
 def test_fd_jacobian_fp32_reference_step(co):
     """fp32 with the reference's eps_rel = 1e-3 (batch_lm.cu:207): first-order truncation, so
     a loose tolerance; the point is the same column layout and step rule."""
