@@ -40,6 +40,9 @@ CO_PREC_FP32_FAST = 2
 PRECISIONS = {"fp32": CO_PREC_FP32, "fp64": CO_PREC_FP64, "fp32_fast": CO_PREC_FP32_FAST}
 
 
+AD_MODES = {"auto": 0, "forward": 1, "reverse": 2}
+
+
 def prec_code(precision: str) -> int:
     try:
         return PRECISIONS[precision]
@@ -89,7 +92,7 @@ class CoOptions(ctypes.Structure):
         ("lambda0", ctypes.c_double), ("xtol", ctypes.c_double),
         ("fp64_audit", ctypes.c_int32), ("early_exit", ctypes.c_int32),
         ("sample_sharded", ctypes.c_int32), ("keep_inputs", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 6),
+        ("ad_mode", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5),
     ]
 
 
@@ -290,14 +293,16 @@ class InProcessCO:
 
     def optimize_ex(self, pop: dict, max_iter: int = 50, precision: str = "fp32",
                     y_shared: bool | None = None, lambda0: float = 1e-3, xtol: float = 1e-6,
-                    fp64_audit: int = -1, early_exit: bool = True, keep_inputs: bool = False):
+                    fp64_audit: int = -1, early_exit: bool = True, keep_inputs: bool = False,
+                    ad_mode: str = "auto"):
         """Extended fit: precision 'fp32' | 'fp64' | 'fp32_fast'; y_shared=True passes one
         target row (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a
         1-D ym). keep_inputs=True reuses the X / shared y left on the device by the previous
         call (pop needs no 'xs' / 'ym' then): the in-loop case of new trees on fixed data.
+        ad_mode 'auto' | 'forward' (tangents for K <= 2) | 'reverse'.
         Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters."""
         return self._fit_ex("co_optimize_ex", pop, max_iter, precision, y_shared, lambda0,
-                            xtol, fp64_audit, early_exit, keep_inputs)
+                            xtol, fp64_audit, early_exit, keep_inputs, ad_mode)
 
     def shard_init(self, unique_id: bytes, nranks: int, rank: int,
                    timeout_s: float = 120.0) -> None:
@@ -322,7 +327,7 @@ class InProcessCO:
                             xtol, fp64_audit, early_exit, keep_inputs)
 
     def _fit_ex(self, entry, pop, max_iter, precision, y_shared, lambda0, xtol, fp64_audit,
-                early_exit, keep_inputs=False):
+                early_exit, keep_inputs=False, ad_mode="auto"):
         if self._torn:
             raise RuntimeError("InProcessCO used after teardown()")
         M, total_c = int(pop["M"]), int(pop["total_c"])
@@ -332,7 +337,8 @@ class InProcessCO:
             y_shared = np.asarray(pop["ym"]).ndim == 1
         hdr = build_header(pop)
         args, keep = self._inputs(pop, y_shared=bool(y_shared), keep_inputs=keep_inputs)
-        opt = self._options(max_iter, precision, y_shared, lambda0, xtol, fp64_audit, early_exit)
+        opt = self._options(max_iter, precision, y_shared, lambda0, xtol, fp64_audit, early_exit,
+                            ad_mode)
         opt.keep_inputs = 1 if keep_inputs else 0
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
@@ -351,9 +357,10 @@ class InProcessCO:
                 "loss_final": loss_final, "iters": iters}
 
     def _options(self, max_iter=50, precision="fp32", y_shared=False, lambda0=1e-3, xtol=1e-6,
-                 fp64_audit=-1, early_exit=True) -> CoOptions:
+                 fp64_audit=-1, early_exit=True, ad_mode="auto") -> CoOptions:
         opt = CoOptions()
         self._lib.co_default_options(ctypes.byref(opt))
+        opt.ad_mode = AD_MODES[ad_mode]
         opt.precision = prec_code(precision)
         opt.max_iter = int(max_iter)
         opt.y_shared = 1 if y_shared else 0
@@ -363,13 +370,15 @@ class InProcessCO:
         opt.early_exit = 1 if early_exit else 0
         return opt
 
-    def load(self, pop: dict, precision: str = "fp32", y_shared: bool | None = None) -> None:
-        """Upload a population once (co_load); fit it with fit_loaded() any number of times."""
+    def load(self, pop: dict, precision: str = "fp32", y_shared: bool | None = None,
+             ad_mode: str = "auto") -> None:
+        """Upload a population once (co_load); fit it with fit_loaded() any number of times.
+        ad_mode fixes the Jacobian mode of the loaded schedule."""
         if y_shared is None:
             y_shared = np.asarray(pop["ym"]).ndim == 1
         hdr = build_header(pop)
         args, keep = self._inputs(pop, y_shared=bool(y_shared))
-        opt = self._options(precision=precision, y_shared=y_shared)
+        opt = self._options(precision=precision, y_shared=y_shared, ad_mode=ad_mode)
         rc = self._lib.co_load(self._handle, ctypes.byref(hdr), *args, ctypes.byref(opt))
         del keep
         if rc != CO_OK:

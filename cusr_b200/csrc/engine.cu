@@ -79,6 +79,8 @@ struct Ctx {
     int prep_prec = -1;     // arithmetic type of the loaded problem (CO_PREC_FP32 / _FP64)
     bool fast = false;      // fp32 launches use the fast-math instantiations (CO_PREC_FP32_FAST)
     int wide_mode = -1;     // block width per bin: -1 by occupancy, 0 narrow, 1 wide
+    int fwd_max = 0;        // trees with K <= fwd_max use the forward-mode classes
+    int fwd_default = 0;    // fwd_max of CO_AD_AUTO
     // the inputs resident in xs / ym (for CoOptions.keep_inputs)
     bool in_valid = false, in_shared = false;
     int in_N = -1, in_nvars = -1;
@@ -310,7 +312,8 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     st.y_shared = y_shared ? 1 : 0;
     const int round = EVAL_ROUND;
     Schedule &sc = pp.sc;
-    build_schedule(pp.pk, pr.metas, M, N, y_shared, fp64, round, ctx->sm_count * 3, &sc);
+    build_schedule(pp.pk, pr.metas, M, N, y_shared, fp64, round, ctx->sm_count * 3, &sc,
+                   ctx->fwd_max);
     st.n_bins = (int)sc.bins.size();
     pp.ldx = ((int64_t)N + round - 1) / round * round;
     pp.y_rows = y_shared ? 1 : M;
@@ -920,9 +923,17 @@ int co_init(int device_id, void **handle_out) {
     }
     // CUSR_EVAL_WIDE=0 / 1 pins the evaluation block width (measurements); unset: per bin
     if (const char *e = std::getenv("CUSR_EVAL_WIDE")) ctx->wide_mode = std::atoi(e) ? 1 : 0;
+    // CUSR_EVAL_FWD=k (0..2): trees with K <= k use forward-mode tangents (measurements)
+    if (const char *e = std::getenv("CUSR_EVAL_FWD"))
+        ctx->fwd_default = ctx->fwd_max = std::min(2, std::max(0, std::atoi(e)));
     ctx->smem_optin = optin;
     *handle_out = ctx;
     return CO_OK;
+}
+
+// Jacobian mode of the next schedule built on this context (CoOptions.ad_mode).
+static void set_ad_mode(Ctx *ctx, int ad_mode) {
+    ctx->fwd_max = ad_mode == CO_AD_FORWARD ? 2 : (ad_mode == CO_AD_REVERSE ? 0 : ctx->fwd_default);
 }
 
 static bool valid_prec(int p) {
@@ -940,6 +951,7 @@ static int optimize_common(void *handle, const PopHeader *h, const int32_t *nt, 
     if (rc != CO_OK) return rc;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
     ctx->fast = opt.precision == CO_PREC_FP32_FAST;
+    set_ad_mode(ctx, opt.ad_mode);
     if (opt.precision == CO_PREC_FP64) return run_fit<double>(ctx, pr, opt, out);
     return run_fit<float>(ctx, pr, opt, out);
 }
@@ -999,6 +1011,7 @@ int co_evaluate(void *handle, const PopHeader *h, const int32_t *nt, const float
     for (size_t i = 0; i < c_f.size(); ++i) c_f[i] = (float)c[i];
     pr.c_init = c_f.data();
     ctx->fast = precision == CO_PREC_FP32_FAST;
+    set_ad_mode(ctx, CO_AD_AUTO);
     if (precision == CO_PREC_FP64)
         return run_eval<double>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
     return run_eval<float>(ctx, pr, y_shared != 0, c, vals_out, jac_out, blocks_out);
@@ -1038,6 +1051,7 @@ int co_load(void *handle, const PopHeader *h, const int32_t *nt, const float *nv
     int rc = check_args(pr);
     if (rc != CO_OK) return rc;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    set_ad_mode(ctx, opt.ad_mode);
     rc = opt.precision == CO_PREC_FP64 ? load<double>(ctx, pr, opt.y_shared != 0)
                                        : load<float>(ctx, pr, opt.y_shared != 0);
     if (rc == CO_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess) return CO_ERR_CUDA;

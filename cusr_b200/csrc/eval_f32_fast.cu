@@ -4,6 +4,6 @@
 // approximate forms and denormals are flushed to zero.
 #define CUSR_T float
 #define CUSR_FN(name) name##_f32_fast
-#define CUSR_KCS(X) X(4) X(8) X(12) X(16) X(32)
+#define CUSR_KCS(X) X(1) X(2) X(4) X(8) X(12) X(16) X(32)
 #define CUSR_FAST 1
 #include "eval_inst.cuh"

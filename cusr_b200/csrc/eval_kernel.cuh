@@ -63,11 +63,15 @@ struct EvalParams {
 __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
 // Shared-memory layout of one block; the host sizes the launch with the same function.
+// KC = 1, 2: forward-mode classes (tangents in registers, no tape, no gradient rows; a spill
+// slot holds the value and its KC tangents).
 template <typename T, int V, int NT, int KC>
 struct EvalSmem {
     static constexpr bool kBig = KC > 16;
+    static constexpr bool kFwd = KC <= 2;
     static constexpr int kGStride = NT * V + (kBig ? 1 : 0);   // gradient row stride (T)
-    static constexpr int kGRows = kBig ? KC + 1 : KC;         // + residual row
+    static constexpr int kGRows = kFwd ? 0 : (kBig ? KC + 1 : KC);   // + residual row
+    static constexpr int kSpillWords = kFwd ? 1 + KC : 1;     // VecT entries per spill slot
     size_t code, cval, x, spill, tape, grad, red, total;
     __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
                                  bool tape_in_smem = true) {
@@ -75,8 +79,8 @@ struct EvalSmem {
         code = o;  o += align16((size_t)(code_cap + 1) * 4);
         cval = o;  o += align16((size_t)CO_MAX_K * sizeof(T));
         x = o;     o += align16((size_t)n_vars * NT * V * 4);
-        spill = o; o += align16((size_t)spill_cap * NT * V * sizeof(T));
-        tape = o;  o += tape_in_smem ? align16((size_t)tape_cap * NT * V * sizeof(T)) : 0;
+        spill = o; o += align16((size_t)spill_cap * kSpillWords * NT * V * sizeof(T));
+        tape = o;  o += (tape_in_smem && !kFwd) ? align16((size_t)tape_cap * NT * V * sizeof(T)) : 0;
         grad = o;  o += align16((size_t)kGRows * kGStride * sizeof(T));
         red = o;   o += align16((size_t)(NT / 32) * nblock_size(KC) * sizeof(T));
         total = o;
@@ -207,6 +211,135 @@ __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code,
                 // every word was checked against this case set on the host
                 // (valid_forward_code / valid_reverse_code), so no bounds check is needed
                 __builtin_unreachable();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Forward-mode sweep (KC = KT <= 2): the same forward program; TOS carries its value and the
+// KT tangents d/dc_k. A VAR leaf has tangent 0, CONST leaf k the unit vector e_k; an operator
+// maps tangents by its local partials with the reverse sweep's zero-annihilating product
+// (t <- safe(d, t); a binary node adds the source operand's term). The result equals the
+// reverse sweep's product of partials along each root-to-leaf path, taken leaf to root.
+// ---------------------------------------------------------------------------------------
+template <typename T, int V, int NT, int KT>
+__device__ __forceinline__ void tan_push(VecT<T, V> *__restrict__ sp, uint32_t sd,
+                                         const T (&tos)[V], const T (&tt)[KT][V]) {
+    VecT<T, V> *s = sp + (int)sd * (1 + KT) * NT;
+    s[0] = pack<T, V>(tos);
+#pragma unroll
+    for (int k = 0; k < KT; ++k) s[(1 + k) * NT] = pack<T, V>(tt[k]);
+}
+
+template <typename T, int V, int NT, int KT, uint32_t OP, uint32_t MODE, bool SW>
+__device__ __forceinline__ void tan_bin(uint32_t w, const T *__restrict__ c_s,
+                                        const VecF<V> *__restrict__ xt,
+                                        const VecT<T, V> *__restrict__ sp, T (&tos)[V],
+                                        T (&tt)[KT][V]) {
+    T s[V];
+    T ts[KT][V];
+    if constexpr (MODE == M_VAR) {
+        const VecF<V> xv = xt[w_idx(w) * NT];
+        CUSR_FOR_V s[j] = (T)xv.v[j];
+    } else if constexpr (MODE == M_CONST) {
+        const T cv = c_s[w_idx(w)];
+        CUSR_FOR_V s[j] = cv;
+    } else {
+        const VecT<T, V> *q = sp + (int)w_sd(w) * (1 + KT) * NT;
+        const VecT<T, V> t = q[0];
+        CUSR_FOR_V s[j] = t.v[j];
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            const VecT<T, V> u = q[(1 + k) * NT];
+            CUSR_FOR_V ts[k][j] = u.v[j];
+        }
+    }
+    CUSR_FOR_V {
+        T o, da, db;
+        binary_op<T>(OP, SW ? s[j] : tos[j], SW ? tos[j] : s[j], o, da, db);
+        const T dt = SW ? db : da, ds = SW ? da : db;
+#pragma unroll
+        for (int k = 0; k < KT; ++k) {
+            T t = safe_mul(dt, tt[k][j]);
+            if constexpr (MODE == M_CONST) {
+                if ((uint32_t)k == w_idx(w)) t += ds;
+            } else if constexpr (MODE == M_POP) {
+                t += safe_mul(ds, ts[k][j]);
+            }
+            tt[k][j] = t;
+        }
+        tos[j] = o;
+    }
+}
+
+template <typename T, int V, int NT, int KT, uint32_t OP>
+__device__ __forceinline__ void tan_un(T (&tos)[V], T (&tt)[KT][V]) {
+    CUSR_FOR_V {
+        T r, d;
+        unary_op<T>(OP, tos[j], r, d);
+        tos[j] = r;
+#pragma unroll
+        for (int k = 0; k < KT; ++k) tt[k][j] = safe_mul(d, tt[k][j]);
+    }
+}
+
+template <typename T, int V, int NT, int KT>
+__device__ __forceinline__ void tangent_sweep(const uint32_t *__restrict__ code, int n,
+                                              const T *__restrict__ c_s,
+                                              const VecF<V> *__restrict__ xt,
+                                              VecT<T, V> *__restrict__ sp, T (&tos)[V],
+                                              T (&tt)[KT][V]) {
+    uint32_t wn = code[0];
+    for (int pc = 0; pc < n; ++pc) {
+        const uint32_t w = wn;
+        wn = code[pc + 1];
+        switch (w_code(w)) {
+            case XOP_PUSH_VAR:
+                tan_push<T, V, NT, KT>(sp, w_sd(w), tos, tt);
+                [[fallthrough]];
+            case XOP_LOAD_VAR: {
+                const VecF<V> xv = xt[w_idx(w) * NT];
+                CUSR_FOR_V {
+                    tos[j] = (T)xv.v[j];
+#pragma unroll
+                    for (int k = 0; k < KT; ++k) tt[k][j] = T(0);
+                }
+                break;
+            }
+            case XOP_PUSH_CONST:
+                tan_push<T, V, NT, KT>(sp, w_sd(w), tos, tt);
+                [[fallthrough]];
+            case XOP_LOAD_CONST: {
+                const uint32_t idx = w_idx(w);
+                const T cv = c_s[idx];
+                CUSR_FOR_V {
+                    tos[j] = cv;
+#pragma unroll
+                    for (int k = 0; k < KT; ++k) tt[k][j] = (uint32_t)k == idx ? T(1) : T(0);
+                }
+                break;
+            }
+#define CUSR_UN(OPC) case xop_un(OPC): tan_un<T, V, NT, KT, OPC>(tos, tt); break;
+            CUSR_UN(OP_SIN) CUSR_UN(OP_COS) CUSR_UN(OP_TAN) CUSR_UN(OP_SINH)
+            CUSR_UN(OP_COSH) CUSR_UN(OP_TANH) CUSR_UN(OP_LOG) CUSR_UN(OP_LOGABS)
+            CUSR_UN(OP_EXP) CUSR_UN(OP_INV) CUSR_UN(OP_NEG) CUSR_UN(OP_ABS)
+            CUSR_UN(OP_SQRT) CUSR_UN(OP_SQRTABS) CUSR_UN(OP_UZERO)
+#undef CUSR_UN
+#define CUSR_B(OPC, MODE, SW)                                                          \
+    case xop_bin(OPC, MODE, SW):                                                       \
+        tan_bin<T, V, NT, KT, OPC, MODE, SW>(w, c_s, xt, sp, tos, tt);                 \
+        break;
+#define CUSR_B6(OPC) CUSR_B(OPC, M_VAR, 0) CUSR_B(OPC, M_VAR, 1) CUSR_B(OPC, M_CONST, 0) \
+                     CUSR_B(OPC, M_CONST, 1) CUSR_B(OPC, M_POP, 0) CUSR_B(OPC, M_POP, 1)
+#define CUSR_B3(OPC) CUSR_B(OPC, M_VAR, 0) CUSR_B(OPC, M_CONST, 0) CUSR_B(OPC, M_POP, 0)
+            CUSR_B3(OP_ADD) CUSR_B6(OP_SUB) CUSR_B3(OP_MUL) CUSR_B6(OP_DIV)
+            CUSR_B6(OP_POW) CUSR_B6(OP_POWABS) CUSR_B6(OP_MAX) CUSR_B6(OP_MIN)
+            CUSR_B3(OP_LT) CUSR_B3(OP_GT) CUSR_B3(OP_LE) CUSR_B3(OP_GE) CUSR_B3(OP_BZERO)
+#undef CUSR_B3
+#undef CUSR_B6
+#undef CUSR_B
+            default:
+                __builtin_unreachable();   // host-validated opcodes
         }
     }
 }
@@ -369,6 +502,7 @@ __global__ void __launch_bounds__(NT)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;
     constexpr bool kBig = L::kBig;
+    constexpr bool FWD = GRAD && L::kFwd;   // forward-mode tangents (KC = 1, 2)
     constexpr int GS = L::kGStride;
     constexpr int ROUND = NT * V;
     constexpr int NW = NT / 32;
@@ -408,7 +542,8 @@ lm_eval_kernel(const EvalParams<T> p) {
         const int K = d.K;
         const bool unique = (d.flags & TD_UNIQUE_CONST) != 0;
         const bool grad = GRAD && K > 0;
-        const int n_code = d.n_instr + d.n_bwd;   // the reverse program follows the forward one
+        // the reverse program follows the forward one (forward mode needs only the latter)
+        const int n_code = FWD ? d.n_instr : d.n_instr + d.n_bwd;
         for (int i = tid; i < n_code; i += NT) code_s[i] = p.code[d.code_off + i];
         if (tid == 0) code_s[n_code] = 0u;   // prefetch pad after the reverse program
         for (int i = tid; i < K; i += NT) c_s[i] = p.c[d.c_off + i];
@@ -451,7 +586,12 @@ lm_eval_kernel(const EvalParams<T> p) {
             const VecF<V> yv = *reinterpret_cast<const VecF<V> *>(yrow + si);
 
             T f[V];
-            forward_sweep<T, V, NT, GRAD>(code_s, d.n_instr, c_s, xt, spt, tpt, f);
+            T tt[FWD ? KC : 1][V];
+            if constexpr (FWD) {
+                tangent_sweep<T, V, NT, KC>(code_s, d.n_instr, c_s, xt, spt, f, tt);
+            } else {
+                forward_sweep<T, V, NT, GRAD>(code_s, d.n_instr, c_s, xt, spt, tpt, f);
+            }
             T r[V];
             bool valid[V];
             CUSR_FOR_V {
@@ -462,7 +602,28 @@ lm_eval_kernel(const EvalParams<T> p) {
             if (p.vals) {
                 CUSR_FOR_V if (valid[j]) p.vals[(int64_t)wi.x * p.N + si + j] = f[j];
             }
-            if (grad) {
+            if constexpr (FWD) {
+              if (grad) {
+                if (p.jac) {
+                    T *jrow = p.jac + (int64_t)wi.x * p.jac_kmax * p.N;
+#pragma unroll
+                    for (int k = 0; k < KC; ++k)
+                        if (k < K) { CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = tt[k][j]; }
+                }
+                CUSR_FOR_V {
+#pragma unroll
+                    for (int i = 0; i < KC; ++i) {
+                        if (i < K) {
+                            const T gi = valid[j] ? tt[i][j] : T(0);
+                            jtr[i] += gi * r[j];
+#pragma unroll
+                            for (int l = 0; l <= i; ++l)
+                                acc[i * (i + 1) / 2 + l] += gi * (valid[j] ? tt[l][j] : T(0));
+                        }
+                    }
+                }
+              }
+            } else if (grad) {
                 if (!unique) {
                     for (int k = 0; k < K; ++k) {
                         CUSR_FOR_V gt[k * GS + j] = T(0);

@@ -471,7 +471,9 @@ int tape_class(int n_tape) {
 #endif
 }
 
-int kc_class(int K, bool fp64) {
+// K <= fwd_max (0, 1 or 2) goes to the forward-mode classes 1 and 2 (tangents in registers).
+int kc_class(int K, bool fp64, int fwd_max) {
+    if (K <= fwd_max) return K <= 1 ? 1 : 2;
     if (fp64) {
         if (K <= 4) return 4;
         if (K <= 8) return 8;
@@ -485,7 +487,8 @@ int kc_class(int K, bool fp64) {
 }
 
 void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
-                    bool y_shared, bool fp64, int round, int resident, Schedule *out) {
+                    bool y_shared, bool fp64, int round, int resident, Schedule *out,
+                    int fwd_max) {
     out->bins.clear();
     out->desc.assign((size_t)M, TreeDesc{});
     out->round = round;
@@ -524,8 +527,8 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         q_off += P;
         // forward + reverse sweep per instruction, plus the normal-equation update
         cost[(size_t)m] = (double)N * (2.0 * ct.n_instr + 0.5 * ct.K * (ct.K + 1) * 0.25);
-        const int kc = kc_class(ct.K, fp64);
-        const int tc = tape_class(ct.n_tape);
+        const int kc = kc_class(ct.K, fp64, fwd_max);
+        const int tc = kc <= 2 ? 0 : tape_class(ct.n_tape);   // forward mode keeps no tape
         const size_t key = (size_t)kc * 16 + (size_t)tc;
         if (bin_of_class[key] < 0) {
             bin_of_class[key] = (int)out->bins.size();

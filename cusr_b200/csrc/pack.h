@@ -63,15 +63,17 @@ struct Schedule {
     int64_t total_items = 0;
 };
 
-// K classes for fp32 and fp64 arithmetic (largest class = cooperative accumulation).
-int kc_class(int K, bool fp64);
+// K classes for fp32 and fp64 arithmetic (largest class = cooperative accumulation; 1 and 2
+// = forward-mode tangents, for K <= fwd_max).
+int kc_class(int K, bool fp64, int fwd_max = 0);
 // Tape-size classes (slot bounds 8, 16, 24, 32, 48, 64, 96, 128, 192, 256).
 int tape_class(int n_tape);
 
 // Build the schedule: bins, per-tree descriptors, chunking (round = samples per round of a
 // block, resident = concurrently resident blocks on the device).
 void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
-                    bool y_shared, bool fp64, int round, int resident, Schedule *out);
+                    bool y_shared, bool fp64, int round, int resident, Schedule *out,
+                    int fwd_max = 0);
 
 // Reference evaluation of a compiled program on the host (fp64), forward value plus the
 // reverse sweep into grad[0..K). Used by the CPU tests of the compiler.

@@ -134,8 +134,15 @@ typedef struct CoOptions {
                             /* (new trees and c_init every generation, fixed data) skip  */
                             /* the re-upload. CO_ERR_NULLARG if nothing compatible is    */
                             /* resident. (co_optimize_ex, co_optimize_sharded, co_load)  */
-    int32_t reserved[6];
+    int32_t ad_mode;        /* Jacobian: CO_AD_AUTO (reverse mode everywhere: measured   */
+                            /* fastest on B200), CO_AD_FORWARD (forward-mode tangents    */
+                            /* for K <= 2, reverse above), CO_AD_REVERSE                 */
+    int32_t reserved[5];
 } CoOptions;
+
+#define CO_AD_AUTO    0
+#define CO_AD_FORWARD 1
+#define CO_AD_REVERSE 2
 
 /* Fill `opt` with the reference defaults (fp32, 50 iterations, lambda0 1e-3, xtol 1e-6,
  * audit auto, early exit on). */

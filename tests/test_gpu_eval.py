@@ -375,3 +375,46 @@ def test_fd_jacobian_fp32_reference_step(co):
     """fp32 with the reference's eps_rel = 1e-3 (batch_lm.cu:207): first-order truncation, so
     a loose tolerance; the point is the same column layout and step rule."""
     _fd_check(co, synth.make_config("pr1", M=64, N=200, seed=4), "fp32", 0.0, 2e-2, 0.9)
+
+
+@pytest.fixture(scope="module")
+def co_fwd():
+    """A context whose evaluations use forward-mode tangents for K <= 2 (CUSR_EVAL_FWD=2 is
+    read when the context is created)."""
+    import os
+
+    old = os.environ.get("CUSR_EVAL_FWD")
+    os.environ["CUSR_EVAL_FWD"] = "2"
+    try:
+        c = InProcessCO(device_id=0)
+    finally:
+        if old is None:
+            del os.environ["CUSR_EVAL_FWD"]
+        else:
+            os.environ["CUSR_EVAL_FWD"] = old
+    yield c
+    c.teardown()
+
+
+def _small_k_pop(seed):
+    """PR1 trees restricted to K <= 2 (the forward-mode classes) plus a few larger ones."""
+    pop = synth.make_config("pr1", M=160, N=256, seed=seed)
+    Ks = np.asarray(pop["metas"])[:, 3]
+    idx = np.concatenate([np.flatnonzero(Ks <= 2), np.flatnonzero(Ks > 2)[:8]])
+    return popio.slice_pop(pop, idx)
+
+
+@pytest.mark.parametrize("precision,tol", [("fp64", 1e-10), ("fp32", 1e-3)])
+def test_forward_mode_jacobian_matches_oracle(co_fwd, precision, tol):
+    _check_jacobian(co_fwd, _small_k_pop(21), precision, tol)
+
+
+def test_forward_mode_blocks_match_reverse(co, co_fwd):
+    """Normal-equation blocks from forward tangents equal the reverse sweep's to rounding."""
+    pop = _small_k_pop(22)
+    a = co.evaluate(pop, precision="fp64", values=False, blocks=True)["blocks"]
+    b = co_fwd.evaluate(pop, precision="fp64", values=False, blocks=True)["blocks"]
+    for x, y in zip(a, b):
+        fin = np.isfinite(x) & np.isfinite(y)
+        assert np.array_equal(np.isfinite(x), np.isfinite(y))
+        np.testing.assert_allclose(y[fin], x[fin], rtol=1e-11, atol=1e-11 * np.abs(x[fin]).max(initial=1.0))
