@@ -156,3 +156,40 @@ def replicate_ym(pop: dict) -> dict:
     out = dict(pop)
     out["ym"] = ym
     return out
+
+
+def _ranges(starts: np.ndarray, lengths: np.ndarray) -> np.ndarray:
+    """Concatenation of arange(s, s + n) for every (s, n) pair (vectorised)."""
+    lengths = np.asarray(lengths, np.int64)
+    total = int(lengths.sum())
+    if total == 0:
+        return np.zeros(0, np.int64)
+    ends = np.cumsum(lengths)
+    first = np.repeat(np.asarray(starts, np.int64) - (ends - lengths), lengths)
+    return first + np.arange(total, dtype=np.int64)
+
+
+def replicate(pop: dict, copies: int, c_init=None) -> dict:
+    """Population whose tree j = m * copies + s is a copy of tree m (programs and targets);
+    `c_init` (optional, [M * copies, ...] flattened in that order) replaces the constants.
+    Shared-y populations stay shared; per-tree targets are repeated."""
+    M, S = int(pop["M"]), int(copies)
+    metas = np.asarray(pop["metas"], np.int64).reshape(M, 4)
+    off, n, coff, K = metas[:, 0], metas[:, 1], metas[:, 2], metas[:, 3]
+    n_r, K_r = np.repeat(n, S), np.repeat(K, S)
+    node_idx = _ranges(np.repeat(off, S), n_r)
+    c_idx = _ranges(np.repeat(coff, S), K_r)
+    new_metas = np.stack([np.cumsum(n_r) - n_r, n_r, np.cumsum(K_r) - K_r, K_r], 1)
+    ym = np.asarray(pop["ym"], np.float32)
+    out = dict(pop)
+    out.update(M=M * S, total_nodes=int(n_r.sum()), total_c=int(K_r.sum()),
+               nt=np.asarray(pop["nt"], np.int32)[node_idx],
+               nv=np.asarray(pop["nv"], np.float32)[node_idx],
+               ci=np.asarray(pop["ci"], np.int32)[node_idx],
+               metas=new_metas.astype(np.int32),
+               c_init=(np.asarray(pop["c_init"], np.float32)[c_idx] if c_init is None
+                       else np.asarray(c_init, np.float32).reshape(-1)),
+               ym=ym if ym.ndim == 1 else np.repeat(ym, S, axis=0))
+    if out["c_init"].size != out["total_c"]:
+        raise ValueError("c_init does not match the replicated constants")
+    return out

@@ -1,0 +1,79 @@
+"""Multi-start host logic (replication, start points, best-start selection, batching), with a
+stand-in optimizer on the CPU; the device fit itself is covered in test_gpu_fit.py."""
+from __future__ import annotations
+
+import numpy as np
+
+from cusr_b200 import multistart, popio, synth
+
+
+def test_replicate_copies_programs_and_constants():
+    pop = synth.make_config("pr1", M=9, N=13, seed=1)
+    r = popio.replicate(pop, 4)
+    assert r["M"] == 36 and r["total_c"] == 4 * pop["total_c"]
+    for m in range(9):
+        for s in range(4):
+            a, b = popio.tree_view(pop, m), popio.tree_view(r, 4 * m + s)
+            for x, y in zip(a[:3], b[:3]):
+                np.testing.assert_array_equal(x, y)
+            np.testing.assert_array_equal(popio.tree_consts(pop, pop["c_init"], m),
+                                          popio.tree_consts(r, r["c_init"], 4 * m + s))
+    phys = synth.make_config("physics", M=3, N=5, seed=2)     # per-tree targets repeat
+    rp = popio.replicate(phys, 2)
+    np.testing.assert_array_equal(rp["ym"][3], phys["ym"][1])
+
+
+def test_start_points_first_is_c_init_and_deterministic():
+    pop = synth.make_config("pr1", M=20, N=8, seed=3)
+    a = multistart.start_points(pop, 8, seed=5)
+    b = multistart.start_points(pop, 8, seed=5)
+    np.testing.assert_array_equal(a, b)
+    r = popio.replicate(pop, 8, c_init=a)
+    for m in range(20):
+        np.testing.assert_array_equal(popio.tree_consts(r, r["c_init"], 8 * m),
+                                      popio.tree_consts(pop, pop["c_init"], m))
+    assert not np.array_equal(a, multistart.start_points(pop, 8, seed=6))
+
+
+class _FakeCO:
+    """loss_final = sum((c - 1)^2) per tree; c_final = c_init (no fitting)."""
+
+    def optimize_ex(self, pop, max_iter=50, precision="fp64", xtol=1e-6):
+        M = int(pop["M"])
+        metas = np.asarray(pop["metas"]).reshape(M, 4)
+        c = np.asarray(pop["c_init"], np.float64)
+        lf = np.array([np.sum((c[o:o + k] - 1.0) ** 2) for _, _, o, k in metas])
+        lf[::7] = np.nan                                     # some failed starts
+        return {"c_final": c.copy(), "status": np.arange(M, dtype=np.int32) % 5,
+                "loss_init": lf.copy(), "loss_final": lf, "iters": np.full(M, 3, np.int32)}
+
+
+def test_select_best_and_batching():
+    pop = synth.make_config("pr1", M=30, N=8, seed=4)
+    co = _FakeCO()
+    one = multistart.fit_multistart(co, pop, starts=6, seed=0)
+    K = np.asarray(pop["metas"])[:, 3]
+    # the chosen start is the argmin of the finite losses, its constants are returned
+    pts = multistart.start_points(pop, 6, seed=0)
+    r = popio.replicate(pop, 6, c_init=pts)
+    for m in range(30):
+        losses = []
+        for s in range(6):
+            j = 6 * m + s
+            cs = popio.tree_consts(r, r["c_init"], j).astype(np.float64)
+            losses.append(np.inf if j % 7 == 0 else np.sum((cs - 1.0) ** 2))
+        best = int(np.argmin(losses))
+        assert one["start"][m] == best
+        np.testing.assert_array_equal(popio.tree_consts(pop, one["c_final"], m),
+                                      popio.tree_consts(r, r["c_init"], 6 * m + best))
+    assert one["c_final"].size == pop["total_c"] and one["status"].shape == (30,)
+    assert np.all(K[one["start"] == 0] >= 0)
+
+
+def test_batched_multistart_shapes():
+    pop = synth.make_config("pr1", M=30, N=8, seed=4)
+    out = multistart.fit_multistart(_FakeCO(), pop, starts=6, max_batch=40)   # 6 trees a batch
+    assert out["c_final"].size == pop["total_c"]
+    for k in ("status", "loss_init", "loss_final", "start", "iters"):
+        assert out[k].shape == (30,), k
+    assert np.all((out["start"] >= 0) & (out["start"] < 6))
