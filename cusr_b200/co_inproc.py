@@ -92,7 +92,8 @@ class CoOptions(ctypes.Structure):
         ("lambda0", ctypes.c_double), ("xtol", ctypes.c_double),
         ("fp64_audit", ctypes.c_int32), ("early_exit", ctypes.c_int32),
         ("sample_sharded", ctypes.c_int32), ("keep_inputs", ctypes.c_int32),
-        ("ad_mode", ctypes.c_int32), ("reserved", ctypes.c_int32 * 5),
+        ("ad_mode", ctypes.c_int32), ("damping_always", ctypes.c_int32),
+        ("damping_floor", ctypes.c_double), ("reserved", ctypes.c_int32 * 2),
     ]
 
 
@@ -294,15 +295,19 @@ class InProcessCO:
     def optimize_ex(self, pop: dict, max_iter: int = 50, precision: str = "fp32",
                     y_shared: bool | None = None, lambda0: float = 1e-3, xtol: float = 1e-6,
                     fp64_audit: int = -1, early_exit: bool = True, keep_inputs: bool = False,
-                    ad_mode: str = "auto"):
+                    ad_mode: str = "auto", damping_floor: float = 0.0,
+                    damping_always: bool = False):
         """Extended fit: precision 'fp32' | 'fp64' | 'fp32_fast'; y_shared=True passes one
         target row (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a
         1-D ym). keep_inputs=True reuses the X / shared y left on the device by the previous
         call (pop needs no 'xs' / 'ym' then): the in-loop case of new trees on fixed data.
-        ad_mode 'auto' | 'forward' (tangents for K <= 2) | 'reverse'.
+        ad_mode 'auto' | 'forward' (tangents for K <= 2) | 'reverse'. damping_floor > 0
+        retries a system the reference damping diag*(1+lam) cannot factor with
+        diag + lam*max(diag, f*max diag) (damping_always: use that damping on every solve).
         Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters."""
         return self._fit_ex("co_optimize_ex", pop, max_iter, precision, y_shared, lambda0,
-                            xtol, fp64_audit, early_exit, keep_inputs, ad_mode)
+                            xtol, fp64_audit, early_exit, keep_inputs, ad_mode, damping_floor,
+                            damping_always)
 
     def shard_init(self, unique_id: bytes, nranks: int, rank: int,
                    timeout_s: float = 120.0) -> None:
@@ -327,7 +332,8 @@ class InProcessCO:
                             xtol, fp64_audit, early_exit, keep_inputs)
 
     def _fit_ex(self, entry, pop, max_iter, precision, y_shared, lambda0, xtol, fp64_audit,
-                early_exit, keep_inputs=False, ad_mode="auto"):
+                early_exit, keep_inputs=False, ad_mode="auto", damping_floor=0.0,
+                damping_always=False):
         if self._torn:
             raise RuntimeError("InProcessCO used after teardown()")
         M, total_c = int(pop["M"]), int(pop["total_c"])
@@ -340,6 +346,8 @@ class InProcessCO:
         opt = self._options(max_iter, precision, y_shared, lambda0, xtol, fp64_audit, early_exit,
                             ad_mode)
         opt.keep_inputs = 1 if keep_inputs else 0
+        opt.damping_floor = float(damping_floor)
+        opt.damping_always = 1 if damping_always else 0
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)

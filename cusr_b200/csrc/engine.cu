@@ -522,6 +522,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     sp.pending = P<int32_t>(ctx->pending);
     sp.n_eval = P<int32_t>(ctx->n_eval);
     sp.reduced = nullptr;
+    sp.damping_floor = opt.damping_floor > 0.0 ? opt.damping_floor : 0.0;
+    sp.damping_always = opt.damping_always ? 1 : 0;
     sp.xtol = (T)opt.xtol;
 
     const int max_iter = std::max(0, opt.max_iter);

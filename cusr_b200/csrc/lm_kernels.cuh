@@ -30,6 +30,8 @@ struct StepParams {
     int32_t *n_eval;         // evaluations consumed per tree (initial pass + trials)
     const T *reduced;        // sample-sharded mode: per-tree sums all-reduced over ranks
                              // (q_off layout, replaces the chunk partials), else null
+    double damping_floor;    // 0: reference damping diag * (1 + lam)
+    int damping_always;      // with a floor: floored damping on every solve (else fallback)
     int *n_running;          // trees still running after this step (early exit)
     int initial;             // the evaluated point is c_init
     int do_solve;            // solve a new step for every running tree
@@ -133,26 +135,50 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                 const T *b = p.blk + d.q_off;
                 const int tri = K * (K + 1) / 2;
                 const double fac = (double)(T(1) + lam);
-                for (int i = 0; i < K; ++i) {
-                    bv[i] = -(double)b[tri + i];
-                    for (int l = 0; l <= i; ++l) {
-                        const double v = (double)b[i * (i + 1) / 2 + l];
-                        A[i * K + l] = v;
-                        A[l * K + i] = v;
+                // damped system; `floored`: diag + lam * max(diag, floor * max diag)
+                auto build = [&](bool floored) {
+                    double fl = 0.0;
+                    if (floored) {
+                        for (int i = 0; i < K; ++i) fl = fmax(fl, (double)b[i * (i + 1) / 2 + i]);
+                        fl *= p.damping_floor;
                     }
-                    A[i * K + i] *= fac;
-                }
-                bool ok = true;
-                for (int j = 0; j < K && ok; ++j) {
-                    double s = A[j * K + j];
-                    for (int k = 0; k < j; ++k) s -= A[j * K + k] * A[j * K + k];
-                    if (s <= 0.0) { ok = false; break; }
-                    A[j * K + j] = sqrt(s);
-                    for (int i = j + 1; i < K; ++i) {
-                        double t = A[i * K + j];
-                        for (int k = 0; k < j; ++k) t -= A[i * K + k] * A[j * K + k];
-                        A[i * K + j] = t / A[j * K + j];
+                    for (int i = 0; i < K; ++i) {
+                        bv[i] = -(double)b[tri + i];
+                        for (int l = 0; l <= i; ++l) {
+                            const double v = (double)b[i * (i + 1) / 2 + l];
+                            A[i * K + l] = v;
+                            A[l * K + i] = v;
+                        }
+                        if (floored) {
+                            const double v = A[i * K + i];
+                            A[i * K + i] = v + (double)lam * (v > fl ? v : fl);
+                        } else {
+                            A[i * K + i] *= fac;
+                        }
                     }
+                };
+                auto cholesky = [&]() -> bool {
+                    for (int j = 0; j < K; ++j) {
+                        double s = A[j * K + j];
+                        for (int k = 0; k < j; ++k) s -= A[j * K + k] * A[j * K + k];
+                        if (s <= 0.0) return false;
+                        A[j * K + j] = sqrt(s);
+                        for (int i = j + 1; i < K; ++i) {
+                            double t = A[i * K + j];
+                            for (int k = 0; k < j; ++k) t -= A[i * K + k] * A[j * K + k];
+                            A[i * K + j] = t / A[j * K + j];
+                        }
+                    }
+                    return true;
+                };
+                const bool always = p.damping_floor > 0.0 && p.damping_always;
+                build(always);
+                bool ok = cholesky();
+                // robust mode: a system the reference damping cannot factor (a zero or
+                // negligible Jacobian column) is retried with the damping floor
+                if (!ok && p.damping_floor > 0.0 && !always) {
+                    build(true);
+                    ok = cholesky();
                 }
                 if (!ok) {
                     p.iters[m] += 1;

@@ -137,7 +137,12 @@ typedef struct CoOptions {
     int32_t ad_mode;        /* Jacobian: CO_AD_AUTO (reverse mode everywhere: measured   */
                             /* fastest on B200), CO_AD_FORWARD (forward-mode tangents    */
                             /* for K <= 2, reverse above), CO_AD_REVERSE                 */
-    int32_t reserved[5];
+    int32_t damping_always; /* with damping_floor > 0: 1 = always the floored damping    */
+    double  damping_floor;  /* 0 (default): the reference Marquardt damping only,        */
+                            /* diag *= 1+lam (a zero Jacobian column -> FAIL_CHOLESKY).   */
+                            /* f > 0: a system that damping cannot factor is retried with */
+                            /* diag + lam * max(diag, f * max(diag)) (robust fits)        */
+    int32_t reserved[2];
 } CoOptions;
 
 #define CO_AD_AUTO    0

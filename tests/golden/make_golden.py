@@ -15,6 +15,8 @@ Everything written here comes from the reference's own code and files:
   interp_vectors.npz             reference interpreter values (interp.eval_tree_arrays, fp64)
                                  on PR1-config trees from cusr_b200.synth and on pop1000
   pr1_scipy.npz                  reference ScipyPop fits of the PR1 configuration (seed 0)
+  configs_scipy.npz              reference ScipyPop fits of 64-tree samples of the mid,
+                                 physics, long and scale configurations (seed 7, reduced N)
   jac_sample.npz                 the reference's reverse-AD Jacobian samples
                                  (experiments/revad_v5/jac_sample_fixed.jsonl)
 The tests read only these files; the reference is not needed at test time.
@@ -42,7 +44,37 @@ def _pop_arrays(prefix: str, pop: dict) -> dict:
     return out
 
 
+# (config, trees, samples) of the configs_scipy.npz samples: every configuration of the
+# benchmark grammar at a size the reference's CPU fit finishes in seconds
+CONFIG_SAMPLES = (("mid", 64, 1000), ("physics", 64, 1000), ("long", 64, 512), ("scale", 64, 1000))
+
+
+def make_config_samples() -> None:
+    """configs_scipy.npz: reference ScipyPop fits of sampled configurations."""
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(ROOT))
+    from cusr.benchmark import backends, interp  # reference code
+
+    from cusr_b200 import synth
+
+    arr = {}
+    for name, M, N in CONFIG_SAMPLES:
+        pop = synth.make_config(name, M=M, N=N, seed=7)
+        ref_pop = _as_ref(pop)
+        sc = backends.ScipyPop(nproc=os.cpu_count()).fit_pop(ref_pop)
+        arr.update(_pop_arrays(name, pop))
+        arr[f"{name}/scipy/c_final"] = sc.c_final
+        arr[f"{name}/scipy/status"] = sc.status
+        arr[f"{name}/scipy/loss64"] = interp.loss_pop(ref_pop, sc.c_final)
+        arr[f"{name}/init/loss64"] = interp.loss_pop(ref_pop, pop["c_init"].astype(np.float64))
+        print(name, "fitted", flush=True)
+    np.savez_compressed(HERE / "configs_scipy.npz", **arr)
+
+
 def main() -> None:
+    if "--configs" in sys.argv:
+        make_config_samples()
+        return
     sys.path.insert(0, str(REF))
     sys.path.insert(0, str(ROOT))
     from cusr.benchmark import backends, interp, popio  # reference code
