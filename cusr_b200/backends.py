@@ -30,15 +30,19 @@ class FitResult:
 
 
 class B200Pop:
-    """In-process engine backend. precision 'fp32' (the reference kernel's arithmetic) or
-    'fp64'; shared target rows are detected and uploaded once."""
+    """In-process engine backend. precision 'fp32' (IEEE functions), 'fp32_fast' (the
+    reference kernel's fast-math arithmetic) or 'fp64'; shared target rows are detected and
+    uploaded once. starts > 1: robust multi-start fits (cusr_b200.multistart; max_iter then
+    defaults to 200)."""
 
-    def __init__(self, max_iter: int = 50, precision: str = "fp32", device_id: int = 0,
-                 name: str | None = None):
-        self.max_iter = int(max_iter)
+    def __init__(self, max_iter: int | None = None, precision: str = "fp32", device_id: int = 0,
+                 name: str | None = None, starts: int = 1):
+        self.starts = max(1, int(starts))
+        self.max_iter = int(max_iter if max_iter is not None else (200 if self.starts > 1 else 50))
         self.precision = precision
         self.device_id = int(device_id)
-        self.name = name or f"b200:{precision}"
+        self.name = name or (f"b200:{precision}" if self.starts == 1
+                             else f"b200:{precision}:ms{self.starts}")
 
     def fit_pop(self, pop: dict) -> FitResult:
         t0 = time.perf_counter()
@@ -48,14 +52,22 @@ class B200Pop:
         if shared and ym.ndim == 2:
             pop = dict(pop)
             pop["ym"] = ym[0] if ym.shape[0] else ym.reshape(-1)
-        res = co.optimize_ex(pop, max_iter=self.max_iter, precision=self.precision,
-                             y_shared=shared)
+        if self.starts > 1:
+            from . import multistart
+
+            t_fit = time.perf_counter()
+            res = multistart.fit_multistart(co, pop, starts=self.starts, max_iter=self.max_iter,
+                                            precision=self.precision)
+            t_fit = time.perf_counter() - t_fit
+        else:
+            res = co.optimize_ex(pop, max_iter=self.max_iter, precision=self.precision,
+                                 y_shared=shared)
         st = co.stats()
         raw = res["status"]
         return FitResult(self.name, res["c_final"].astype(np.float64), _STATUS_MAP[raw],
                          res["iters"].astype(np.int32), time.perf_counter() - t0,
-                         st["device_ms"] / 1e3,
+                         st["device_ms"] / 1e3 if self.starts == 1 else t_fit,
                          meta=dict(dtype=self.precision, raw_status_counts={
                              int(k): int(v) for k, v in zip(*np.unique(raw, return_counts=True))},
-                             criteria=f"reference LM (lambda0 1e-3, xtol 1e-6), "
-                                      f"max_iter={self.max_iter}"))
+                             criteria=f"reference LM (lambda0 1e-3), max_iter={self.max_iter}"
+                                      + (f", {self.starts} starts" if self.starts > 1 else "")))

@@ -357,3 +357,21 @@ def test_ad_modes_give_the_same_fits(co):
     both = np.isfinite(a) & np.isfinite(b)
     rel = np.abs(a[both] - b[both]) / np.maximum(np.abs(a[both]), 1e-30)
     assert np.mean(rel <= 1e-6) >= 0.95
+
+
+def test_fitresult_backend_single_and_multistart():
+    """backends.B200Pop.fit_pop -> FitResult with the runner's fields and status convention
+    (backends.py:81-89, 746); the multi-start backend is as good or better per tree."""
+    from cusr_b200.backends import B200Pop
+
+    pop = synth.make_config("pr1", M=64, N=400, seed=12)
+    one = B200Pop(precision="fp64").fit_pop(pop)
+    ms = B200Pop(precision="fp64", starts=16).fit_pop(pop)
+    for r in (one, ms):
+        assert r.c_final.shape == (pop["total_c"],) and r.status.shape == (64,)
+        assert set(np.unique(r.status)) <= {0, 1, 2, 3}
+        assert r.wall_core > 0 and r.wall_e2e >= r.wall_core
+    l1 = interp.loss_pop(pop, one.c_final)
+    l2 = interp.loss_pop(pop, ms.c_final)
+    fin = np.isfinite(l1)
+    assert np.mean(l2[fin] <= l1[fin] * (1 + 1e-9) + 1e-15) >= 0.95
