@@ -56,7 +56,7 @@ struct Ctx {
     int sm_count = 0;
     cudaStream_t stream = nullptr;
     // bins of one pass run on these streams concurrently, so one bin's tail overlaps the next
-    static constexpr int kBinStreams = 4;
+    static constexpr int kBinStreams = 8;
     cudaStream_t bin_streams[kBinStreams] = {};
     cudaEvent_t ev_fork = nullptr, ev_join[kBinStreams] = {};
     DBuf tape_gs[kBinStreams];
@@ -79,6 +79,7 @@ struct Ctx {
     int prep_prec = -1;     // arithmetic type of the loaded problem (CO_PREC_FP32 / _FP64)
     bool fast = false;      // fp32 launches use the fast-math instantiations (CO_PREC_FP32_FAST)
     int wide_mode = -1;     // block width per bin: -1 by occupancy, 0 narrow, 1 wide
+    int n_bin_streams = kBinStreams;   // streams the bins of a pass are spread over
     int fwd_max = 0;        // trees with K <= fwd_max use the forward-mode classes
     int fwd_default = 0;    // fwd_max of CO_AD_AUTO
     // the inputs resident in xs / ym (for CoOptions.keep_inputs)
@@ -200,7 +201,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         CK(cudaGetLastError());
         ctx->stats.kernel_launches++;
     }
-    const int n_streams = std::min(n_bins, (int)Ctx::kBinStreams);
+    const int n_streams = std::min(n_bins, ctx->n_bin_streams);
     CK(cudaEventRecord(ctx->ev_fork, ctx->stream));
     for (int si = 0; si < n_streams; ++si) CK(cudaStreamWaitEvent(ctx->bin_streams[si], ctx->ev_fork, 0));
     for (int b = 0; b < n_bins; ++b) {
@@ -898,15 +899,7 @@ int co_init(int device_id, void **handle_out) {
         {"pinned counter", cudaMallocHost(&ctx->h_nrun, 2 * sizeof(int))},
         {"event 0", cudaEventCreateWithFlags(&ctx->ev_nrun[0], cudaEventDisableTiming)},
         {"event 1", cudaEventCreateWithFlags(&ctx->ev_nrun[1], cudaEventDisableTiming)},
-        {"bin stream 0", cudaStreamCreateWithFlags(&ctx->bin_streams[0], cudaStreamNonBlocking)},
-        {"bin stream 1", cudaStreamCreateWithFlags(&ctx->bin_streams[1], cudaStreamNonBlocking)},
-        {"bin stream 2", cudaStreamCreateWithFlags(&ctx->bin_streams[2], cudaStreamNonBlocking)},
-        {"bin stream 3", cudaStreamCreateWithFlags(&ctx->bin_streams[3], cudaStreamNonBlocking)},
         {"fork event", cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming)},
-        {"join event 0", cudaEventCreateWithFlags(&ctx->ev_join[0], cudaEventDisableTiming)},
-        {"join event 1", cudaEventCreateWithFlags(&ctx->ev_join[1], cudaEventDisableTiming)},
-        {"join event 2", cudaEventCreateWithFlags(&ctx->ev_join[2], cudaEventDisableTiming)},
-        {"join event 3", cudaEventCreateWithFlags(&ctx->ev_join[3], cudaEventDisableTiming)},
         {"sync event", cudaEventCreateWithFlags(&ctx->ev_sync, cudaEventDisableTiming)},
         {"fit event 0", cudaEventCreate(&ctx->ev_fit[0])},
         {"fit event 1", cudaEventCreate(&ctx->ev_fit[1])},
@@ -914,6 +907,17 @@ int co_init(int device_id, void **handle_out) {
         {"fp32 fast-math kernels", eval_prepare_f32_fast()},
         {"fp64 kernels", eval_prepare_f64()},
     };
+    for (int i = 0; i < Ctx::kBinStreams; ++i) {
+        cudaError_t e = cudaStreamCreateWithFlags(&ctx->bin_streams[i], cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_join[i], cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            fprintf(stderr, "[cusr_b200] device %d setup (bin stream %d): %s\n", device_id, i,
+                    cudaGetErrorString(e));
+            cudaGetLastError();
+            co_teardown(ctx);
+            return CO_ERR_CUDA;
+        }
+    }
     for (const Step &st : steps) {
         if (st.e != cudaSuccess) {
             fprintf(stderr, "[cusr_b200] device %d setup (%s): %s\n", device_id, st.what,
@@ -925,6 +929,9 @@ int co_init(int device_id, void **handle_out) {
     }
     // CUSR_EVAL_WIDE=0 / 1 pins the evaluation block width (measurements); unset: per bin
     if (const char *e = std::getenv("CUSR_EVAL_WIDE")) ctx->wide_mode = std::atoi(e) ? 1 : 0;
+    // CUSR_BIN_STREAMS=1..8: streams the bins of a pass run on (measurements)
+    if (const char *e = std::getenv("CUSR_BIN_STREAMS"))
+        ctx->n_bin_streams = std::min((int)Ctx::kBinStreams, std::max(1, std::atoi(e)));
     // CUSR_EVAL_FWD=k (0..2): trees with K <= k use forward-mode tangents (measurements)
     if (const char *e = std::getenv("CUSR_EVAL_FWD"))
         ctx->fwd_default = ctx->fwd_max = std::min(2, std::max(0, std::atoi(e)));
@@ -1177,7 +1184,8 @@ void co_teardown(void *handle) {
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
                     &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
                     &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac, &ctx->red,
-                    &ctx->tape_gs[0], &ctx->tape_gs[1], &ctx->tape_gs[2], &ctx->tape_gs[3]};
+                    &ctx->tape_gs[0], &ctx->tape_gs[1], &ctx->tape_gs[2], &ctx->tape_gs[3],
+                    &ctx->tape_gs[4], &ctx->tape_gs[5], &ctx->tape_gs[6], &ctx->tape_gs[7]};
     for (DBuf *b : bufs) release(*b);
     for (cudaEvent_t e : ctx->events) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->ev_nrun)
