@@ -12,6 +12,11 @@
 //      with no host round trip inside the loop (a lagged counter read lets the host stop
 //      launching once every tree has finished);
 //   5. fp64 audit for fp32 fits; D2H of the outputs.
+// The bins of a pass run concurrently on the context's bin streams (fork / join events on
+// the context stream); each bin takes the narrow or the wide block instantiation, whichever
+// keeps more warps resident. In the sample-sharded mode (co_optimize_sharded) the per-tree
+// sums of every pass are all-reduced over the NCCL group before the step kernel reads them,
+// and every wait is bounded by the group's deadline (shard_comm.h).
 // Device buffers grow by byte capacity and never shrink (co_lib.cu:129-153); every call
 // re-seeds all per-tree state from c_init (co_lib.cu:284-305).
 #include <cuda_runtime.h>
