@@ -5,10 +5,13 @@ lib_path, variant).optimize(pop, max_iter)` returning {'c_final', 'status', 'los
 'loss_final'}, the process-wide `get_inproc_co(device_id, variant)` singleton, `COError`
 with the same return-code messages, and the `PopHeader` / `TreeMeta` ctypes mirrors.
 
-Additions: `optimize_ex` (fp64 arithmetic, shared targets, lambda0 / xtol knobs, fp64
-outputs, per-tree iteration counts) and `stats()` (phase timings and work counters of the
-last call). There is no fallback path: if the shared library is missing the constructor
-raises, and every fit runs on the GPU.
+Additions: `optimize_ex` (precision fp32 / fp64 / fp32_fast, shared targets, lambda0 /
+xtol, Jacobian mode, robust damping, resident inputs across calls, fp64 outputs, per-tree
+iteration counts), `load` / `fit_loaded` (population resident in HBM), `evaluate` and
+`jacobian_fd` (one fused pass; finite-difference Jacobian), `shard_unique_id` /
+`shard_init` / `optimize_sharded` (sample-sharded fits over NCCL) and `stats()` (phase
+timings and work counters of the last call). There is no fallback path: if the shared
+library is missing the constructor raises, and every fit runs on the GPU.
 """
 from __future__ import annotations
 
