@@ -17,6 +17,9 @@ Everything written here comes from the reference's own code and files:
   pr1_scipy.npz                  reference ScipyPop fits of the PR1 configuration (seed 0)
   configs_scipy.npz              reference ScipyPop fits of 64-tree samples of the mid,
                                  physics, long and scale configurations (seed 7, reduced N)
+  fp32_honesty.npz               the reference's fp32-honesty regression fixtures
+                                 (cusr/kernel/tests/fp32_honesty_regression/*.bin, shared y
+                                 stored once) and its manifest's per-tree baseline flags
   jac_sample.npz                 the reference's reverse-AD Jacobian samples
                                  (experiments/revad_v5/jac_sample_fixed.jsonl)
 The tests read only these files; the reference is not needed at test time.
@@ -71,9 +74,33 @@ def make_config_samples() -> None:
     np.savez_compressed(HERE / "configs_scipy.npz", **arr)
 
 
+def make_honesty() -> None:
+    """fp32_honesty.npz: the fp32-honesty regression fixtures of the reference."""
+    sys.path.insert(0, str(REF))
+    from cusr.benchmark import popio  # reference loader
+
+    d = REF / "cusr" / "kernel" / "tests" / "fp32_honesty_regression"
+    manifest = json.loads((d / "manifest.json").read_text())
+    arr = {"names": np.asarray(sorted(manifest["fixtures"]))}
+    for i, name in enumerate(sorted(manifest["fixtures"])):
+        fx = manifest["fixtures"][name]
+        pop = popio.load_pop_bin(d / fx["file"])
+        pop = {k: pop[k] for k in pop}
+        ym = np.asarray(pop["ym"], np.float32).reshape(int(pop["M"]), int(pop["N"]))
+        assert np.all(ym == ym[0]), name          # every fixture shares one target row
+        pop["ym"] = ym[0]
+        arr.update(_pop_arrays(f"f{i}", pop))
+        arr[f"f{i}/fd_serious"] = np.asarray([t["fd"]["serious"] for t in fx["trees"]])
+        arr[f"f{i}/ad_serious"] = np.asarray([t["ad"]["serious"] for t in fx["trees"]])
+    np.savez_compressed(HERE / "fp32_honesty.npz", **arr)
+
+
 def main() -> None:
     if "--configs" in sys.argv:
         make_config_samples()
+        return
+    if "--honesty" in sys.argv:
+        make_honesty()
         return
     sys.path.insert(0, str(REF))
     sys.path.insert(0, str(ROOT))

@@ -375,3 +375,34 @@ def test_fitresult_backend_single_and_multistart():
     l2 = interp.loss_pop(pop, ms.c_final)
     fin = np.isfinite(l1)
     assert np.mean(l2[fin] <= l1[fin] * (1 + 1e-9) + 1e-15) >= 0.95
+
+
+def _honesty_pops():
+    z = np.load(GOLDEN / "fp32_honesty.npz")
+    for i, name in enumerate(z["names"]):
+        yield str(name), load_npz_pop(z, f"f{i}"), z[f"f{i}/ad_serious"]
+
+
+@pytest.mark.parametrize("precision,max_iter", [("fp32", 50), ("fp32_fast", 50),
+                                                ("fp32_fast", 1000)])
+def test_fp32_honesty_regression(co, precision, max_iter):
+    """The reference's fp32-honesty regression (cusr/kernel/tests/fp32_honesty_regression):
+    257 trees on which its fast-math AD kernel reports CONVERGED with c_final worse in exact
+    fp64 than c_init (208 of them > 2x worse). The property: a tree reported converged must
+    not be worse in fp64 than its start. Checked with the reference's own numerics
+    (fp32_fast) as well as IEEE fp32; the fp64 audit keeps it."""
+    conv_worse, serious_base, n = [], 0, 0
+    for name, pop, ad_serious in _honesty_pops():
+        res = co.optimize_ex(pop, max_iter=max_iter, precision=precision)
+        l0 = interp.loss_pop(pop, pop["c_init"].astype(np.float64))
+        lf = interp.loss_pop(pop, res["c_final"])
+        for m in range(int(pop["M"])):
+            n += 1
+            serious_base += int(ad_serious[m])
+            worse = (not np.isfinite(lf[m])) or lf[m] > l0[m] * (1 + 1e-6) + 1e-9
+            if int(res["status"][m]) == 0 and worse:
+                conv_worse.append((name, m, float(lf[m] / l0[m])))
+    _report(f"fp32_honesty_{precision}_{max_iter}", {"trees": n, "reference_ad_serious": serious_base,
+                                                     "converged_but_worse": conv_worse})
+    assert n == 257 and serious_base == 208
+    assert conv_worse == []

@@ -135,3 +135,14 @@ def test_reference_kernel_golden_is_consistent():
     lf = interp.loss_pop(pop, g["refkernel/c_final"].astype(np.float64))
     np.testing.assert_allclose(lf, g["refkernel/loss64"], rtol=1e-12)
     assert np.bincount(g["refkernel/status"], minlength=5).sum() == 1000
+
+
+def test_fp32_honesty_fixture_matches_manifest_counts():
+    """The committed copy of the reference's fp32-honesty fixtures: 17 problems, 257 trees,
+    the manifest's baseline offender counts (AD 208, FD 57 serious)."""
+    z = np.load(GOLDEN / "fp32_honesty.npz")
+    assert len(z["names"]) == 17
+    n = sum(int(z[f"f{i}/M"]) for i in range(17))
+    ad = sum(int(z[f"f{i}/ad_serious"].sum()) for i in range(17))
+    fd = sum(int(z[f"f{i}/fd_serious"].sum()) for i in range(17))
+    assert (n, ad, fd) == (257, 208, 57)
