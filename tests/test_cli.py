@@ -83,3 +83,45 @@ def test_cli_fit_matches_library(tmp_path, precision):
              "--precision", precision)
     assert q.returncode == 0 and q.stdout == ""
     np.testing.assert_array_equal(np.fromfile(tmp_path / "c_final.bin", np.float32), c_final)
+
+
+@pytest.mark.gpu
+def test_parity_gate_through_cli(tmp_path):
+    """The reference's kernel replacement gate (cusr/kernel/tests/test_parity_gate.py with
+    verify.py's definitions) on its own pop.bin fixture, run through the command line as the
+    gate runs the binary: loss-down rate (K>0) >= 93%, gpu_loss <= max(1.05x, +1e-10) of the
+    scipy fit on trees both converged >= 90%, within 10x >= 99%."""
+    from _helpers import pop1000
+    from oracle import interp
+
+    pop, g = pop1000()
+    p = tmp_path / "pop.bin"
+    popio.save_pop_bin(pop, p)
+    r = _run(p, tmp_path)
+    assert r.returncode == 0, r.stderr
+    status = np.fromfile(tmp_path / "status.bin", np.int32)
+    c_final = np.fromfile(tmp_path / "c_final.bin", np.float32).astype(np.float64)
+    gpu_loss = interp.loss_pop(pop, c_final)
+    gpu_init = interp.loss_pop(pop, pop["c_init"].astype(np.float64))
+    sc_loss, sc_ok = g["scipy/loss64"], g["scipy/status"] == 0
+    K = np.asarray(pop["metas"])[:, 3]
+    elig = (K > 0) & np.isfinite(gpu_loss) & np.isfinite(gpu_init)
+    loss_down = float(np.mean(gpu_loss[elig] < gpu_init[elig]))
+    both = (K > 0) & sc_ok & (status == 0)
+    fin = both & np.isfinite(gpu_loss) & np.isfinite(sc_loss)
+
+    def env(k):
+        return float(np.sum(gpu_loss[fin] <= np.maximum(k * sc_loss[fin], sc_loss[fin] + 1e-10))
+                     / max(int(both.sum()), 1))
+
+    rates = {"loss_down": loss_down, "within_1.05": env(1.05), "within_10": env(10.0),
+             "both_converged": int(both.sum())}
+    import json
+    import os
+
+    if os.path.isdir("gpurun_out"):
+        with open("gpurun_out/parity_gate_pop1000.json", "w") as f:
+            json.dump(rates, f)
+    assert rates["loss_down"] >= 0.93, rates
+    assert rates["within_1.05"] >= 0.90, rates
+    assert rates["within_10"] >= 0.99, rates
