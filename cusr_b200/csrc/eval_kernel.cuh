@@ -659,12 +659,24 @@ lm_eval_kernel(const EvalParams<T> p) {
                             for (int k = 0; k < K; ++k) gt[k * GS + j] = T(0);
                     }
                     __syncwarp();
+                    // entry by entry over the warp's 32 * V samples; only the ceil(E / 32)
+                    // entry groups this tree has (warp-uniform bound: a K = 17 tree does a
+                    // third of the work of K = 32); four partial sums per entry for ILP
                     const int sbase = warp * 32 * V;
-                    for (int s = 0; s < 32 * V; ++s) {
+                    const int nu = (nblock_size(K) + 31) >> 5;
 #pragma unroll
-                        for (int u = 0; u < NACC; ++u) {
-                            if (boff_i[u] >= 0)
-                                bacc[u] += g_s[boff_i[u] + sbase + s] * g_s[boff_l[u] + sbase + s];
+                    for (int u = 0; u < NACC; ++u) {
+                        if (u < nu && boff_i[u] >= 0) {
+                            const T *gi = g_s + boff_i[u] + sbase, *gl = g_s + boff_l[u] + sbase;
+                            T a0 = T(0), a1 = T(0), a2 = T(0), a3 = T(0);
+#pragma unroll 4
+                            for (int s = 0; s < 32 * V; s += 4) {
+                                a0 += gi[s] * gl[s];
+                                a1 += gi[s + 1] * gl[s + 1];
+                                a2 += gi[s + 2] * gl[s + 2];
+                                a3 += gi[s + 3] * gl[s + 3];
+                            }
+                            bacc[u] += (a0 + a1) + (a2 + a3);
                         }
                     }
                     __syncwarp();
