@@ -65,12 +65,18 @@ __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) 
 // Shared-memory layout of one block; the host sizes the launch with the same function.
 // KC = 1, 2: forward-mode classes (tangents in registers, no tape, no gradient rows; a spill
 // slot holds the value and its KC tangents).
+// KC = 4..16 with CUSR_JTJ_DMMA: the normal equations come from fp64 tensor-core products
+// of the gradient rows (+ residual row), so the rows get a bank-spreading pad.
+#ifndef CUSR_JTJ_DMMA
+#define CUSR_JTJ_DMMA 1
+#endif
 template <typename T, int V, int NT, int KC>
 struct EvalSmem {
     static constexpr bool kBig = KC > 16;
     static constexpr bool kFwd = KC <= 2;
-    static constexpr int kGStride = NT * V + (kBig ? 1 : 0);   // gradient row stride (T)
-    static constexpr int kGRows = kFwd ? 0 : (kBig ? KC + 1 : KC);   // + residual row
+    static constexpr bool kMma = CUSR_JTJ_DMMA && !kBig && !kFwd;
+    static constexpr int kGStride = NT * V + (kBig ? 1 : (kMma ? 4 : 0));   // row stride (T)
+    static constexpr int kGRows = kFwd ? 0 : ((kBig || kMma) ? KC + 1 : KC);   // + residual
     static constexpr int kSpillWords = kFwd ? 1 + KC : 1;     // VecT entries per spill slot
     size_t code, cval, x, spill, tape, grad, red, total;
     __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
@@ -485,6 +491,14 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
     }
 }
 
+// D(8x8) += A(8x4) B(4x8) on the fp64 tensor cores (mma.sync m8n8k4 .f64). Fragments: a
+// lane holds A[lane / 4][lane % 4], B[lane % 4][lane / 4] and D[lane / 4][2 (lane % 4) + q].
+__device__ __forceinline__ void dmma_884(double (&c)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(c[0]), "+d"(c[1])
+                 : "d"(a), "d"(b));
+}
+
 // ---------------------------------------------------------------------------------------
 // The fused evaluation kernel.
 //   T     arithmetic type (float / double)
@@ -503,6 +517,9 @@ lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;
     constexpr bool kBig = L::kBig;
     constexpr bool FWD = GRAD && L::kFwd;   // forward-mode tangents (KC = 1, 2)
+    constexpr bool kMma = GRAD && L::kMma;  // normal equations on the fp64 tensor cores
+    constexpr int NTL = kMma ? (KC + 1 + 7) / 8 : 1;   // 8-row tiles of [g; r]
+    constexpr int NTILE = NTL * (NTL + 1) / 2;         // lower-triangle tiles
     constexpr int GS = L::kGStride;
     constexpr int ROUND = NT * V;
     constexpr int NW = NT / 32;
@@ -550,13 +567,18 @@ lm_eval_kernel(const EvalParams<T> p) {
         __syncthreads();
         const uint32_t *bcode_s = code_s + d.n_instr;
 
-        // accumulators (register path) / lane-owned Gram entries (big-K path)
-        T acc[kBig ? 1 : (NTRI > 0 ? NTRI : 1)];
-        T jtr[kBig ? 1 : KC];
+        // accumulators (register path) / lane-owned Gram entries (big-K path) / fp64
+        // tensor-core fragments of the [g; r] Gram matrix (kMma)
+        T acc[(kBig || kMma) ? 1 : (NTRI > 0 ? NTRI : 1)];
+        T jtr[(kBig || kMma) ? 1 : KC];
+        double cm[kMma ? NTILE : 1][2];
+#pragma unroll
+        for (int t = 0; t < (kMma ? NTILE : 1); ++t) cm[t][0] = cm[t][1] = 0.0;
         T lsum = T(0);
         T bacc[NACC];
         int boff_i[NACC], boff_l[NACC];
-        if constexpr (!kBig) {
+        if constexpr (kMma) {
+        } else if constexpr (!kBig) {
 #pragma unroll
             for (int e = 0; e < NTRI; ++e) acc[e] = T(0);
 #pragma unroll
@@ -636,7 +658,35 @@ lm_eval_kernel(const EvalParams<T> p) {
                         CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = gt[k * GS + j];
                     }
                 }
-                if constexpr (!kBig) {
+                if constexpr (kMma) {
+                    // residual as row K, zero gradients of samples past N; then the warp
+                    // accumulates the (K+1)^2 Gram matrix of its 32 V samples as 8x8 fp64
+                    // tiles, four samples per product
+                    CUSR_FOR_V {
+                        gt[K * GS + j] = r[j];
+                        if (!valid[j])
+                            for (int k = 0; k < K; ++k) gt[k * GS + j] = T(0);
+                    }
+                    __syncwarp();
+                    const T *gw = g_s + warp * 32 * V + (lane & 3);
+                    const int grp = lane >> 2;
+#pragma unroll 2
+                    for (int s4 = 0; s4 < 32 * V; s4 += 4) {
+                        double a[NTL];
+#pragma unroll
+                        for (int t = 0; t < NTL; ++t) {
+                            const int row = 8 * t + grp;
+                            a[t] = row <= K ? (double)gw[row * GS + s4] : 0.0;
+                        }
+                        int c = 0;
+#pragma unroll
+                        for (int ti = 0; ti < NTL; ++ti) {
+#pragma unroll
+                            for (int tl = 0; tl <= ti; ++tl) dmma_884(cm[c++], a[ti], a[tl]);
+                        }
+                    }
+                    __syncwarp();
+                } else if constexpr (!kBig) {
                     CUSR_FOR_V {
                         T g[KC];
 #pragma unroll
@@ -696,6 +746,30 @@ lm_eval_kernel(const EvalParams<T> p) {
 #pragma unroll
                 for (int w = 0; w < NW; ++w) s += red_s[w];
                 dst[nblock_size(K) - 1] = s;
+            }
+        } else if constexpr (kMma) {
+            // packed (K+1)x(K+1) lower triangle == the partial layout (JtJ, Jtr, sum r^2)
+            T *rw = red_s + warp * nblock_size(KC);
+            const int grp = lane >> 2, q2 = 2 * (lane & 3);
+            int c = 0;
+#pragma unroll
+            for (int ti = 0; ti < NTL; ++ti) {
+#pragma unroll
+                for (int tl = 0; tl <= ti; ++tl, ++c) {
+                    const int i = 8 * ti + grp;
+#pragma unroll
+                    for (int qq = 0; qq < 2; ++qq) {
+                        const int l = 8 * tl + q2 + qq;
+                        if (l <= i && i <= K) rw[i * (i + 1) / 2 + l] = (T)cm[c][qq];
+                    }
+                }
+            }
+            __syncthreads();
+            for (int e = tid; e < P; e += NT) {
+                T s = T(0);
+#pragma unroll
+                for (int w = 0; w < NW; ++w) s += red_s[w * nblock_size(KC) + e];
+                dst[e] = s;
             }
         } else if constexpr (!kBig) {
             T *rw = red_s + warp * nblock_size(KC);
