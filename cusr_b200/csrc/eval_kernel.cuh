@@ -65,8 +65,9 @@ __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) 
 // Shared-memory layout of one block; the host sizes the launch with the same function.
 // KC = 1, 2: forward-mode classes (tangents in registers, no tape, no gradient rows; a spill
 // slot holds the value and its KC tangents).
-// KC = 4..16 with CUSR_JTJ_DMMA: the normal equations come from fp64 tensor-core products
-// of the gradient rows (+ residual row), so the rows get a bank-spreading pad.
+// KC >= 4 with CUSR_JTJ_DMMA: the normal equations come from fp64 tensor-core products of
+// the gradient rows (+ residual row), so the rows get a bank-spreading pad (stride = 4 mod 32
+// banks: the eight fragment rows of a load land in distinct banks).
 #ifndef CUSR_JTJ_DMMA
 #define CUSR_JTJ_DMMA 1
 #endif
@@ -74,8 +75,8 @@ template <typename T, int V, int NT, int KC>
 struct EvalSmem {
     static constexpr bool kBig = KC > 16;
     static constexpr bool kFwd = KC <= 2;
-    static constexpr bool kMma = CUSR_JTJ_DMMA && !kBig && !kFwd;
-    static constexpr int kGStride = NT * V + (kBig ? 1 : (kMma ? 4 : 0));   // row stride (T)
+    static constexpr bool kMma = CUSR_JTJ_DMMA && !kFwd;
+    static constexpr int kGStride = NT * V + (kMma ? 4 : (kBig ? 1 : 0));   // row stride (T)
     static constexpr int kGRows = kFwd ? 0 : ((kBig || kMma) ? KC + 1 : KC);   // + residual
     static constexpr int kSpillWords = kFwd ? 1 + KC : 1;     // VecT entries per spill slot
     size_t code, cval, x, spill, tape, grad, red, total;
