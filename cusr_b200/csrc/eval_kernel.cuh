@@ -18,12 +18,15 @@
 //     over V samples and the V chains give independent instructions);
 //   * the forward and reverse programs (program.h; warp-uniform, every opcode specialised so
 //     each case is straight-line code) and the constants sit in shared memory; each thread's
-//     spill stack, reverse tape, gradient rows and input row are private shared-memory
-//     columns laid out [slot][thread] (conflict-free, no block barriers inside an item);
-//   * the normal-equation sums for K <= 16 live in registers (KC = constant-count class,
-//     rows >= K are skipped with warp-uniform branches); for K in 17..32 each warp builds the
-//     (K+1)x(K+1) Gram matrix of [g; r] from a padded shared-memory tile, lanes owning
-//     entries.
+//     spill stack, reverse tape and input row are private shared-memory columns laid out
+//     [slot][thread] (conflict-free, no block barriers inside an item);
+//   * the gradient rows (df/dc_k over the thread's samples) and the residual row are written
+//     into tape slots the reverse program no longer needs (the compiler's row table names
+//     them), so they take no shared memory of their own;
+//   * each warp forms the (K+1)x(K+1) Gram matrix of [g; r] over its samples on the fp64
+//     tensor cores, straight from those rows; its packed lower triangle is the partial layout
+//     (JtJ, Jtr, sum r^2). KC = constant-count class of the bin (K <= KC); KC = 1, 2 run the
+//     forward-mode tangent sweep instead, with the sums in registers.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -65,21 +68,16 @@ __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) 
 // Shared-memory layout of one block; the host sizes the launch with the same function.
 // KC = 1, 2: forward-mode classes (tangents in registers, no tape, no gradient rows; a spill
 // slot holds the value and its KC tangents).
-// KC >= 4 with CUSR_JTJ_DMMA: the normal equations come from fp64 tensor-core products of
-// the gradient rows (+ residual row), so the rows get a bank-spreading pad (stride = 4 mod 32
-// banks: the eight fragment rows of a load land in distinct banks).
-#ifndef CUSR_JTJ_DMMA
-#define CUSR_JTJ_DMMA 1
-#endif
+// KC >= 4: reverse mode; a tape slot is NT VecT entries plus a pad of 4 elements of T, so
+// that a slot used as a gradient row starts 4 banks (fp32) further on than the slot before:
+// the eight rows of a tensor-core fragment load land in distinct banks when the compiler
+// gives them distinct slot residues mod 8.
 template <typename T, int V, int NT, int KC>
 struct EvalSmem {
-    static constexpr bool kBig = KC > 16;
     static constexpr bool kFwd = KC <= 2;
-    static constexpr bool kMma = CUSR_JTJ_DMMA && !kFwd;
-    static constexpr int kGStride = NT * V + (kMma ? 4 : (kBig ? 1 : 0));   // row stride (T)
-    static constexpr int kGRows = kFwd ? 0 : ((kBig || kMma) ? KC + 1 : KC);   // + residual
+    static constexpr int kTapeStride = NT + 4 / V;            // VecT entries per tape slot
     static constexpr int kSpillWords = kFwd ? 1 + KC : 1;     // VecT entries per spill slot
-    size_t code, cval, x, spill, tape, grad, red, total;
+    size_t code, cval, x, spill, tape, red, total;
     __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
                                  bool tape_in_smem = true) {
         size_t o = 0;
@@ -87,8 +85,8 @@ struct EvalSmem {
         cval = o;  o += align16((size_t)CO_MAX_K * sizeof(T));
         x = o;     o += align16((size_t)n_vars * NT * V * 4);
         spill = o; o += align16((size_t)spill_cap * kSpillWords * NT * V * sizeof(T));
-        tape = o;  o += (tape_in_smem && !kFwd) ? align16((size_t)tape_cap * NT * V * sizeof(T)) : 0;
-        grad = o;  o += align16((size_t)kGRows * kGStride * sizeof(T));
+        tape = o;
+        o += (tape_in_smem && !kFwd) ? align16((size_t)tape_cap * kTapeStride * V * sizeof(T)) : 0;
         red = o;   o += align16((size_t)(NT / 32) * nblock_size(KC) * sizeof(T));
         total = o;
     }
@@ -119,6 +117,7 @@ __device__ __forceinline__ void fwd_bin(uint32_t w, const T *__restrict__ c_s,
                                         const VecF<V> *__restrict__ xt,
                                         const VecT<T, V> *__restrict__ sp,
                                         VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
+    constexpr int TSTR = NT + 4 / V;   // tape slot stride (EvalSmem::kTapeStride)
     T s[V];
     if constexpr (MODE == M_VAR) {
         const VecF<V> xv = xt[w_idx(w) * NT];
@@ -141,16 +140,16 @@ __device__ __forceinline__ void fwd_bin(uint32_t w, const T *__restrict__ c_s,
         const int ts = (int)w_ts(w);
         if constexpr (OP == OP_MUL) {
             if constexpr (MODE == M_CONST) {
-                tp[ts * NT] = pack<T, V>(ds);
+                tp[ts * TSTR] = pack<T, V>(ds);
             } else if constexpr (MODE == M_POP) {
-                tp[ts * NT] = pack<T, V>(dt);
-                tp[(ts + 1) * NT] = pack<T, V>(ds);
+                tp[ts * TSTR] = pack<T, V>(dt);
+                tp[(ts + 1) * TSTR] = pack<T, V>(ds);
             }
         } else if constexpr (OP == OP_DIV || OP == OP_POW || OP == OP_POWABS) {
-            tp[ts * NT] = pack<T, V>(dt);
-            if constexpr (MODE != M_VAR) tp[(ts + 1) * NT] = pack<T, V>(ds);
+            tp[ts * TSTR] = pack<T, V>(dt);
+            if constexpr (MODE != M_VAR) tp[(ts + 1) * TSTR] = pack<T, V>(ds);
         } else if constexpr (OP == OP_MAX || OP == OP_MIN) {
-            tp[ts * NT] = pack<T, V>(dt);
+            tp[ts * TSTR] = pack<T, V>(dt);
         }
     }
     CUSR_FOR_V tos[j] = o[j];
@@ -158,13 +157,14 @@ __device__ __forceinline__ void fwd_bin(uint32_t w, const T *__restrict__ c_s,
 
 template <typename T, int V, int NT, bool GRAD, uint32_t OP>
 __device__ __forceinline__ void fwd_un(uint32_t w, VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
+    constexpr int TSTR = NT + 4 / V;
     T d[V];
     CUSR_FOR_V {
         T r;
         unary_op<T>(OP, tos[j], r, d[j]);
         tos[j] = r;
     }
-    if constexpr (GRAD && OP != OP_NEG && OP != OP_UZERO) tp[w_ts(w) * NT] = pack<T, V>(d);
+    if constexpr (GRAD && OP != OP_NEG && OP != OP_UZERO) tp[w_ts(w) * TSTR] = pack<T, V>(d);
 }
 
 template <typename T, int V, int NT, bool GRAD>
@@ -351,42 +351,44 @@ __device__ __forceinline__ void tangent_sweep(const uint32_t *__restrict__ code,
     }
 }
 
-// gradient row access: [k][thread*V + j], rows padded in the cooperative (big-K) layout
-template <typename T, int V, int GSTRIDE>
-__device__ __forceinline__ void grad_put(T *__restrict__ gt, int k, const T (&a)[V],
-                                         bool unique) {
-    T *row = gt + k * GSTRIDE;
-    if (unique) {
-        CUSR_FOR_V row[j] = a[j];
+// gradient row write: tape column entry `slot` of this thread (stride TS), stored, or added
+// to for a constant that occurs more than once (B_ACC)
+template <typename T, int V, int TS>
+__device__ __forceinline__ void row_put(VecT<T, V> *tp, uint32_t slot, const T (&a)[V],
+                                        uint32_t w) {
+    VecT<T, V> *q = tp + (int)slot * TS;
+    if (w & B_ACC) {
+        VecT<T, V> o = *q;
+        CUSR_FOR_V o.v[j] += a[j];
+        *q = o;
     } else {
-        CUSR_FOR_V row[j] += a[j];
+        *q = pack<T, V>(a);
     }
 }
 
 // ---------------------------------------------------------------------------------------
-// Reverse sweep over the reverse program: adjoints from the root to the leaves; gradient
-// row k receives df/dc_k (gt = g_s + tid * V).
+// Reverse sweep over the reverse program: adjoints from the root to the leaves; the gradient
+// row of constant k (df/dc_k) is written to the tape slot the instruction names.
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int NT, int GSTRIDE>
+template <typename T, int V, int NT>
 __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code, int n,
                                               const T *__restrict__ c_s,
                                               const VecF<V> *__restrict__ xt,
-                                              VecT<T, V> *__restrict__ sp,
-                                              const VecT<T, V> *__restrict__ tp,
-                                              T *__restrict__ gt, bool unique) {
+                                              VecT<T, V> *__restrict__ sp, VecT<T, V> *tp) {
     typedef VecT<T, V> VT;
+    constexpr int TSTR = NT + 4 / V;
     T adj[V];
     CUSR_FOR_V adj[j] = T(1);
     uint32_t wn = code[0];
     for (int pc = 0; pc < n; ++pc) {
         const uint32_t w = wn;
         wn = code[pc + 1];
-        switch (w_code(w)) {
+        switch (w_bop(w)) {
             case B_GRAD:
-                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
+                row_put<T, V, TSTR>(tp, w_idx(w), adj, w);
                 break;
             case B_GRAD_RESTORE: {
-                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
+                row_put<T, V, TSTR>(tp, w_idx(w), adj, w);
                 const VT t = sp[w_sd(w) * NT];
                 CUSR_FOR_V adj[j] = t.v[j];
                 break;
@@ -399,7 +401,7 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
             case B_GRAD_NEG: {
                 T a[V];
                 CUSR_FOR_V a[j] = -adj[j];
-                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                row_put<T, V, TSTR>(tp, w_idx(w), a, w);
                 break;
             }
             case B_SPILL:
@@ -415,7 +417,7 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
                 CUSR_FOR_V adj[j] = -adj[j];
                 break;
             case B_GRAD_THEN_NEG:
-                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), adj, unique);
+                row_put<T, V, TSTR>(tp, w_idx(w), adj, w);
                 CUSR_FOR_V adj[j] = -adj[j];
                 break;
             case B_SPILL_THEN_NEG:
@@ -428,34 +430,34 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
                 break;
             }
             case B_SCALE_T0: {
-                const VT t0 = tp[w_ts(w) * NT];
+                const VT t0 = tp[w_ts(w) * TSTR];
                 CUSR_FOR_V adj[j] = safe_mul(adj[j], t0.v[j]);
                 break;
             }
             case B_MULC: {
-                const VT t0 = tp[w_ts(w) * NT];
+                const VT t0 = tp[w_ts(w) * TSTR];
                 const T cv = c_s[w_idx(w)];
                 T a[V];
                 CUSR_FOR_V { a[j] = safe_mul(adj[j], t0.v[j]); adj[j] = safe_mul(adj[j], cv); }
-                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                row_put<T, V, TSTR>(tp, w_sd(w), a, w);
                 break;
             }
             case B_GRAD_T1_T0:
             case B_SPILL_T1_T0: {
                 const int ts = (int)w_ts(w);
-                const VT t0 = tp[ts * NT], t1 = tp[(ts + 1) * NT];
+                const VT t0 = tp[ts * TSTR], t1 = tp[(ts + 1) * TSTR];
                 T a[V];
                 CUSR_FOR_V { a[j] = safe_mul(adj[j], t1.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
-                if (w_code(w) == B_GRAD_T1_T0) grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                if (w_bop(w) == B_GRAD_T1_T0) row_put<T, V, TSTR>(tp, w_idx(w), a, w);
                 else sp[w_sd(w) * NT] = pack<T, V>(a);
                 break;
             }
             case B_GRAD_1MT0_T0:
             case B_SPILL_1MT0_T0: {
-                const VT t0 = tp[w_ts(w) * NT];
+                const VT t0 = tp[w_ts(w) * TSTR];
                 T a[V];
                 CUSR_FOR_V { a[j] = safe_mul(adj[j], T(1) - t0.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
-                if (w_code(w) == B_GRAD_1MT0_T0) grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                if (w_bop(w) == B_GRAD_1MT0_T0) row_put<T, V, TSTR>(tp, w_idx(w), a, w);
                 else sp[w_sd(w) * NT] = pack<T, V>(a);
                 break;
             }
@@ -465,7 +467,7 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
             case B_GRAD_ZERO: {
                 T a[V];
                 CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
-                grad_put<T, V, GSTRIDE>(gt, (int)w_idx(w), a, unique);
+                row_put<T, V, TSTR>(tp, w_idx(w), a, w);
                 break;
             }
             case B_SPILL_ZERO: {
@@ -475,13 +477,19 @@ __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code,
                 break;
             }
             case B_SCALE2_T: {
-                const VT t0 = tp[w_ts(w) * NT], t1 = tp[w_idx(w) * NT];
+                const VT t0 = tp[w_ts(w) * TSTR], t1 = tp[w_idx(w) * TSTR];
                 CUSR_FOR_V adj[j] = safe_mul(safe_mul(adj[j], t0.v[j]), t1.v[j]);
                 break;
             }
             case B_SCALE_1MT0: {
-                const VT t0 = tp[w_ts(w) * NT];
+                const VT t0 = tp[w_ts(w) * TSTR];
                 CUSR_FOR_V adj[j] = safe_mul(adj[j], T(1) - t0.v[j]);
+                break;
+            }
+            case B_ROW_ZERO: {
+                T a[V];
+                CUSR_FOR_V a[j] = T(0);
+                tp[w_idx(w) * TSTR] = pack<T, V>(a);
                 break;
             }
             default:
@@ -512,20 +520,23 @@ __device__ __forceinline__ void dmma_884(double (&c)[2], double a, double b) {
 //         --use_fast_math flags (approximate transcendentals, division and square root,
 //         denormals flushed); the source is the same, only the name differs
 // ---------------------------------------------------------------------------------------
+// Register budget: fp32 classes K <= 16 and the value-only pass are held to 64 registers per
+// thread (eight 128-thread blocks per SM, as many as shared memory allows for the common tape
+// sizes); the K <= 32 class keeps its 15 accumulator tiles in registers at four blocks; fp64
+// (twice the shared memory per thread) is held to six and two blocks.
 template <typename T, int V, int NT, int KC, bool GRAD, bool TG, bool FAST>
-__global__ void __launch_bounds__(NT)
+__global__ void __launch_bounds__(
+    NT, (!GRAD ? 1024 : sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : 768)) / NT)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;
-    constexpr bool kBig = L::kBig;
-    constexpr bool FWD = GRAD && L::kFwd;   // forward-mode tangents (KC = 1, 2)
-    constexpr bool kMma = GRAD && L::kMma;  // normal equations on the fp64 tensor cores
-    constexpr int NTL = kMma ? (KC + 1 + 7) / 8 : 1;   // 8-row tiles of [g; r]
-    constexpr int NTILE = NTL * (NTL + 1) / 2;         // lower-triangle tiles
-    constexpr int GS = L::kGStride;
+    constexpr bool FWD = GRAD && L::kFwd;    // forward-mode tangents (KC = 1, 2)
+    constexpr bool REV = GRAD && !L::kFwd;   // reverse sweep + tensor-core normal equations
+    constexpr int NTL = REV ? (KC + 1 + 7) / 8 : 1;   // 8-row tiles of [g; r]
+    constexpr int NTILE = NTL * (NTL + 1) / 2;        // lower-triangle tiles
+    constexpr int TSTR = L::kTapeStride;              // VecT entries per tape slot
     constexpr int ROUND = NT * V;
     constexpr int NW = NT / 32;
     constexpr int NTRI = KC * (KC + 1) / 2;
-    constexpr int NACC = kBig ? (nblock_size(32) + 31) / 32 : 1;  // entries per lane (big-K)
 
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_item;
@@ -534,13 +545,13 @@ lm_eval_kernel(const EvalParams<T> p) {
     T *c_s = reinterpret_cast<T *>(smem + lay.cval);
     VecF<V> *x_s = reinterpret_cast<VecF<V> *>(smem + lay.x);
     VecT<T, V> *spill_s = reinterpret_cast<VecT<T, V> *>(smem + lay.spill);
-    // reverse tape: private shared-memory columns, or (TG, trees whose tape would not fit
+    // reverse tape (and, in slots the reverse sweep has finished with, the gradient and
+    // residual rows): private shared-memory columns, or (TG, trees whose tape would not fit
     // beside a second resident block) this block's slab of a global scratch buffer, read
-    // back by the same thread and served from L1/L2
+    // back by the threads of the same warp and served from L1/L2
     VecT<T, V> *tape_s =
-        TG ? reinterpret_cast<VecT<T, V> *>(p.tape_g) + (int64_t)blockIdx.x * p.tape_cap * NT
+        TG ? reinterpret_cast<VecT<T, V> *>(p.tape_g) + (int64_t)blockIdx.x * p.tape_cap * TSTR
            : reinterpret_cast<VecT<T, V> *>(smem + lay.tape);
-    T *g_s = reinterpret_cast<T *>(smem + lay.grad);
     T *red_s = reinterpret_cast<T *>(smem + lay.red);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -548,7 +559,6 @@ lm_eval_kernel(const EvalParams<T> p) {
     VecF<V> *xt = x_s + tid;
     VecT<T, V> *spt = spill_s + tid;
     VecT<T, V> *tpt = tape_s + tid;
-    T *gt = g_s + tid * V;
 
     for (;;) {
         if (tid == 0) s_item = atomicAdd(p.counter, 1);
@@ -558,46 +568,39 @@ lm_eval_kernel(const EvalParams<T> p) {
         const int2 wi = p.items[it];
         const TreeDesc d = p.desc[wi.x];
         const int K = d.K;
-        const bool unique = (d.flags & TD_UNIQUE_CONST) != 0;
         const bool grad = GRAD && K > 0;
-        // the reverse program follows the forward one (forward mode needs only the latter)
-        const int n_code = FWD ? d.n_instr : d.n_instr + d.n_bwd;
+        // forward program; for reverse mode the reverse program and its row table follow
+        const int n_code = REV ? d.n_instr + d.n_bwd + row_table_words(K) : d.n_instr;
         for (int i = tid; i < n_code; i += NT) code_s[i] = p.code[d.code_off + i];
-        if (tid == 0) code_s[n_code] = 0u;   // prefetch pad after the reverse program
+        if (tid == 0) code_s[n_code] = 0u;   // prefetch pad after the last staged word
         for (int i = tid; i < K; i += NT) c_s[i] = p.c[d.c_off + i];
         __syncthreads();
         const uint32_t *bcode_s = code_s + d.n_instr;
+        // tape slot of row r (r < K: gradient of constant r, r = K: residual)
+        const uint8_t *rtab = reinterpret_cast<const uint8_t *>(bcode_s + d.n_bwd);
 
-        // accumulators (register path) / lane-owned Gram entries (big-K path) / fp64
-        // tensor-core fragments of the [g; r] Gram matrix (kMma)
-        T acc[(kBig || kMma) ? 1 : (NTRI > 0 ? NTRI : 1)];
-        T jtr[(kBig || kMma) ? 1 : KC];
-        double cm[kMma ? NTILE : 1][2];
+        // forward mode: sums in registers; reverse mode: fp64 tensor-core fragments of the
+        // [g; r] Gram matrix, each lane loading the rows 8 t + lane / 4 of the tiles
+        T acc[FWD ? NTRI : 1];
+        T jtr[FWD ? KC : 1];
+        double cm[REV ? NTILE : 1][2];
+        int roff[NTL];
 #pragma unroll
-        for (int t = 0; t < (kMma ? NTILE : 1); ++t) cm[t][0] = cm[t][1] = 0.0;
-        T lsum = T(0);
-        T bacc[NACC];
-        int boff_i[NACC], boff_l[NACC];
-        if constexpr (kMma) {
-        } else if constexpr (!kBig) {
+        for (int t = 0; t < (REV ? NTILE : 1); ++t) cm[t][0] = cm[t][1] = 0.0;
+        if constexpr (FWD) {
 #pragma unroll
             for (int e = 0; e < NTRI; ++e) acc[e] = T(0);
 #pragma unroll
             for (int e = 0; e < KC; ++e) jtr[e] = T(0);
-        } else {
-            // lane owns entries e = lane + 32u of the packed (K+1)x(K+1) lower triangle
-            const int E = nblock_size(K);
+        }
+        if constexpr (REV) {
 #pragma unroll
-            for (int u = 0; u < NACC; ++u) {
-                bacc[u] = T(0);
-                int e = lane + 32 * u, i = 0;
-                if (e >= E) e = -1;
-                if (e >= 0) { while ((i + 1) * (i + 2) / 2 <= e) ++i; }
-                const int l = (e >= 0) ? e - i * (i + 1) / 2 : 0;
-                boff_i[u] = (e >= 0) ? i * GS : -1;
-                boff_l[u] = l * GS;
+            for (int t = 0; t < NTL; ++t) {
+                const int row = 8 * t + (lane >> 2);
+                roff[t] = (grad && row <= K) ? (int)rtab[row] * TSTR * V : -1;
             }
         }
+        T lsum = T(0);
 
         const int64_t s0 = (int64_t)wi.y * p.chunk;
         const int64_t s_end = (int64_t)p.N < s0 + p.chunk ? (int64_t)p.N : s0 + p.chunk;
@@ -647,91 +650,43 @@ lm_eval_kernel(const EvalParams<T> p) {
                 }
               }
             } else if (grad) {
-                if (!unique) {
-                    for (int k = 0; k < K; ++k) {
-                        CUSR_FOR_V gt[k * GS + j] = T(0);
-                    }
-                }
-                reverse_sweep<T, V, NT, GS>(bcode_s, d.n_bwd, c_s, xt, spt, tpt, gt, unique);
+                reverse_sweep<T, V, NT>(bcode_s, d.n_bwd, c_s, xt, spt, tpt);
                 if (p.jac) {
                     T *jrow = p.jac + (int64_t)wi.x * p.jac_kmax * p.N;
                     for (int k = 0; k < K; ++k) {
-                        CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = gt[k * GS + j];
+                        const VecT<T, V> g = tpt[(int)rtab[k] * TSTR];
+                        CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = g.v[j];
                     }
                 }
-                if constexpr (kMma) {
-                    // residual as row K, zero gradients of samples past N; then the warp
-                    // accumulates the (K+1)^2 Gram matrix of its 32 V samples as 8x8 fp64
-                    // tiles, four samples per product
-                    CUSR_FOR_V {
-                        gt[K * GS + j] = r[j];
-                        if (!valid[j])
-                            for (int k = 0; k < K; ++k) gt[k * GS + j] = T(0);
+                // residual row; gradients of samples past N are zeroed (only the last round
+                // of a tree's last chunk has any)
+                tpt[(int)rtab[K] * TSTR] = pack<T, V>(r);
+                if (si + V > p.N) {
+                    for (int k = 0; k < K; ++k) {
+                        VecT<T, V> *q = tpt + (int)rtab[k] * TSTR;
+                        VecT<T, V> g = *q;
+                        CUSR_FOR_V if (!valid[j]) g.v[j] = T(0);
+                        *q = g;
                     }
-                    __syncwarp();
-                    const T *gw = g_s + warp * 32 * V + (lane & 3);
-                    const int grp = lane >> 2;
+                }
+                __syncwarp();
+                // the warp accumulates the (K+1)^2 Gram matrix of its 32 V samples as 8x8
+                // fp64 tiles, four samples per product
+                const T *tw = reinterpret_cast<const T *>(tape_s) + warp * 32 * V + (lane & 3);
 #pragma unroll 2
-                    for (int s4 = 0; s4 < 32 * V; s4 += 4) {
-                        double a[NTL];
+                for (int s4 = 0; s4 < 32 * V; s4 += 4) {
+                    double a[NTL];
 #pragma unroll
-                        for (int t = 0; t < NTL; ++t) {
-                            const int row = 8 * t + grp;
-                            a[t] = row <= K ? (double)gw[row * GS + s4] : 0.0;
-                        }
-                        int c = 0;
+                    for (int t = 0; t < NTL; ++t) a[t] = roff[t] >= 0 ? (double)tw[roff[t] + s4] : 0.0;
+                    int c = 0;
 #pragma unroll
-                        for (int ti = 0; ti < NTL; ++ti) {
+                    for (int ti = 0; ti < NTL; ++ti) {
 #pragma unroll
-                            for (int tl = 0; tl <= ti; ++tl) dmma_884(cm[c++], a[ti], a[tl]);
-                        }
+                        for (int tl = 0; tl <= ti; ++tl) dmma_884(cm[c++], a[ti], a[tl]);
                     }
-                    __syncwarp();
-                } else if constexpr (!kBig) {
-                    CUSR_FOR_V {
-                        T g[KC];
-#pragma unroll
-                        for (int k = 0; k < KC; ++k)
-                            if (k < K) g[k] = valid[j] ? gt[k * GS + j] : T(0);
-#pragma unroll
-                        for (int i = 0; i < KC; ++i) {
-                            if (i < K) {
-                                jtr[i] += g[i] * r[j];
-#pragma unroll
-                                for (int l = 0; l <= i; ++l) acc[i * (i + 1) / 2 + l] += g[i] * g[l];
-                            }
-                        }
-                    }
-                } else {
-                    // stage the residual as row K, zero invalid samples' gradients
-                    CUSR_FOR_V {
-                        gt[K * GS + j] = r[j];
-                        if (!valid[j])
-                            for (int k = 0; k < K; ++k) gt[k * GS + j] = T(0);
-                    }
-                    __syncwarp();
-                    // entry by entry over the warp's 32 * V samples; only the ceil(E / 32)
-                    // entry groups this tree has (warp-uniform bound: a K = 17 tree does a
-                    // third of the work of K = 32); four partial sums per entry for ILP
-                    const int sbase = warp * 32 * V;
-                    const int nu = (nblock_size(K) + 31) >> 5;
-#pragma unroll
-                    for (int u = 0; u < NACC; ++u) {
-                        if (u < nu && boff_i[u] >= 0) {
-                            const T *gi = g_s + boff_i[u] + sbase, *gl = g_s + boff_l[u] + sbase;
-                            T a0 = T(0), a1 = T(0), a2 = T(0), a3 = T(0);
-#pragma unroll 4
-                            for (int s = 0; s < 32 * V; s += 4) {
-                                a0 += gi[s] * gl[s];
-                                a1 += gi[s + 1] * gl[s + 1];
-                                a2 += gi[s + 2] * gl[s + 2];
-                                a3 += gi[s + 3] * gl[s + 3];
-                            }
-                            bacc[u] += (a0 + a1) + (a2 + a3);
-                        }
-                    }
-                    __syncwarp();
                 }
+                // the next round's forward sweep overwrites these slots
+                __syncwarp();
             }
         }
 
@@ -748,7 +703,7 @@ lm_eval_kernel(const EvalParams<T> p) {
                 for (int w = 0; w < NW; ++w) s += red_s[w];
                 dst[nblock_size(K) - 1] = s;
             }
-        } else if constexpr (kMma) {
+        } else if constexpr (REV) {
             // packed (K+1)x(K+1) lower triangle == the partial layout (JtJ, Jtr, sum r^2)
             T *rw = red_s + warp * nblock_size(KC);
             const int grp = lane >> 2, q2 = 2 * (lane & 3);
@@ -772,7 +727,7 @@ lm_eval_kernel(const EvalParams<T> p) {
                 for (int w = 0; w < NW; ++w) s += red_s[w * nblock_size(KC) + e];
                 dst[e] = s;
             }
-        } else if constexpr (!kBig) {
+        } else {
             T *rw = red_s + warp * nblock_size(KC);
 #pragma unroll
             for (int i = 0; i < KC; ++i) {
@@ -794,18 +749,6 @@ lm_eval_kernel(const EvalParams<T> p) {
             }
             lsum = warp_sum(lsum);
             if (lane == 0) rw[tri + K] = lsum;
-            __syncthreads();
-            for (int e = tid; e < P; e += NT) {
-                T s = T(0);
-#pragma unroll
-                for (int w = 0; w < NW; ++w) s += red_s[w * nblock_size(KC) + e];
-                dst[e] = s;
-            }
-        } else {
-            T *rw = red_s + warp * nblock_size(KC);
-#pragma unroll
-            for (int u = 0; u < NACC; ++u)
-                if (boff_i[u] >= 0) rw[lane + 32 * u] = bacc[u];
             __syncthreads();
             for (int e = tid; e < P; e += NT) {
                 T s = T(0);

@@ -257,6 +257,92 @@ struct Gen {
     }
 };
 
+// Tape slots a reverse word reads.
+int reverse_reads(uint32_t w, uint32_t (&s)[2]) {
+    switch (w_bop(w)) {
+        case B_SCALE_T0: case B_MULC: case B_GRAD_1MT0_T0: case B_SPILL_1MT0_T0:
+        case B_SCALE_1MT0:
+            s[0] = w_ts(w);
+            return 1;
+        case B_GRAD_T1_T0: case B_SPILL_T1_T0:
+            s[0] = w_ts(w); s[1] = w_ts(w) + 1;
+            return 2;
+        case B_SCALE2_T:
+            s[0] = w_ts(w); s[1] = w_idx(w);
+            return 2;
+        default:
+            return 0;
+    }
+}
+
+// Gradient rows in dead tape slots. A tape slot is dead once the reverse program has read it
+// for the last time; slots it never reads (the dump slots of inactive nodes, the unused
+// partial of a node with one active operand) are dead from the start. Row k goes to a slot
+// that is dead at the reverse program's first write of constant k — a word reads its tape
+// entries before it writes its row, and every thread touches only its own column — and the
+// residual row and one shared zero row (constants that do not occur in the tree) take slots
+// that are dead at the end. A row finds a new slot past the tape only when no dead one is
+// left. Among dead slots the lowest whose residue mod 8 no other row of the same 8-row group
+// holds is taken: the rows are padded so that residues map to distinct shared-memory banks of
+// the tensor-core fragment loads. Rewrites the row writes of `rev` (slot fields, B_ACC for
+// the second and later writes of a constant), appends B_ROW_ZERO when a zero row is needed,
+// and returns the slot of each row (K + 1 entries, the residual last) and the slot count.
+bool place_rows(std::vector<uint32_t> &rev, int n_tape, int K, std::vector<int> &row_slot,
+                int &n_slots) {
+    const int P = (int)rev.size();
+    std::vector<int> last(256, -1);            // last reverse word reading the slot
+    for (int p = 0; p < P; ++p) {
+        uint32_t s[2];
+        const int n = reverse_reads(rev[(size_t)p], s);
+        for (int i = 0; i < n; ++i) last[s[i]] = p;
+    }
+    std::vector<char> taken(256, 0);
+    std::vector<uint8_t> group_res((size_t)K / 8 + 1, 0);   // residues mod 8 used per 8-row group
+    n_slots = n_tape;
+    auto pick = [&](int row, int p) -> int {   // p = -1: dead at the end
+        int best = -1;
+        for (int s = 0; s < n_tape; ++s) {
+            if (taken[(size_t)s] || (p >= 0 && last[(size_t)s] > p)) continue;
+            if (!(group_res[(size_t)row / 8] & (1u << (s & 7)))) { best = s; break; }
+            if (best < 0) best = s;
+        }
+        if (best < 0) best = n_slots++;
+        if (best > PROG_MAX_TAPE) return -1;
+        taken[(size_t)best] = 1;
+        group_res[(size_t)row / 8] |= (uint8_t)(1u << (best & 7));
+        return best;
+    };
+    row_slot.assign((size_t)K + 1, -1);
+    for (int p = 0; p < P; ++p) {
+        uint32_t w = rev[(size_t)p];
+        const uint32_t b = w_bop(w);
+        if (!is_row_write(b)) continue;
+        const int k = (int)w_idx(w);
+        bool acc = true;
+        if (row_slot[(size_t)k] < 0) {
+            row_slot[(size_t)k] = pick(k, p);
+            if (row_slot[(size_t)k] < 0) return false;
+            acc = false;
+        }
+        const uint32_t code = b | (acc ? B_ACC : 0u);
+        const uint32_t slot = (uint32_t)row_slot[(size_t)k];
+        w = b == B_MULC ? enc(code, w_idx(w), slot, w_ts(w)) : enc(code, slot, w_sd(w), w_ts(w));
+        rev[(size_t)p] = w;
+    }
+    int zero = -1;
+    for (int k = 0; k < K; ++k) {
+        if (row_slot[(size_t)k] >= 0) continue;
+        if (zero < 0) {
+            zero = pick(k, -1);
+            if (zero < 0) return false;
+            rev.push_back(enc(B_ROW_ZERO, (uint32_t)zero, 0, 0));
+        }
+        row_slot[(size_t)k] = zero;
+    }
+    row_slot[(size_t)K] = pick(K, -1);
+    return row_slot[(size_t)K] >= 0;
+}
+
 }  // namespace
 
 int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, int K,
@@ -346,13 +432,28 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
     if (g.overflow) { code.resize((size_t)ct.code_off); return CO_ERR_BOUNDS; }
     ct.n_instr = (int32_t)code.size() - ct.code_off;
     ct.bcode_off = (int32_t)code.size();
+    int n_slots = g.tape;
+    std::vector<int> row_slot;
     {
         std::vector<uint32_t> rev;
         g.rev = &rev;
         g.rgen(0, false, 0);
+        if (!place_rows(rev, g.tape, K, row_slot, n_slots)) {
+            code.resize((size_t)ct.code_off);
+            return CO_ERR_BOUNDS;
+        }
         code.insert(code.end(), rev.begin(), rev.end());
     }
     ct.n_bwd = (int32_t)code.size() - ct.bcode_off;
+    // the row table follows the reverse program
+    for (int i = 0; i < row_table_words(K); ++i) {
+        uint32_t t = 0;
+        for (int b = 0; b < 4; ++b) {
+            const int r = 4 * i + b;
+            if (r <= K) t |= (uint32_t)row_slot[(size_t)r] << (8 * b);
+        }
+        code.push_back(t);
+    }
     // the interpreter dispatches without a bounds check: every word must be a known opcode
     for (int i = 0; i < ct.n_instr; ++i)
         if (!valid_forward_code(w_code(code[(size_t)(ct.code_off + i)]))) return CO_ERR_BADTREE;
@@ -361,7 +462,7 @@ int compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n, i
     ct.n_nodes = n;
     ct.K = K;
     ct.n_spill = g.max_dep;
-    ct.n_tape = g.tape;
+    ct.n_tape = n_slots;
     ct.unique_const = unique;
     return CO_OK;
 }
@@ -451,7 +552,7 @@ int compile_population(const PopHeader *h, const int32_t *nt, const float *nv,
         out->code.insert(out->code.end(), codes[(size_t)p].begin(), codes[(size_t)p].end());
     }
     for (const CompiledTree &ct : out->trees) {
-        out->max_instr = std::max(out->max_instr, ct.n_instr + ct.n_bwd);
+        out->max_instr = std::max(out->max_instr, ct.n_instr + ct.n_bwd + row_table_words(ct.K));
         out->max_spill = std::max(out->max_spill, ct.n_spill);
         out->max_tape = std::max(out->max_tape, ct.n_tape);
         out->max_K = std::max(out->max_K, ct.K);
@@ -538,7 +639,7 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         }
         Bin &b = out->bins[(size_t)bin_of_class[key]];
         b.trees.push_back(m);
-        b.max_instr = std::max(b.max_instr, ct.n_instr + ct.n_bwd);
+        b.max_instr = std::max(b.max_instr, ct.n_instr + ct.n_bwd + row_table_words(ct.K));
         b.max_spill = std::max(b.max_spill, ct.n_spill);
         b.max_tape = std::max(b.max_tape, ct.n_tape);
         b.max_items += n_chunks;
@@ -565,8 +666,8 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
 
 double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, int n_bwd,
                          const double *x, const double *c, int K, double *grad) {
-    double spill[PROG_MAX_SPILL + 1];
-    double tape[PROG_MAX_TAPE + 2];
+    double spill[PROG_MAX_SPILL + 1] = {};
+    double tape[PROG_MAX_TAPE + 2] = {};
     double tos = 0.0;
     for (int pc = 0; pc < n_fwd; ++pc) {
         const uint32_t w = fwd[pc];
@@ -603,37 +704,42 @@ double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, in
     }
     const double value = tos;
     if (!grad) return value;
-    for (int k = 0; k < K; ++k) grad[k] = 0.0;
+    // gradient rows live in tape slots (row table after the reverse program)
     double adj = 1.0;
     for (int pc = 0; pc < n_bwd; ++pc) {
         const uint32_t w = bwd[pc];
         const uint32_t idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
         const double t0 = tape[ts], t1 = tape[ts + 1];
-        switch (w_code(w)) {
-            case B_GRAD: grad[idx] += adj; break;
-            case B_GRAD_RESTORE: grad[idx] += adj; adj = spill[sd]; break;
+        const bool acc = (w_code(w) & B_ACC) != 0;
+        auto row = [&](uint32_t slot, double v) { tape[slot] = acc ? tape[slot] + v : v; };
+        switch (w_bop(w)) {
+            case B_GRAD: row(idx, adj); break;
+            case B_GRAD_RESTORE: row(idx, adj); adj = spill[sd]; break;
             case B_RESTORE: adj = spill[sd]; break;
-            case B_GRAD_NEG: grad[idx] += -adj; break;
+            case B_GRAD_NEG: row(idx, -adj); break;
             case B_SPILL: spill[sd] = adj; break;
             case B_SPILL_NEG: spill[sd] = -adj; break;
             case B_NEG: adj = -adj; break;
-            case B_GRAD_THEN_NEG: grad[idx] += adj; adj = -adj; break;
+            case B_GRAD_THEN_NEG: row(idx, adj); adj = -adj; break;
             case B_SPILL_THEN_NEG: spill[sd] = adj; adj = -adj; break;
             case B_SCALE_X: adj = safe_mul(adj, x[idx]); break;
             case B_SCALE_T0: adj = safe_mul(adj, t0); break;
-            case B_MULC: grad[idx] += safe_mul(adj, t0); adj = safe_mul(adj, c[idx]); break;
-            case B_GRAD_T1_T0: grad[idx] += safe_mul(adj, t1); adj = safe_mul(adj, t0); break;
+            case B_MULC: row(sd, safe_mul(adj, t0)); adj = safe_mul(adj, c[idx]); break;
+            case B_GRAD_T1_T0: row(idx, safe_mul(adj, t1)); adj = safe_mul(adj, t0); break;
             case B_SPILL_T1_T0: spill[sd] = safe_mul(adj, t1); adj = safe_mul(adj, t0); break;
-            case B_GRAD_1MT0_T0: grad[idx] += safe_mul(adj, 1.0 - t0); adj = safe_mul(adj, t0); break;
+            case B_GRAD_1MT0_T0: row(idx, safe_mul(adj, 1.0 - t0)); adj = safe_mul(adj, t0); break;
             case B_SPILL_1MT0_T0: spill[sd] = safe_mul(adj, 1.0 - t0); adj = safe_mul(adj, t0); break;
             case B_ZERO: adj = 0.0; break;
-            case B_GRAD_ZERO: adj = 0.0; break;
+            case B_GRAD_ZERO: row(idx, 0.0); adj = 0.0; break;
             case B_SPILL_ZERO: spill[sd] = 0.0; adj = 0.0; break;
             case B_SCALE_1MT0: adj = safe_mul(adj, 1.0 - t0); break;
             case B_SCALE2_T: adj = safe_mul(safe_mul(adj, t0), tape[w_idx(w)]); break;
+            case B_ROW_ZERO: tape[idx] = 0.0; break;
             default: break;
         }
     }
+    const uint32_t *tab = bwd + n_bwd;
+    for (int k = 0; k < K; ++k) grad[k] = tape[(tab[k / 4] >> (8 * (k % 4))) & 255u];
     return value;
 }
 

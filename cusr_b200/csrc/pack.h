@@ -76,7 +76,8 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
                     int fwd_max = 0);
 
 // Reference evaluation of a compiled program on the host (fp64), forward value plus the
-// reverse sweep into grad[0..K). Used by the CPU tests of the compiler.
+// reverse sweep into grad[0..K) (read through the row table that follows the n_bwd reverse
+// words). Used by the CPU tests of the compiler.
 double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, int n_bwd,
                          const double *x, const double *c, int K, double *grad);
 void decode_xop(uint32_t xop, uint32_t &op, uint32_t &mode, uint32_t &swap);

@@ -14,6 +14,11 @@
 //   reverse  — the adjoint sweep, in reverse order, with the instructions that have no reverse
 //              work left out (`+ x`, a leaf load that starts a chain) and every other one
 //              reduced to one of a few specialised adjoint updates.
+//   row table — after the reverse program, K + 1 bytes packed four to a word: the tape slot
+//              holding gradient row k (df/dc_k over the thread's samples), then the slot that
+//              takes the residual row. Gradient rows live in tape slots the reverse program
+//              has already read for the last time (place_rows in pack.cpp), so they need no
+//              storage of their own.
 //
 // Every opcode is specialised by operator, operand source and operand order, so the
 // interpreter's cases are straight-line code.
@@ -23,6 +28,9 @@
 //   [8,16)  idx       variable index or constant rank
 //   [16,24) sd        spill slot
 //   [24,32) ts        first tape slot
+// A reverse instruction that writes a gradient row names the row's tape slot in `idx`
+// (B_MULC, which needs `idx` for the constant, in `sd`); the B_ACC bit of its opcode byte
+// adds to the row instead of storing it (second and later occurrences of a constant).
 #pragma once
 #include <stdint.h>
 
@@ -106,8 +114,18 @@ enum BOp : uint32_t {
     B_SPILL_ZERO,        // spill[sd] <- 0; adj <- 0
     B_SCALE_1MT0,        // adj <- safe(adj, 1 - t0)
     B_SCALE2_T,          // adj <- safe(safe(adj, t0), tape[idx])   (two chained unary nodes)
+    B_ROW_ZERO,          // row[idx] <- 0   (the shared row of constants absent from the tree)
     B_COUNT
 };
+// "grad[k]" above is the gradient row of constant k, held in the tape slot the word names
+constexpr uint32_t B_ACC = 32u;       // opcode-byte flag of a row write: add instead of store
+__host__ __device__ inline uint32_t w_bop(uint32_t w) { return w & 31u; }
+__host__ __device__ inline bool is_row_write(uint32_t b) {
+    return b == B_GRAD || b == B_GRAD_RESTORE || b == B_GRAD_NEG || b == B_GRAD_THEN_NEG ||
+           b == B_MULC || b == B_GRAD_T1_T0 || b == B_GRAD_1MT0_T0 || b == B_GRAD_ZERO;
+}
+// 32-bit words of the row table of a tree with K constants (K + 1 bytes)
+__host__ __device__ constexpr inline int row_table_words(int K) { return (K + 4) / 4; }
 
 constexpr int PROG_MAX_SPILL = 63;   // spill slots
 constexpr int PROG_MAX_TAPE  = 255;  // ts field (+1 for two-slot entries)
@@ -122,7 +140,11 @@ __host__ __device__ inline bool valid_forward_code(uint32_t c) {
                            op == OP_LE || op == OP_GE || op == OP_BZERO;
     return !(unordered && swap);
 }
-__host__ __device__ inline bool valid_reverse_code(uint32_t c) { return c < B_COUNT; }
+__host__ __device__ inline bool valid_reverse_code(uint32_t c) {
+    if (c & ~63u) return false;
+    if ((c & 31u) >= B_COUNT) return false;
+    return !(c & B_ACC) || is_row_write(c & 31u);
+}
 
 // Per-tree descriptor uploaded to the device (64 bytes).
 struct TreeDesc {

@@ -10,14 +10,16 @@ extern "C" {
 #endif
 
 /* Compile one prefix tree (n_nodes nodes, K constants, n_vars inputs) into at most `cap`
- * program words: the forward program followed by the reverse program.
+ * program words: the forward program, the reverse program, then the row table ((K + 4) / 4
+ * words: the tape slot of each gradient row and of the residual row, one byte each).
  * info_out[5] = {n_forward, n_spill, n_tape, unique_const, n_reverse}.
  * Returns CO_OK / CO_ERR_BOUNDS / CO_ERR_BADTREE / CO_ERR_NULLARG (cap too small). */
 int cusr_compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int n_nodes, int K,
                       int n_vars, uint32_t *code_out, int cap, int32_t *info_out);
 
 /* Run a compiled program on the host in fp64 at one sample: returns the value, and writes
- * df/dc_k to grad[0..K) when grad is not NULL (same two programs as the device). */
+ * df/dc_k to grad[0..K) when grad is not NULL (same programs as the device; `bwd` points at
+ * the reverse program, which the row table follows). */
 double cusr_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, int n_bwd,
                          const double *x, const double *c, int K, double *grad);
 

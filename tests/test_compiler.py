@@ -26,15 +26,25 @@ def compile_tree(nt, nv, ci, K, n_vars):
     rc = LIB.cusr_compile_tree(nt.ctypes.data_as(VP), nv.ctypes.data_as(VP), ci.ctypes.data_as(VP),
                                len(nt), int(K), int(n_vars), code.ctypes.data_as(VP), 2048,
                                info.ctypes.data_as(VP))
-    return rc, (code[: info[0]].copy(), code[info[0]: info[0] + info[4]].copy()), info
+    nf, nb = int(info[0]), int(info[4])
+    fwd, bwd = code[:nf].copy(), code[nf:nf + nb].copy()
+    table = code[nf + nb:nf + nb + (int(K) + 4) // 4].copy()
+    return rc, (fwd, bwd, table), info
+
+
+def row_slots(table, K):
+    """Tape slot of each gradient row (K entries) and of the residual row."""
+    b = np.asarray(table, np.uint32).view(np.uint8)
+    return [int(s) for s in b[:K + 1]]
 
 
 def run_program(code, x, c, K):
-    fwd, bwd = code
+    fwd, bwd, table = code
+    rev = np.ascontiguousarray(np.concatenate([bwd, table]), np.uint32)
     x = np.ascontiguousarray(x, np.float64)
     c = np.ascontiguousarray(c if len(c) else [0.0], np.float64)
     g = np.zeros(max(K, 1))
-    v = LIB.cusr_eval_program(fwd.ctypes.data_as(VP), len(fwd), bwd.ctypes.data_as(VP), len(bwd),
+    v = LIB.cusr_eval_program(fwd.ctypes.data_as(VP), len(fwd), rev.ctypes.data_as(VP), len(bwd),
                               x.ctypes.data_as(VP), c.ctypes.data_as(VP), int(K),
                               g.ctypes.data_as(VP))
     return v, g[:K]
@@ -144,9 +154,9 @@ def test_deep_spill_stack():
 def test_reverse_program_drops_no_op_instructions():
     # c0 * x0 + x1: the "+ x1" has no reverse work
     nt, nv, ci = make_tree([("b", 1), ("b", 3), ("c",), ("v", 0), ("v", 1)])
-    rc, (fwd, bwd), info = compile_tree(nt, nv, ci, 1, 2)
+    rc, (fwd, bwd, table), info = compile_tree(nt, nv, ci, 1, 2)
     assert rc == 0 and len(bwd) < len(fwd)
-    v, g = run_program((fwd, bwd), np.array([2.0, 3.0]), np.array([0.5]), 1)
+    v, g = run_program((fwd, bwd, table), np.array([2.0, 3.0]), np.array([0.5]), 1)
     assert v == pytest.approx(4.0) and g[0] == pytest.approx(2.0)
 
 
@@ -184,3 +194,98 @@ def test_program_limits():
     nt, nv, ci = make_tree(nodes)
     rc, _, _ = compile_tree(nt, nv, ci, 0, 1)
     assert rc == co_inproc.CO_ERR_BOUNDS
+
+
+# reverse opcodes (cusr_b200/csrc/program.h, enum BOp) and the row-write flag
+(B_GRAD, B_GRAD_RESTORE, B_RESTORE, B_GRAD_NEG, B_SPILL, B_SPILL_NEG, B_NEG, B_GRAD_THEN_NEG,
+ B_SPILL_THEN_NEG, B_SCALE_X, B_SCALE_T0, B_MULC, B_GRAD_T1_T0, B_SPILL_T1_T0, B_GRAD_1MT0_T0,
+ B_SPILL_1MT0_T0, B_ZERO, B_GRAD_ZERO, B_SPILL_ZERO, B_SCALE_1MT0, B_SCALE2_T, B_ROW_ZERO) = range(22)
+B_ACC = 32
+ROW_WRITES = {B_GRAD, B_GRAD_RESTORE, B_GRAD_NEG, B_GRAD_THEN_NEG, B_MULC, B_GRAD_T1_T0,
+              B_GRAD_1MT0_T0, B_GRAD_ZERO}
+
+
+def tape_reads(w):
+    op, idx, ts = w & 31, (w >> 8) & 255, w >> 24
+    if op in (B_SCALE_T0, B_MULC, B_GRAD_1MT0_T0, B_SPILL_1MT0_T0, B_SCALE_1MT0):
+        return [ts]
+    if op in (B_GRAD_T1_T0, B_SPILL_T1_T0):
+        return [ts, ts + 1]
+    if op == B_SCALE2_T:
+        return [ts, idx]
+    return []
+
+
+def row_of(w):
+    return ((w >> 16) & 255) if (w & 31) == B_MULC else ((w >> 8) & 255)
+
+
+def forward_tape_slots(fwd):
+    """Slots the forward program writes (one past the highest)."""
+    hi = 0
+    for w in fwd:
+        code, ts = int(w) & 255, int(w) >> 24
+        if code >= 8:   # operators; two-slot partials may use ts + 1
+            hi = max(hi, ts + 2)
+    return hi
+
+
+@pytest.mark.parametrize("name", ["metric", "long"])
+def test_gradient_rows_live_in_dead_tape_slots(name):
+    pop = synth.make_config(name, M=300, N=16, seed=3)
+    extra = []
+    for m in range(pop["M"]):
+        nt, nv, ci, _y, K = interp.tree_view(pop, m)
+        if K == 0:
+            continue
+        rc, (fwd, bwd, table), info = compile_tree(nt, nv, ci, K, pop["n_vars"])
+        assert rc == 0
+        slots = row_slots(table, K)
+        n_slots = int(info[2])
+        assert all(s < n_slots for s in slots)
+        bwd = [int(w) for w in bwd]
+        present = sorted({int(k) for k in ci[nt == 1]})
+        # distinct rows for distinct constants, one shared zero row for absent ones, the
+        # residual row apart from all of them
+        grad_slots = {slots[k] for k in present}
+        assert len(grad_slots) == len(present)
+        assert slots[K] not in grad_slots
+        absent = [k for k in range(K) if k not in present]
+        if absent:
+            zero = {slots[k] for k in absent}
+            assert len(zero) == 1 and not (zero & grad_slots) and slots[K] not in zero
+            assert bwd[-1] & 31 == B_ROW_ZERO and (bwd[-1] >> 8) & 255 == slots[absent[0]]
+        # the first write of each row stores, later ones add; a row's slot is never read as
+        # tape after its first write
+        first = {}
+        for p, w in enumerate(bwd):
+            op = w & 31
+            if op in ROW_WRITES:
+                s = row_of(w)
+                assert s in grad_slots
+                if s not in first:
+                    first[s] = p
+                    assert not (w & B_ACC)
+                else:
+                    assert w & B_ACC
+            else:
+                assert not (w & B_ACC)
+        for p, w in enumerate(bwd):
+            for s in tape_reads(w):
+                assert s not in first or p <= first[s], (m, p, s)
+        extra.append(n_slots - forward_tape_slots(fwd))
+    # rows almost always fit in slots the reverse sweep has finished with
+    assert np.mean(extra) < 1.0
+
+
+def test_absent_constant_gets_the_zero_row():
+    # c0 * x0 + c2 with K = 3 (rank 1 unused): its gradient is exactly 0
+    nt, nv, ci = make_tree([("b", 1), ("b", 3), ("c",), ("v", 0), ("c",)])
+    ci = np.array([-1, -1, 0, -1, 2], np.int32)
+    rc, code, info = compile_tree(nt, nv, ci, 3, 1)
+    assert rc == 0
+    fwd, bwd, table = code
+    assert int(bwd[-1]) & 31 == B_ROW_ZERO
+    v, g = run_program(code, np.array([1.5]), np.array([2.0, 7.0, -1.0]), 3)
+    assert v == pytest.approx(2.0 * 1.5 - 1.0)
+    np.testing.assert_array_equal(g, [1.5, 0.0, 1.0])
