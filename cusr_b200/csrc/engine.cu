@@ -277,7 +277,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         p.tape_g = nullptr;
         if (tg) {
             // one global tape per stream: bins on different streams run concurrently
-            GROW(ctx->tape_gs[si], (size_t)grid * p.tape_cap * tape_slot_elems(nt) * sizeof(T));
+            GROW(ctx->tape_gs[si], (size_t)grid * p.tape_cap * nt * EVAL_V * sizeof(T));
             p.tape_g = ctx->tape_gs[si].ptr;
         }
         CK(Launch<T>::eval(kc, grad, tg, ctx->fast, wide, p, (int)grid, smem, ctx->bin_streams[si]));

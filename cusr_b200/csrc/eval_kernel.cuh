@@ -71,13 +71,15 @@ __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) 
 // KC >= 4: reverse mode; a tape slot is NT VecT entries plus a pad of 4 elements of T, so
 // that a slot used as a gradient row starts 4 banks (fp32) further on than the slot before:
 // the eight rows of a tensor-core fragment load land in distinct banks when the compiler
-// gives them distinct slot residues mod 8.
+// gives them distinct slot residues mod 8. When the tape lives in global memory (trees too
+// long for shared memory), the KC + 1 gradient and residual rows get a shared-memory region
+// of their own, row k for constant k and row K for the residual.
 template <typename T, int V, int NT, int KC>
 struct EvalSmem {
     static constexpr bool kFwd = KC <= 2;
     static constexpr int kTapeStride = NT + 4 / V;            // VecT entries per tape slot
     static constexpr int kSpillWords = kFwd ? 1 + KC : 1;     // VecT entries per spill slot
-    size_t code, cval, x, spill, tape, red, total;
+    size_t code, cval, x, spill, tape, rows, red, total;
     __host__ __device__ EvalSmem(int code_cap, int n_vars, int spill_cap, int tape_cap,
                                  bool tape_in_smem = true) {
         size_t o = 0;
@@ -87,6 +89,8 @@ struct EvalSmem {
         spill = o; o += align16((size_t)spill_cap * kSpillWords * NT * V * sizeof(T));
         tape = o;
         o += (tape_in_smem && !kFwd) ? align16((size_t)tape_cap * kTapeStride * V * sizeof(T)) : 0;
+        rows = o;
+        o += (!tape_in_smem && !kFwd) ? align16((size_t)(KC + 1) * kTapeStride * V * sizeof(T)) : 0;
         red = o;   o += align16((size_t)(NT / 32) * nblock_size(KC) * sizeof(T));
         total = o;
     }
@@ -112,12 +116,11 @@ __device__ __forceinline__ VecT<T, V> pack(const T (&a)[V]) {
 // Forward sweep. xt / sp / tp point at this thread's column (x_s + tid, ...); slot k of a
 // column is element k * NT.
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int NT, bool GRAD, uint32_t OP, uint32_t MODE, bool SW>
+template <typename T, int V, int NT, int TSTR, bool GRAD, uint32_t OP, uint32_t MODE, bool SW>
 __device__ __forceinline__ void fwd_bin(uint32_t w, const T *__restrict__ c_s,
                                         const VecF<V> *__restrict__ xt,
                                         const VecT<T, V> *__restrict__ sp,
                                         VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
-    constexpr int TSTR = NT + 4 / V;   // tape slot stride (EvalSmem::kTapeStride)
     T s[V];
     if constexpr (MODE == M_VAR) {
         const VecF<V> xv = xt[w_idx(w) * NT];
@@ -155,9 +158,8 @@ __device__ __forceinline__ void fwd_bin(uint32_t w, const T *__restrict__ c_s,
     CUSR_FOR_V tos[j] = o[j];
 }
 
-template <typename T, int V, int NT, bool GRAD, uint32_t OP>
+template <typename T, int V, int TSTR, bool GRAD, uint32_t OP>
 __device__ __forceinline__ void fwd_un(uint32_t w, VecT<T, V> *__restrict__ tp, T (&tos)[V]) {
-    constexpr int TSTR = NT + 4 / V;
     T d[V];
     CUSR_FOR_V {
         T r;
@@ -167,7 +169,8 @@ __device__ __forceinline__ void fwd_un(uint32_t w, VecT<T, V> *__restrict__ tp, 
     if constexpr (GRAD && OP != OP_NEG && OP != OP_UZERO) tp[w_ts(w) * TSTR] = pack<T, V>(d);
 }
 
-template <typename T, int V, int NT, bool GRAD>
+// TSTR: VecT entries between consecutive tape slots
+template <typename T, int V, int NT, int TSTR, bool GRAD>
 __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code, int n,
                                               const T *__restrict__ c_s,
                                               const VecF<V> *__restrict__ xt,
@@ -194,7 +197,7 @@ __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code,
                 CUSR_FOR_V tos[j] = cv;
                 break;
             }
-#define CUSR_UN(OPC) case xop_un(OPC): fwd_un<T, V, NT, GRAD, OPC>(w, tp, tos); break;
+#define CUSR_UN(OPC) case xop_un(OPC): fwd_un<T, V, TSTR, GRAD, OPC>(w, tp, tos); break;
             CUSR_UN(OP_SIN) CUSR_UN(OP_COS) CUSR_UN(OP_LOG) CUSR_UN(OP_LOGABS)
             CUSR_UN(OP_SQRT) CUSR_UN(OP_SQRTABS)
             CUSR_UN(OP_TAN) CUSR_UN(OP_SINH) CUSR_UN(OP_COSH) CUSR_UN(OP_TANH)
@@ -202,7 +205,7 @@ __device__ __forceinline__ void forward_sweep(const uint32_t *__restrict__ code,
 #undef CUSR_UN
 #define CUSR_B(OPC, MODE, SW)                                                          \
     case xop_bin(OPC, MODE, SW):                                                       \
-        fwd_bin<T, V, NT, GRAD, OPC, MODE, SW>(w, c_s, xt, sp, tp, tos);               \
+        fwd_bin<T, V, NT, TSTR, GRAD, OPC, MODE, SW>(w, c_s, xt, sp, tp, tos);         \
         break;
 // operand order matters: every (mode, order); commutative ones are emitted unswapped
 #define CUSR_B6(OPC) CUSR_B(OPC, M_VAR, 0) CUSR_B(OPC, M_VAR, 1) CUSR_B(OPC, M_CONST, 0) \
@@ -351,13 +354,24 @@ __device__ __forceinline__ void tangent_sweep(const uint32_t *__restrict__ code,
     }
 }
 
-// gradient row write: tape column entry `slot` of this thread (stride TS), stored, or added
-// to for a constant that occurs more than once (B_ACC)
-template <typename T, int V, int TS>
-__device__ __forceinline__ void row_put(VecT<T, V> *tp, uint32_t slot, const T (&a)[V],
-                                        uint32_t w) {
-    VecT<T, V> *q = tp + (int)slot * TS;
-    if (w & B_ACC) {
+// Where a thread's gradient rows are: in its tape column, at the row slots the compiler chose
+// (ROWS = false), or, for a global tape, in its column of the shared-memory row region, row k
+// for constant k (ROWS = true). RS = VecT entries between rows.
+template <typename T, int V, int RS, bool ROWS>
+struct RowCol {
+    VecT<T, V> *rp;
+    __device__ __forceinline__ VecT<T, V> *at(uint32_t k, uint32_t slot) const {
+        return rp + (int)(ROWS ? k : slot) * RS;
+    }
+};
+
+// gradient row write of word w: this thread's entry of the row, stored, or added to for the
+// second and later occurrences of a constant (the B_ACC opcodes)
+template <typename T, int V, int RS, bool ROWS, bool ACC>
+__device__ __forceinline__ void row_put(const RowCol<T, V, RS, ROWS> &rc, uint32_t w,
+                                        const T (&a)[V]) {
+    VecT<T, V> *q = rc.at(w_idx(w), w_row(w));
+    if constexpr (ACC) {
         VecT<T, V> o = *q;
         CUSR_FOR_V o.v[j] += a[j];
         *q = o;
@@ -368,130 +382,117 @@ __device__ __forceinline__ void row_put(VecT<T, V> *tp, uint32_t slot, const T (
 
 // ---------------------------------------------------------------------------------------
 // Reverse sweep over the reverse program: adjoints from the root to the leaves; the gradient
-// row of constant k (df/dc_k) is written to the tape slot the instruction names.
+// row of constant k (df/dc_k) is written to the row slot the instruction names. Every
+// (opcode, store / add) pair is its own case of the dispatch, so each is straight-line code.
 // ---------------------------------------------------------------------------------------
-template <typename T, int V, int NT>
+template <uint32_t B, bool ACC, typename T, int V, int NT, int TSTR, int RS, bool ROWS>
+__device__ __forceinline__ void rev_step(uint32_t w, T (&adj)[V], const T *__restrict__ c_s,
+                                         const VecF<V> *__restrict__ xt,
+                                         VecT<T, V> *__restrict__ sp, VecT<T, V> *tp,
+                                         const RowCol<T, V, RS, ROWS> &rc) {
+    typedef VecT<T, V> VT;
+    if constexpr (B == B_GRAD) {
+        row_put<T, V, RS, ROWS, ACC>(rc, w, adj);
+    } else if constexpr (B == B_GRAD_RESTORE) {
+        row_put<T, V, RS, ROWS, ACC>(rc, w, adj);
+        const VT t = sp[w_sd(w) * NT];
+        CUSR_FOR_V adj[j] = t.v[j];
+    } else if constexpr (B == B_RESTORE) {
+        const VT t = sp[w_sd(w) * NT];
+        CUSR_FOR_V adj[j] = t.v[j];
+    } else if constexpr (B == B_GRAD_NEG) {
+        T a[V];
+        CUSR_FOR_V a[j] = -adj[j];
+        row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+    } else if constexpr (B == B_SPILL) {
+        sp[w_sd(w) * NT] = pack<T, V>(adj);
+    } else if constexpr (B == B_SPILL_NEG) {
+        T a[V];
+        CUSR_FOR_V a[j] = -adj[j];
+        sp[w_sd(w) * NT] = pack<T, V>(a);
+    } else if constexpr (B == B_NEG) {
+        CUSR_FOR_V adj[j] = -adj[j];
+    } else if constexpr (B == B_GRAD_THEN_NEG) {
+        row_put<T, V, RS, ROWS, ACC>(rc, w, adj);
+        CUSR_FOR_V adj[j] = -adj[j];
+    } else if constexpr (B == B_SPILL_THEN_NEG) {
+        sp[w_sd(w) * NT] = pack<T, V>(adj);
+        CUSR_FOR_V adj[j] = -adj[j];
+    } else if constexpr (B == B_SCALE_X) {
+        const VecF<V> xv = xt[w_idx(w) * NT];
+        CUSR_FOR_V adj[j] = safe_mul(adj[j], (T)xv.v[j]);
+    } else if constexpr (B == B_SCALE_T0) {
+        const VT t0 = tp[w_ts(w) * TSTR];
+        CUSR_FOR_V adj[j] = safe_mul(adj[j], t0.v[j]);
+    } else if constexpr (B == B_MULC) {
+        const VT t0 = tp[w_ts(w) * TSTR];
+        const T cv = c_s[w_idx(w)];
+        T a[V];
+        CUSR_FOR_V { a[j] = safe_mul(adj[j], t0.v[j]); adj[j] = safe_mul(adj[j], cv); }
+        row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+    } else if constexpr (B == B_GRAD_T1_T0 || B == B_SPILL_T1_T0) {
+        const int ts = (int)w_ts(w);
+        const VT t0 = tp[ts * TSTR], t1 = tp[(ts + 1) * TSTR];
+        T a[V];
+        CUSR_FOR_V { a[j] = safe_mul(adj[j], t1.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
+        if constexpr (B == B_GRAD_T1_T0) row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        else sp[w_sd(w) * NT] = pack<T, V>(a);
+    } else if constexpr (B == B_GRAD_1MT0_T0 || B == B_SPILL_1MT0_T0) {
+        const VT t0 = tp[w_ts(w) * TSTR];
+        T a[V];
+        CUSR_FOR_V { a[j] = safe_mul(adj[j], T(1) - t0.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
+        if constexpr (B == B_GRAD_1MT0_T0) row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        else sp[w_sd(w) * NT] = pack<T, V>(a);
+    } else if constexpr (B == B_ZERO) {
+        CUSR_FOR_V adj[j] = T(0);
+    } else if constexpr (B == B_GRAD_ZERO) {
+        T a[V];
+        CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
+        row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+    } else if constexpr (B == B_SPILL_ZERO) {
+        T a[V];
+        CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
+        sp[w_sd(w) * NT] = pack<T, V>(a);
+    } else if constexpr (B == B_SCALE2_T) {
+        const VT t0 = tp[w_ts(w) * TSTR], t1 = tp[w_idx(w) * TSTR];
+        CUSR_FOR_V adj[j] = safe_mul(safe_mul(adj[j], t0.v[j]), t1.v[j]);
+    } else if constexpr (B == B_SCALE_1MT0) {
+        const VT t0 = tp[w_ts(w) * TSTR];
+        CUSR_FOR_V adj[j] = safe_mul(adj[j], T(1) - t0.v[j]);
+    } else if constexpr (B == B_ROW_ZERO) {
+        // the shared zero row of absent constants (a row region is zeroed per tree instead)
+        if constexpr (!ROWS) {
+            T a[V];
+            CUSR_FOR_V a[j] = T(0);
+            tp[w_ts(w) * TSTR] = pack<T, V>(a);
+        }
+    }
+}
+
+template <typename T, int V, int NT, int TSTR, int RS, bool ROWS>
 __device__ __forceinline__ void reverse_sweep(const uint32_t *__restrict__ code, int n,
                                               const T *__restrict__ c_s,
                                               const VecF<V> *__restrict__ xt,
-                                              VecT<T, V> *__restrict__ sp, VecT<T, V> *tp) {
-    typedef VecT<T, V> VT;
-    constexpr int TSTR = NT + 4 / V;
+                                              VecT<T, V> *__restrict__ sp, VecT<T, V> *tp,
+                                              const RowCol<T, V, RS, ROWS> rc) {
     T adj[V];
     CUSR_FOR_V adj[j] = T(1);
     uint32_t wn = code[0];
     for (int pc = 0; pc < n; ++pc) {
         const uint32_t w = wn;
         wn = code[pc + 1];
-        switch (w_bop(w)) {
-            case B_GRAD:
-                row_put<T, V, TSTR>(tp, w_idx(w), adj, w);
-                break;
-            case B_GRAD_RESTORE: {
-                row_put<T, V, TSTR>(tp, w_idx(w), adj, w);
-                const VT t = sp[w_sd(w) * NT];
-                CUSR_FOR_V adj[j] = t.v[j];
-                break;
-            }
-            case B_RESTORE: {
-                const VT t = sp[w_sd(w) * NT];
-                CUSR_FOR_V adj[j] = t.v[j];
-                break;
-            }
-            case B_GRAD_NEG: {
-                T a[V];
-                CUSR_FOR_V a[j] = -adj[j];
-                row_put<T, V, TSTR>(tp, w_idx(w), a, w);
-                break;
-            }
-            case B_SPILL:
-                sp[w_sd(w) * NT] = pack<T, V>(adj);
-                break;
-            case B_SPILL_NEG: {
-                T a[V];
-                CUSR_FOR_V a[j] = -adj[j];
-                sp[w_sd(w) * NT] = pack<T, V>(a);
-                break;
-            }
-            case B_NEG:
-                CUSR_FOR_V adj[j] = -adj[j];
-                break;
-            case B_GRAD_THEN_NEG:
-                row_put<T, V, TSTR>(tp, w_idx(w), adj, w);
-                CUSR_FOR_V adj[j] = -adj[j];
-                break;
-            case B_SPILL_THEN_NEG:
-                sp[w_sd(w) * NT] = pack<T, V>(adj);
-                CUSR_FOR_V adj[j] = -adj[j];
-                break;
-            case B_SCALE_X: {
-                const VecF<V> xv = xt[w_idx(w) * NT];
-                CUSR_FOR_V adj[j] = safe_mul(adj[j], (T)xv.v[j]);
-                break;
-            }
-            case B_SCALE_T0: {
-                const VT t0 = tp[w_ts(w) * TSTR];
-                CUSR_FOR_V adj[j] = safe_mul(adj[j], t0.v[j]);
-                break;
-            }
-            case B_MULC: {
-                const VT t0 = tp[w_ts(w) * TSTR];
-                const T cv = c_s[w_idx(w)];
-                T a[V];
-                CUSR_FOR_V { a[j] = safe_mul(adj[j], t0.v[j]); adj[j] = safe_mul(adj[j], cv); }
-                row_put<T, V, TSTR>(tp, w_sd(w), a, w);
-                break;
-            }
-            case B_GRAD_T1_T0:
-            case B_SPILL_T1_T0: {
-                const int ts = (int)w_ts(w);
-                const VT t0 = tp[ts * TSTR], t1 = tp[(ts + 1) * TSTR];
-                T a[V];
-                CUSR_FOR_V { a[j] = safe_mul(adj[j], t1.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
-                if (w_bop(w) == B_GRAD_T1_T0) row_put<T, V, TSTR>(tp, w_idx(w), a, w);
-                else sp[w_sd(w) * NT] = pack<T, V>(a);
-                break;
-            }
-            case B_GRAD_1MT0_T0:
-            case B_SPILL_1MT0_T0: {
-                const VT t0 = tp[w_ts(w) * TSTR];
-                T a[V];
-                CUSR_FOR_V { a[j] = safe_mul(adj[j], T(1) - t0.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
-                if (w_bop(w) == B_GRAD_1MT0_T0) row_put<T, V, TSTR>(tp, w_idx(w), a, w);
-                else sp[w_sd(w) * NT] = pack<T, V>(a);
-                break;
-            }
-            case B_ZERO:
-                CUSR_FOR_V adj[j] = T(0);
-                break;
-            case B_GRAD_ZERO: {
-                T a[V];
-                CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
-                row_put<T, V, TSTR>(tp, w_idx(w), a, w);
-                break;
-            }
-            case B_SPILL_ZERO: {
-                T a[V];
-                CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
-                sp[w_sd(w) * NT] = pack<T, V>(a);
-                break;
-            }
-            case B_SCALE2_T: {
-                const VT t0 = tp[w_ts(w) * TSTR], t1 = tp[w_idx(w) * TSTR];
-                CUSR_FOR_V adj[j] = safe_mul(safe_mul(adj[j], t0.v[j]), t1.v[j]);
-                break;
-            }
-            case B_SCALE_1MT0: {
-                const VT t0 = tp[w_ts(w) * TSTR];
-                CUSR_FOR_V adj[j] = safe_mul(adj[j], T(1) - t0.v[j]);
-                break;
-            }
-            case B_ROW_ZERO: {
-                T a[V];
-                CUSR_FOR_V a[j] = T(0);
-                tp[w_idx(w) * TSTR] = pack<T, V>(a);
-                break;
-            }
+        switch (w_code(w)) {
+#define CUSR_R(B) case B: rev_step<B, false, T, V, NT, TSTR, RS, ROWS>(w, adj, c_s, xt, sp, tp, rc); break;
+#define CUSR_RA(B) CUSR_R(B) \
+    case B | B_ACC: rev_step<B, true, T, V, NT, TSTR, RS, ROWS>(w, adj, c_s, xt, sp, tp, rc); break;
+            CUSR_RA(B_GRAD) CUSR_RA(B_GRAD_RESTORE) CUSR_R(B_RESTORE) CUSR_RA(B_GRAD_NEG)
+            CUSR_R(B_SPILL) CUSR_R(B_SPILL_NEG) CUSR_R(B_NEG) CUSR_RA(B_GRAD_THEN_NEG)
+            CUSR_R(B_SPILL_THEN_NEG) CUSR_R(B_SCALE_X) CUSR_R(B_SCALE_T0) CUSR_RA(B_MULC)
+            CUSR_RA(B_GRAD_T1_T0) CUSR_R(B_SPILL_T1_T0) CUSR_RA(B_GRAD_1MT0_T0)
+            CUSR_R(B_SPILL_1MT0_T0) CUSR_R(B_ZERO) CUSR_RA(B_GRAD_ZERO) CUSR_R(B_SPILL_ZERO)
+            CUSR_R(B_SCALE_1MT0) CUSR_R(B_SCALE2_T) CUSR_R(B_ROW_ZERO)
+#undef CUSR_RA
+#undef CUSR_R
             default:
                 // every word was checked against this case set on the host
                 // (valid_forward_code / valid_reverse_code), so no bounds check is needed
@@ -520,20 +521,23 @@ __device__ __forceinline__ void dmma_884(double (&c)[2], double a, double b) {
 //         --use_fast_math flags (approximate transcendentals, division and square root,
 //         denormals flushed); the source is the same, only the name differs
 // ---------------------------------------------------------------------------------------
-// Register budget: fp32 classes K <= 16 and the value-only pass are held to 64 registers per
-// thread (eight 128-thread blocks per SM, as many as shared memory allows for the common tape
-// sizes); the K <= 32 class keeps its 15 accumulator tiles in registers at four blocks; fp64
+// Register budget: fp32 classes K <= 16 are held to 64 registers per thread (eight 128-thread
+// blocks per SM, as many as shared memory allows for the common tape sizes); the value-only
+// pass keeps the compiler's own allocation; the K <= 32 class keeps its 15 accumulator tiles in registers at four blocks; fp64
 // (twice the shared memory per thread) is held to six and two blocks.
 template <typename T, int V, int NT, int KC, bool GRAD, bool TG, bool FAST>
 __global__ void __launch_bounds__(
-    NT, (!GRAD ? 1024 : sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : 768)) / NT)
+    NT, (!GRAD ? 1152 : sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : 768)) / NT)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;
     constexpr bool FWD = GRAD && L::kFwd;    // forward-mode tangents (KC = 1, 2)
     constexpr bool REV = GRAD && !L::kFwd;   // reverse sweep + tensor-core normal equations
     constexpr int NTL = REV ? (KC + 1 + 7) / 8 : 1;   // 8-row tiles of [g; r]
     constexpr int NTILE = NTL * (NTL + 1) / 2;        // lower-triangle tiles
-    constexpr int TSTR = L::kTapeStride;              // VecT entries per tape slot
+    // VecT entries per tape slot: padded in shared memory (slots double as gradient rows);
+    // a global tape keeps the rows in shared memory and its slots 128-byte aligned
+    constexpr int TSTR = TG ? NT : L::kTapeStride;
+    constexpr int RSTR = L::kTapeStride;              // VecT entries per gradient row
     constexpr int ROUND = NT * V;
     constexpr int NW = NT / 32;
     constexpr int NTRI = KC * (KC + 1) / 2;
@@ -545,20 +549,24 @@ lm_eval_kernel(const EvalParams<T> p) {
     T *c_s = reinterpret_cast<T *>(smem + lay.cval);
     VecF<V> *x_s = reinterpret_cast<VecF<V> *>(smem + lay.x);
     VecT<T, V> *spill_s = reinterpret_cast<VecT<T, V> *>(smem + lay.spill);
-    // reverse tape (and, in slots the reverse sweep has finished with, the gradient and
-    // residual rows): private shared-memory columns, or (TG, trees whose tape would not fit
-    // beside a second resident block) this block's slab of a global scratch buffer, read
-    // back by the threads of the same warp and served from L1/L2
+    // reverse tape: private shared-memory columns, whose slots the reverse sweep has finished
+    // with also take the gradient and residual rows; or (TG, trees whose tape would not fit
+    // beside a second resident block) this block's slab of a global scratch buffer, read back
+    // by the same thread and served from L1/L2, with the rows in the shared row region
     VecT<T, V> *tape_s =
         TG ? reinterpret_cast<VecT<T, V> *>(p.tape_g) + (int64_t)blockIdx.x * p.tape_cap * TSTR
            : reinterpret_cast<VecT<T, V> *>(smem + lay.tape);
     T *red_s = reinterpret_cast<T *>(smem + lay.red);
+    // global tape: the gradient and residual rows live in a shared-memory region of their own
+    VecT<T, V> *rows_s = reinterpret_cast<VecT<T, V> *>(smem + lay.rows);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n_items = *p.n_items;
     VecF<V> *xt = x_s + tid;
     VecT<T, V> *spt = spill_s + tid;
     VecT<T, V> *tpt = tape_s + tid;
+    const RowCol<T, V, RSTR, TG> rc{TG ? rows_s + tid : tpt};
+    const T *row_base = reinterpret_cast<const T *>(TG ? rows_s : tape_s);
 
     for (;;) {
         if (tid == 0) s_item = atomicAdd(p.counter, 1);
@@ -574,6 +582,12 @@ lm_eval_kernel(const EvalParams<T> p) {
         for (int i = tid; i < n_code; i += NT) code_s[i] = p.code[d.code_off + i];
         if (tid == 0) code_s[n_code] = 0u;   // prefetch pad after the last staged word
         for (int i = tid; i < K; i += NT) c_s[i] = p.c[d.c_off + i];
+        if constexpr (REV && TG) {
+            // rows of constants absent from the tree are never written: zero them once
+            VecT<T, V> z;
+            CUSR_FOR_V z.v[j] = T(0);
+            for (int k = 0; k < K; ++k) rc.at(k, 0)[0] = z;
+        }
         __syncthreads();
         const uint32_t *bcode_s = code_s + d.n_instr;
         // tape slot of row r (r < K: gradient of constant r, r = K: residual)
@@ -597,7 +611,7 @@ lm_eval_kernel(const EvalParams<T> p) {
 #pragma unroll
             for (int t = 0; t < NTL; ++t) {
                 const int row = 8 * t + (lane >> 2);
-                roff[t] = (grad && row <= K) ? (int)rtab[row] * TSTR * V : -1;
+                roff[t] = !(grad && row <= K) ? -1 : (TG ? row : (int)rtab[row]) * RSTR * V;
             }
         }
         T lsum = T(0);
@@ -616,7 +630,7 @@ lm_eval_kernel(const EvalParams<T> p) {
             if constexpr (FWD) {
                 tangent_sweep<T, V, NT, KC>(code_s, d.n_instr, c_s, xt, spt, f, tt);
             } else {
-                forward_sweep<T, V, NT, GRAD>(code_s, d.n_instr, c_s, xt, spt, tpt, f);
+                forward_sweep<T, V, NT, TSTR, GRAD>(code_s, d.n_instr, c_s, xt, spt, tpt, f);
             }
             T r[V];
             bool valid[V];
@@ -650,20 +664,20 @@ lm_eval_kernel(const EvalParams<T> p) {
                 }
               }
             } else if (grad) {
-                reverse_sweep<T, V, NT>(bcode_s, d.n_bwd, c_s, xt, spt, tpt);
+                reverse_sweep<T, V, NT, TSTR, RSTR, TG>(bcode_s, d.n_bwd, c_s, xt, spt, tpt, rc);
                 if (p.jac) {
                     T *jrow = p.jac + (int64_t)wi.x * p.jac_kmax * p.N;
                     for (int k = 0; k < K; ++k) {
-                        const VecT<T, V> g = tpt[(int)rtab[k] * TSTR];
+                        const VecT<T, V> g = *rc.at(k, rtab[k]);
                         CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = g.v[j];
                     }
                 }
                 // residual row; gradients of samples past N are zeroed (only the last round
                 // of a tree's last chunk has any)
-                tpt[(int)rtab[K] * TSTR] = pack<T, V>(r);
+                *rc.at(K, rtab[K]) = pack<T, V>(r);
                 if (si + V > p.N) {
                     for (int k = 0; k < K; ++k) {
-                        VecT<T, V> *q = tpt + (int)rtab[k] * TSTR;
+                        VecT<T, V> *q = rc.at(k, rtab[k]);
                         VecT<T, V> g = *q;
                         CUSR_FOR_V if (!valid[j]) g.v[j] = T(0);
                         *q = g;
@@ -672,7 +686,7 @@ lm_eval_kernel(const EvalParams<T> p) {
                 __syncwarp();
                 // the warp accumulates the (K+1)^2 Gram matrix of its 32 V samples as 8x8
                 // fp64 tiles, four samples per product
-                const T *tw = reinterpret_cast<const T *>(tape_s) + warp * 32 * V + (lane & 3);
+                const T *tw = row_base + warp * 32 * V + (lane & 3);
 #pragma unroll 2
                 for (int s4 = 0; s4 < 32 * V; s4 += 4) {
                     double a[NTL];

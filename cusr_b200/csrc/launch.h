@@ -20,8 +20,6 @@ constexpr int EVAL_THREADS = EVAL_NT;
 constexpr int EVAL_NT_WIDE = 2 * EVAL_NT;
 // sample granularity of the input layout and of the work chunks: one round of a wide block
 constexpr int EVAL_ROUND = EVAL_NT_WIDE * EVAL_V;
-// elements of T per reverse-tape slot of an nt-thread block (EvalSmem::kTapeStride * V)
-constexpr int tape_slot_elems(int nt) { return (nt + 4 / EVAL_V) * EVAL_V; }
 
 // kc: constant-count class (4, 8, 12, 16, 32 for fp32; 4, 8, 32 for fp64).
 // grad = false launches the value-only variant (fp64 audit); tg = reverse tape in global

@@ -284,7 +284,7 @@ int reverse_reads(uint32_t w, uint32_t (&s)[2]) {
 // that are dead at the end. A row finds a new slot past the tape only when no dead one is
 // left. Among dead slots the lowest whose residue mod 8 no other row of the same 8-row group
 // holds is taken: the rows are padded so that residues map to distinct shared-memory banks of
-// the tensor-core fragment loads. Rewrites the row writes of `rev` (slot fields, B_ACC for
+// the tensor-core fragment loads. Rewrites the row writes of `rev` (slot field, B_ACC for
 // the second and later writes of a constant), appends B_ROW_ZERO when a zero row is needed,
 // and returns the slot of each row (K + 1 entries, the residual last) and the slot count.
 bool place_rows(std::vector<uint32_t> &rev, int n_tape, int K, std::vector<int> &row_slot,
@@ -326,7 +326,7 @@ bool place_rows(std::vector<uint32_t> &rev, int n_tape, int K, std::vector<int> 
         }
         const uint32_t code = b | (acc ? B_ACC : 0u);
         const uint32_t slot = (uint32_t)row_slot[(size_t)k];
-        w = b == B_MULC ? enc(code, w_idx(w), slot, w_ts(w)) : enc(code, slot, w_sd(w), w_ts(w));
+        w = b == B_GRAD_RESTORE ? enc(code, w_idx(w), w_sd(w), slot) : enc(code, w_idx(w), slot, w_ts(w));
         rev[(size_t)p] = w;
     }
     int zero = -1;
@@ -335,7 +335,7 @@ bool place_rows(std::vector<uint32_t> &rev, int n_tape, int K, std::vector<int> 
         if (zero < 0) {
             zero = pick(k, -1);
             if (zero < 0) return false;
-            rev.push_back(enc(B_ROW_ZERO, (uint32_t)zero, 0, 0));
+            rev.push_back(enc(B_ROW_ZERO, 0, 0, (uint32_t)zero));
         }
         row_slot[(size_t)k] = zero;
     }
@@ -711,30 +711,31 @@ double host_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, in
         const uint32_t idx = w_idx(w), sd = w_sd(w), ts = w_ts(w);
         const double t0 = tape[ts], t1 = tape[ts + 1];
         const bool acc = (w_code(w) & B_ACC) != 0;
-        auto row = [&](uint32_t slot, double v) { tape[slot] = acc ? tape[slot] + v : v; };
+        const uint32_t rs = w_row(w);
+        auto row = [&](double v) { tape[rs] = acc ? tape[rs] + v : v; };
         switch (w_bop(w)) {
-            case B_GRAD: row(idx, adj); break;
-            case B_GRAD_RESTORE: row(idx, adj); adj = spill[sd]; break;
+            case B_GRAD: row(adj); break;
+            case B_GRAD_RESTORE: row(adj); adj = spill[sd]; break;
             case B_RESTORE: adj = spill[sd]; break;
-            case B_GRAD_NEG: row(idx, -adj); break;
+            case B_GRAD_NEG: row(-adj); break;
             case B_SPILL: spill[sd] = adj; break;
             case B_SPILL_NEG: spill[sd] = -adj; break;
             case B_NEG: adj = -adj; break;
-            case B_GRAD_THEN_NEG: row(idx, adj); adj = -adj; break;
+            case B_GRAD_THEN_NEG: row(adj); adj = -adj; break;
             case B_SPILL_THEN_NEG: spill[sd] = adj; adj = -adj; break;
             case B_SCALE_X: adj = safe_mul(adj, x[idx]); break;
             case B_SCALE_T0: adj = safe_mul(adj, t0); break;
-            case B_MULC: row(sd, safe_mul(adj, t0)); adj = safe_mul(adj, c[idx]); break;
-            case B_GRAD_T1_T0: row(idx, safe_mul(adj, t1)); adj = safe_mul(adj, t0); break;
+            case B_MULC: row(safe_mul(adj, t0)); adj = safe_mul(adj, c[idx]); break;
+            case B_GRAD_T1_T0: row(safe_mul(adj, t1)); adj = safe_mul(adj, t0); break;
             case B_SPILL_T1_T0: spill[sd] = safe_mul(adj, t1); adj = safe_mul(adj, t0); break;
-            case B_GRAD_1MT0_T0: row(idx, safe_mul(adj, 1.0 - t0)); adj = safe_mul(adj, t0); break;
+            case B_GRAD_1MT0_T0: row(safe_mul(adj, 1.0 - t0)); adj = safe_mul(adj, t0); break;
             case B_SPILL_1MT0_T0: spill[sd] = safe_mul(adj, 1.0 - t0); adj = safe_mul(adj, t0); break;
             case B_ZERO: adj = 0.0; break;
-            case B_GRAD_ZERO: row(idx, 0.0); adj = 0.0; break;
+            case B_GRAD_ZERO: row(0.0); adj = 0.0; break;
             case B_SPILL_ZERO: spill[sd] = 0.0; adj = 0.0; break;
             case B_SCALE_1MT0: adj = safe_mul(adj, 1.0 - t0); break;
             case B_SCALE2_T: adj = safe_mul(safe_mul(adj, t0), tape[w_idx(w)]); break;
-            case B_ROW_ZERO: tape[idx] = 0.0; break;
+            case B_ROW_ZERO: tape[ts] = 0.0; break;
             default: break;
         }
     }

@@ -28,9 +28,11 @@
 //   [8,16)  idx       variable index or constant rank
 //   [16,24) sd        spill slot
 //   [24,32) ts        first tape slot
-// A reverse instruction that writes a gradient row names the row's tape slot in `idx`
-// (B_MULC, which needs `idx` for the constant, in `sd`); the B_ACC bit of its opcode byte
-// adds to the row instead of storing it (second and later occurrences of a constant).
+// A reverse instruction that writes a gradient row keeps the constant's rank in `idx` and
+// names the row's tape slot in `sd` (in `ts` for B_GRAD_RESTORE, whose `sd` is the spill slot
+// it restores from); with the B_ACC bit in its opcode byte (a separate opcode of the
+// interpreter) it adds to the row instead of storing it (second and later occurrences of a
+// constant).
 #pragma once
 #include <stdint.h>
 
@@ -114,12 +116,16 @@ enum BOp : uint32_t {
     B_SPILL_ZERO,        // spill[sd] <- 0; adj <- 0
     B_SCALE_1MT0,        // adj <- safe(adj, 1 - t0)
     B_SCALE2_T,          // adj <- safe(safe(adj, t0), tape[idx])   (two chained unary nodes)
-    B_ROW_ZERO,          // row[idx] <- 0   (the shared row of constants absent from the tree)
+    B_ROW_ZERO,          // tape[ts] <- 0   (the shared row of constants absent from the tree)
     B_COUNT
 };
 // "grad[k]" above is the gradient row of constant k, held in the tape slot the word names
 constexpr uint32_t B_ACC = 32u;       // opcode-byte flag of a row write: add instead of store
 __host__ __device__ inline uint32_t w_bop(uint32_t w) { return w & 31u; }
+// the field of a row-writing word that names the row's tape slot
+__host__ __device__ inline uint32_t w_row(uint32_t w) {
+    return (w & 31u) == B_GRAD_RESTORE ? w_ts(w) : w_sd(w);
+}
 __host__ __device__ inline bool is_row_write(uint32_t b) {
     return b == B_GRAD || b == B_GRAD_RESTORE || b == B_GRAD_NEG || b == B_GRAD_THEN_NEG ||
            b == B_MULC || b == B_GRAD_T1_T0 || b == B_GRAD_1MT0_T0 || b == B_GRAD_ZERO;

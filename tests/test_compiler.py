@@ -217,7 +217,8 @@ def tape_reads(w):
 
 
 def row_of(w):
-    return ((w >> 16) & 255) if (w & 31) == B_MULC else ((w >> 8) & 255)
+    """Row slot named by a row-writing word (ts for B_GRAD_RESTORE, else sd)."""
+    return (w >> 24) if (w & 31) == B_GRAD_RESTORE else ((w >> 16) & 255)
 
 
 def forward_tape_slots(fwd):
@@ -254,7 +255,7 @@ def test_gradient_rows_live_in_dead_tape_slots(name):
         if absent:
             zero = {slots[k] for k in absent}
             assert len(zero) == 1 and not (zero & grad_slots) and slots[K] not in zero
-            assert bwd[-1] & 31 == B_ROW_ZERO and (bwd[-1] >> 8) & 255 == slots[absent[0]]
+            assert bwd[-1] & 31 == B_ROW_ZERO and bwd[-1] >> 24 == slots[absent[0]]
         # the first write of each row stores, later ones add; a row's slot is never read as
         # tape after its first write
         first = {}
@@ -262,7 +263,7 @@ def test_gradient_rows_live_in_dead_tape_slots(name):
             op = w & 31
             if op in ROW_WRITES:
                 s = row_of(w)
-                assert s in grad_slots
+                assert s in grad_slots and s == slots[(w >> 8) & 255]
                 if s not in first:
                     first[s] = p
                     assert not (w & B_ACC)
