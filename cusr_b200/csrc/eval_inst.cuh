@@ -16,6 +16,29 @@ cudaError_t one(const EvalParams<CUSR_T> &p, int grid, size_t smem, cudaStream_t
     lm_eval_kernel<CUSR_T, EVAL_V, NT, KC, G, TG, (CUSR_FAST != 0)><<<grid, NT, smem, s>>>(p);
     return cudaGetLastError();
 }
+// value-only pass (its own kernel; shared-memory layout of the KC = 4 class, one tape slot)
+cudaError_t value_one(const EvalParams<CUSR_T> &p, int grid, size_t smem, cudaStream_t s) {
+    lm_value_kernel<CUSR_T, EVAL_V, EVAL_NT, (CUSR_FAST != 0)><<<grid, EVAL_NT, smem, s>>>(p);
+    return cudaGetLastError();
+}
+int value_occ(size_t smem) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_value_kernel<CUSR_T, EVAL_V, EVAL_NT, (CUSR_FAST != 0)>,
+                                                      EVAL_NT, smem) != cudaSuccess)
+        return 0;
+    return n;
+}
+cudaError_t value_prep() {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess)
+        e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, lm_value_kernel<CUSR_T, EVAL_V, EVAL_NT, (CUSR_FAST != 0)>);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(lm_value_kernel<CUSR_T, EVAL_V, EVAL_NT, (CUSR_FAST != 0)>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+}
 template <int KC, bool G, bool TG, int NT = EVAL_NT> int occ(size_t smem) {
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, lm_eval_kernel<CUSR_T, EVAL_V, NT, KC, G, TG, (CUSR_FAST != 0)>,
@@ -40,7 +63,7 @@ template <int KC, bool G, bool TG, int NT = EVAL_NT> cudaError_t prep() {
 
 cudaError_t CUSR_FN(eval_launch)(int kc, bool grad, bool tg, bool wide, const EvalParams<CUSR_T> &p,
                                  int grid, size_t smem, cudaStream_t s) {
-    if (!grad) return one<4, false, false>(p, grid, smem, s);
+    if (!grad) return value_one(p, grid, smem, s);
 #define X(KC)                                                                                  \
     if (kc == KC) {                                                                            \
         if (wide) return tg ? one<KC, true, true, EVAL_NT_WIDE>(p, grid, smem, s)              \
@@ -66,7 +89,7 @@ size_t CUSR_FN(eval_smem)(int kc, int code_cap, int n_vars, int spill_cap, int t
 }
 
 int CUSR_FN(eval_blocks_per_sm)(int kc, bool grad, bool tg, bool wide, size_t smem) {
-    if (!grad) return occ<4, false, false>(smem);
+    if (!grad) return value_occ(smem);
 #define X(KC)                                                                        \
     if (kc == KC) {                                                                  \
         if (wide) return tg ? occ<KC, true, true, EVAL_NT_WIDE>(smem)                \
@@ -79,7 +102,7 @@ int CUSR_FN(eval_blocks_per_sm)(int kc, bool grad, bool tg, bool wide, size_t sm
 }
 
 cudaError_t CUSR_FN(eval_prepare)() {
-    cudaError_t e = prep<4, false, false>();
+    cudaError_t e = value_prep();
     if (e != cudaSuccess) return e;
 #define X(KC)                                                                       \
     if ((e = prep<KC, true, false>()) != cudaSuccess) return e;                      \

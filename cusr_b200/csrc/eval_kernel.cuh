@@ -367,10 +367,11 @@ struct RowCol {
 
 // gradient row write of word w: this thread's entry of the row, stored, or added to for the
 // second and later occurrences of a constant (the B_ACC opcodes)
-template <typename T, int V, int RS, bool ROWS, bool ACC>
+template <uint32_t B, typename T, int V, int RS, bool ROWS, bool ACC>
 __device__ __forceinline__ void row_put(const RowCol<T, V, RS, ROWS> &rc, uint32_t w,
                                         const T (&a)[V]) {
-    VecT<T, V> *q = rc.at(w_idx(w), w_row(w));
+    // the slot field of opcode B (w_row, resolved at compile time)
+    VecT<T, V> *q = rc.at(w_idx(w), B == B_GRAD_RESTORE ? w_ts(w) : w_sd(w));
     if constexpr (ACC) {
         VecT<T, V> o = *q;
         CUSR_FOR_V o.v[j] += a[j];
@@ -392,9 +393,9 @@ __device__ __forceinline__ void rev_step(uint32_t w, T (&adj)[V], const T *__res
                                          const RowCol<T, V, RS, ROWS> &rc) {
     typedef VecT<T, V> VT;
     if constexpr (B == B_GRAD) {
-        row_put<T, V, RS, ROWS, ACC>(rc, w, adj);
+        row_put<B, T, V, RS, ROWS, ACC>(rc, w, adj);
     } else if constexpr (B == B_GRAD_RESTORE) {
-        row_put<T, V, RS, ROWS, ACC>(rc, w, adj);
+        row_put<B, T, V, RS, ROWS, ACC>(rc, w, adj);
         const VT t = sp[w_sd(w) * NT];
         CUSR_FOR_V adj[j] = t.v[j];
     } else if constexpr (B == B_RESTORE) {
@@ -403,7 +404,7 @@ __device__ __forceinline__ void rev_step(uint32_t w, T (&adj)[V], const T *__res
     } else if constexpr (B == B_GRAD_NEG) {
         T a[V];
         CUSR_FOR_V a[j] = -adj[j];
-        row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        row_put<B, T, V, RS, ROWS, ACC>(rc, w, a);
     } else if constexpr (B == B_SPILL) {
         sp[w_sd(w) * NT] = pack<T, V>(adj);
     } else if constexpr (B == B_SPILL_NEG) {
@@ -413,7 +414,7 @@ __device__ __forceinline__ void rev_step(uint32_t w, T (&adj)[V], const T *__res
     } else if constexpr (B == B_NEG) {
         CUSR_FOR_V adj[j] = -adj[j];
     } else if constexpr (B == B_GRAD_THEN_NEG) {
-        row_put<T, V, RS, ROWS, ACC>(rc, w, adj);
+        row_put<B, T, V, RS, ROWS, ACC>(rc, w, adj);
         CUSR_FOR_V adj[j] = -adj[j];
     } else if constexpr (B == B_SPILL_THEN_NEG) {
         sp[w_sd(w) * NT] = pack<T, V>(adj);
@@ -429,26 +430,26 @@ __device__ __forceinline__ void rev_step(uint32_t w, T (&adj)[V], const T *__res
         const T cv = c_s[w_idx(w)];
         T a[V];
         CUSR_FOR_V { a[j] = safe_mul(adj[j], t0.v[j]); adj[j] = safe_mul(adj[j], cv); }
-        row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        row_put<B, T, V, RS, ROWS, ACC>(rc, w, a);
     } else if constexpr (B == B_GRAD_T1_T0 || B == B_SPILL_T1_T0) {
         const int ts = (int)w_ts(w);
         const VT t0 = tp[ts * TSTR], t1 = tp[(ts + 1) * TSTR];
         T a[V];
         CUSR_FOR_V { a[j] = safe_mul(adj[j], t1.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
-        if constexpr (B == B_GRAD_T1_T0) row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        if constexpr (B == B_GRAD_T1_T0) row_put<B, T, V, RS, ROWS, ACC>(rc, w, a);
         else sp[w_sd(w) * NT] = pack<T, V>(a);
     } else if constexpr (B == B_GRAD_1MT0_T0 || B == B_SPILL_1MT0_T0) {
         const VT t0 = tp[w_ts(w) * TSTR];
         T a[V];
         CUSR_FOR_V { a[j] = safe_mul(adj[j], T(1) - t0.v[j]); adj[j] = safe_mul(adj[j], t0.v[j]); }
-        if constexpr (B == B_GRAD_1MT0_T0) row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        if constexpr (B == B_GRAD_1MT0_T0) row_put<B, T, V, RS, ROWS, ACC>(rc, w, a);
         else sp[w_sd(w) * NT] = pack<T, V>(a);
     } else if constexpr (B == B_ZERO) {
         CUSR_FOR_V adj[j] = T(0);
     } else if constexpr (B == B_GRAD_ZERO) {
         T a[V];
         CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
-        row_put<T, V, RS, ROWS, ACC>(rc, w, a);
+        row_put<B, T, V, RS, ROWS, ACC>(rc, w, a);
     } else if constexpr (B == B_SPILL_ZERO) {
         T a[V];
         CUSR_FOR_V { a[j] = T(0); adj[j] = T(0); }
@@ -770,6 +771,78 @@ lm_eval_kernel(const EvalParams<T> p) {
                 for (int w = 0; w < NW; ++w) s += red_s[w * nblock_size(KC) + e];
                 dst[e] = s;
             }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Value-only pass: per-tree sum of squared residuals (and, optionally, per-sample values) at
+// the given constants: the loss of K = 0 trees, the fp64 audit of fp32 fits and the value
+// passes of the finite-difference Jacobian. Same items, shared-memory layout (the KC = 4
+// class with a one-slot tape) and forward interpreter as the fused kernel, without tape,
+// gradient or normal equations; writes the last entry of each item's partial slot.
+// ---------------------------------------------------------------------------------------
+template <typename T, int V, int NT, bool FAST>
+__global__ void __launch_bounds__(NT) lm_value_kernel(const EvalParams<T> p) {
+    typedef EvalSmem<T, V, NT, 4> L;
+    constexpr int ROUND = NT * V;
+    constexpr int NW = NT / 32;
+
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int s_item;
+    const L lay(p.code_cap, p.n_vars, p.spill_cap, 1, true);
+    uint32_t *code_s = reinterpret_cast<uint32_t *>(smem + lay.code);
+    T *c_s = reinterpret_cast<T *>(smem + lay.cval);
+    VecF<V> *x_s = reinterpret_cast<VecF<V> *>(smem + lay.x);
+    VecT<T, V> *spill_s = reinterpret_cast<VecT<T, V> *>(smem + lay.spill);
+    T *red_s = reinterpret_cast<T *>(smem + lay.red);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n_items = *p.n_items;
+    VecF<V> *xt = x_s + tid;
+    VecT<T, V> *spt = spill_s + tid;
+
+    for (;;) {
+        if (tid == 0) s_item = atomicAdd(p.counter, 1);
+        __syncthreads();
+        const int it = s_item;
+        if (it >= n_items) break;
+        const int2 wi = p.items[it];
+        const TreeDesc d = p.desc[wi.x];
+        for (int i = tid; i < d.n_instr; i += NT) code_s[i] = p.code[d.code_off + i];
+        if (tid == 0) code_s[d.n_instr] = 0u;   // prefetch pad
+        for (int i = tid; i < d.K; i += NT) c_s[i] = p.c[d.c_off + i];
+        __syncthreads();
+
+        T lsum = T(0);
+        const int64_t s0 = (int64_t)wi.y * p.chunk;
+        const int64_t s_end = (int64_t)p.N < s0 + p.chunk ? (int64_t)p.N : s0 + p.chunk;
+        const float *yrow = p.ym + d.y_off;
+        for (int64_t base = s0; base < s_end; base += ROUND) {
+            const int64_t si = base + (int64_t)tid * V;
+            for (int v = 0; v < p.n_vars; ++v)
+                xt[v * NT] = *reinterpret_cast<const VecF<V> *>(p.xs + (int64_t)v * p.ldx + si);
+            const VecF<V> yv = *reinterpret_cast<const VecF<V> *>(yrow + si);
+            T f[V];
+            forward_sweep<T, V, NT, NT, false>(code_s, d.n_instr, c_s, xt, spt, nullptr, f);
+            CUSR_FOR_V {
+                const bool valid = si + j < p.N;
+                const T r = valid ? f[j] - (T)yv.v[j] : T(0);
+                lsum += r * r;
+            }
+            if (p.vals) {
+                CUSR_FOR_V if (si + j < p.N) p.vals[(int64_t)wi.x * p.N + si + j] = f[j];
+            }
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) red_s[warp] = lsum;
+        __syncthreads();
+        if (tid == 0) {
+            T s = T(0);
+#pragma unroll
+            for (int w = 0; w < NW; ++w) s += red_s[w];
+            p.partials[d.p_off + (int64_t)wi.y * nblock_size(d.K) + nblock_size(d.K) - 1] = s;
         }
         __syncthreads();
     }
