@@ -290,13 +290,14 @@ int reverse_reads(uint32_t w, uint32_t (&s)[2]) {
 bool place_rows(std::vector<uint32_t> &rev, int n_tape, int K, std::vector<int> &row_slot,
                 int &n_slots) {
     const int P = (int)rev.size();
-    std::vector<int> last(256, -1);            // last reverse word reading the slot
+    int last[256];                             // last reverse word reading the slot
+    for (int i = 0; i < 256; ++i) last[i] = -1;
     for (int p = 0; p < P; ++p) {
         uint32_t s[2];
         const int n = reverse_reads(rev[(size_t)p], s);
         for (int i = 0; i < n; ++i) last[s[i]] = p;
     }
-    std::vector<char> taken(256, 0);
+    char taken[256] = {};
     std::vector<uint8_t> group_res((size_t)K / 8 + 1, 0);   // residues mod 8 used per 8-row group
     n_slots = n_tape;
     auto pick = [&](int row, int p) -> int {   // p = -1: dead at the end
