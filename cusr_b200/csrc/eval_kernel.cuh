@@ -516,19 +516,20 @@ __device__ __forceinline__ void dmma_884(double (&c)[2], double a, double b) {
 //   V     samples per thread
 //   NT    threads per block
 //   KC    constant-count class of the bin (trees with K <= KC)
-//   GRAD  false: value and sum r^2 only (K = 0 trees never need more; the fp64 audit)
+//   GRAD  gradients and normal equations (the engine launches GRAD = true only; value-only
+//         passes run lm_value_kernel below); a tree with K = 0 takes the value-and-loss path
 //   TG    reverse tape in global scratch instead of shared memory
 //   FAST  instantiated in the translation unit built with the reference kernel's
 //         --use_fast_math flags (approximate transcendentals, division and square root,
 //         denormals flushed); the source is the same, only the name differs
 // ---------------------------------------------------------------------------------------
 // Register budget: fp32 classes K <= 16 are held to 64 registers per thread (eight 128-thread
-// blocks per SM, as many as shared memory allows for the common tape sizes); the value-only
-// pass keeps the compiler's own allocation; the K <= 32 class keeps its 15 accumulator tiles in registers at four blocks; fp64
-// (twice the shared memory per thread) is held to six and two blocks.
+// blocks per SM, as many as shared memory allows for the common tape sizes); the K <= 32
+// class keeps its 15 accumulator tiles in registers at four blocks; fp64 (twice the shared
+// memory per thread) is held to six and two blocks.
 template <typename T, int V, int NT, int KC, bool GRAD, bool TG, bool FAST>
 __global__ void __launch_bounds__(
-    NT, (!GRAD ? 1152 : sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : 768)) / NT)
+    NT, (sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : 768)) / NT)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;
     constexpr bool FWD = GRAD && L::kFwd;    // forward-mode tangents (KC = 1, 2)
