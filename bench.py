@@ -434,20 +434,21 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
 
 def run_profile_case(args) -> None:
     """Small case of the same kernel for ncu captures: --profile-trees trees (default 8,192)
-    of the metric configuration (same N, same tree distribution), a few LM iterations."""
+    of the metric configuration, or of --config NAME (same N, same tree distribution), a few
+    LM iterations."""
     from cusr_b200 import InProcessCO, synth
 
-    pop = synth.make_config(CONFIG, M=args.profile_trees, seed=0)
+    pop = synth.make_config(args.config or CONFIG, M=args.profile_trees, seed=0)
     metas = np.asarray(pop["metas"])
     K = metas[:, 3]
     bins = {}
-    for kc, lo, hi in ((4, 0, 4), (8, 5, 8), (12, 9, 12)):
+    for kc, lo, hi in ((4, 0, 4), (8, 5, 8), (12, 9, 12), (16, 13, 16), (32, 17, 32)):
         sel = (K >= lo) & (K <= hi)
         bins[str(kc)] = {"trees": int(sel.sum()), "nodes": int(metas[sel, 1].sum()),
                          "tree_samples": int(sel.sum()) * int(pop["N"])}
     print(json.dumps({"profile_bins": bins}), flush=True)
     co = InProcessCO(device_id=0)
-    co.load(pop, precision="fp32", y_shared=True)
+    co.load(pop, precision=pop["precision"])
     res = co.fit_loaded(max_iter=args.profile_iters)
     st = co.stats()
     print(json.dumps({"profile_case": True, "trees": int(pop["M"]), "N": int(pop["N"]),
