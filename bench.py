@@ -479,11 +479,11 @@ def main() -> None:
     ap.add_argument("--M", type=int, default=None)
     ap.add_argument("--N", type=int, default=None)
     args = ap.parse_args()
-    if args.config:
-        run_config(args)
-        return
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.config:
+        run_config(args)
         return
     world, rank, local = dist_setup()
     try:
