@@ -779,8 +779,9 @@ lm_eval_kernel(const EvalParams<T> p) {
 
 // ---------------------------------------------------------------------------------------
 // Value-only pass: per-tree sum of squared residuals (and, optionally, per-sample values) at
-// the given constants: the loss of K = 0 trees, the fp64 audit of fp32 fits and the value
-// passes of the finite-difference Jacobian. Same items, shared-memory layout (the KC = 4
+// the given constants: the fp64 audit of fp32 fits and the value passes of the
+// finite-difference Jacobian (K = 0 trees of a gradient launch take the fused kernel's
+// value-and-loss path). Same items, shared-memory layout (the KC = 4
 // class with a one-slot tape) and forward interpreter as the fused kernel, without tape,
 // gradient or normal equations; writes the last entry of each item's partial slot.
 // ---------------------------------------------------------------------------------------

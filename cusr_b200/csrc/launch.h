@@ -22,9 +22,9 @@ constexpr int EVAL_NT_WIDE = 2 * EVAL_NT;
 constexpr int EVAL_ROUND = EVAL_NT_WIDE * EVAL_V;
 
 // kc: constant-count class (4, 8, 12, 16, 32 for fp32; 4, 8, 32 for fp64).
-// grad = false launches the value-only kernel (lm_value_kernel: the fp64 audit, losses of
-// K = 0 trees, finite-difference value passes); tg = reverse tape in global scratch
-// (EvalParams::tape_g) instead of shared memory.
+// grad = false launches the value-only kernel (lm_value_kernel: the fp64 audit and the
+// finite-difference value passes); tg = reverse tape in global scratch (EvalParams::tape_g)
+// instead of shared memory.
 // wide = EVAL_NT_WIDE threads per block (grad launches only)
 cudaError_t eval_launch_f32(int kc, bool grad, bool tg, bool wide, const EvalParams<float> &p,
                             int grid, size_t smem, cudaStream_t s);
