@@ -22,7 +22,8 @@
 //     [slot][thread] (conflict-free, no block barriers inside an item);
 //   * the gradient rows (df/dc_k over the thread's samples) and the residual row are written
 //     into tape slots the reverse program no longer needs (the compiler's row table names
-//     them), so they take no shared memory of their own;
+//     them), so they take no shared memory of their own (a launch whose tape is in global
+//     memory keeps them in a small shared-memory row region instead);
 //   * each warp forms the (K+1)x(K+1) Gram matrix of [g; r] over its samples on the fp64
 //     tensor cores, straight from those rows; its packed lower triangle is the partial layout
 //     (JtJ, Jtr, sum r^2). KC = constant-count class of the bin (K <= KC); KC = 1, 2 run the
