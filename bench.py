@@ -16,7 +16,13 @@ and the time is the max over ranks. Results are gathered to rank 0 once, outside
 per step), device-timed with CUDA events on the engine's stream. `e2e`: the same metric through
 the public extended entry point (co_optimize_ex) from pinned host buffers, H2D and D2H inside.
 `--impl reference`: the reference's CPU path (ScipyPop restated in oracle/scipy_lm.py:
-scipy least_squares LM per tree, one process per host core) on a bounded sample of trees.
+scipy least_squares LM per tree, one process per host core) on a bounded sample of trees; its
+line also carries `reference_gpu`, the reference's own CUDA LM path (batch_lm_revad built from
+its sources for sm_100a by oracle/Makefile) timed on the same 16,384-tree population, when that
+binary is present. `--impl reference_gpu` prints that measurement as its own line.
+
+Reports that are files (the nvidia-smi clock samples) go to --out-dir, default
+$CUSR_REPORT_DIR, else a temporary directory.
 """
 from __future__ import annotations
 
@@ -26,6 +32,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -151,18 +158,33 @@ def pinned_copy(pop: dict) -> dict:
     return out
 
 
+def out_dir(args) -> Path:
+    d = args.out_dir or os.environ.get("CUSR_REPORT_DIR") or tempfile.mkdtemp(prefix="cusr_bench_")
+    p = Path(d)
+    p.mkdir(parents=True, exist_ok=True)
+    return p
+
+
 def profile_value(key: str):
-    """A number recorded in the committed ncu summary of the evaluation kernel
-    (profiles/lm_eval_kernel_metric.md, lines `key: value`)."""
+    """A figure recorded in the committed ncu summary of the evaluation kernel
+    (profiles/lm_eval_kernel_metric.md, lines `key: value`): NOT measured by this run, so it is
+    returned with its source and the commit it was captured at."""
     if not PROFILE_SUMMARY.exists():
         return None
+    val, commit = None, None
     for line in PROFILE_SUMMARY.read_text().splitlines():
-        if line.strip().startswith(key + ":"):
+        t = line.strip()
+        if t.startswith(key + ":"):
             try:
-                return float(line.split(":", 1)[1].strip().split()[0])
+                val = float(t.split(":", 1)[1].strip().split()[0])
             except ValueError:
-                return None
-    return None
+                val = None
+        elif t.startswith("captured_at:"):
+            commit = t.split(":", 1)[1].strip()
+    if val is None:
+        return None
+    return {"value": val, "source": str(PROFILE_SUMMARY.relative_to(ROOT)),
+            "captured_at": commit, "measured_in_this_run": False}
 
 
 def cpu_baseline(pop: dict, target_s: float = 15.0) -> dict:
@@ -186,6 +208,52 @@ def cpu_baseline(pop: dict, target_s: float = 15.0) -> dict:
             "sample": f"{len(idx)} of {M} trees (stratified), N={pop['N']}, scipy "
                       f"least_squares lm xtol=ftol=1e-10 max_nfev=200, fp64, {wall:.1f} s",
             "wall_s": wall}
+
+
+def reference_gpu(pop: dict, runs: int = 3, warmup: int = 1) -> dict:
+    """The reference's own CUDA LM path on `pop`: oracle/_ref/batch_lm_revad_prof (its sources
+    built for sm_100a, fast-math fp32, host-driven loop, 50 iterations), timed by its own
+    PROFILE_JSON loop_ms; trees/s = (M - K0 trees) / loop_ms, its convention
+    (experiments/e6_kernel_sweep/sweep_e6.py:126-132). Median of `runs` runs after `warmup`."""
+    from oracle import ref_gpu
+
+    try:
+        with ref_gpu.RefGPU(pop) as rg:
+            for _ in range(warmup):
+                rg.run(max_iter=50)
+            outs = [rg.run(max_iter=50) for _ in range(runs)]
+            n_nodes = int(np.asarray(rg.pop["metas"])[:, 1].sum())
+    except (FileNotFoundError, ValueError, RuntimeError, subprocess.TimeoutExpired) as e:
+        return {"unavailable": str(e)[:300]}
+    loops = sorted(o["loop_ms"] for o in outs)
+    med = loops[len(loops) // 2]
+    last = outs[-1]
+    M = int(pop["M"])
+    return {"value": (M - int(np.sum(np.asarray(pop["metas"])[:, 3] == 0))) / (med / 1e3),
+            "unit": "fits/s", "loop_ms_runs": loops, "loop_ms": med,
+            "iters_run": int(last["profile"]["iters_run"]),
+            "total_ms": float(last["profile"]["total_ms"]),
+            "statuses": np.bincount(last["status"], minlength=5).tolist(),
+            "binary": "oracle/_ref/batch_lm_revad_prof: cusr/kernel/batch_lm_revad.cu built for "
+                      "sm_100a with the reference's flags (-O2 --use_fast_math) and -DPROFILE",
+            "population": f"the same {M} trees (metric config, seed 0); log|x| and sqrt|x| "
+                          f"encoded as LOG(ABS(x)) / SQRT(ABS(x)) ({n_nodes} nodes)",
+            "convention": "trees/s = (M - K0) / loop_ms (LM loop only, setup and load excluded)"}
+
+
+def run_reference_gpu(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    pop = make_population(1)
+    rg = reference_gpu(pop, runs=max(1, min(args.steps, 5)), warmup=max(1, min(args.warmup, 2)))
+    line = {"impl": "reference_gpu", "metric": METRIC, "value": rg.get("value"),
+            "unit": "fits/s", "n_gpus": 1, "steps": len(rg.get("loop_ms_runs", [])),
+            "warmup": max(1, min(args.warmup, 2)),
+            "ms_per_step": rg.get("loop_ms"), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "pop 16k, N=10k, 50 iters (metric config, seed 0)"},
+            "reference_gpu": rg}
+    print(json.dumps(line), flush=True)
 
 
 def run_reference(args, world: int, rank: int) -> None:
@@ -223,6 +291,8 @@ def run_reference(args, world: int, rank: int) -> None:
         "e2e": {"value": value, "unit": "fits/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if not args.no_reference_gpu:
+        line["reference_gpu"] = reference_gpu(pop)
     print(json.dumps(line), flush=True)
 
 
@@ -240,9 +310,7 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
     for _ in range(args.warmup):
         co.fit_loaded(max_iter=50)
     barrier(world)
-    out_dir = ROOT / "gpurun_out"
-    out_dir.mkdir(exist_ok=True)
-    clocks = ClockSampler(local if world > 1 else 0, out_dir / f"clocks_rank{rank}.csv")
+    clocks = ClockSampler(local if world > 1 else 0, out_dir(args) / f"clocks_rank{rank}.csv")
     dev_ms, eval_ms, eval_launches, launches, flops, node_evals = [], 0.0, 0, 0, 0.0, 0
     res = None
     for _ in range(args.steps):
@@ -306,12 +374,15 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
         "frac": (achieved / fp32_peak) if achieved and fp32_peak else None,
         "peak_source": "measured FP32 FMA probe (co_probe_peak, same run); MEASURED_PEAKS.json "
                        "holds only HBM and bf16 tensor peaks",
-        "traffic": profile_value("traffic_bytes_per_launch"),
-        "traffic_note": "dram read+write bytes of one evaluation launch (ncu, committed "
-                        "profile summary); inputs and partial sums are L2-resident",
+        "traffic": (profile_value("traffic_bytes_per_launch") or {}).get("value"),
+        "traffic_source": profile_value("traffic_bytes_per_launch"),
+        "traffic_note": "dram read+write bytes of one evaluation launch from the committed ncu "
+                        "capture (not measured in this run); inputs and partial sums are "
+                        "L2-resident",
         "issue": {"bound": "issue", "achieved_pct": profile_value("issue_active_pct"),
-                  "note": "issue slots busy on the evaluation kernel (ncu): the interpreter is "
-                          "bound by instruction issue latency, not FMA or HBM throughput"},
+                  "note": "issue slots busy on the evaluation kernel, from the committed ncu "
+                          "capture (not measured in this run): the interpreter is bound by "
+                          "instruction issue, not FMA or HBM throughput"},
         "avg_launch_ms": avg_launch_ms,
         "flops_def": "per evaluated (tree, sample): 2 per operator node (value + adjoint) + "
                      "2 per normal-equation entry (K+1)(K+2)/2",
@@ -463,8 +534,12 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference_gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="--impl reference: skip timing the reference's CUDA path")
+    ap.add_argument("--out-dir", default=None,
+                    help="directory for report files (default $CUSR_REPORT_DIR, else a temp dir)")
     ap.add_argument("--profile-case", action="store_true",
                     help="run the small ncu case (--profile-trees trees) instead of the benchmark")
     ap.add_argument("--profile-iters", type=int, default=2)
@@ -491,6 +566,8 @@ def main() -> None:
             run_sample_sharded(args, world, rank, local)
         elif args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.impl == "reference_gpu":
+            run_reference_gpu(args, world, rank)
         else:
             run_ours(args, world, rank, local)
     finally:

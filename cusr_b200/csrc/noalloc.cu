@@ -154,11 +154,16 @@ int evaluate_noalloc(int dev, const PopHeader *h, const int32_t *nt, const float
     }
 
     unsigned char *S = ds->scratch;
+    // From here on work is queued on `stream` and reads or writes the shared array: an error
+    // path first waits for whatever was queued (its own result ignored), so no copy or kernel
+    // of this call still uses the array when the next call takes the lock.
 #define NA_CK(x)                                                                             \
     do {                                                                                     \
         cudaError_t _e = (x);                                                                \
         if (_e != cudaSuccess) {                                                             \
             fprintf(stderr, "[cusr_b200] co_evaluate_noalloc: %s\n", cudaGetErrorString(_e)); \
+            cudaStreamSynchronize(stream);                                                   \
+            cudaGetLastError();                                                              \
             return CO_ERR_CUDA;                                                              \
         }                                                                                    \
     } while (0)

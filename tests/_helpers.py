@@ -2,11 +2,30 @@
 from __future__ import annotations
 
 import json
+import os
 from pathlib import Path
 
 import numpy as np
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def report_dir() -> Path | None:
+    """Directory for the measurement reports GPU tests write beside their assertions
+    (parity fractions, error quantiles): CUSR_REPORT_DIR when set, else None (no report)."""
+    d = os.environ.get("CUSR_REPORT_DIR")
+    if not d:
+        return None
+    p = Path(d)
+    p.mkdir(parents=True, exist_ok=True)
+    return p
+
+
+def write_report(name: str, data) -> None:
+    """Write `data` as JSON to <report_dir>/<name> when a report directory is configured."""
+    d = report_dir()
+    if d is not None:
+        (d / name).write_text(json.dumps(data, indent=1, default=float))
 
 VAR, CONST, UFUNC, BFUNC = 0, 1, 2, 3
 

@@ -22,6 +22,11 @@ Everything written here comes from the reference's own code and files:
                                  stored once) and its manifest's per-tree baseline flags
   jac_sample.npz                 the reference's reverse-AD Jacobian samples
                                  (experiments/revad_v5/jac_sample_fixed.jsonl)
+  metric_scipy.npz               reference ScipyPop fits of a 256-tree stratified sample of
+                                 the headline metric population at its full N (--metric)
+  configs_full_scipy.npz         reference ScipyPop fits of 32-tree samples of the mid,
+                                 physics, long and scale configurations at their own N
+                                 (--configs-full; inputs stored as a digest)
 The tests read only these files; the reference is not needed at test time.
 """
 from __future__ import annotations
@@ -35,7 +40,24 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("CUSR_REFERENCE", "/root/reference"))
+
+
+def _reference() -> Path:
+    """The reference checkout, from CUSR_REFERENCE (required: there is no default path)."""
+    ref = os.environ.get("CUSR_REFERENCE")
+    if not ref or not (Path(ref) / "cusr" / "benchmark").is_dir():
+        sys.exit("set CUSR_REFERENCE to the reference (TensorConv/CuSR) checkout")
+    return Path(ref)
+
+
+def pop_digest(pop: dict) -> str:
+    """sha256 over the population arrays (bytecode, metas, c_init, inputs, targets)."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for k in ("nt", "nv", "ci", "metas", "c_init", "xs", "ym"):
+        h.update(np.ascontiguousarray(pop[k]).tobytes())
+    return h.hexdigest()
 
 
 def _pop_arrays(prefix: str, pop: dict) -> dict:
@@ -54,6 +76,7 @@ CONFIG_SAMPLES = (("mid", 64, 1000), ("physics", 64, 1000), ("long", 64, 512), (
 
 def make_config_samples() -> None:
     """configs_scipy.npz: reference ScipyPop fits of sampled configurations."""
+    REF = _reference()
     sys.path.insert(0, str(REF))
     sys.path.insert(0, str(ROOT))
     from cusr.benchmark import backends, interp  # reference code
@@ -74,8 +97,73 @@ def make_config_samples() -> None:
     np.savez_compressed(HERE / "configs_scipy.npz", **arr)
 
 
+# stratified sample of the headline metric population (16,384 trees, seed 0) at its full
+# N = 10,000: the trees behind the benchmarked fits/s, fitted by the reference's CPU backend
+METRIC_SAMPLE = 256
+
+
+def metric_sample_index(M: int = 16384, n: int = METRIC_SAMPLE) -> np.ndarray:
+    """Tree indices of the metric sample: evenly spaced over the population."""
+    return np.unique(np.linspace(0, M - 1, n).astype(np.int64))
+
+
+def make_metric_sample() -> None:
+    """metric_scipy.npz: reference ScipyPop fits of 256 trees of the metric population
+    (synth 'metric', seed 0, N = 10,000, shared target row)."""
+    REF = _reference()
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(ROOT))
+    from cusr.benchmark import backends, interp  # reference code
+
+    from cusr_b200 import popio, synth
+
+    full = synth.make_config("metric", seed=0)
+    idx = metric_sample_index(int(full["M"]))
+    pop = popio.slice_pop(full, idx)
+    ref_pop = _as_ref(pop)
+    sc = backends.ScipyPop(nproc=os.cpu_count()).fit_pop(ref_pop)
+    arr = _pop_arrays("pop", pop)
+    arr.update({"index": idx, "scipy/c_final": sc.c_final, "scipy/status": sc.status,
+                "scipy/nfev": sc.n_iter, "scipy/loss64": interp.loss_pop(ref_pop, sc.c_final),
+                "init/loss64": interp.loss_pop(ref_pop, pop["c_init"].astype(np.float64))})
+    np.savez_compressed(HERE / "metric_scipy.npz", **arr)
+
+
+# (config, trees) of configs_full_scipy.npz: 32-tree samples of the configurations at their
+# own N (mid 10,000; physics 100,000; long 4,096; scale 20,000)
+CONFIG_SAMPLES_FULL = (("mid", 32), ("physics", 32), ("long", 32), ("scale", 32))
+
+
+def make_config_samples_full() -> None:
+    """configs_full_scipy.npz: reference ScipyPop fits of sampled configurations at full N."""
+    REF = _reference()
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(ROOT))
+    from cusr.benchmark import backends, interp  # reference code
+
+    from cusr_b200 import synth
+
+    arr = {}
+    for name, M in CONFIG_SAMPLES_FULL:
+        pop = synth.make_config(name, M=M, seed=11)
+        ref_pop = _as_ref(pop)
+        sc = backends.ScipyPop(nproc=os.cpu_count()).fit_pop(ref_pop)
+        # the inputs and targets are large at full N: stored as a digest, the tests regenerate
+        # them with cusr_b200.synth (seeded) and check the digest
+        arr.update({k: v for k, v in _pop_arrays(name, pop).items()
+                    if not k.endswith(("/xs", "/ym"))})
+        arr[f"{name}/digest"] = np.asarray(pop_digest(pop))
+        arr[f"{name}/scipy/c_final"] = sc.c_final
+        arr[f"{name}/scipy/status"] = sc.status
+        arr[f"{name}/scipy/loss64"] = interp.loss_pop(ref_pop, sc.c_final)
+        arr[f"{name}/init/loss64"] = interp.loss_pop(ref_pop, pop["c_init"].astype(np.float64))
+        print(name, "fitted", flush=True)
+    np.savez_compressed(HERE / "configs_full_scipy.npz", **arr)
+
+
 def make_honesty() -> None:
     """fp32_honesty.npz: the fp32-honesty regression fixtures of the reference."""
+    REF = _reference()
     sys.path.insert(0, str(REF))
     from cusr.benchmark import popio  # reference loader
 
@@ -102,6 +190,13 @@ def main() -> None:
     if "--honesty" in sys.argv:
         make_honesty()
         return
+    if "--metric" in sys.argv:
+        make_metric_sample()
+        return
+    if "--configs-full" in sys.argv:
+        make_config_samples_full()
+        return
+    REF = _reference()
     sys.path.insert(0, str(REF))
     sys.path.insert(0, str(ROOT))
     from cusr.benchmark import backends, interp, popio  # reference code

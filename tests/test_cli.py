@@ -116,12 +116,9 @@ def test_parity_gate_through_cli(tmp_path):
 
     rates = {"loss_down": loss_down, "within_1.05": env(1.05), "within_10": env(10.0),
              "both_converged": int(both.sum())}
-    import json
-    import os
+    from _helpers import write_report
 
-    if os.path.isdir("gpurun_out"):
-        with open("gpurun_out/parity_gate_pop1000.json", "w") as f:
-            json.dump(rates, f)
+    write_report("parity_gate_pop1000.json", rates)
     assert rates["loss_down"] >= 0.93, rates
     assert rates["within_1.05"] >= 0.90, rates
     assert rates["within_10"] >= 0.99, rates

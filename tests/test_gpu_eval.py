@@ -81,10 +81,9 @@ def test_values_fp32_fast_match_oracle(co):
 def _report_fast_values(co, pop):
     """Error statistics of the fast-math values against the fp64 oracle and the IEEE fp32
     path (written next to the GPU run's other parity reports)."""
-    import json
-    import os
+    from _helpers import report_dir, write_report
 
-    if not os.path.isdir("gpurun_out"):
+    if report_dir() is None:
         return
     fast = co.evaluate(pop, precision="fp32_fast", values=True)["values"]
     ieee = co.evaluate(pop, precision="fp32", values=True)["values"]
@@ -100,11 +99,11 @@ def _report_fast_values(co, pop):
             rel_i.append(np.abs(ieee[m][fin] - y[fin]) / np.abs(y[fin]))
     rf, ri = np.concatenate(rel_f), np.concatenate(rel_i)
     q = [0.5, 0.9, 0.99, 0.999]
-    with open(f"gpurun_out/fast_values_M{pop['M']}_N{pop['N']}.json", "w") as f:
-        json.dump({"fast_rel_quantiles": np.nanquantile(rf, q).tolist(),
-                   "ieee_rel_quantiles": np.nanquantile(ri, q).tolist(),
-                   "fast_within_1e-5": float(np.mean(rf <= 1e-5)),
-                   "ieee_within_1e-5": float(np.mean(ri <= 1e-5))}, f)
+    write_report(f"fast_values_M{pop['M']}_N{pop['N']}.json",
+                 {"fast_rel_quantiles": np.nanquantile(rf, q).tolist(),
+                  "ieee_rel_quantiles": np.nanquantile(ri, q).tolist(),
+                  "fast_within_1e-5": float(np.mean(rf <= 1e-5)),
+                  "ieee_within_1e-5": float(np.mean(ri <= 1e-5))})
 
 
 def test_values_mid_config_both_precisions(co):

@@ -4,19 +4,17 @@ audit invariant, determinism, context reuse, and the error codes."""
 from __future__ import annotations
 
 import ctypes
-import json
 from pathlib import Path
 
 import numpy as np
 import pytest
 
-from _helpers import GOLDEN, fixture_pop, fixture_truth, load_npz_pop, pop1000
+from _helpers import GOLDEN, fixture_pop, fixture_truth, load_npz_pop, pop1000, write_report
 from cusr_b200 import InProcessCO, co_inproc, get_inproc_co, popio, synth
 from oracle import interp, lm
 
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
-REPORT = ROOT / "gpurun_out"
 
 
 @pytest.fixture(scope="module")
@@ -27,8 +25,7 @@ def co():
 
 
 def _report(name, data):
-    REPORT.mkdir(exist_ok=True)
-    (REPORT / f"parity_{name}.json").write_text(json.dumps(data, indent=1, default=float))
+    write_report(f"parity_{name}.json", data)
 
 
 def _c(res, fx):

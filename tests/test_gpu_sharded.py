@@ -108,15 +108,14 @@ def test_sample_sharded_matches_single_gpu(precision, max_iter, min_status, ltol
     both = np.isfinite(lf) & np.isfinite(lf_full)
     rel = np.abs(lf[both] - lf_full[both]) / np.maximum(np.abs(lf_full[both]), 1e-30)
     close = float(np.mean(rel <= ltol))
-    if os.path.isdir("gpurun_out"):
-        import json
+    from _helpers import write_report
 
-        pairs = {}
-        for a, b in zip(r0["status"].tolist(), full["status"].tolist()):
-            pairs[f"{a}-{b}"] = pairs.get(f"{a}-{b}", 0) + 1
-        with open(f"gpurun_out/sharded_{precision}_{max_iter}.json", "w") as f:
-            json.dump({"status_pairs": pairs, "same_status": same_status, "close": close,
-                       "rel_quantiles": np.quantile(rel, [0.5, 0.9, 0.99, 1.0]).tolist()}, f)
+    pairs = {}
+    for a, b in zip(r0["status"].tolist(), full["status"].tolist()):
+        pairs[f"{a}-{b}"] = pairs.get(f"{a}-{b}", 0) + 1
+    write_report(f"sharded_{precision}_{max_iter}.json",
+                 {"status_pairs": pairs, "same_status": same_status, "close": close,
+                  "rel_quantiles": np.quantile(rel, [0.5, 0.9, 0.99, 1.0]).tolist()})
     assert same_status >= min_status, same_status
     assert close >= min_close, close
 

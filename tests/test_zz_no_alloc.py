@@ -13,7 +13,8 @@ import ctypes
 import numpy as np
 import pytest
 
-from cusr_b200 import InProcessCO, co_inproc, synth
+from _helpers import make_tree
+from cusr_b200 import InProcessCO, co_inproc, popio, synth
 
 pytestmark = pytest.mark.gpu
 
@@ -95,3 +96,20 @@ def test_noalloc_rejects_populations_beyond_the_fixed_array():
     big = synth.make_config("mid", M=16, N=2_000_000, seed=23)
     rc, _ = _call(fn, big)
     assert rc == co_inproc.CO_ERR_BOUNDS
+
+
+def test_noalloc_rejects_trees_whose_tape_needs_global_memory():
+    """A tree whose reverse tape does not fit in shared memory beside a second resident block
+    (the allocating entry would put it in a global-memory tape): CO_ERR_BOUNDS before any
+    work is queued, and the caller's output buffer is left as it was."""
+    fn = _bind()
+    depth = 150                                   # sin(sin(...sin(c * x0)...)): 151 tape slots
+    nodes = [("u", 14)] * depth + [("b", 3), ("c",), ("v", 0)]
+    nt, nv, ci = make_tree(nodes)
+    rng = np.random.default_rng(5)
+    xs = rng.uniform(-1, 1, size=(512, 1)).astype(np.float32)
+    pop = popio.build_pop([(nt, nv, ci, np.array([0.5], np.float32))], xs,
+                          np.zeros(512, np.float32))
+    rc, blocks = _call(fn, pop)
+    assert rc == co_inproc.CO_ERR_BOUNDS
+    assert np.all(np.isnan(blocks))
