@@ -32,8 +32,9 @@ class FitResult:
 class B200Pop:
     """In-process engine backend. precision 'fp32' (IEEE functions), 'fp32_fast' (the
     reference kernel's fast-math arithmetic) or 'fp64'; shared target rows are detected and
-    uploaded once. starts > 1: robust multi-start fits (cusr_b200.multistart; max_iter then
-    defaults to 200)."""
+    uploaded once. starts > 1: the parity-grade multi-start fit (cusr_b200.multistart: the
+    device start axis, trust-region and reference-schedule starts; max_iter then defaults to
+    200)."""
 
     def __init__(self, max_iter: int | None = None, precision: str = "fp32", device_id: int = 0,
                  name: str | None = None, starts: int = 1):
@@ -55,10 +56,9 @@ class B200Pop:
         if self.starts > 1:
             from . import multistart
 
-            t_fit = time.perf_counter()
             res = multistart.fit_multistart(co, pop, starts=self.starts, max_iter=self.max_iter,
-                                            precision=self.precision)
-            t_fit = time.perf_counter() - t_fit
+                                            precision=self.precision,
+                                            wave1=min(8, self.starts - 1))
         else:
             res = co.optimize_ex(pop, max_iter=self.max_iter, precision=self.precision,
                                  y_shared=shared)
@@ -66,8 +66,10 @@ class B200Pop:
         raw = res["status"]
         return FitResult(self.name, res["c_final"].astype(np.float64), _STATUS_MAP[raw],
                          res["iters"].astype(np.int32), time.perf_counter() - t0,
-                         st["device_ms"] / 1e3 if self.starts == 1 else t_fit,
+                         st["device_ms"] / 1e3,
                          meta=dict(dtype=self.precision, raw_status_counts={
                              int(k): int(v) for k, v in zip(*np.unique(raw, return_counts=True))},
-                             criteria=f"reference LM (lambda0 1e-3), max_iter={self.max_iter}"
-                                      + (f", {self.starts} starts" if self.starts > 1 else "")))
+                             criteria=(f"reference LM (lambda0 1e-3), max_iter={self.max_iter}"
+                                       if self.starts == 1 else
+                                       f"{self.starts} starts (trust region + reference LM), "
+                                       f"max_iter={self.max_iter}, best final loss")))

@@ -44,6 +44,9 @@ PRECISIONS = {"fp32": CO_PREC_FP32, "fp64": CO_PREC_FP64, "fp32_fast": CO_PREC_F
 
 
 AD_MODES = {"auto": 0, "forward": 1, "reverse": 2}
+# LM algorithm: the reference schedule (co_lib.cu) or MINPACK's trust region (the reference's
+# scipy backend)
+ALGORITHMS = {"reference": 0, "trust_region": 1}
 
 
 def prec_code(precision: str) -> int:
@@ -96,7 +99,11 @@ class CoOptions(ctypes.Structure):
         ("fp64_audit", ctypes.c_int32), ("early_exit", ctypes.c_int32),
         ("sample_sharded", ctypes.c_int32), ("keep_inputs", ctypes.c_int32),
         ("ad_mode", ctypes.c_int32), ("damping_always", ctypes.c_int32),
-        ("damping_floor", ctypes.c_double), ("reserved", ctypes.c_int32 * 2),
+        ("damping_floor", ctypes.c_double),
+        ("algorithm", ctypes.c_int32), ("n_starts", ctypes.c_int32),
+        ("tr_starts", ctypes.c_int32), ("wave1", ctypes.c_int32),
+        ("ftol", ctypes.c_double), ("gtol", ctypes.c_double), ("agree_tol", ctypes.c_double),
+        ("start_seed", ctypes.c_uint64), ("reserved", ctypes.c_int32 * 2),
     ]
 
 
@@ -109,7 +116,9 @@ class CoStats(ctypes.Structure):
         ("eval_launches", ctypes.c_int64), ("kernel_launches", ctypes.c_int64),
         ("iters_run", ctypes.c_int32), ("n_bins", ctypes.c_int32),
         ("y_shared", ctypes.c_int32), ("precision", ctypes.c_int32),
-        ("n_reverted", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7),
+        ("n_reverted", ctypes.c_int32), ("n_starts", ctypes.c_int32),
+        ("fits_run", ctypes.c_int64), ("trees_retired", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 3),
     ]
 
 
@@ -151,6 +160,7 @@ SIGNATURES = {
     "co_jacobian_fd": ([ctypes.c_void_p, ctypes.POINTER(PopHeader), _I32, _F32, _I32,
                         ctypes.POINTER(TreeMeta), _F64, _F32, _F32, ctypes.c_int, ctypes.c_int,
                         ctypes.c_double, _F64], ctypes.c_int),
+    "co_last_starts": ([ctypes.c_void_p, _I32], ctypes.c_int),
     "co_shard_unique_id": ([ctypes.POINTER(ctypes.c_ubyte)], ctypes.c_int),
     "co_shard_init": ([ctypes.c_void_p, ctypes.POINTER(ctypes.c_ubyte), ctypes.c_int,
                        ctypes.c_int, ctypes.c_double], ctypes.c_int),
@@ -210,6 +220,41 @@ def build_header(pop: dict) -> PopHeader:
     for i in range(7):
         h.reserved[i] = 0
     return h
+
+
+def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 1,
+                  tr_starts: int = 0, wave1: int = 0, ftol: float = 1e-10, gtol: float = 1e-8,
+                  agree_tol: float = 1e-7, seed: int = 0) -> CoOptions:
+    """Fill the algorithm / start-axis fields of `opt`:
+      algorithm  'reference' (the reference LM schedule) | 'trust_region' (MINPACK lmder: max_iter
+                 then counts function evaluations, the first included, like scipy's max_nfev)
+      n_starts   fits per tree (start 0 = c_init; the others generated on the device)
+      tr_starts  > 0: starts 0..tr_starts-1 use the trust region, the others the reference
+                 schedule (alternately with the floored damping on every solve)
+      wave1      0 < wave1 < n_starts: run starts 0..wave1-1 first, then the rest only for trees
+                 whose first-wave fits do not agree within agree_tol
+      ftol, gtol trust-region tolerances; seed: start points"""
+    try:
+        opt.algorithm = ALGORITHMS[algorithm]
+    except KeyError:
+        raise ValueError(f"algorithm must be one of {sorted(ALGORITHMS)}") from None
+    opt.n_starts = int(n_starts)
+    opt.tr_starts = int(tr_starts)
+    opt.wave1 = int(wave1)
+    opt.ftol = float(ftol)
+    opt.gtol = float(gtol)
+    opt.agree_tol = float(agree_tol)
+    opt.start_seed = int(seed) & (2 ** 64 - 1)
+    return opt
+
+
+# The parity-grade fit: every tree fitted from 20 starts in one device batch (4 with the
+# trust-region LM of the reference's scipy backend, 16 with the reference schedule and the
+# damping floor), in two waves (trees whose first 8 fits agree skip the other 12), fp64,
+# scipy's tolerances; the lowest final loss is kept.
+PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
+              algorithm="trust_region", n_starts=20, tr_starts=4, wave1=8, ftol=1e-10,
+              gtol=1e-8)
 
 
 class InProcessCO:
@@ -299,7 +344,7 @@ class InProcessCO:
                     y_shared: bool | None = None, lambda0: float = 1e-3, xtol: float = 1e-6,
                     fp64_audit: int = -1, early_exit: bool = True, keep_inputs: bool = False,
                     ad_mode: str = "auto", damping_floor: float = 0.0,
-                    damping_always: bool = False):
+                    damping_always: bool = False, **starts):
         """Extended fit: precision 'fp32' | 'fp64' | 'fp32_fast'; y_shared=True passes one
         target row (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a
         1-D ym). keep_inputs=True reuses the X / shared y left on the device by the previous
@@ -307,10 +352,13 @@ class InProcessCO:
         ad_mode 'auto' | 'forward' (tangents for K <= 2) | 'reverse'. damping_floor > 0
         retries a system the reference damping diag*(1+lam) cannot factor with
         diag + lam*max(diag, f*max diag) (damping_always: use that damping on every solve).
-        Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters."""
+        `starts` (see start_options): algorithm 'reference' | 'trust_region', n_starts,
+        tr_starts, wave1, ftol, gtol, agree_tol, seed.
+        Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters (and,
+        with n_starts > 1, 'start': the start each tree's outputs came from)."""
         return self._fit_ex("co_optimize_ex", pop, max_iter, precision, y_shared, lambda0,
                             xtol, fp64_audit, early_exit, keep_inputs, ad_mode, damping_floor,
-                            damping_always)
+                            damping_always, starts)
 
     def shard_init(self, unique_id: bytes, nranks: int, rank: int,
                    timeout_s: float = 120.0) -> None:
@@ -336,7 +384,7 @@ class InProcessCO:
 
     def _fit_ex(self, entry, pop, max_iter, precision, y_shared, lambda0, xtol, fp64_audit,
                 early_exit, keep_inputs=False, ad_mode="auto", damping_floor=0.0,
-                damping_always=False):
+                damping_always=False, starts=None):
         if self._torn:
             raise RuntimeError("InProcessCO used after teardown()")
         M, total_c = int(pop["M"]), int(pop["total_c"])
@@ -351,6 +399,7 @@ class InProcessCO:
         opt.keep_inputs = 1 if keep_inputs else 0
         opt.damping_floor = float(damping_floor)
         opt.damping_always = 1 if damping_always else 0
+        start_options(opt, **(starts or {}))
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)
@@ -364,8 +413,11 @@ class InProcessCO:
         del keep
         if rc != CO_OK:
             raise COError(rc, entry)
-        return {"c_final": c_final, "status": status, "loss_init": loss_init,
-                "loss_final": loss_final, "iters": iters}
+        out = {"c_final": c_final, "status": status, "loss_init": loss_init,
+               "loss_final": loss_final, "iters": iters}
+        if opt.n_starts > 1:
+            out["start"] = self.last_starts(M)
+        return out
 
     def _options(self, max_iter=50, precision="fp32", y_shared=False, lambda0=1e-3, xtol=1e-6,
                  fp64_audit=-1, early_exit=True, ad_mode="auto") -> CoOptions:
@@ -382,31 +434,37 @@ class InProcessCO:
         return opt
 
     def load(self, pop: dict, precision: str = "fp32", y_shared: bool | None = None,
-             ad_mode: str = "auto") -> None:
+             ad_mode: str = "auto", n_starts: int = 1) -> None:
         """Upload a population once (co_load); fit it with fit_loaded() any number of times.
-        ad_mode fixes the Jacobian mode of the loaded schedule."""
+        ad_mode fixes the Jacobian mode of the loaded schedule, n_starts the fits per tree."""
         if y_shared is None:
             y_shared = np.asarray(pop["ym"]).ndim == 1
         hdr = build_header(pop)
         args, keep = self._inputs(pop, y_shared=bool(y_shared))
         opt = self._options(precision=precision, y_shared=y_shared, ad_mode=ad_mode)
+        opt.n_starts = int(n_starts)
         rc = self._lib.co_load(self._handle, ctypes.byref(hdr), *args, ctypes.byref(opt))
         del keep
         if rc != CO_OK:
             raise COError(rc, "co_load")
-        self._loaded = (int(pop["M"]), int(pop["total_c"]), precision)
+        self._loaded = (int(pop["M"]), int(pop["total_c"]), precision, int(n_starts))
 
     def fit_loaded(self, max_iter: int = 50, lambda0: float = 1e-3, xtol: float = 1e-6,
                    fp64_audit: int = -1, early_exit: bool = True,
-                   sample_sharded: bool = False, precision: str | None = None) -> dict:
+                   sample_sharded: bool = False, precision: str | None = None,
+                   damping_floor: float = 0.0, **starts) -> dict:
         """LM fit of the resident population from its c_init (inputs already in HBM).
         sample_sharded=True: the loaded samples are this rank's slice and the normal
         equations are summed over the shard_init group each iteration. `precision` may switch
-        between 'fp32' and 'fp32_fast' on an fp32 load (default: the load's)."""
-        M, total_c, loaded_prec = self._loaded
+        between 'fp32' and 'fp32_fast' on an fp32 load (default: the load's). `starts` as in
+        optimize_ex (n_starts is the load's)."""
+        M, total_c, loaded_prec, n_starts = self._loaded
         precision = precision or loaded_prec
         opt = self._options(max_iter, precision, False, lambda0, xtol, fp64_audit, early_exit)
         opt.sample_sharded = 1 if sample_sharded else 0
+        opt.damping_floor = float(damping_floor)
+        start_options(opt, **starts)
+        opt.n_starts = n_starts
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)
@@ -418,8 +476,19 @@ class InProcessCO:
             loss_final.ctypes.data_as(_F64), iters.ctypes.data_as(_I32))
         if rc != CO_OK:
             raise COError(rc, "co_fit_loaded")
-        return {"c_final": c_final, "status": status, "loss_init": loss_init,
-                "loss_final": loss_final, "iters": iters}
+        out = {"c_final": c_final, "status": status, "loss_init": loss_init,
+               "loss_final": loss_final, "iters": iters}
+        if n_starts > 1:
+            out["start"] = self.last_starts(M)
+        return out
+
+    def last_starts(self, M: int) -> np.ndarray:
+        """The start each tree's outputs of the last fit came from (co_last_starts)."""
+        out = np.zeros(max(int(M), 1), np.int32)
+        rc = self._lib.co_last_starts(self._handle, out.ctypes.data_as(_I32))
+        if rc != CO_OK:
+            raise COError(rc, "co_last_starts")
+        return out[:int(M)]
 
     def evaluate(self, pop: dict, c=None, precision: str = "fp32", values: bool = True,
                  jacobian: bool = False, blocks: bool = False) -> dict:

@@ -35,6 +35,7 @@
 #include "lm_kernels.cuh"
 #include "pack.h"
 #include "shard_comm.h"
+#include "starts.cuh"
 
 namespace cusr {
 
@@ -54,6 +55,10 @@ struct Prep {
     Schedule sc;
     int64_t ldx = 0, y_rows = 0;
     bool y_shared = false;
+    // start axis: S fits per tree (fit i = tree i / S, start i % S); S = 1 is the plain fit
+    int S = 1;
+    int64_t M_fit = 0, total_c_fit = 0;
+    std::vector<int32_t> tree_coff;   // per tree: offset of its constants in c_init
 };
 
 struct Ctx {
@@ -71,7 +76,11 @@ struct Ctx {
     DBuf partials, blk;
     DBuf c64, l64, n_rev;
     DBuf vals, jac;
+    // start axis and trust-region state (per fit), tree-level inputs and outputs
+    DBuf c_tree, tree_coff, imode, tr, diag, outer, resolved, n_retired;
+    DBuf out_c, out_status, out_li, out_lf, out_iters, out_start;
     int *h_nrun = nullptr;                  // pinned, one slot per iteration parity
+    std::vector<int32_t> h_start;           // winning start per tree of the last fit
     std::vector<cudaEvent_t> events;        // timing events, reused across calls
     cudaEvent_t ev_nrun[2] = {nullptr, nullptr};
     bool step_attr_set[2] = {false, false};
@@ -293,7 +302,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
 }
 
 template <typename T>
-int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
+int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp, int S = 1) {
     const PopHeader *h = pr.h;
     const int M = h->M_prob, N = h->N, n_vars = h->n_vars;
     const int64_t total_c = h->total_c;
@@ -303,6 +312,37 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     // ---- compile + schedule (host) ----
     int rc = compile_population(h, pr.nt, pr.nv, pr.ci, pr.metas, &pp.pk);
     if (rc != CO_OK) return rc;
+    // start axis: S fits per tree sharing its program, constants of their own
+    S = std::max(1, S);
+    if ((int64_t)M * S > INT32_MAX / 2) return CO_ERR_BOUNDS;
+    pp.S = S;
+    pp.M_fit = (int64_t)M * S;
+    pp.tree_coff.resize((size_t)M);
+    for (int m = 0; m < M; ++m) pp.tree_coff[(size_t)m] = pr.metas[m].c_offset;
+    PackResult pk_fit;
+    std::vector<TreeMeta> metas_fit;
+    const PackResult *pks = &pp.pk;
+    const TreeMeta *ms = pr.metas;
+    pp.total_c_fit = total_c;
+    if (S > 1) {
+        pk_fit.trees.reserve((size_t)pp.M_fit);
+        metas_fit.reserve((size_t)pp.M_fit);
+        int64_t coff = 0;
+        for (int m = 0; m < M; ++m)
+            for (int s_ = 0; s_ < S; ++s_) {
+                pk_fit.trees.push_back(pp.pk.trees[(size_t)m]);
+                TreeMeta tm = pr.metas[m];
+                tm.c_offset = (int32_t)coff;
+                coff += tm.K;
+                metas_fit.push_back(tm);
+            }
+        if (coff > INT32_MAX) return CO_ERR_BOUNDS;
+        pp.total_c_fit = coff;
+        pks = &pk_fit;
+        ms = metas_fit.data();
+    }
+    const int M_fit = (int)pp.M_fit;
+    const int64_t total_c_fit = pp.total_c_fit;
     if (pr.keep_inputs &&
         !(ctx->in_valid && ctx->in_shared && ctx->in_N == N && ctx->in_nvars == n_vars))
         return CO_ERR_NULLARG;
@@ -318,8 +358,8 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     st.y_shared = y_shared ? 1 : 0;
     const int round = EVAL_ROUND;
     Schedule &sc = pp.sc;
-    build_schedule(pp.pk, pr.metas, M, N, y_shared, fp64, round, ctx->sm_count * 3, &sc,
-                   ctx->fwd_max);
+    build_schedule(*pks, ms, M_fit, N, y_shared, fp64, round, ctx->sm_count * 3, &sc,
+                   ctx->fwd_max, S);
     st.n_bins = (int)sc.bins.size();
     pp.ldx = ((int64_t)N + round - 1) / round * round;
     pp.y_rows = y_shared ? 1 : M;
@@ -328,8 +368,8 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     // ---- device buffers (grow-only) ----
     CK(cudaSetDevice(ctx->device));
     GROW(ctx->code, pp.pk.code.size() * sizeof(uint32_t));
-    GROW(ctx->desc, (size_t)M * sizeof(TreeDesc));
-    GROW(ctx->bin_trees, (size_t)M * sizeof(int32_t));
+    GROW(ctx->desc, (size_t)M_fit * sizeof(TreeDesc));
+    GROW(ctx->bin_trees, (size_t)M_fit * sizeof(int32_t));
     GROW(ctx->bin_tree_off, (sc.bins.size() + 1) * sizeof(int64_t));
     GROW(ctx->bin_item_off, sc.bins.size() * sizeof(int64_t));
     GROW(ctx->items, (size_t)sc.total_items * sizeof(int2));
@@ -338,18 +378,32 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     GROW(ctx->xs_raw, (size_t)N * n_vars * sizeof(float));
     GROW(ctx->xs, (size_t)n_vars * ldx * sizeof(float));
     GROW(ctx->ym, (size_t)y_rows * ldx * sizeof(float));
-    GROW(ctx->c, total_c * sizeof(T));
-    GROW(ctx->ctry, total_c * sizeof(T));
-    GROW(ctx->delta, total_c * sizeof(T));
-    GROW(ctx->cinit_f, total_c * sizeof(float));
-    GROW(ctx->lam, (size_t)M * sizeof(T));
-    GROW(ctx->loss, (size_t)M * sizeof(T));
-    GROW(ctx->loss_init, (size_t)M * sizeof(T));
-    GROW(ctx->status, (size_t)M * sizeof(int32_t));
-    GROW(ctx->iters, (size_t)M * sizeof(int32_t));
-    GROW(ctx->pending, (size_t)M * sizeof(int32_t));
-    GROW(ctx->n_eval, (size_t)M * sizeof(int32_t));
+    GROW(ctx->c, total_c_fit * sizeof(T));
+    GROW(ctx->ctry, total_c_fit * sizeof(T));
+    GROW(ctx->delta, total_c_fit * sizeof(T));
+    GROW(ctx->cinit_f, total_c_fit * sizeof(float));
+    GROW(ctx->diag, total_c_fit * sizeof(double));
+    GROW(ctx->lam, (size_t)M_fit * sizeof(T));
+    GROW(ctx->loss, (size_t)M_fit * sizeof(T));
+    GROW(ctx->loss_init, (size_t)M_fit * sizeof(T));
+    GROW(ctx->status, (size_t)M_fit * sizeof(int32_t));
+    GROW(ctx->iters, (size_t)M_fit * sizeof(int32_t));
+    GROW(ctx->pending, (size_t)M_fit * sizeof(int32_t));
+    GROW(ctx->n_eval, (size_t)M_fit * sizeof(int32_t));
+    GROW(ctx->outer, (size_t)M_fit * sizeof(int32_t));
+    GROW(ctx->imode, (size_t)M_fit);
+    GROW(ctx->tr, (size_t)M_fit * TR_FIELDS * sizeof(double));
     GROW(ctx->n_run, 2 * sizeof(int));
+    GROW(ctx->c_tree, total_c * sizeof(float));
+    GROW(ctx->tree_coff, (size_t)M * sizeof(int32_t));
+    GROW(ctx->resolved, (size_t)M);
+    GROW(ctx->n_retired, sizeof(int));
+    GROW(ctx->out_c, total_c * sizeof(T));
+    GROW(ctx->out_status, (size_t)M * sizeof(int32_t));
+    GROW(ctx->out_li, (size_t)M * sizeof(T));
+    GROW(ctx->out_lf, (size_t)M * sizeof(T));
+    GROW(ctx->out_iters, (size_t)M * sizeof(int32_t));
+    GROW(ctx->out_start, (size_t)M * sizeof(int32_t));
     GROW(ctx->partials, (size_t)sc.partial_elems * sizeof(T));
     GROW(ctx->blk, (size_t)sc.block_elems * sizeof(T));
 
@@ -357,7 +411,7 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     cudaStream_t s = ctx->stream;
     std::vector<int32_t> bin_trees;
     std::vector<int64_t> bin_tree_off, bin_item_off;
-    bin_trees.reserve((size_t)M);
+    bin_trees.reserve((size_t)M_fit);
     for (const Bin &b : sc.bins) {
         bin_tree_off.push_back((int64_t)bin_trees.size());
         bin_item_off.push_back(b.item_off);
@@ -368,7 +422,9 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
         CK(cudaMemcpyAsync(ctx->code.ptr, pp.pk.code.data(), pp.pk.code.size() * sizeof(uint32_t),
                            cudaMemcpyHostToDevice, s));
     if (M > 0) {
-        CK(cudaMemcpyAsync(ctx->desc.ptr, sc.desc.data(), (size_t)M * sizeof(TreeDesc),
+        CK(cudaMemcpyAsync(ctx->desc.ptr, sc.desc.data(), (size_t)M_fit * sizeof(TreeDesc),
+                           cudaMemcpyHostToDevice, s));
+        CK(cudaMemcpyAsync(ctx->tree_coff.ptr, pp.tree_coff.data(), (size_t)M * sizeof(int32_t),
                            cudaMemcpyHostToDevice, s));
         CK(cudaMemcpyAsync(ctx->bin_trees.ptr, bin_trees.data(),
                            bin_trees.size() * sizeof(int32_t), cudaMemcpyHostToDevice, s));
@@ -402,8 +458,9 @@ int prepare(Ctx *ctx, const Problem &pr, bool y_shared_in, Prep &pp) {
     ctx->in_N = N;
     ctx->in_nvars = n_vars;
     }
+    // the caller's c_init, per tree; the fits' start points are made from it on the device
     if (total_c > 0)
-        CK(cudaMemcpyAsync(ctx->cinit_f.ptr, pr.c_init, total_c * sizeof(float),
+        CK(cudaMemcpyAsync(ctx->c_tree.ptr, pr.c_init, total_c * sizeof(float),
                            cudaMemcpyHostToDevice, s));
     return CO_OK;
 }
@@ -439,11 +496,11 @@ int shard_reduce_blocks(Ctx *ctx, int M, int64_t block_elems) {
 // Compile, schedule and upload a problem; it stays resident in the context until the next
 // load (inputs in HBM across fits).
 template <typename T>
-int load(Ctx *ctx, const Problem &pr, bool y_shared) {
+int load(Ctx *ctx, const Problem &pr, bool y_shared, int S = 1) {
     ctx->loaded = false;
     ctx->stats = CoStats{};
     ctx->stats.precision = sizeof(T) == 8 ? CO_PREC_FP64 : CO_PREC_FP32;
-    int rc = prepare<T>(ctx, pr, y_shared, ctx->prep);
+    int rc = prepare<T>(ctx, pr, y_shared, ctx->prep, S);
     if (rc != CO_OK) return rc;
     ctx->hdr = *pr.h;
     ctx->n_nodes.resize((size_t)pr.h->M_prob);
@@ -488,33 +545,77 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     const PackResult &pk = pp.pk;
     const Schedule &sc = pp.sc;
     const int64_t ldx = pp.ldx;
+    const int S = pp.S;
+    const int M_fit = (int)pp.M_fit;
+    const int64_t total_c_fit = pp.total_c_fit;
+    st.n_starts = S;
     cudaStream_t s = ctx->stream;
     const bool sharded = opt.sample_sharded != 0;
     if (sharded && !ctx->shard.comm) return CO_ERR_NULLARG;
+    // which fits use the trust-region algorithm: tr_starts > 0 names the first starts,
+    // otherwise `algorithm` applies to every start
+    const int tr_fits = opt.tr_starts > 0 ? std::min(opt.tr_starts, S)
+                                          : (opt.algorithm == CO_ALG_TRUST_REGION ? S : 0);
+    const bool has_tr = tr_fits > 0, has_ref = tr_fits < S;
+    const int wave1 = (S > 1 && opt.wave1 > 0 && opt.wave1 < S) ? opt.wave1 : 0;
+    if (sharded && has_tr) return CO_ERR_NULLARG;   // sample-sharded fits: reference schedule
     CK(cudaEventRecord(ctx->ev_fit[0], s));
-    init_state_kernel<T><<<grid_for(ctx, std::max<int64_t>(total_c, M)), 256, 0, s>>>(
-        P<float>(ctx->cinit_f), total_c, P<T>(ctx->c), P<T>(ctx->ctry), M, (T)opt.lambda0,
-        P<T>(ctx->lam), P<int32_t>(ctx->status), P<int32_t>(ctx->iters),
-        P<int32_t>(ctx->pending), P<int32_t>(ctx->n_eval));
-    CK(cudaGetLastError());
-    st.kernel_launches++;
+    {
+        StartsParams<T> ip;
+        ip.desc = P<TreeDesc>(ctx->desc);
+        ip.tree_coff = P<int32_t>(ctx->tree_coff);
+        ip.c_tree = P<float>(ctx->c_tree);
+        ip.M_fit = M_fit;
+        ip.S = S;
+        ip.wave1 = wave1;
+        ip.tr_starts = tr_fits;
+        ip.damp_alternate = (S > 1 && opt.damping_floor > 0.0) ? 1 : 0;
+        ip.seed = opt.start_seed;
+        ip.lam0 = (T)opt.lambda0;
+        ip.c_start = P<float>(ctx->cinit_f);
+        ip.c = P<T>(ctx->c);
+        ip.ctry = P<T>(ctx->ctry);
+        ip.lam = P<T>(ctx->lam);
+        ip.status = P<int32_t>(ctx->status);
+        ip.iters = P<int32_t>(ctx->iters);
+        ip.pending = P<int32_t>(ctx->pending);
+        ip.n_eval = P<int32_t>(ctx->n_eval);
+        ip.outer = P<int32_t>(ctx->outer);
+        ip.imode = P<uint8_t>(ctx->imode);
+        ip.tr = P<double>(ctx->tr);
+        ip.diag = P<double>(ctx->diag);
+        init_starts_kernel<T><<<grid_for(ctx, M_fit), 256, 0, s>>>(ip);
+        CK(cudaGetLastError());
+        st.kernel_launches++;
+    }
+    if (wave1) {
+        CK(cudaMemsetAsync(ctx->resolved.ptr, 0, (size_t)M, s));
+        CK(cudaMemsetAsync(ctx->n_retired.ptr, 0, sizeof(int), s));
+    }
 
     // ---- step-kernel launch geometry ----
     const size_t step_smem = (size_t)STEP_WARPS * STEP_WARP_D * sizeof(double);
+    const size_t tr_smem = (size_t)TR_WARPS * TR_WARP_D * sizeof(double);
     if (!ctx->step_attr_set[fp64 ? 1 : 0]) {
         CK(cudaFuncSetAttribute(lm_step_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)step_smem));
+        CK(cudaFuncSetAttribute(lm_tr_step_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)tr_smem));
         ctx->step_attr_set[fp64 ? 1 : 0] = true;
     }
-    int step_occ = 0;
+    int step_occ = 0, tr_occ = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&step_occ, lm_step_kernel<T>, STEP_THREADS,
                                                      step_smem));
-    const int step_grid = std::max(1, std::min((M + STEP_WARPS - 1) / STEP_WARPS,
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&tr_occ, lm_tr_step_kernel<T>, TR_THREADS,
+                                                     tr_smem));
+    const int step_grid = std::max(1, std::min((M_fit + STEP_WARPS - 1) / STEP_WARPS,
                                                std::max(1, step_occ) * ctx->sm_count));
+    const int tr_grid = std::max(1, std::min((M_fit + TR_WARPS - 1) / TR_WARPS,
+                                             std::max(1, tr_occ) * ctx->sm_count));
 
     StepParams<T> sp;
     sp.desc = P<TreeDesc>(ctx->desc);
-    sp.M = M;
+    sp.M = M_fit;
     sp.partials = P<T>(ctx->partials);
     sp.blk = P<T>(ctx->blk);
     sp.c = P<T>(ctx->c);
@@ -530,9 +631,38 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     sp.reduced = nullptr;
     sp.damping_floor = opt.damping_floor > 0.0 ? opt.damping_floor : 0.0;
     sp.damping_always = opt.damping_always ? 1 : 0;
+    sp.imode = P<uint8_t>(ctx->imode);
+    sp.max_iter = std::max(0, opt.max_iter);
     sp.xtol = (T)opt.xtol;
 
+    TrParams<T> tp;
+    tp.desc = sp.desc;
+    tp.M = M_fit;
+    tp.partials = sp.partials;
+    tp.blk = sp.blk;
+    tp.c = sp.c;
+    tp.ctry = sp.ctry;
+    tp.delta = sp.delta;
+    tp.loss = sp.loss;
+    tp.loss_init = sp.loss_init;
+    tp.status = sp.status;
+    tp.iters = sp.iters;
+    tp.pending = sp.pending;
+    tp.n_eval = sp.n_eval;
+    tp.imode = sp.imode;
+    tp.tr = P<double>(ctx->tr);
+    tp.diag = P<double>(ctx->diag);
+    tp.outer = P<int32_t>(ctx->outer);
+    tp.max_nfev = std::max(1, opt.max_iter);
+    tp.ftol = opt.ftol;
+    tp.xtol = opt.xtol;
+    tp.gtol = opt.gtol;
+    tp.factor = 100.0;
+
+    // passes: one per LM iteration (reference) / per function evaluation after the first
+    // (trust region); a second wave can start as late as the first wave's last pass
     const int max_iter = std::max(0, opt.max_iter);
+    const int max_passes = wave1 ? 2 * max_iter + 2 : max_iter;
     size_t ev_i = 0;
     auto rec = [&](void) -> cudaEvent_t {
         cudaEvent_t e = event_at(ctx, ev_i++);
@@ -540,24 +670,44 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         return e;
     };
     std::vector<std::pair<size_t, size_t>> eval_spans, step_spans;
+    // the step kernels of one pass (and the wave update), counting running fits into n_running
+    auto steps = [&](int *n_running) -> int {
+        CK(cudaMemsetAsync(n_running, 0, sizeof(int), s));
+        if (has_ref) {
+            sp.n_running = n_running;
+            lm_step_kernel<T><<<step_grid, STEP_THREADS, step_smem, s>>>(sp);
+            CK(cudaGetLastError());
+            st.kernel_launches++;
+        }
+        if (has_tr) {
+            tp.n_running = n_running;
+            lm_tr_step_kernel<T><<<tr_grid, TR_THREADS, tr_smem, s>>>(tp);
+            CK(cudaGetLastError());
+            st.kernel_launches++;
+        }
+        if (wave1) {
+            waves_kernel<T><<<grid_for(ctx, M), 256, 0, s>>>(
+                M, S, wave1, opt.agree_tol, P<T>(ctx->loss), P<int32_t>(ctx->status),
+                P<int32_t>(ctx->pending), P<uint8_t>(ctx->resolved), n_running,
+                P<int>(ctx->n_retired));
+            CK(cudaGetLastError());
+            st.kernel_launches++;
+        }
+        return CO_OK;
+    };
 
-    // ---- initial pass at c_init + solve of iteration 0 ----
+    // ---- initial pass at the start points + solve of iteration 0 ----
     size_t e0 = ev_i; rec();
     rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true);
     if (rc) return rc;
     if (sharded) {
-        rc = shard_reduce_blocks<T>(ctx, M, sc.block_elems);
+        rc = shard_reduce_blocks<T>(ctx, M_fit, sc.block_elems);
         if (rc) return rc;
         sp.reduced = P<T>(ctx->red);
     }
     size_t e1 = ev_i; rec();
-    sp.n_running = P<int>(ctx->n_run);
-    sp.initial = 1;
-    sp.do_solve = max_iter > 0 ? 1 : 0;
-    CK(cudaMemsetAsync(sp.n_running, 0, sizeof(int), s));
-    lm_step_kernel<T><<<step_grid, STEP_THREADS, step_smem, s>>>(sp);
-    CK(cudaGetLastError());
-    st.kernel_launches++;
+    rc = steps(P<int>(ctx->n_run));
+    if (rc) return rc;
     size_t e2 = ev_i; rec();
     eval_spans.push_back({e0, e1});
     step_spans.push_back({e1, e2});
@@ -568,9 +718,9 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
 
     // ---- LM iterations ----
     // At most two iterations are in flight: before launching iteration `it` the host waits
-    // for the running-tree count of step it-2 and stops once no tree is running.
+    // for the running-fit count of step it-2 and stops once no fit is running.
     int iters_run = 0;
-    for (int it = 0; it < max_iter; ++it) {
+    for (int it = 0; it < max_passes; ++it) {
         const int slot = it & 1;
         if (opt.early_exit && it >= 2) {
             if (sharded) {
@@ -586,22 +736,17 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true);
         if (rc) return rc;
         if (sharded) {
-            rc = shard_reduce_blocks<T>(ctx, M, sc.block_elems);
+            rc = shard_reduce_blocks<T>(ctx, M_fit, sc.block_elems);
             if (rc) return rc;
         }
         size_t b = ev_i; rec();
-        sp.n_running = P<int>(ctx->n_run) + slot;
-        sp.initial = 0;
-        sp.do_solve = (it + 1 < max_iter) ? 1 : 0;
-        CK(cudaMemsetAsync(sp.n_running, 0, sizeof(int), s));
-        lm_step_kernel<T><<<step_grid, STEP_THREADS, step_smem, s>>>(sp);
-        CK(cudaGetLastError());
-        st.kernel_launches++;
+        rc = steps(P<int>(ctx->n_run) + slot);
+        if (rc) return rc;
         size_t c = ev_i; rec();
         eval_spans.push_back({a, b});
         step_spans.push_back({b, c});
         if (opt.early_exit) {
-            CK(cudaMemcpyAsync(ctx->h_nrun + slot, sp.n_running, sizeof(int),
+            CK(cudaMemcpyAsync(ctx->h_nrun + slot, P<int>(ctx->n_run) + slot, sizeof(int),
                                cudaMemcpyDeviceToHost, s));
             CK(cudaEventRecord(ctx->ev_nrun[slot], s));
         }
@@ -615,51 +760,68 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     // ---- fp64 audit of fp32 fits (lm_core.cuh:299-351; fp64 fits accept in fp64 already) ----
     const bool audit = !fp64 && opt.fp64_audit != 0 && total_c > 0;
     if (audit) {
-        GROW(ctx->c64, total_c * sizeof(double));
-        GROW(ctx->l64, 2 * (size_t)M * sizeof(double));
+        GROW(ctx->c64, total_c_fit * sizeof(double));
+        GROW(ctx->l64, 2 * (size_t)M_fit * sizeof(double));
         GROW(ctx->n_rev, sizeof(int));
         // per-item partials are not needed any more: reuse the buffer for fp64 sums
         GROW(ctx->partials, (size_t)sc.partial_elems * sizeof(double));
         double *c64 = P<double>(ctx->c64), *l64 = P<double>(ctx->l64);
-        const int g1 = grid_for(ctx, std::max<int64_t>(total_c, M));
+        const int g1 = grid_for(ctx, std::max<int64_t>(total_c_fit, M_fit));
         const float *srcs[2] = {reinterpret_cast<const float *>(ctx->c.ptr), P<float>(ctx->cinit_f)};
         for (int pass = 0; pass < 2; ++pass) {
-            audit_prepare_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, srcs[pass], total_c,
-                                                    c64, P<int32_t>(ctx->pending));
+            audit_prepare_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M_fit, srcs[pass],
+                                                    total_c_fit, c64, P<int32_t>(ctx->pending),
+                                                    P<int32_t>(ctx->n_eval));
             CK(cudaGetLastError());
             rc = launch_pass<double>(ctx, sc, pk, c64, P<double>(ctx->partials), *h, ldx, false);
             if (rc) return rc;
-            audit_loss_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M,
-                                                  P<double>(ctx->partials), l64 + pass * M);
+            audit_loss_kernel<<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M_fit,
+                                                  P<double>(ctx->partials), l64 + (size_t)pass * M_fit);
             CK(cudaGetLastError());
             st.kernel_launches += 2;
         }
         if (sharded) {   // the fp64 losses over all samples: sum the ranks' halves
-            rc = shard_allreduce(ctx->shard, l64, 2 * (size_t)M, true, s);
+            rc = shard_allreduce(ctx->shard, l64, 2 * (size_t)M_fit, true, s);
             if (rc) return rc;
         }
         CK(cudaMemsetAsync(ctx->n_rev.ptr, 0, sizeof(int), s));
-        audit_apply_kernel<T><<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M, l64, l64 + M,
-                                                 P<float>(ctx->cinit_f), P<T>(ctx->c),
-                                                 P<T>(ctx->loss), P<int32_t>(ctx->status),
-                                                 P<int>(ctx->n_rev));
+        audit_apply_kernel<T><<<g1, 256, 0, s>>>(P<TreeDesc>(ctx->desc), M_fit, l64,
+                                                 l64 + M_fit, P<float>(ctx->cinit_f),
+                                                 P<T>(ctx->c), P<T>(ctx->loss),
+                                                 P<int32_t>(ctx->status),
+                                                 P<int32_t>(ctx->n_eval), P<int>(ctx->n_rev));
         CK(cudaGetLastError());
         st.kernel_launches++;
     }
+    // ---- per tree, the start with the lowest final loss (the identity for one start) ----
+    select_best_kernel<T><<<grid_for(ctx, M), 256, 0, s>>>(
+        P<TreeDesc>(ctx->desc), P<int32_t>(ctx->tree_coff), M, S, P<T>(ctx->loss),
+        P<T>(ctx->loss_init), audit ? P<double>(ctx->l64) : nullptr, P<int32_t>(ctx->status),
+        P<int32_t>(ctx->iters), P<int32_t>(ctx->n_eval), P<T>(ctx->c), P<T>(ctx->out_c),
+        P<int32_t>(ctx->out_status), P<T>(ctx->out_li), P<T>(ctx->out_lf),
+        P<int32_t>(ctx->out_iters), P<int32_t>(ctx->out_start));
+    CK(cudaGetLastError());
+    st.kernel_launches++;
 
     // ---- D2H ----
     std::vector<T> hc((size_t)total_c), hli((size_t)M), hlf((size_t)M);
-    std::vector<int32_t> hst((size_t)M), hit((size_t)M), hne((size_t)M);
+    std::vector<int32_t> hst((size_t)M), hit((size_t)M), hne((size_t)M_fit);
     if (total_c > 0)
-        CK(cudaMemcpyAsync(hc.data(), ctx->c.ptr, total_c * sizeof(T), cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(hli.data(), ctx->loss_init.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(hlf.data(), ctx->loss.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(hst.data(), ctx->status.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(hit.data(), ctx->iters.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(hne.data(), ctx->n_eval.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    int n_rev = 0;
+        CK(cudaMemcpyAsync(hc.data(), ctx->out_c.ptr, total_c * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hli.data(), ctx->out_li.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hlf.data(), ctx->out_lf.ptr, (size_t)M * sizeof(T), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hst.data(), ctx->out_status.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hit.data(), ctx->out_iters.ptr, (size_t)M * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(hne.data(), ctx->n_eval.ptr, (size_t)M_fit * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    ctx->h_start.assign((size_t)M, 0);
+    if (S > 1)
+        CK(cudaMemcpyAsync(ctx->h_start.data(), ctx->out_start.ptr, (size_t)M * sizeof(int32_t),
+                           cudaMemcpyDeviceToHost, s));
+    int n_rev = 0, n_ret = 0;
     if (audit)
         CK(cudaMemcpyAsync(&n_rev, ctx->n_rev.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (wave1)
+        CK(cudaMemcpyAsync(&n_ret, ctx->n_retired.ptr, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaEventRecord(ctx->ev_fit[1], s));
     rc = sync_stream(ctx, sharded);
     if (rc) return rc;
@@ -669,26 +831,28 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
             st.device_ms = dms;
     }
     st.n_reverted = n_rev;
+    st.trees_retired = n_ret;
 
     for (int64_t i = 0; i < total_c; ++i) {
         if (out.c_f) out.c_f[i] = (float)hc[(size_t)i];
         if (out.c_d) out.c_d[i] = (double)hc[(size_t)i];
     }
     for (int m = 0; m < M; ++m) {
-        const int32_t s_ = hst[(size_t)m];
-        out.status[m] = (s_ == ST_RUNNING) ? STATUS_MAXITER : s_;
+        out.status[m] = hst[(size_t)m];
         if (out.li_f) out.li_f[m] = (float)hli[(size_t)m];
         if (out.lf_f) out.lf_f[m] = (float)hlf[(size_t)m];
         if (out.li_d) out.li_d[m] = (double)hli[(size_t)m];
         if (out.lf_d) out.lf_d[m] = (double)hlf[(size_t)m];
         if (out.iters) out.iters[m] = hit[(size_t)m];
     }
-    // evaluation counts: initial pass + every evaluated trial, per tree
-    int64_t node_evals = 0, sample_evals = 0;
+    // evaluation counts: initial pass + every evaluated trial, per fit
+    int64_t node_evals = 0, sample_evals = 0, fits_run = 0;
     double flops = 0.0;
-    for (int m = 0; m < M; ++m) {
-        const int64_t evals = hne[(size_t)m];
-        const int K = (int)(h->M_prob ? pk.trees[(size_t)m].K : 0);
+    for (int64_t i = 0; i < M_fit; ++i) {
+        const int64_t evals = hne[(size_t)i];
+        const int m = (int)(i / S);
+        const int K = (int)pk.trees[(size_t)m].K;
+        fits_run += evals > 0 ? 1 : 0;
         node_evals += evals * ctx->n_nodes[(size_t)m] * (int64_t)N;
         sample_evals += evals * (int64_t)N;
         // value + adjoint per operator node, plus the normal-equation update
@@ -697,6 +861,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     st.flops = flops;
     st.node_evals = node_evals;
     st.sample_evals = sample_evals;
+    st.fits_run = fits_run;
 
     // device-time split from the recorded events
     double eval_ms = 0.0, step_ms = 0.0;
@@ -721,7 +886,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
 template <typename T>
 int run_fit(Ctx *ctx, const Problem &pr, const CoOptions &opt, const Outputs &out) {
     auto t_entry = std::chrono::steady_clock::now();
-    int rc = load<T>(ctx, pr, opt.y_shared != 0);
+    int rc = load<T>(ctx, pr, opt.y_shared != 0, opt.n_starts);
     if (rc != CO_OK) return rc;
     return fit_loaded<T>(ctx, opt, out, t_entry);
 }
@@ -858,6 +1023,22 @@ void co_default_options(CoOptions *opt) {
     opt->xtol = 1e-6;
     opt->fp64_audit = -1;
     opt->early_exit = 1;
+    opt->algorithm = CO_ALG_REFERENCE;
+    opt->n_starts = 1;
+    opt->tr_starts = 0;
+    opt->wave1 = 0;
+    opt->ftol = 1e-10;
+    opt->gtol = 1e-8;
+    opt->agree_tol = 1e-7;
+    opt->start_seed = 0;
+}
+
+// Options that every fit entry checks.
+static bool valid_fit_options(const CoOptions &o) {
+    return o.lambda0 > 0.0 && o.xtol >= 0.0 && o.ftol >= 0.0 && o.gtol >= 0.0 &&
+           o.agree_tol >= 0.0 && o.n_starts >= 0 && o.n_starts <= CO_MAX_STARTS &&
+           o.tr_starts >= 0 && o.wave1 >= 0 &&
+           (o.algorithm == CO_ALG_REFERENCE || o.algorithm == CO_ALG_TRUST_REGION);
 }
 
 // Caller options over the defaults: the first struct_size bytes of the caller's struct are
@@ -999,7 +1180,7 @@ int co_optimize_ex(void *handle, const PopHeader *h, const int32_t *nt, const fl
     CoOptions opt;
     if (!read_options(opt_in, &opt)) return CO_ERR_NULLARG;
     if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
-    if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
+    if (!valid_fit_options(opt)) return CO_ERR_NULLARG;
     opt.sample_sharded = 0;
     Outputs out;
     out.c_d = c_final_out;
@@ -1065,9 +1246,10 @@ int co_load(void *handle, const PopHeader *h, const int32_t *nt, const float *nv
     int rc = check_args(pr);
     if (rc != CO_OK) return rc;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
+    if (!valid_fit_options(opt)) return CO_ERR_NULLARG;
     set_ad_mode(ctx, opt.ad_mode);
-    rc = opt.precision == CO_PREC_FP64 ? load<double>(ctx, pr, opt.y_shared != 0)
-                                       : load<float>(ctx, pr, opt.y_shared != 0);
+    rc = opt.precision == CO_PREC_FP64 ? load<double>(ctx, pr, opt.y_shared != 0, opt.n_starts)
+                                       : load<float>(ctx, pr, opt.y_shared != 0, opt.n_starts);
     if (rc == CO_OK && cudaStreamSynchronize(ctx->stream) != cudaSuccess) return CO_ERR_CUDA;
     return rc;
 }
@@ -1084,7 +1266,7 @@ int co_fit_loaded(void *handle, const CoOptions *opt_in, double *c_final_out,
         return CO_ERR_NULLARG;
     ctx->fast = opt.precision == CO_PREC_FP32_FAST;
     if (opt.sample_sharded && !ctx->shard.comm) return CO_ERR_NULLARG;
-    if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
+    if (!valid_fit_options(opt)) return CO_ERR_NULLARG;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return CO_ERR_CUDA;
     Outputs out;
     out.c_d = c_final_out;
@@ -1157,7 +1339,11 @@ int co_optimize_sharded(void *handle, const PopHeader *h, const int32_t *nt, con
     if (!read_options(opt_in, &opt)) return CO_ERR_NULLARG;
     opt.sample_sharded = 1;
     if (!valid_prec(opt.precision)) return CO_ERR_NULLARG;
-    if (!(opt.lambda0 > 0.0) || !(opt.xtol >= 0.0)) return CO_ERR_NULLARG;
+    if (!valid_fit_options(opt)) return CO_ERR_NULLARG;
+    // one fit per tree from c_init with the reference schedule: the per-iteration all-reduce
+    // carries the trees' normal equations
+    if (opt.n_starts > 1 || opt.algorithm != CO_ALG_REFERENCE || opt.tr_starts > 0)
+        return CO_ERR_NULLARG;
     Outputs out;
     out.c_d = c_final_out;
     out.status = status_out;
@@ -1171,6 +1357,13 @@ int co_last_split(double *setup_ms_out, double *loop_ms_out) {
     if (setup_ms_out) *setup_ms_out = g_last_setup_ms;
     if (loop_ms_out) *loop_ms_out = g_last_loop_ms;
     return 0;
+}
+
+int co_last_starts(void *handle, int32_t *start_out) {
+    if (!handle || !start_out) return CO_ERR_NULLARG;
+    Ctx *ctx = (Ctx *)handle;
+    for (size_t m = 0; m < ctx->h_start.size(); ++m) start_out[m] = ctx->h_start[m];
+    return CO_OK;
 }
 
 int co_get_stats(void *handle, CoStats *out) {
@@ -1189,6 +1382,10 @@ void co_teardown(void *handle) {
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
                     &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
                     &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac, &ctx->red,
+                    &ctx->c_tree, &ctx->tree_coff, &ctx->imode, &ctx->tr, &ctx->diag,
+                    &ctx->outer, &ctx->resolved, &ctx->n_retired, &ctx->out_c,
+                    &ctx->out_status, &ctx->out_li, &ctx->out_lf, &ctx->out_iters,
+                    &ctx->out_start,
                     &ctx->tape_gs[0], &ctx->tape_gs[1], &ctx->tape_gs[2], &ctx->tape_gs[3],
                     &ctx->tape_gs[4], &ctx->tape_gs[5], &ctx->tape_gs[6], &ctx->tape_gs[7]};
     for (DBuf *b : bufs) release(*b);

@@ -32,11 +32,17 @@ struct StepParams {
                              // (q_off layout, replaces the chunk partials), else null
     double damping_floor;    // 0: reference damping diag * (1 + lam)
     int damping_always;      // with a floor: floored damping on every solve (else fallback)
+    const uint8_t *imode;    // per fit (start axis, IM_* below), or null: every fit uses the
+                             // reference schedule with the call's damping settings
     int *n_running;          // trees still running after this step (early exit)
-    int initial;             // the evaluated point is c_init
-    int do_solve;            // solve a new step for every running tree
+    int max_iter;            // LM iterations per fit
     T xtol;
 };
+
+// per-fit mode bits (the start axis): the trust-region algorithm (run by lm_tr_step_kernel,
+// skipped here), and the floored damping on every solve for a reference-schedule fit
+constexpr uint8_t IM_TR = 1;
+constexpr uint8_t IM_DAMP_ALWAYS = 2;
 
 constexpr int STEP_THREADS = 256;
 constexpr int STEP_WARPS = STEP_THREADS / 32;
@@ -64,9 +70,14 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
     for (int m = blockIdx.x * STEP_WARPS + warp; m < p.M; m += gridDim.x * STEP_WARPS) {
         int st = p.status[m];
         if (st != ST_RUNNING) continue;
+        const uint8_t mode = p.imode ? p.imode[m] : 0;
+        if (mode & IM_TR) continue;
         const TreeDesc d = p.desc[m];
         const int K = d.K, P = nblock_size(K);
         const int pend = p.pending[m];
+        // the first evaluation of a fit is at its start point (c_init for start 0)
+        const bool initial = p.n_eval[m] == 0;
+        __syncwarp();
         if (pend) {
             if (p.reduced) {
                 for (int e = lane; e < P; e += 32) sums[e] = p.reduced[d.q_off + e];
@@ -87,7 +98,7 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                 p.pending[m] = 0;
                 p.n_eval[m] += 1;
                 const T ltry = T(0.5) * sums[P - 1];
-                if (p.initial) {
+                if (initial) {
                     p.loss_init[m] = ltry;
                     p.loss[m] = ltry;
                     accept = 1;
@@ -130,7 +141,10 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
             for (int e = lane; e < P; e += 32) p.blk[d.q_off + e] = sums[e];
         __syncwarp();
         if (lane == 0) {
-            if (st == ST_RUNNING && p.do_solve) {
+            // every running fit takes one LM iteration per pass (an evaluated trial or a
+            // factorisation failure); after max_iter of them it stops
+            if (st == ST_RUNNING && p.iters[m] >= p.max_iter) st = STATUS_MAXITER;
+            if (st == ST_RUNNING) {
                 T lam = p.lam[m];
                 const T *b = p.blk + d.q_off;
                 const int tri = K * (K + 1) / 2;
@@ -171,7 +185,8 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                     }
                     return true;
                 };
-                const bool always = p.damping_floor > 0.0 && p.damping_always;
+                const bool always = p.damping_floor > 0.0 &&
+                                    (p.damping_always || (mode & IM_DAMP_ALWAYS));
                 build(always);
                 bool ok = cholesky();
                 // robust mode: a system the reference damping cannot factor (a zero or
@@ -284,25 +299,6 @@ __global__ void transpose_x_kernel(const float *__restrict__ xs, int64_t N, int 
     }
 }
 
-// Initial state of every tree: c = c_init, lambda0, RUNNING, initial evaluation pending.
-template <typename T>
-__global__ void init_state_kernel(const float *__restrict__ c_init, int64_t total_c, T *c,
-                                  T *ctry, int M, T lam0, T *lam, int32_t *status,
-                                  int32_t *iters, int32_t *pending, int32_t *n_eval) {
-    const int64_t gs = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_c; i += gs) {
-        c[i] = (T)c_init[i];
-        ctry[i] = (T)c_init[i];
-    }
-    for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += gs) {
-        lam[m] = lam0;
-        status[m] = ST_RUNNING;
-        iters[m] = 0;
-        pending[m] = 1;
-        n_eval[m] = 0;
-    }
-}
-
 // Evaluation entry: constants of the evaluated point (fp64 from the caller), every tree pending.
 template <typename T>
 __global__ void load_point_kernel(const double *__restrict__ c64, int64_t total_c, T *c, int M,
@@ -402,13 +398,15 @@ __global__ void fma_probe_kernel(T *out, int iters, T b, T c) {
 // Trees whose fp64 loss at the delivered constants is non-finite or worse than at c_init
 // are reverted to c_init, a CONVERGED status becomes MAXITER, and the reported final loss
 // becomes the fp64 loss at c_init.
+// Fits that never ran (later-wave starts a tree retired) are not evaluated.
 __global__ void audit_prepare_kernel(const TreeDesc *desc, int M, const float *c_now,
-                                     int64_t total_c, double *c64, int32_t *pending) {
+                                     int64_t total_c, double *c64, int32_t *pending,
+                                     const int32_t *n_eval) {
     const int64_t gs = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total_c; i += gs)
         c64[i] = (double)c_now[i];
     for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += gs)
-        pending[m] = desc[m].K > 0 ? 1 : 0;
+        pending[m] = (desc[m].K > 0 && n_eval[m] > 0) ? 1 : 0;
 }
 
 __global__ void audit_loss_kernel(const TreeDesc *desc, int M, const double *partials,
@@ -426,10 +424,10 @@ __global__ void audit_loss_kernel(const TreeDesc *desc, int M, const double *par
 template <typename T>
 __global__ void audit_apply_kernel(const TreeDesc *desc, int M, const double *lfinal,
                                    const double *linit, const float *c_init, T *c, T *loss,
-                                   int32_t *status, int *n_reverted) {
+                                   int32_t *status, const int32_t *n_eval, int *n_reverted) {
     for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
         const TreeDesc d = desc[m];
-        if (d.K == 0) continue;
+        if (d.K == 0 || n_eval[m] == 0) continue;
         const double lf = lfinal[m], li = linit[m];
         if (!isfinite(lf) || (isfinite(li) && lf > li)) {
             for (int k = 0; k < d.K; ++k) c[d.c_off + k] = (T)c_init[d.c_off + k];

@@ -590,7 +590,7 @@ int kc_class(int K, bool fp64, int fwd_max) {
 
 void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
                     bool y_shared, bool fp64, int round, int resident, Schedule *out,
-                    int fwd_max) {
+                    int fwd_max, int S) {
     out->bins.clear();
     out->desc.assign((size_t)M, TreeDesc{});
     out->round = round;
@@ -617,7 +617,7 @@ void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
         d.n_bwd = ct.n_bwd;
         d.K = ct.K;
         d.c_off = metas[m].c_offset;
-        d.y_off = y_shared ? 0 : (int64_t)m * ldy;
+        d.y_off = y_shared ? 0 : (int64_t)(m / S) * ldy;
         d.p_off = p_off;
         d.q_off = q_off;
         d.n_chunks = n_chunks;

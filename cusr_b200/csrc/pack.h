@@ -71,9 +71,12 @@ int tape_class(int n_tape);
 
 // Build the schedule: bins, per-tree descriptors, chunking (round = samples per round of a
 // block, resident = concurrently resident blocks on the device).
+// With S > 1 the entries are fits (tree m = entry / S, start entry % S): `pk.trees` and
+// `metas` hold one record per fit (the fits of a tree share its program), the target row is
+// the tree's.
 void build_schedule(const PackResult &pk, const TreeMeta *metas, int M, int N,
                     bool y_shared, bool fp64, int round, int resident, Schedule *out,
-                    int fwd_max = 0);
+                    int fwd_max = 0, int S = 1);
 
 // Reference evaluation of a compiled program on the host (fp64), forward value plus the
 // reverse sweep into grad[0..K) (read through the row table that follows the n_bwd reverse

@@ -1,0 +1,433 @@
+// tr_step.cuh — the trust-region Levenberg–Marquardt step (Moré 1977, "The Levenberg-
+// Marquardt algorithm: implementation and theory"; the algorithm of MINPACK's lmder, which
+// the reference's CPU backend runs through scipy.optimize.least_squares(method='lm'),
+// cusr/benchmark/backends.py:97-120), one warp per fit, on the normal equations the fused
+// evaluation pass already produces.
+//
+// Per fit the state is the scaling D (per constant), the trust radius Delta, the LM parameter
+// par, |f| at the accepted point, |D x| and |D p| of the last step. After each evaluated trial:
+//   actred = 1 - (|f_try| / |f|)^2 (-1 when |f_try| >= 10 |f|), prered = (|J p|^2 +
+//   2 par |D p|^2) / |f|^2, ratio = actred / prered; ratio <= 1/4 shrinks Delta (by the
+//   directional-derivative factor, within [1/10, 1/2]), ratio >= 3/4 (or par = 0) sets
+//   Delta = 2 |D p|; ratio >= 1e-4 accepts the trial (its J, J^T f, |f|^2 become current,
+//   since the pass evaluated them at the trial point); convergence: |actred| <= ftol and
+//   prered <= ftol, or Delta <= xtol |D x|, or at the next accepted point
+//   max_j |(J^T f)_j| / (|f| |J_j|) <= gtol; D_j = max(D_j, |J_j|).
+// The step p solves (J^T J + par D^2) p = -J^T f with par chosen so that | |D p| - Delta | <=
+// Delta / 10 (or par = 0 when the Gauss-Newton step is inside the region): Newton iteration on
+// 1 / |D p| - 1 / Delta with the safeguards [parl, paru] and at most 10 factorisations.
+// MINPACK works on the QR factors of J; here the same equations are solved through Cholesky
+// factors of J^T J + par D^2 (the Gram matrix of the pass, accumulated in fp64): lanes own rows,
+// right-looking updates, so a K <= 32 factorisation takes O(K^2) warp steps. The Gauss-Newton
+// step uses symmetric (diagonal) pivoting, which orders the columns as QR column pivoting does,
+// and stops at the first non-positive pivot: a rank-deficient J gives the basic solution on
+// the independent columns (MINPACK's QR keeps rounding-size pivots there instead).
+#pragma once
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+#include "lm_kernels.cuh"
+
+namespace cusr {
+
+// per-fit state of the trust-region algorithm (fp64), in TrParams::tr
+enum TrField { TR_DELTA = 0, TR_PAR, TR_FNORM, TR_XNORM, TR_PNORM, TR_GNORM, TR_FIELDS };
+
+template <typename T>
+struct TrParams {
+    const TreeDesc *desc;
+    int M;
+    const T *partials;
+    T *blk, *c, *ctry, *delta, *loss, *loss_init;
+    int32_t *status, *iters, *pending, *n_eval;
+    const uint8_t *imode;
+    double *tr;          // [M][TR_FIELDS]
+    double *diag;        // per constant (TreeDesc::c_off)
+    int32_t *outer;      // outer iterations (accepted points) per fit
+    int *n_running;
+    int max_nfev;        // evaluations per fit, the initial one included
+    double ftol, xtol, gtol, factor;
+};
+
+constexpr int TR_THREADS = 128;
+constexpr int TR_WARPS = TR_THREADS / 32;
+constexpr int TR_LD = CO_MAX_K + 1;                     // padded row stride (doubles)
+// per warp: A, W (K x K, full symmetric), the summed block (561 values, as doubles)
+constexpr int TR_WARP_D = 2 * CO_MAX_K * TR_LD + 576;
+
+__device__ __forceinline__ double tr_wsum(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double tr_wmax(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Euclidean norm of a lane-distributed vector (the lanes >= K hold 0)
+__device__ __forceinline__ double tr_norm(double v) { return sqrt(tr_wsum(v * v)); }
+
+// W (rows 0..K-1 owned by lanes) = L L^T in place (lower triangle), unpivoted. false if a
+// pivot is not positive (the test reads shared memory every lane sees: warp-uniform).
+__device__ bool tr_chol(double *W, int K, int lane) {
+    for (int j = 0; j < K; ++j) {
+        __syncwarp();
+        const double djj = W[j * TR_LD + j];
+        if (!(djj > 0.0)) return false;
+        const double ljj = sqrt(djj);
+        __syncwarp();
+        if (lane > j && lane < K) W[lane * TR_LD + j] /= ljj;
+        if (lane == j) W[j * TR_LD + j] = ljj;
+        __syncwarp();
+        if (lane > j && lane < K) {
+            const double lij = W[lane * TR_LD + j];
+            for (int k = j + 1; k <= lane; ++k) W[lane * TR_LD + k] -= lij * W[k * TR_LD + j];
+        }
+    }
+    __syncwarp();
+    return true;
+}
+
+// solve L y = b (lane i holds b_i, returns y_i), L lower in W
+__device__ double tr_fsub(const double *W, int K, int lane, double b) {
+    double y = 0.0;
+    for (int k = 0; k < K; ++k) {
+        double yk = 0.0;
+        if (lane == k) yk = b / W[k * TR_LD + k];
+        yk = __shfl_sync(0xffffffffu, yk, k);
+        if (lane == k) y = yk;
+        if (lane > k && lane < K) b -= W[lane * TR_LD + k] * yk;
+    }
+    return y;
+}
+// solve L^T x = y (lane i holds y_i, returns x_i)
+__device__ double tr_bsub(const double *W, int K, int lane, double y) {
+    double x = 0.0;
+    for (int k = K - 1; k >= 0; --k) {
+        double xk = 0.0;
+        if (lane == k) xk = y / W[k * TR_LD + k];
+        xk = __shfl_sync(0xffffffffu, xk, k);
+        if (lane == k) x = xk;
+        if (lane < k) y -= W[k * TR_LD + lane] * xk;
+    }
+    return x;
+}
+
+// Symmetrically pivoted Cholesky of W = A (full, lanes own rows): at step b the largest
+// remaining diagonal is the pivot perm[b]; the column values l_i are kept in W[i][perm[b]].
+// Returns the rank r (pivots taken before the first non-positive one).
+__device__ int tr_pchol(double *W, int K, int lane, int *perm) {
+    bool done = lane >= K;
+    int r = 0;
+    for (int b = 0; b < K; ++b) {
+        __syncwarp();
+        double v = done ? -1.0 : W[lane * TR_LD + lane];
+        int p = lane;
+        // argmax with ties to the lower index: every lane ends with the same (v, p)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const double v2 = __shfl_xor_sync(0xffffffffu, v, o);
+            const int p2 = __shfl_xor_sync(0xffffffffu, p, o);
+            if (v2 > v || (v2 == v && p2 < p)) { v = v2; p = p2; }
+        }
+        if (!(v > 0.0)) break;
+        const double lpp = sqrt(v);
+        double li = 0.0;
+        if (!done && lane != p) li = W[lane * TR_LD + p] / lpp;
+        __syncwarp();
+        if (!done && lane != p) W[lane * TR_LD + p] = li;
+        if (lane == p) { W[p * TR_LD + p] = lpp; done = true; }
+        if (lane == 0) perm[b] = p;
+        // trailing update of the rows and columns still remaining
+        const bool act = !done;
+        for (int k = 0; k < K; ++k) {
+            const double lk = __shfl_sync(0xffffffffu, li, k);
+            const int dk = __shfl_sync(0xffffffffu, (int)done, k);
+            if (act && !dk) W[lane * TR_LD + k] -= li * lk;
+        }
+        ++r;
+    }
+    __syncwarp();
+    return r;
+}
+
+// Gauss-Newton step on the pivoted factor: x = -(A^+) g on the r independent columns,
+// 0 on the others (lane i holds g_i, returns x_i). Lanes work in pivot order: lane a takes
+// row perm[a]; L[a][k] = W[perm[a]][perm[k]].
+__device__ double tr_gn_step(const double *W, int r, int lane, const int *perm, double g) {
+    const int pa = lane < r ? perm[lane] : 0;
+    double b = __shfl_sync(0xffffffffu, -g, pa);
+    if (lane >= r) b = 0.0;
+    double y = 0.0;
+    for (int k = 0; k < r; ++k) {          // forward: L y = b
+        const int pk = perm[k];
+        double yk = 0.0;
+        if (lane == k) yk = b / W[pk * TR_LD + pk];
+        yk = __shfl_sync(0xffffffffu, yk, k);
+        if (lane == k) y = yk;
+        if (lane > k && lane < r) b -= W[pa * TR_LD + pk] * yk;
+    }
+    double z = 0.0;
+    for (int k = r - 1; k >= 0; --k) {     // back: L^T z = y
+        const int pk = perm[k];
+        double zk = 0.0;
+        if (lane == k) zk = y / W[pk * TR_LD + pk];
+        zk = __shfl_sync(0xffffffffu, zk, k);
+        if (lane == k) z = zk;
+        if (lane < k) y -= W[pk * TR_LD + pa] * zk;
+    }
+    // back to the original order: lane i takes z of the pivot position holding i
+    double x = 0.0;
+    for (int a = 0; a < r; ++a) {
+        const double za = __shfl_sync(0xffffffffu, z, a);
+        if (lane == perm[a]) x = za;
+    }
+    return x;
+}
+
+// forward solve with the full-rank pivoted factor (L w = v[perm]), returns |w|
+__device__ double tr_pfsub_norm(const double *W, int K, int lane, const int *perm, double v) {
+    const int pa = lane < K ? perm[lane] : 0;
+    double b = __shfl_sync(0xffffffffu, v, pa);
+    if (lane >= K) b = 0.0;
+    double w = 0.0;
+    for (int k = 0; k < K; ++k) {
+        const int pk = perm[k];
+        double wk = 0.0;
+        if (lane == k) wk = b / W[pk * TR_LD + pk];
+        wk = __shfl_sync(0xffffffffu, wk, k);
+        if (lane == k) w = wk;
+        if (lane > k && lane < K) b -= W[pa * TR_LD + pk] * wk;
+    }
+    return tr_norm(w);
+}
+
+// W = A + par diag(d^2), rows owned by lanes
+__device__ __forceinline__ void tr_load(double *W, const double *A, int K, int lane, double par,
+                                        double d) {
+    if (lane < K) {
+        for (int k = 0; k < K; ++k) W[lane * TR_LD + k] = A[lane * TR_LD + k];
+        W[lane * TR_LD + lane] += par * d * d;
+    }
+    __syncwarp();
+}
+
+// The LM parameter and step for trust radius delta (MINPACK lmpar, on normal equations).
+// Lane i holds g_i = (J^T f)_i and d_i; returns x_i (the step) and updates par.
+__device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lane, double g,
+                           double d, double delta, double &par) {
+    const double dwarf = DBL_MIN;
+    // Gauss-Newton direction
+    tr_load(W, A, K, lane, 0.0, d);
+    const int r = tr_pchol(W, K, lane, perm);
+    double x = r > 0 ? tr_gn_step(W, r, lane, perm, g) : 0.0;
+    if (lane >= K) x = 0.0;
+    double dxnorm = tr_norm(d * x);
+    double fp = dxnorm - delta;
+    if (fp <= 0.1 * delta) {
+        par = 0.0;
+        return x;
+    }
+    // lower bound (J of full rank): the Newton step of 1/|Dx| - 1/delta at par = 0
+    double parl = 0.0;
+    if (r == K) {
+        const double v = lane < K ? d * (d * x) / dxnorm : 0.0;
+        const double t = tr_pfsub_norm(W, K, lane, perm, v);
+        parl = ((fp / delta) / t) / t;
+    }
+    // upper bound
+    const double gnorm = tr_norm(lane < K ? g / d : 0.0);
+    double paru = gnorm / delta;
+    if (paru == 0.0) paru = dwarf / fmin(delta, 0.1);
+    par = fmax(par, parl);
+    par = fmin(par, paru);
+    if (par == 0.0) par = gnorm / dxnorm;
+    for (int iter = 1;; ++iter) {
+        if (par == 0.0) par = fmax(dwarf, 0.001 * paru);
+        tr_load(W, A, K, lane, par, d);
+        // a system that rounding left indefinite (dependent columns, par tiny against the
+        // scale of J^T J) is factored with par raised until it is positive definite
+        int guard = 0;
+        while (!tr_chol(W, K, lane) && guard < 64) {
+            const double amax = tr_wmax(lane < K ? fabs(A[lane * TR_LD + lane]) : 0.0);
+            const double dmin = -tr_wmax(lane < K ? -(d * d) : -DBL_MAX);
+            par = fmax(fmax(2.0 * par, 1e-15 * amax / dmin), dwarf);
+            tr_load(W, A, K, lane, par, d);
+            ++guard;
+        }
+        const double y = tr_fsub(W, K, lane, lane < K ? -g : 0.0);
+        x = tr_bsub(W, K, lane, y);
+        if (lane >= K) x = 0.0;
+        dxnorm = tr_norm(d * x);
+        const double temp = fp;
+        fp = dxnorm - delta;
+        if (fabs(fp) <= 0.1 * delta || (parl == 0.0 && fp <= temp && temp < 0.0) || iter == 10)
+            return x;
+        const double v = lane < K ? d * (d * x) / dxnorm : 0.0;
+        const double t = tr_norm(tr_fsub(W, K, lane, v));
+        const double parc = ((fp / delta) / t) / t;
+        if (fp > 0.0) parl = fmax(parl, par);
+        if (fp < 0.0) paru = fmin(paru, par);
+        par = fmax(parl, par + parc);
+    }
+}
+
+// One trust-region step for every running fit of mode IM_TR whose trial was evaluated.
+template <typename T>
+__global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T> p) {
+    extern __shared__ double tr_sm[];
+    __shared__ int s_perm[TR_WARPS][CO_MAX_K];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    double *A = tr_sm + warp * TR_WARP_D;
+    double *W = A + CO_MAX_K * TR_LD;
+    double *sums = W + CO_MAX_K * TR_LD;
+    int *perm = s_perm[warp];
+    const double eps = sizeof(T) == 8 ? DBL_EPSILON : (double)FLT_EPSILON;
+    for (int m = blockIdx.x * TR_WARPS + warp; m < p.M; m += gridDim.x * TR_WARPS) {
+        if (!(p.imode[m] & IM_TR)) continue;
+        int st = p.status[m];
+        if (st != ST_RUNNING || !p.pending[m]) continue;
+        const TreeDesc dsc = p.desc[m];
+        const int K = dsc.K, P = nblock_size(K), tri = K * (K + 1) / 2;
+        for (int e = lane; e < P; e += 32) {
+            const T *src = p.partials + dsc.p_off + e;
+            T s = T(0);
+            for (int ch = 0; ch < dsc.n_chunks; ++ch) s += src[(int64_t)ch * P];
+            sums[e] = (double)s;
+        }
+        __syncwarp();
+        double *trs = p.tr + (int64_t)m * TR_FIELDS;
+        const double ssq = sums[P - 1];              // |f_try|^2
+        const T ltry = T(0.5) * (T)ssq;
+        const int ne = p.n_eval[m];                  // evaluations before this one
+        const bool initial = ne == 0;
+        __syncwarp();
+        if (lane == 0) {
+            p.pending[m] = 0;
+            p.n_eval[m] = ne + 1;
+        }
+        double delta = trs[TR_DELTA], par = trs[TR_PAR], fnorm = trs[TR_FNORM];
+        double xnorm = trs[TR_XNORM], pnorm = trs[TR_PNORM], gnorm = trs[TR_GNORM];
+        int outer = p.outer[m];
+        bool accept = false, done = false;
+        double d = lane < K ? p.diag[dsc.c_off + lane] : 1.0;
+        if (initial) {
+            if (lane == 0) { p.loss_init[m] = ltry; p.loss[m] = ltry; }
+            if (K == 0) { st = STATUS_K0_SKIP; done = true; }
+            else if (!isfinite(ssq)) { st = STATUS_FAIL_NAN; done = true; }
+            else { accept = true; fnorm = sqrt(ssq); outer = 1; }
+        } else {
+            if (lane == 0) p.iters[m] += 1;
+            const double fnorm1 = isfinite(ssq) ? sqrt(ssq) : INFINITY;
+            // |J p|^2 = p^T A p with A = the accepted point's J^T J (packed lower in blk)
+            const T *bq = p.blk + dsc.q_off;
+            const double pk = lane < K ? (double)p.delta[dsc.c_off + lane] : 0.0;
+            double ap = 0.0;
+            for (int l = 0; l < K; ++l) {
+                const double pl = __shfl_sync(0xffffffffu, pk, l);
+                if (lane < K) {
+                    const int hi = lane > l ? lane : l, lo = lane > l ? l : lane;
+                    ap += (double)bq[hi * (hi + 1) / 2 + lo] * pl;
+                }
+            }
+            const double jp2 = fmax(tr_wsum(pk * ap), 0.0);
+            const double actred = (0.1 * fnorm1 < fnorm) ? 1.0 - (fnorm1 / fnorm) * (fnorm1 / fnorm) : -1.0;
+            const double t1 = sqrt(jp2) / fnorm, t2 = sqrt(par) * pnorm / fnorm;
+            const double prered = t1 * t1 + t2 * t2 / 0.5;
+            const double dirder = -(t1 * t1 + t2 * t2);
+            const double ratio = prered != 0.0 ? actred / prered : 0.0;
+            if (ratio <= 0.25) {
+                double temp = actred >= 0.0 ? 0.5 : 0.5 * dirder / (dirder + 0.5 * actred);
+                if (0.1 * fnorm1 >= fnorm || temp < 0.1) temp = 0.1;
+                delta = temp * fmin(delta, pnorm / 0.1);
+                par = par / temp;
+            } else if (par == 0.0 || ratio >= 0.75) {
+                delta = pnorm / 0.5;
+                par = 0.5 * par;
+            }
+            if (ratio >= 1e-4) {
+                accept = true;
+                fnorm = fnorm1;
+                outer += 1;
+                const double cn = lane < K ? d * (double)p.ctry[dsc.c_off + lane] : 0.0;
+                xnorm = tr_norm(cn);
+                if (lane < K) p.c[dsc.c_off + lane] = p.ctry[dsc.c_off + lane];
+                if (lane == 0) p.loss[m] = ltry;
+            }
+            if (fabs(actred) <= p.ftol && prered <= p.ftol && 0.5 * ratio <= 1.0) done = true;
+            if (delta <= p.xtol * xnorm) done = true;
+            if (fabs(actred) <= eps && prered <= eps && 0.5 * ratio <= 1.0) done = true;
+            if (delta <= eps * xnorm) done = true;
+            if (done) {
+                st = STATUS_CONVERGED;
+            } else if (ne + 1 >= p.max_nfev) {     // evaluation budget (MINPACK maxfev)
+                st = STATUS_MAXITER;
+                done = true;
+            }
+        }
+        __syncwarp();
+        if (accept) {
+            // the new point's J^T J, J^T f must be finite to take a step from it
+            bool bad = false;
+            for (int e = lane; e < P; e += 32) bad |= !isfinite(sums[e]);
+            if (__any_sync(0xffffffffu, bad) && !done) {
+                st = STATUS_FAIL_NAN;
+                done = true;
+            }
+            for (int e = lane; e < P; e += 32) p.blk[dsc.q_off + e] = (T)sums[e];
+        }
+        __syncwarp();
+        if (!done) {
+            // current point's J^T J (full) and J^T f, from the accepted block
+            const T *bq = p.blk + dsc.q_off;
+            if (lane < K)
+                for (int l = 0; l < K; ++l) {
+                    const int hi = lane > l ? lane : l, lo = lane > l ? l : lane;
+                    A[lane * TR_LD + l] = (double)bq[hi * (hi + 1) / 2 + lo];
+                }
+            __syncwarp();
+            const double g = lane < K ? (double)bq[tri + lane] : 0.0;
+            if (accept) {
+                // outer iteration: column norms, the scaling, the gradient test
+                const double acn = lane < K ? sqrt(fmax(A[lane * TR_LD + lane], 0.0)) : 0.0;
+                if (outer == 1) {
+                    d = (lane < K && acn != 0.0) ? acn : 1.0;
+                    const double cn = lane < K ? d * (double)p.c[dsc.c_off + lane] : 0.0;
+                    xnorm = tr_norm(cn);
+                    delta = xnorm != 0.0 ? p.factor * xnorm : p.factor;
+                }
+                double gl = 0.0;
+                if (fnorm != 0.0 && lane < K && acn != 0.0) gl = fabs(g / fnorm) / acn;
+                gnorm = tr_wmax(gl);
+                if (gnorm <= p.gtol || gnorm <= eps) {
+                    st = STATUS_CONVERGED;
+                    done = true;
+                }
+                d = fmax(d, acn);
+            }
+            if (!done) {
+                const double x = tr_lmpar(A, W, perm, K, lane, g, d, delta, par);
+                pnorm = tr_norm(lane < K ? d * x : 0.0);
+                if (outer == 1) delta = fmin(delta, pnorm);
+                if (lane < K) {
+                    const T xk = (T)x;
+                    p.delta[dsc.c_off + lane] = xk;
+                    p.ctry[dsc.c_off + lane] = p.c[dsc.c_off + lane] + xk;
+                }
+                if (lane == 0) p.pending[m] = 1;
+            }
+        }
+        if (lane < K) p.diag[dsc.c_off + lane] = d;
+        if (lane == 0) {
+            trs[TR_DELTA] = delta; trs[TR_PAR] = par; trs[TR_FNORM] = fnorm;
+            trs[TR_XNORM] = xnorm; trs[TR_PNORM] = pnorm; trs[TR_GNORM] = gnorm;
+            p.outer[m] = outer;
+            p.status[m] = st;
+            if (st == ST_RUNNING) atomicAdd(p.n_running, 1);
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace cusr

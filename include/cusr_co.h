@@ -142,6 +142,31 @@ typedef struct CoOptions {
                             /* diag *= 1+lam (a zero Jacobian column -> FAIL_CHOLESKY).   */
                             /* f > 0: a system that damping cannot factor is retried with */
                             /* diag + lam * max(diag, f * max(diag)) (robust fits)        */
+    /* ---- algorithm and start axis (fields past this point take their defaults when ---- */
+    /* ---- struct_size ends before them) ---------------------------------------------- */
+    int32_t algorithm;      /* CO_ALG_REFERENCE (default): the reference LM schedule      */
+                            /* (lambda x0.1 / x10, co_lib.cu:438-455); CO_ALG_TRUST_REGION:*/
+                            /* the trust-region LM of MINPACK lmder (More 1977), the       */
+                            /* algorithm of the reference's scipy backend; max_iter then   */
+                            /* bounds function evaluations per fit, the first included     */
+                            /* (scipy's max_nfev); xtol / ftol / gtol are MINPACK's         */
+    int32_t n_starts;       /* fits per tree (0 or 1: one, from c_init). S > 1: start 0 is  */
+                            /* c_init, starts 1.. are points around it and fresh draws,     */
+                            /* generated on the device from start_seed; the programs are    */
+                            /* compiled and stored once per tree; every output is the start */
+                            /* with the lowest final loss (fp64 audit loss for fp32 fits)  */
+    int32_t tr_starts;      /* > 0: starts 0 .. tr_starts-1 use the trust-region LM, the    */
+                            /* others the reference schedule (with damping_floor as a       */
+                            /* fallback, every second one with the floored damping always); */
+                            /* 0: `algorithm` applies to every start                        */
+    int32_t wave1;          /* 0: all starts at once. W in (0, n_starts): starts 0..W-1 run */
+                            /* first; a tree whose first-wave fits agree (two or more within */
+                            /* agree_tol of the best) retires its other starts unrun, the  */
+                            /* others start them                                           */
+    double  ftol;           /* trust region: relative reduction tolerance (default 1e-10)   */
+    double  gtol;           /* trust region: gradient tolerance (default 1e-8, scipy's)     */
+    double  agree_tol;      /* wave agreement, relative (default 1e-7)                      */
+    uint64_t start_seed;    /* start points (default 0)                                     */
     int32_t reserved[2];
 } CoOptions;
 
@@ -149,8 +174,13 @@ typedef struct CoOptions {
 #define CO_AD_FORWARD 1
 #define CO_AD_REVERSE 2
 
+#define CO_ALG_REFERENCE    0
+#define CO_ALG_TRUST_REGION 1
+#define CO_MAX_STARTS       1024
+
 /* Fill `opt` with the reference defaults (fp32, 50 iterations, lambda0 1e-3, xtol 1e-6,
- * audit auto, early exit on). */
+ * audit auto, early exit on, the reference schedule, one start; trust-region tolerances
+ * ftol 1e-10, gtol 1e-8; wave agreement 1e-7). */
 void co_default_options(CoOptions *opt);
 
 /* Extended fit. Same inputs as co_optimize (ym may be a single shared row, see
@@ -183,8 +213,11 @@ typedef struct CoStats {
     int32_t n_bins;         /* scheduler bins used                                      */
     int32_t y_shared;       /* 1 if targets were kept as one shared row                 */
     int32_t precision;      /* CO_PREC_* of the call                                    */
-    int32_t n_reverted;     /* trees reverted to c_init by the fp64 audit               */
-    int32_t reserved[7];
+    int32_t n_reverted;     /* fits reverted to their start by the fp64 audit           */
+    int32_t n_starts;       /* fits per tree of the call                                */
+    int64_t fits_run;       /* fits (tree x start) evaluated at least once              */
+    int32_t trees_retired;  /* trees whose later starts were retired unrun (wave1)      */
+    int32_t reserved[3];
 } CoStats;
 
 /* Resident problem: co_load compiles, schedules and uploads a population (programs,
@@ -241,6 +274,11 @@ int  co_jacobian_fd(void *handle, const PopHeader *header,
                     const TreeMeta *metas, const double *c,
                     const float *xs, const float *ym, int precision, int y_shared,
                     double eps, double *jac_out);
+
+/* The start each tree's outputs of the last fit on `handle` came from (0 = its c_init), for
+ * fits with CoOptions.n_starts > 1; start_out[M_prob] of that fit. (No counterpart in the
+ * reference, which fits every tree once.) */
+int  co_last_starts(void *handle, int32_t *start_out);
 
 /* Statistics of the last co_optimize* / co_fit_loaded call on `handle`. */
 int  co_get_stats(void *handle, CoStats *out);

@@ -23,6 +23,11 @@ int cusr_compile_tree(const int32_t *nt, const float *nv, const int32_t *ci, int
 double cusr_eval_program(const uint32_t *fwd, int n_fwd, const uint32_t *bwd, int n_bwd,
                          const double *x, const double *c, int K, double *grad);
 
+/* The start points the engine generates for tree m (CoOptions.n_starts, start_seed), computed
+ * on the host with the same formulas: out[s * K + k] for starts 0..S-1 of a tree whose c_init
+ * is c0[0..K). */
+void cusr_start_points(uint64_t seed, int64_t m, int S, int K, const float *c0, float *out);
+
 #ifdef __cplusplus
 }
 #endif

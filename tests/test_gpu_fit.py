@@ -125,14 +125,16 @@ def test_pr1_fit_parity_vs_reference_scipy(co):
     assert frac >= 0.6
 
 
-def _multistart_parity(co, name, pop, ref):
-    """North-star parity with multi-start fits (cusr_b200.multistart defaults: 256 starts,
-    c_init first; half with the reference damping and a fallback floor, half with the floor
-    always; best final loss kept): the fraction of trees whose fp64 loss is within 1e-6
-    relative of, or better than, the reference scipy fit. Divergent trees are listed."""
+def _multistart_parity(co, name, pop, ref, **kw):
+    """North-star parity with the parity-grade fit (cusr_b200.multistart defaults: the device
+    start axis, 20 starts per tree — 4 trust-region, 16 reference-schedule with the damping
+    floor — in two waves, fp64, the best final loss kept): the fraction of trees whose fp64 loss
+    is within 1e-6 relative of, or better than, the reference scipy fit. Divergent trees are
+    listed."""
     from cusr_b200 import multistart
 
-    res = multistart.fit_multistart(co, pop)
+    res = multistart.fit_multistart(co, pop, **kw)
+    st = co.stats()
     ours = interp.loss_pop(pop, res["c_final"])
     K = np.asarray(pop["metas"])[:, 3]
     elig = (K > 0) & np.isfinite(ref)
@@ -140,20 +142,23 @@ def _multistart_parity(co, name, pop, ref):
     frac = float(np.mean(ok[elig]))
     bad = [int(m) for m in np.flatnonzero(elig & ~ok)]
     _report(f"{name}_multistart_vs_scipy", {
-        "within_1e-6_or_better": frac, "n_eligible": int(elig.sum()), "starts": 256,
+        "within_1e-6_or_better": frac, "n_eligible": int(elig.sum()),
+        "starts": int(st["n_starts"]), "fits_run": int(st["fits_run"]),
+        "trees_retired": int(st["trees_retired"]), "device_ms": st["device_ms"],
         "strictly_better_than_scipy": float(np.mean((ours < ref * (1 - 1e-6))[elig])),
+        "winning_start_histogram": np.bincount(res["start"], minlength=int(st["n_starts"])).tolist(),
         "divergent": bad, "ratios": {str(m): float(ours[m] / ref[m]) for m in bad}})
     return frac
 
 
 def test_pr1_multistart_parity_vs_reference_scipy(co):
-    """Measured 99.6% (single start: 66%)."""
+    """PR1 with its reference scipy fits (single start: 66%)."""
     z = np.load(GOLDEN / "pr1_scipy.npz")
     assert _multistart_parity(co, "pr1", load_npz_pop(z, "pop"), z["scipy/loss64"]) >= 0.99
 
 
 def test_pop1000_multistart_parity_vs_reference_scipy(co):
-    """The reference's own pop.bin fixture and its scipy fits: measured 99.8%."""
+    """The reference's own pop.bin fixture and its scipy fits."""
     pop, g = pop1000()
     assert _multistart_parity(co, "pop1000", pop, g["scipy/loss64"]) >= 0.99
 
@@ -161,10 +166,137 @@ def test_pop1000_multistart_parity_vs_reference_scipy(co):
 @pytest.mark.parametrize("name", ["mid", "physics", "long", "scale"])
 def test_config_multistart_parity_vs_reference_scipy(co, name):
     """64-tree samples of the other BASELINE configurations (reduced N) with the reference's
-    scipy fits (tests/golden/configs_scipy.npz): measured 100% on each."""
+    scipy fits (tests/golden/configs_scipy.npz)."""
     z = np.load(GOLDEN / "configs_scipy.npz")
     pop = load_npz_pop(z, name)
     assert _multistart_parity(co, name, pop, z[f"{name}/scipy/loss64"]) >= 0.99
+
+
+def _digest(pop):
+    import hashlib
+
+    h = hashlib.sha256()
+    for k in ("nt", "nv", "ci", "metas", "c_init", "xs", "ym"):
+        h.update(np.ascontiguousarray(pop[k]).tobytes())
+    return h.hexdigest()
+
+
+@pytest.mark.parametrize("name", ["mid", "physics", "long", "scale"])
+def test_config_multistart_parity_full_n(co, name):
+    """32-tree samples of the configurations at their own N (mid 10,000, physics 100,000,
+    long 4,096, scale 20,000) with the reference's scipy fits (configs_full_scipy.npz; the
+    inputs are regenerated from the seeded generator and checked against the stored
+    digest)."""
+    z = np.load(GOLDEN / "configs_full_scipy.npz")
+    pop = synth.make_config(name, M=int(z[f"{name}/M"]), seed=11)
+    assert _digest(pop) == str(z[f"{name}/digest"])
+    assert _multistart_parity(co, f"{name}_fullN", pop, z[f"{name}/scipy/loss64"]) >= 0.96
+
+
+def test_metric_sample_parity_modes(co):
+    """The configuration behind the headline fits/s: a 256-tree stratified sample of the metric
+    population at its full N = 10,000 with the reference's scipy fits (metric_scipy.npz).
+    Reports the north-star fraction (fp64 loss within 1e-6 of, or better than, scipy) of the
+    benchmarked single-start fp32 mode, of the reference's fast-math numerics, of fp64, of one
+    trust-region start, and of the parity-grade multi-start fit."""
+    from cusr_b200 import multistart
+
+    z = np.load(GOLDEN / "metric_scipy.npz")
+    pop = load_npz_pop(z, "pop")
+    ref = z["scipy/loss64"]
+    K = np.asarray(pop["metas"])[:, 3]
+    elig = (K > 0) & np.isfinite(ref)
+
+    def frac(c):
+        blk = co.evaluate(pop, c=c, precision="fp64", values=False, blocks=True)["blocks"]
+        l64 = np.array([b[-1] for b in blk])
+        return float(np.mean((l64 <= ref * (1 + 1e-6) + 1e-12)[elig]))
+
+    rep = {}
+    for prec in ("fp32", "fp32_fast", "fp64"):
+        rep[f"single_{prec}"] = frac(co.optimize_ex(pop, max_iter=50, precision=prec)["c_final"])
+    rep["trust_region_fp64"] = frac(co.optimize_ex(pop, max_iter=200, precision="fp64",
+                                                   xtol=1e-10, algorithm="trust_region")["c_final"])
+    res = multistart.fit_multistart(co, pop)
+    st = co.stats()
+    rep["parity_mode"] = frac(res["c_final"])
+    rep["parity_mode_fits_run"] = int(st["fits_run"])
+    rep["parity_mode_trees_retired"] = int(st["trees_retired"])
+    rep["parity_mode_device_ms"] = st["device_ms"]
+    _report("metric_sample_modes_vs_scipy", rep)
+    assert rep["single_fp32"] >= 0.45 and rep["parity_mode"] >= 0.97, rep
+
+
+def test_trust_region_fp64_matches_oracle(co):
+    """One trust-region start per tree on PR1 (fp64, 200 evaluations, scipy's tolerances)
+    against oracle/tr_lm.py, the CPU restatement of the same algorithm: the same final loss
+    (within 1e-6) on most trees (the rest part at rounding level in chaotic trajectories), and
+    the north-star fraction against scipy at the level the restatement reaches (0.82)."""
+    from oracle import tr_lm
+
+    z = np.load(GOLDEN / "pr1_scipy.npz")
+    pop = load_npz_pop(z, "pop")
+    res = co.optimize_ex(pop, max_iter=200, precision="fp64", xtol=1e-10,
+                         algorithm="trust_region")
+    orc = tr_lm.fit_pop(pop)
+    ours = interp.loss_pop(pop, res["c_final"])
+    theirs = interp.loss_pop(pop, orc["c_final"])
+    ref = z["scipy/loss64"]
+    K = pop["metas"][:, 3]
+    fin = (K > 0) & np.isfinite(theirs) & np.isfinite(ref)
+    same = np.abs(ours - theirs) <= 1e-6 * np.abs(theirs) + 1e-12
+    better = ours <= theirs * (1 + 1e-6) + 1e-12
+    vs_scipy = float(np.mean((ours <= ref * (1 + 1e-6) + 1e-12)[fin]))
+    _report("pr1_trust_region_vs_oracle", {
+        "same_1e-6": float(np.mean(same[fin])), "same_or_better": float(np.mean(better[fin])),
+        "vs_scipy": vs_scipy,
+        "oracle_vs_scipy": float(np.mean((theirs <= ref * (1 + 1e-6) + 1e-12)[fin])),
+        "status": np.bincount(res["status"], minlength=5).tolist(),
+        "iters_median": float(np.median(res["iters"]))})
+    assert np.mean(same[fin]) >= 0.75
+    assert vs_scipy >= 0.74
+
+
+def test_start_axis_points_match_generator(co):
+    """With max_iter = 0 every fit stops at its start point: each tree reports the start point
+    of the start with the lowest initial loss, which must be the host restatement's point of
+    that start (multistart.start_points), and start 0 is c_init."""
+    from cusr_b200 import multistart
+
+    pop = synth.make_config("pr1", M=64, N=300, seed=17)
+    S, seed = 12, 99
+    res = co.optimize_ex(pop, max_iter=0, precision="fp64", n_starts=S, seed=seed)
+    pts = multistart.start_points(pop, S, seed)
+    K = pop["metas"][:, 3]
+    offs = np.concatenate([[0], np.cumsum(S * K)])
+    for m in range(int(pop["M"])):
+        s = int(res["start"][m])
+        k = int(K[m])
+        want = pts[offs[m] + s * k: offs[m] + (s + 1) * k]
+        got = popio.tree_consts(pop, res["c_final"], m).astype(np.float32)
+        # the device's double log / cos / exp may round differently from the host's by an
+        # ulp before the cast to float
+        assert np.all(np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32)) <= 1), m
+    kk = K > 0
+    assert np.all(res["loss_final"][kk] <= res["loss_init"][kk] * (1 + 1e-12) + 1e-300)
+
+
+def test_waves_retire_agreeing_trees(co):
+    """Two waves: trees whose first-wave fits agree skip the later starts; the outcome is as
+    good as running every start on nearly all trees, for fewer fits."""
+    from cusr_b200 import multistart
+
+    z = np.load(GOLDEN / "pr1_scipy.npz")
+    pop = load_npz_pop(z, "pop")
+    all_at_once = multistart.fit_multistart(co, pop, wave1=0)
+    n_all = co.stats()["fits_run"]
+    waved = multistart.fit_multistart(co, pop)
+    st = co.stats()
+    assert st["trees_retired"] > 0 and st["fits_run"] < n_all
+    la = interp.loss_pop(pop, all_at_once["c_final"])
+    lw = interp.loss_pop(pop, waved["c_final"])
+    fin = np.isfinite(la)
+    assert np.mean((lw <= la * (1 + 1e-6) + 1e-12)[fin]) >= 0.97
 
 
 def test_pop1000_vs_reference_kernel_golden(co):
@@ -363,7 +495,7 @@ def test_fitresult_backend_single_and_multistart():
 
     pop = synth.make_config("pr1", M=64, N=400, seed=12)
     one = B200Pop(precision="fp64").fit_pop(pop)
-    ms = B200Pop(precision="fp64", starts=16).fit_pop(pop)
+    ms = B200Pop(precision="fp64", starts=20).fit_pop(pop)
     for r in (one, ms):
         assert r.c_final.shape == (pop["total_c"],) and r.status.shape == (64,)
         assert set(np.unique(r.status)) <= {0, 1, 2, 3}

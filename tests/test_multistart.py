@@ -1,101 +1,84 @@
-"""Multi-start host logic (replication, start points, best-start selection, batching), with a
-stand-in optimizer on the CPU; the device fit itself is covered in test_gpu_fit.py."""
+"""Multi-start host side: the start-point generator's host restatement against the engine's
+own formulas compiled for the host (cusr_start_points), determinism, start 0 = c_init, the
+kinds' spread; and the parity preset's options reach the ABI. The device fits themselves are
+in test_gpu_fit.py."""
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
+import pytest
 
-from cusr_b200 import multistart, popio, synth
+from cusr_b200 import co_inproc, multistart, synth
 
 
-def test_replicate_copies_programs_and_constants():
-    pop = synth.make_config("pr1", M=9, N=13, seed=1)
-    r = popio.replicate(pop, 4)
-    assert r["M"] == 36 and r["total_c"] == 4 * pop["total_c"]
-    for m in range(9):
-        for s in range(4):
-            a, b = popio.tree_view(pop, m), popio.tree_view(r, 4 * m + s)
-            for x, y in zip(a[:3], b[:3]):
-                np.testing.assert_array_equal(x, y)
-            np.testing.assert_array_equal(popio.tree_consts(pop, pop["c_init"], m),
-                                          popio.tree_consts(r, r["c_init"], 4 * m + s))
-    phys = synth.make_config("physics", M=3, N=5, seed=2)     # per-tree targets repeat
-    rp = popio.replicate(phys, 2)
-    np.testing.assert_array_equal(rp["ym"][3], phys["ym"][1])
+def _host_points(lib, pop, S, seed):
+    out = []
+    for m in range(int(pop["M"])):
+        _o, _n, c_off, K = (int(v) for v in pop["metas"][m])
+        c0 = np.ascontiguousarray(pop["c_init"][c_off:c_off + K], np.float32)
+        buf = np.zeros(max(S * K, 1), np.float32)
+        lib.cusr_start_points(ctypes.c_uint64(seed), ctypes.c_int64(m), S, K,
+                              c0.ctypes.data_as(ctypes.c_void_p), buf.ctypes.data_as(ctypes.c_void_p))
+        out.append(buf[:S * K])
+    return np.concatenate(out)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    path = co_inproc.default_lib_path()
+    if not path.exists():
+        pytest.skip("library not built")
+    lib = ctypes.CDLL(str(path))
+    lib.cusr_start_points.restype = None
+    return lib
+
+
+def test_start_points_match_engine_formulas(lib):
+    pop = synth.make_config("pr1", M=40, N=8, seed=3)
+    for S, seed in ((1, 0), (9, 0), (20, 12345), (33, 2 ** 63 + 7)):
+        mine = multistart.start_points(pop, S, seed)
+        host = _host_points(lib, pop, S, seed)
+        assert mine.shape == host.shape
+        # the same formulas in numpy and C: equal floats, at most one float ulp apart where
+        # the two libm's round log / cos / exp differently
+        assert np.array_equal(mine, host) or np.max(
+            np.abs(mine.view(np.int32).astype(np.int64) - host.view(np.int32))) <= 1
 
 
 def test_start_points_first_is_c_init_and_deterministic():
     pop = synth.make_config("pr1", M=20, N=8, seed=3)
     a = multistart.start_points(pop, 8, seed=5)
-    b = multistart.start_points(pop, 8, seed=5)
-    np.testing.assert_array_equal(a, b)
-    r = popio.replicate(pop, 8, c_init=a)
-    for m in range(20):
-        np.testing.assert_array_equal(popio.tree_consts(r, r["c_init"], 8 * m),
-                                      popio.tree_consts(pop, pop["c_init"], m))
+    np.testing.assert_array_equal(a, multistart.start_points(pop, 8, seed=5))
     assert not np.array_equal(a, multistart.start_points(pop, 8, seed=6))
+    K = pop["metas"][:, 3]
+    off = 0
+    for m in range(20):
+        k = int(K[m])
+        c0 = pop["c_init"][pop["metas"][m][2]:pop["metas"][m][2] + k]
+        np.testing.assert_array_equal(a[off:off + k], c0)          # start 0
+        off += 8 * k
 
 
-class _FakeCO:
-    """loss_final = sum((c - 1)^2) per tree; c_final = c_init (no fitting)."""
-
-    def optimize_ex(self, pop, max_iter=50, precision="fp64", xtol=1e-6, damping_floor=0.0,
-                    damping_always=False):
-        M = int(pop["M"])
-        metas = np.asarray(pop["metas"]).reshape(M, 4)
-        c = np.asarray(pop["c_init"], np.float64)
-        lf = np.array([np.sum((c[o:o + k] - 1.0) ** 2) for _, _, o, k in metas])
-        lf[::7] = np.nan                                     # some failed starts
-        return {"c_final": c.copy(), "status": np.arange(M, dtype=np.int32) % 5,
-                "loss_init": lf.copy(), "loss_final": lf, "iters": np.full(M, 3, np.int32)}
-
-
-def test_select_best_and_batching():
-    pop = synth.make_config("pr1", M=30, N=8, seed=4)
-    co = _FakeCO()
-    one = multistart.fit_multistart(co, pop, starts=6, seed=0, damping_floor=0.0)
-    K = np.asarray(pop["metas"])[:, 3]
-    # the chosen start is the argmin of the finite losses, its constants are returned
-    pts = multistart.start_points(pop, 6, seed=0)
-    r = popio.replicate(pop, 6, c_init=pts)
-    for m in range(30):
-        losses = []
-        for s in range(6):
-            j = 6 * m + s
-            cs = popio.tree_consts(r, r["c_init"], j).astype(np.float64)
-            losses.append(np.inf if j % 7 == 0 else np.sum((cs - 1.0) ** 2))
-        best = int(np.argmin(losses))
-        assert one["start"][m] == best
-        np.testing.assert_array_equal(popio.tree_consts(pop, one["c_final"], m),
-                                      popio.tree_consts(r, r["c_init"], 6 * m + best))
-    assert one["c_final"].size == pop["total_c"] and one["status"].shape == (30,)
-    assert np.all(K[one["start"] == 0] >= 0)
+def test_start_kinds_spread():
+    """Fresh N(0,1) / N(0,9) starts have those spreads."""
+    pop = synth.make_config("pr1", M=256, N=4, seed=1)
+    S = 9
+    pts = multistart.start_points(pop, S, seed=0).astype(np.float64)
+    K = pop["metas"][:, 3]
+    start = np.repeat(np.tile(np.arange(S), 256), np.repeat(K, S))
+    fresh1 = pts[(start > 0) & ((start - 1) % 4 == 2)]
+    fresh3 = pts[(start > 0) & ((start - 1) % 4 == 3)]
+    assert abs(np.std(fresh1) - 1.0) < 0.1 and abs(np.mean(fresh1)) < 0.1
+    assert abs(np.std(fresh3) - 3.0) < 0.3
 
 
-def test_batched_multistart_shapes():
-    pop = synth.make_config("pr1", M=30, N=8, seed=4)
-    out = multistart.fit_multistart(_FakeCO(), pop, starts=6, max_batch=40)   # 6 trees a batch
-    assert out["c_final"].size == pop["total_c"]
-    out = multistart.fit_multistart(_FakeCO(), pop, starts=6, max_batch=40, damping_floor=0.0)
-    assert out["c_final"].size == pop["total_c"]
-    for k in ("status", "loss_init", "loss_final", "start", "iters"):
-        assert out[k].shape == (30,), k
-    assert np.all((out["start"] >= 0) & (out["start"] < 6))
-
-
-def test_damping_halves_keep_start_order():
-    """With a damping floor the starts are fitted as two halves (fallback floor / floor
-    always); the merged result is indexed like one fit of all starts."""
-    pop = synth.make_config("pr1", M=11, N=8, seed=6)
-
-    class Rec(_FakeCO):
-        calls = []
-
-        def optimize_ex(self, pop, **kw):
-            Rec.calls.append(kw.get("damping_always", False))
-            return super().optimize_ex(pop, **kw)
-
-    a = multistart.fit_multistart(Rec(), pop, starts=7, damping_floor=1e-3)
-    assert Rec.calls == [False, True]
-    # the same points fitted in one call select the same start when losses do not depend on
-    # the damping (the stand-in optimizer ignores it) — up to the NaN pattern of each call
-    assert a["c_final"].size == pop["total_c"] and np.all((a["start"] >= 0) & (a["start"] < 7))
+def test_parity_preset_reaches_options():
+    opt = co_inproc.CoOptions()
+    co_inproc.start_options(opt, **{k: v for k, v in co_inproc.PARITY.items()
+                                    if k in ("algorithm", "n_starts", "tr_starts", "wave1",
+                                             "ftol", "gtol")})
+    assert opt.algorithm == 1 and opt.n_starts == 20 and opt.tr_starts == 4 and opt.wave1 == 8
+    assert opt.ftol == 1e-10 and opt.gtol == 1e-8
+    with pytest.raises(ValueError):
+        co_inproc.start_options(opt, algorithm="newton")

@@ -146,3 +146,42 @@ def test_fp32_honesty_fixture_matches_manifest_counts():
     ad = sum(int(z[f"f{i}/ad_serious"].sum()) for i in range(17))
     fd = sum(int(z[f"f{i}/fd_serious"].sum()) for i in range(17))
     assert (n, ad, fd) == (257, 208, 57)
+
+
+def test_trust_region_restatement_follows_scipy_minpack():
+    """oracle/tr_lm.py against the reference backend's own optimizer, scipy least_squares(
+    method='lm') (MINPACK lmder), handed the same exact Jacobian: on trees whose Jacobian at
+    c_init is of full rank (smallest singular value > 1e-8 of the largest) both take the same
+    evaluations and end at the same loss; rank-deficient trees part ways by design (MINPACK's
+    QR keeps rounding-size pivots, the restatement the basic solution)."""
+    from scipy.optimize import least_squares
+
+    from oracle import tr_lm
+
+    z = np.load(GOLDEN / "pr1_scipy.npz")
+    pop = load_npz_pop(z, "pop")
+    same = []
+    for m in range(0, int(pop["M"]), 2):
+        nt, nv, ci, y, K = interp.tree_view(pop, m)
+        if K == 0:
+            continue
+        off = int(pop["metas"][m][2])
+        c0 = np.asarray(pop["c_init"][off:off + K], np.float64)
+        _v, J = interp.value_and_jacobian(nt, nv, ci, pop["xs"], c0)
+        if not np.all(np.isfinite(J)):
+            continue
+        sv = np.linalg.svd(J, compute_uv=False)
+        if not sv[-1] > 1e-8 * sv[0]:
+            continue
+        y64 = np.asarray(y, np.float64)
+        with np.errstate(all="ignore"):
+            r = least_squares(lambda c: interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c) - y64,
+                              c0, jac=lambda c: interp.value_and_jacobian(nt, nv, ci,
+                                                                          pop["xs"], c)[1],
+                              method="lm", xtol=1e-10, ftol=1e-10, max_nfev=200)
+            c, _info, nfev = tr_lm.fit_tree(nt, nv, ci, pop["xs"], y, c0)
+            ls = np.sum((interp.eval_tree_arrays(nt, nv, ci, pop["xs"], r.x) - y64) ** 2)
+            lo = np.sum((interp.eval_tree_arrays(nt, nv, ci, pop["xs"], c) - y64) ** 2)
+        same.append(abs(lo - ls) <= 1e-6 * abs(ls) and r.nfev == nfev)
+    assert len(same) >= 40
+    assert np.mean(same) >= 0.8, np.mean(same)
