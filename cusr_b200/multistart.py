@@ -76,15 +76,33 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
                    precision: str = PARITY["precision"], seed: int = 0,
                    damping_floor: float = PARITY["damping_floor"],
                    tr_starts: int = PARITY["tr_starts"], wave1: int = PARITY["wave1"],
-                   **kw) -> dict:
+                   polish: bool = PARITY["polish"], **kw) -> dict:
     """Fit every tree of `pop` from `starts` starting points (the first is its c_init) in one
     device call (InProcessCO.optimize_ex with n_starts) and return the best start's
     c_final / status / loss_init / loss_final / iters with its index ('start').
+    polish: a second device call continues every tree's best fit with the trust-region LM
+    (from its constants rounded to the fp32 of the ABI) and keeps whichever is lower.
 
-    Defaults: the parity preset (co_inproc.PARITY) — 20 starts, the first 4 with the
-    trust-region LM, the others with the reference schedule and the damping floor, two waves
-    (trees whose first 8 fits agree skip the rest), fp64, scipy's tolerances."""
+    Defaults: the parity preset (co_inproc.PARITY)."""
     algorithm = "trust_region" if tr_starts > 0 else kw.pop("algorithm", "reference")
-    return co.optimize_ex(pop, max_iter=max_iter, precision=precision, xtol=xtol,
-                          damping_floor=damping_floor, algorithm=algorithm, n_starts=starts,
-                          tr_starts=tr_starts, wave1=wave1, seed=seed, **kw)
+    res = co.optimize_ex(pop, max_iter=max_iter, precision=precision, xtol=xtol,
+                         damping_floor=damping_floor, algorithm=algorithm, n_starts=starts,
+                         tr_starts=tr_starts, wave1=wave1, seed=seed, **kw)
+    if not polish:
+        return res
+    stats = co.stats()
+    again = dict(pop)
+    again["c_init"] = np.asarray(res["c_final"], np.float32)
+    pol = co.optimize_ex(again, max_iter=max_iter, precision=precision, xtol=xtol,
+                         algorithm="trust_region", **{k: v for k, v in kw.items()
+                                                      if k in ("y_shared", "ftol", "gtol")})
+    better = np.asarray(pol["loss_final"]) < np.asarray(res["loss_final"])
+    M = int(pop["M"])
+    K = np.asarray(pop["metas"], np.int64).reshape(M, 4)[:, 3]
+    out = {k: np.where(better, pol[k], res[k]) for k in ("status", "loss_final", "iters")}
+    out["loss_init"] = res["loss_init"]
+    out["start"] = res.get("start", np.zeros(M, np.int32))
+    out["polished"] = better
+    out["c_final"] = np.where(np.repeat(better, K), pol["c_final"], res["c_final"])
+    out["stats"] = stats
+    return out
