@@ -3,9 +3,9 @@
     python -m cusr_b200.build            # incremental
     python -m cusr_b200.build --force    # rebuild everything
 
-The library is also exposed under the file names the CuSR ctypes loader looks for
-(libcusr_co_ad.so, libcusr_co_fd.so), so the reference's `co_inproc.InProcessCO` can bind it
-unchanged.
+The library is also exposed under the file name the CuSR ctypes loader looks for
+(libcusr_co_ad.so), and libcusr_co_fd.so is built beside it (the FD variant's acceptance
+order, over this library), so the reference's `co_inproc.InProcessCO` binds either unchanged.
 """
 from __future__ import annotations
 
@@ -22,7 +22,11 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 OBJ = HERE / "_build"
 LIB = HERE / "libcusr_b200.so"
-ALIASES = ("libcusr_co_ad.so", "libcusr_co_fd.so")
+ALIASES = ("libcusr_co_ad.so",)
+# the FD variant's name: its own small library (co_optimize with the FD acceptance order) over
+# libcusr_b200.so
+FD_LIB = HERE / "libcusr_co_fd.so"
+FD_SOURCE = "fd_variant.cpp"
 # command-line front end with the reference binary's interface, and the names the reference's
 # subprocess callers use for it
 CLI = HERE / "batch_lm_b200"
@@ -87,6 +91,12 @@ def build(force: bool = False, verbose: bool = False, defines: tuple = (), obj_d
              *map(str, objs), "-lcudart", "-ldl"])
     if lib is not None:
         return LIB
+    fd_src = CSRC / FD_SOURCE
+    if FD_LIB.is_symlink():
+        FD_LIB.unlink()
+    if force or _stale(FD_LIB, [fd_src, LIB, *hdrs]):
+        run(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-I{INCLUDE}", str(fd_src), "-o",
+             str(FD_LIB), f"-L{HERE}", f"-l:{LIB.name}", "-Wl,-rpath,$ORIGIN"])
     cli_src = CSRC / CLI_SOURCE
     if force or _stale(CLI, [cli_src, LIB, *hdrs]):
         run(["g++", "-O2", "-std=c++17", f"-I{INCLUDE}", str(cli_src), "-o", str(CLI),

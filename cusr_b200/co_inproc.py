@@ -103,7 +103,8 @@ class CoOptions(ctypes.Structure):
         ("algorithm", ctypes.c_int32), ("n_starts", ctypes.c_int32),
         ("tr_starts", ctypes.c_int32), ("wave1", ctypes.c_int32),
         ("ftol", ctypes.c_double), ("gtol", ctypes.c_double), ("agree_tol", ctypes.c_double),
-        ("start_seed", ctypes.c_uint64), ("reserved", ctypes.c_int32 * 2),
+        ("start_seed", ctypes.c_uint64), ("fd_ordering", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 1),
     ]
 
 
@@ -248,12 +249,13 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
     return opt
 
 
-# The parity-grade fit: every tree fitted from 20 starts in one device batch (4 with the
-# trust-region LM of the reference's scipy backend, 16 with the reference schedule and the
-# damping floor), in two waves (trees whose first 8 fits agree skip the other 12), fp64,
-# scipy's tolerances; the lowest final loss is kept.
+# The parity-grade fit: every tree fitted from 64 starts in one device batch (16 with the
+# trust-region LM of the reference's scipy backend, 48 with the reference schedule and the
+# damping floor), in two waves (trees whose first 8 fits agree skip the other 56), fp64,
+# scipy's tolerances, then a trust-region polish of each tree's best fit; the lowest final
+# loss is kept.
 PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
-              algorithm="trust_region", n_starts=20, tr_starts=4, wave1=8, ftol=1e-10,
+              algorithm="trust_region", n_starts=64, tr_starts=16, wave1=8, ftol=1e-10,
               gtol=1e-8, polish=True)
 
 

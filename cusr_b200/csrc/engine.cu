@@ -633,6 +633,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     sp.damping_always = opt.damping_always ? 1 : 0;
     sp.imode = P<uint8_t>(ctx->imode);
     sp.max_iter = std::max(0, opt.max_iter);
+    sp.fd_order = opt.fd_ordering ? 1 : 0;
     sp.xtol = (T)opt.xtol;
 
     TrParams<T> tp;

@@ -36,6 +36,7 @@ struct StepParams {
                              // reference schedule with the call's damping settings
     int *n_running;          // trees still running after this step (early exit)
     int max_iter;            // LM iterations per fit
+    int fd_order;            // the FD variant's acceptance order (co_lib.cu:456-471)
     T xtol;
 };
 
@@ -116,7 +117,24 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                             cn2 += ck * ck;
                         }
                         const T dn = Mth<T>::sqrt(dn2), cn = Mth<T>::sqrt(cn2);
-                        if (ltry <= p.loss[m]) {
+                        if (p.fd_order) {
+                            // FD variant: a small step converges (and is kept) first, then
+                            // a strict improvement is accepted
+                            if (dn < p.xtol * (cn + p.xtol) || ltry < p.loss[m]) {
+                                accept = 1;
+                                p.loss[m] = ltry;
+                                for (int k = 0; k < K; ++k) p.c[d.c_off + k] = p.ctry[d.c_off + k];
+                                if (dn < p.xtol * (cn + p.xtol)) {
+                                    st = STATUS_CONVERGED;
+                                } else {
+                                    lam *= T(0.1);
+                                    if (lam < T(1e-12)) lam = T(1e-12);
+                                }
+                            } else {
+                                lam *= T(10);
+                                if (lam > T(1e12)) st = STATUS_FAIL_NAN;
+                            }
+                        } else if (ltry <= p.loss[m]) {
                             accept = 1;
                             p.loss[m] = ltry;
                             for (int k = 0; k < K; ++k) p.c[d.c_off + k] = p.ctry[d.c_off + k];

@@ -92,7 +92,8 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
         return res
     stats = co.stats()
     again = dict(pop)
-    again["c_init"] = np.asarray(res["c_final"], np.float32)
+    with np.errstate(over="ignore"):            # fits that ran off to huge constants
+        again["c_init"] = np.asarray(res["c_final"], np.float32)
     pol = co.optimize_ex(again, max_iter=max_iter, precision=precision, xtol=xtol,
                          algorithm="trust_region", **{k: v for k, v in kw.items()
                                                       if k in ("y_shared", "ftol", "gtol")})

@@ -1,7 +1,7 @@
 /* cusr_co.h — C ABI of the cusr-b200 batched Levenberg–Marquardt constant-fitting engine.
  *
  * One shared library, libcusr_b200.so (also installed under the names the CuSR loader
- * expects, libcusr_co_ad.so / libcusr_co_fd.so), exports:
+ * expects, see below), exports:
  *
  *   - the four entry points of the reference in-process drop-in, with identical
  *     signatures, argument meaning and return codes, so the reference's ctypes loader
@@ -12,6 +12,10 @@
  *         co_teardown    replaces cusr/kernel/co_lib.h:73    (co_lib.cu:549-568)
  *   - co_optimize_ex / co_get_stats: the extended entry (precision, shared targets,
  *     damping / tolerance knobs, fp64 outputs, per-tree iteration counts, timings).
+ *
+ * libcusr_co_ad.so is this library under the AD variant's name; libcusr_co_fd.so is a small
+ * library of its own whose co_optimize has the FD variant's acceptance order
+ * (CoOptions.fd_ordering) and which takes every other symbol from this one.
  *
  * pop.bin structures (PopHeader 64 B, TreeMeta 16 B) keep the byte layout of
  * cusr/kernel/pop_format.h:32-51 because the file format and the ABI carry them.
@@ -167,7 +171,11 @@ typedef struct CoOptions {
     double  gtol;           /* trust region: gradient tolerance (default 1e-8, scipy's)     */
     double  agree_tol;      /* wave agreement, relative (default 1e-7)                      */
     uint64_t start_seed;    /* start points (default 0)                                     */
-    int32_t reserved[2];
+    int32_t fd_ordering;    /* reference schedule, 1: the FD variant's acceptance order     */
+                            /* (co_lib.cu:456-471): a step below xtol is CONVERGED and kept */
+                            /* before the improvement test, improvement is strict (<);      */
+                            /* 0 (default): the AD variant's (improvement first, <=)        */
+    int32_t reserved[1];
 } CoOptions;
 
 #define CO_AD_AUTO    0

@@ -24,6 +24,8 @@ Everything written here comes from the reference's own code and files:
                                  (experiments/revad_v5/jac_sample_fixed.jsonl)
   metric_scipy.npz               reference ScipyPop fits of a 256-tree stratified sample of
                                  the headline metric population at its full N (--metric)
+  fd_pop1000.npz                 the reference FD variant's outputs on the pop.bin fixture
+                                 (--fd)
   configs_full_scipy.npz         reference ScipyPop fits of 32-tree samples of the mid,
                                  physics, long and scale configurations at their own N
                                  (--configs-full; inputs stored as a digest)
@@ -161,6 +163,22 @@ def make_config_samples_full() -> None:
     np.savez_compressed(HERE / "configs_full_scipy.npz", **arr)
 
 
+def make_fd_golden() -> None:
+    """fd_pop1000.npz: the reference FD variant's outputs on its pop.bin fixture
+    (cusr/kernel/tests/golden/fd/pop1000: status, c_final; 50 iterations,
+    tests/test_inproc_parity.py:44) and their fp64 losses."""
+    REF = _reference()
+    sys.path.insert(0, str(REF))
+    from cusr.benchmark import interp, popio  # reference code
+
+    pop = popio.load_pop_bin(REF / "data" / "fixtures" / "pop.bin")
+    gd = REF / "cusr" / "kernel" / "tests" / "golden" / "fd" / "pop1000"
+    c = np.fromfile(gd / "c_final.bin", np.float32)
+    st = np.fromfile(gd / "status.bin", np.int32)
+    np.savez_compressed(HERE / "fd_pop1000.npz", status=st, c_final=c,
+                        loss64=interp.loss_pop(pop, c.astype(np.float64)))
+
+
 def make_honesty() -> None:
     """fp32_honesty.npz: the fp32-honesty regression fixtures of the reference."""
     REF = _reference()
@@ -192,6 +210,9 @@ def main() -> None:
         return
     if "--metric" in sys.argv:
         make_metric_sample()
+        return
+    if "--fd" in sys.argv:
+        make_fd_golden()
         return
     if "--configs-full" in sys.argv:
         make_config_samples_full()

@@ -67,3 +67,17 @@ def test_reference_loader_binds_library_and_reports_no_device():
     assert cdll.co_last_split(ctypes.byref(s), ctypes.byref(l)) == 0
     cdll.co_teardown.argtypes = [ctypes.c_void_p]
     cdll.co_teardown(None)                 # NULL-safe, as the reference's
+
+
+def test_fd_library_has_its_own_co_optimize():
+    """libcusr_co_fd.so defines co_optimize (the FD acceptance order) and takes co_init,
+    co_last_split, co_teardown and the extended symbols from libcusr_b200.so."""
+    fd = ctypes.CDLL(str(_lib("libcusr_co_fd.so").resolve()))
+    base = ctypes.CDLL(str(_lib("libcusr_b200.so").resolve()))
+
+    def addr(f):
+        return ctypes.cast(f, ctypes.c_void_p).value
+
+    assert addr(fd.co_optimize) != addr(base.co_optimize)
+    for sym in ("co_init", "co_teardown", "co_last_split", "co_optimize_ex"):
+        assert addr(getattr(fd, sym)) == addr(getattr(base, sym)), sym
