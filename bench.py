@@ -296,6 +296,43 @@ def run_reference(args, world: int, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def parity_mode(co, pop: dict) -> dict:
+    """The parity-grade fit (cusr_b200.multistart defaults: 64 starts per tree on the device,
+    16 trust-region / 48 reference-schedule, two waves, fp64, trust-region polish): fits/s on a
+    2,048-tree stratified slice of the metric population (device time of the multi-start call
+    plus the polish call), and the north-star fraction — fp64 loss within 1e-6 of, or better
+    than, the reference scipy fit — on the 256-tree scipy sample of the same population
+    (tests/golden/metric_scipy.npz, made by the reference's ScipyPop)."""
+    from cusr_b200 import multistart, popio
+
+    sub = popio.slice_pop(pop, np.unique(np.linspace(0, int(pop["M"]) - 1, 2048).astype(np.int64)))
+    multistart.fit_multistart(co, popio.slice_pop(sub, 64))            # warm-up
+    res = multistart.fit_multistart(co, sub)
+    st = res["stats"]
+    ms = st["device_ms"] + co.stats()["device_ms"]
+    golden = ROOT / "tests" / "golden" / "metric_scipy.npz"
+    frac = None
+    if golden.exists():
+        z = np.load(golden)
+        sample = {k: z[f"pop/{k}"] for k in ("nt", "nv", "ci", "metas", "c_init", "xs", "ym")}
+        sample.update({k: int(z[f"pop/{k}"]) for k in ("M", "total_nodes", "total_c", "N",
+                                                        "n_vars", "K_max", "max_stack")})
+        r = multistart.fit_multistart(co, sample)
+        blk = co.evaluate(sample, c=r["c_final"], precision="fp64", values=False,
+                          blocks=True)["blocks"]
+        l64 = np.array([b[-1] for b in blk])
+        ref = z["scipy/loss64"]
+        elig = (sample["metas"][:, 3] > 0) & np.isfinite(ref)
+        frac = float(np.mean((l64 <= ref * (1 + 1e-6) + 1e-12)[elig]))
+    return {"value": int(sub["M"]) / (ms / 1e3), "unit": "fits/s",
+            "within_1e-6_or_better": frac, "starts": int(st["n_starts"]),
+            "fits_run": int(st["fits_run"]), "trees_retired": int(st["trees_retired"]),
+            "trees": int(sub["M"]), "dtype": "f64", "device_ms": ms,
+            "note": "the parity-grade mode (64 device-side starts, trust-region + reference "
+                    "schedule, fp64) on a 2,048-tree slice of the metric population; the "
+                    "fraction on the 256-tree reference scipy sample of that population"}
+
+
 def run_ours(args, world: int, rank: int, local: int) -> None:
     from cusr_b200 import InProcessCO, shard
 
@@ -411,6 +448,8 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
         "clocks": clk,
         "node_evals_per_s": roofline["node_evals_per_s"],
     }
+    if world == 1 and not args.no_parity_mode:
+        line["parity_mode"] = parity_mode(co, pop)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(pop)
     print(json.dumps(line), flush=True)
@@ -519,8 +558,12 @@ def run_profile_case(args) -> None:
                          "tree_samples": int(sel.sum()) * int(pop["N"])}
     print(json.dumps({"profile_bins": bins}), flush=True)
     co = InProcessCO(device_id=0)
-    co.load(pop, precision=pop["precision"])
-    res = co.fit_loaded(max_iter=args.profile_iters)
+    precision = args.profile_precision or pop["precision"]
+    co.load(pop, precision=precision)
+    kw = {}
+    if args.profile_alg == "trust_region":
+        kw = dict(algorithm="trust_region", xtol=1e-10)
+    res = co.fit_loaded(max_iter=args.profile_iters, **kw)
     st = co.stats()
     print(json.dumps({"profile_case": True, "trees": int(pop["M"]), "N": int(pop["N"]),
                       "iters": args.profile_iters, "device_ms": st["device_ms"],
@@ -536,6 +579,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference", "reference_gpu"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity-mode", action="store_true",
+                    help="skip the parity-grade mode's measurement")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="--impl reference: skip timing the reference's CUDA path")
     ap.add_argument("--out-dir", default=None,
@@ -544,6 +589,10 @@ def main() -> None:
                     help="run the small ncu case (--profile-trees trees) instead of the benchmark")
     ap.add_argument("--profile-iters", type=int, default=2)
     ap.add_argument("--profile-trees", type=int, default=8192)
+    ap.add_argument("--profile-alg", choices=["reference", "trust_region"], default="reference",
+                    help="--profile-case: the LM algorithm of the fit")
+    ap.add_argument("--profile-precision", default=None,
+                    help="--profile-case: fp32 | fp64 | fp32_fast (default: the config's)")
     ap.add_argument("--config", default=None,
                     help="bench one BASELINE configuration instead of the headline metric: "
                          "pr1, mid, physics, long, scale, sharded")
