@@ -104,7 +104,8 @@ class CoOptions(ctypes.Structure):
         ("tr_starts", ctypes.c_int32), ("wave1", ctypes.c_int32),
         ("ftol", ctypes.c_double), ("gtol", ctypes.c_double), ("agree_tol", ctypes.c_double),
         ("start_seed", ctypes.c_uint64), ("fd_ordering", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 1),
+        ("n_devices", ctypes.c_int32), ("device_ids", ctypes.c_int32 * 8),
+        ("reserved", ctypes.c_int32 * 2),
     ]
 
 
@@ -346,7 +347,7 @@ class InProcessCO:
                     y_shared: bool | None = None, lambda0: float = 1e-3, xtol: float = 1e-6,
                     fp64_audit: int = -1, early_exit: bool = True, keep_inputs: bool = False,
                     ad_mode: str = "auto", damping_floor: float = 0.0,
-                    damping_always: bool = False, **starts):
+                    damping_always: bool = False, devices=None, **starts):
         """Extended fit: precision 'fp32' | 'fp64' | 'fp32_fast'; y_shared=True passes one
         target row (pop['ym'] may then be (N,) or (M, N) with identical rows; None = auto: a
         1-D ym). keep_inputs=True reuses the X / shared y left on the device by the previous
@@ -355,9 +356,13 @@ class InProcessCO:
         retries a system the reference damping diag*(1+lam) cannot factor with
         diag + lam*max(diag, f*max diag) (damping_always: use that damping on every solve).
         `starts` (see start_options): algorithm 'reference' | 'trust_region', n_starts,
-        tr_starts, wave1, ftol, gtol, agree_tol, seed.
+        tr_starts, wave1, ftol, gtol, agree_tol, seed. devices=[d0, d1, ...] (up to 8): the
+        trees are split into cost-balanced shards fitted concurrently on those devices in this
+        one call (CoOptions.n_devices / device_ids).
         Returns fp64 c_final / loss_init / loss_final plus status and per-tree iters (and,
         with n_starts > 1, 'start': the start each tree's outputs came from)."""
+        if devices is not None:
+            starts = dict(starts, devices=list(devices))
         return self._fit_ex("co_optimize_ex", pop, max_iter, precision, y_shared, lambda0,
                             xtol, fp64_audit, early_exit, keep_inputs, ad_mode, damping_floor,
                             damping_always, starts)
@@ -401,7 +406,15 @@ class InProcessCO:
         opt.keep_inputs = 1 if keep_inputs else 0
         opt.damping_floor = float(damping_floor)
         opt.damping_always = 1 if damping_always else 0
-        start_options(opt, **(starts or {}))
+        starts = dict(starts or {})
+        devices = starts.pop("devices", None)
+        start_options(opt, **starts)
+        if devices:
+            if len(devices) > len(opt.device_ids):
+                raise ValueError(f"at most {len(opt.device_ids)} devices per call")
+            opt.n_devices = len(devices)
+            for i, d in enumerate(devices):
+                opt.device_ids[i] = int(d)
         c_final = np.zeros(total_c, np.float64)
         status = np.zeros(M, np.int32)
         loss_init = np.zeros(M, np.float64)

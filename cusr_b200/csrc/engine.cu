@@ -28,6 +28,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <thread>
 #include <vector>
 
 #include "../../include/cusr_co.h"
@@ -103,6 +104,8 @@ struct Ctx {
     // sample-sharded mode
     ShardComm shard;
     DBuf red;
+    // multi-device fits (CoOptions.n_devices): the contexts of the other shards, by shard slot
+    Ctx *peers[CO_MAX_DEVICES] = {};
     cudaEvent_t ev_sync = nullptr;
     CoStats stats{};
 };
@@ -1036,6 +1039,9 @@ void co_default_options(CoOptions *opt) {
 
 // Options that every fit entry checks.
 static bool valid_fit_options(const CoOptions &o) {
+    if (o.n_devices < 0 || o.n_devices > CO_MAX_DEVICES) return false;
+    for (int i = 0; i < (o.n_devices > 1 ? o.n_devices : 0); ++i)
+        if (o.device_ids[i] < 0) return false;
     return o.lambda0 > 0.0 && o.xtol >= 0.0 && o.ftol >= 0.0 && o.gtol >= 0.0 &&
            o.agree_tol >= 0.0 && o.n_starts >= 0 && o.n_starts <= CO_MAX_STARTS &&
            o.tr_starts >= 0 && o.wave1 >= 0 &&
@@ -1152,6 +1158,163 @@ static int optimize_common(void *handle, const PopHeader *h, const int32_t *nt, 
     return run_fit<float>(ctx, pr, opt, out);
 }
 
+// One fit spread over several devices (CoOptions.n_devices): the trees are split into
+// cost-balanced shards (longest processing time first on nodes x (1 + K); the samples are
+// common to all trees), each shard is fitted by the context of its device on a host thread of
+// its own (the handle's context for its own device, a child context per other slot, created
+// on first use and kept), and the outputs are written back in the caller's tree order. A
+// target matrix whose rows are all equal is passed to the shards as one shared row.
+static int optimize_multi(Ctx *ctx, const PopHeader *h, const int32_t *nt, const float *nv,
+                          const int32_t *ci, const TreeMeta *metas, const float *c_init,
+                          const float *xs, const float *ym, const CoOptions &opt,
+                          const Outputs &out) {
+    const int nd = opt.n_devices, M = h->M_prob, N = h->N;
+    if (opt.keep_inputs || opt.sample_sharded) return CO_ERR_NULLARG;
+    Problem pr{h, nt, nv, ci, metas, c_init, xs, ym};
+    int rc = check_args(pr);
+    if (rc != CO_OK) return rc;
+    // contexts per shard slot
+    std::vector<Ctx *> cx((size_t)nd, nullptr);
+    bool own_used = false;
+    for (int i = 0; i < nd; ++i) {
+        const int dev = opt.device_ids[i];
+        if (dev == ctx->device && !own_used) {
+            cx[(size_t)i] = ctx;
+            own_used = true;
+            continue;
+        }
+        if (ctx->peers[i] && ctx->peers[i]->device != dev) {
+            co_teardown(ctx->peers[i]);
+            ctx->peers[i] = nullptr;
+        }
+        if (!ctx->peers[i]) {
+            void *hnd = nullptr;
+            rc = co_init(dev, &hnd);
+            if (rc != CO_OK) return rc;
+            ctx->peers[i] = (Ctx *)hnd;
+        }
+        cx[(size_t)i] = ctx->peers[i];
+    }
+    // LPT shards
+    std::vector<int> order((size_t)M), owner((size_t)M);
+    for (int m = 0; m < M; ++m) order[(size_t)m] = m;
+    auto cost = [&](int m) { return (double)metas[m].n_nodes * (1.0 + metas[m].K); };
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost(a) > cost(b); });
+    std::vector<double> load((size_t)nd, 0.0);
+    for (int m : order) {
+        const int sl = (int)(std::min_element(load.begin(), load.end()) - load.begin());
+        owner[(size_t)m] = sl;
+        load[(size_t)sl] += cost(m);
+    }
+    // one shared target row when every row is equal
+    bool shared = opt.y_shared != 0;
+    if (!shared && M > 0 && N > 0) {
+        shared = true;
+        for (int m = 1; m < M && shared; ++m)
+            if (std::memcmp(ym, ym + (size_t)m * N, (size_t)N * sizeof(float)) != 0) shared = false;
+    }
+    struct Shard {
+        std::vector<int32_t> trees, nt, ci, status, iters;
+        std::vector<float> nv, c0, ym;
+        std::vector<TreeMeta> metas;
+        std::vector<double> c, li, lf;
+        PopHeader h{};
+        int rc = CO_OK;
+    };
+    std::vector<Shard> sh((size_t)nd);
+    for (int m = 0; m < M; ++m) sh[(size_t)owner[(size_t)m]].trees.push_back(m);
+    for (Shard &d : sh) {
+        int32_t node = 0, coff = 0;
+        for (int m : d.trees) {
+            const TreeMeta &tm = metas[m];
+            d.metas.push_back(TreeMeta{node, tm.n_nodes, coff, tm.K});
+            d.nt.insert(d.nt.end(), nt + tm.node_offset, nt + tm.node_offset + tm.n_nodes);
+            d.nv.insert(d.nv.end(), nv + tm.node_offset, nv + tm.node_offset + tm.n_nodes);
+            d.ci.insert(d.ci.end(), ci + tm.node_offset, ci + tm.node_offset + tm.n_nodes);
+            d.c0.insert(d.c0.end(), c_init + tm.c_offset, c_init + tm.c_offset + tm.K);
+            if (!shared) d.ym.insert(d.ym.end(), ym + (size_t)m * N, ym + (size_t)(m + 1) * N);
+            node += tm.n_nodes;
+            coff += tm.K;
+        }
+        d.h = *h;
+        d.h.M_prob = (int32_t)d.trees.size();
+        d.h.total_nodes = node;
+        d.h.total_c = coff;
+        d.c.resize((size_t)coff);
+        d.li.resize(d.trees.size());
+        d.lf.resize(d.trees.size());
+        d.status.resize(d.trees.size());
+        d.iters.resize(d.trees.size());
+    }
+    CoOptions o = opt;
+    o.n_devices = 0;
+    o.y_shared = shared ? 1 : 0;
+    std::vector<std::thread> th;
+    for (int i = 0; i < nd; ++i) {
+        th.emplace_back([&, i]() {
+            Shard &d = sh[(size_t)i];
+            Outputs so;
+            so.c_d = d.c.data();
+            so.status = d.status.data();
+            so.li_d = d.li.data();
+            so.lf_d = d.lf.data();
+            so.iters = d.iters.data();
+            d.rc = optimize_common(cx[(size_t)i], &d.h, d.nt.data(), d.nv.data(), d.ci.data(),
+                                   d.metas.data(), d.c0.data(), xs, shared ? ym : d.ym.data(),
+                                   o, so);
+        });
+    }
+    for (std::thread &t : th) t.join();
+    for (const Shard &d : sh)
+        if (d.rc != CO_OK) return d.rc;
+    // outputs in the caller's order; statistics: device time of the slowest shard, work summed
+    CoStats agg{};
+    ctx->h_start.assign((size_t)M, 0);
+    for (int i = 0; i < nd; ++i) {
+        const Shard &d = sh[(size_t)i];
+        const Ctx *c = cx[(size_t)i];
+        for (size_t j = 0; j < d.trees.size(); ++j) {
+            const int m = d.trees[j];
+            const TreeMeta &tm = metas[m];
+            const TreeMeta &sm = d.metas[j];
+            for (int k = 0; k < tm.K; ++k) {
+                const double v = d.c[(size_t)sm.c_offset + k];
+                if (out.c_d) out.c_d[tm.c_offset + k] = v;
+                if (out.c_f) out.c_f[tm.c_offset + k] = (float)v;
+            }
+            out.status[m] = d.status[j];
+            if (out.li_d) out.li_d[m] = d.li[j];
+            if (out.lf_d) out.lf_d[m] = d.lf[j];
+            if (out.li_f) out.li_f[m] = (float)d.li[j];
+            if (out.lf_f) out.lf_f[m] = (float)d.lf[j];
+            if (out.iters) out.iters[m] = d.iters[j];
+            if (j < c->h_start.size()) ctx->h_start[(size_t)m] = c->h_start[j];
+        }
+        const CoStats &s_ = c->stats;
+        agg.setup_ms = std::max(agg.setup_ms, s_.setup_ms);
+        agg.loop_ms = std::max(agg.loop_ms, s_.loop_ms);
+        agg.finish_ms = std::max(agg.finish_ms, s_.finish_ms);
+        agg.eval_ms = std::max(agg.eval_ms, s_.eval_ms);
+        agg.step_ms = std::max(agg.step_ms, s_.step_ms);
+        agg.device_ms = std::max(agg.device_ms, s_.device_ms);
+        agg.flops += s_.flops;
+        agg.node_evals += s_.node_evals;
+        agg.sample_evals += s_.sample_evals;
+        agg.eval_launches += s_.eval_launches;
+        agg.kernel_launches += s_.kernel_launches;
+        agg.iters_run = std::max(agg.iters_run, s_.iters_run);
+        agg.n_bins += s_.n_bins;
+        agg.n_reverted += s_.n_reverted;
+        agg.fits_run += s_.fits_run;
+        agg.trees_retired += s_.trees_retired;
+        agg.n_starts = s_.n_starts;
+        agg.precision = s_.precision;
+        agg.y_shared = s_.y_shared;
+    }
+    ctx->stats = agg;
+    return CO_OK;
+}
+
 int co_optimize(void *handle, const PopHeader *h, const int32_t *nt, const float *nv,
                 const int32_t *ci, const TreeMeta *metas, const float *c_init, const float *xs,
                 const float *ym, int max_iter, float *c_final_out, int32_t *status_out,
@@ -1189,6 +1352,8 @@ int co_optimize_ex(void *handle, const PopHeader *h, const int32_t *nt, const fl
     out.li_d = loss_init_out;
     out.lf_d = loss_final_out;
     out.iters = iters_out;
+    if (opt.n_devices > 1)
+        return optimize_multi((Ctx *)handle, h, nt, nv, ci, metas, c_init, xs, ym, opt, out);
     return optimize_common(handle, h, nt, nv, ci, metas, c_init, xs, ym, opt, out);
 }
 
@@ -1376,6 +1541,10 @@ int co_get_stats(void *handle, CoStats *out) {
 void co_teardown(void *handle) {
     if (!handle) return;
     Ctx *ctx = (Ctx *)handle;
+    for (Ctx *&peer : ctx->peers) {
+        if (peer) co_teardown(peer);
+        peer = nullptr;
+    }
     cudaSetDevice(ctx->device);
     DBuf *bufs[] = {&ctx->code, &ctx->desc, &ctx->bin_trees, &ctx->bin_tree_off,
                     &ctx->bin_item_off, &ctx->items, &ctx->n_items, &ctx->counter,

@@ -81,6 +81,7 @@ typedef struct TreeMeta {
 #define CO_MAX_STACK    64    /* header.max_stack bound, as in the reference          */
 #define CO_MAX_NODES    1023  /* per tree                                              */
 #define CO_MAX_VARS     255
+#define CO_MAX_DEVICES  8     /* devices of one multi-device call (CoOptions.device_ids)     */
 
 /* ---- reference-compatible entry points ------------------------------------------ */
 
@@ -175,7 +176,13 @@ typedef struct CoOptions {
                             /* (co_lib.cu:456-471): a step below xtol is CONVERGED and kept */
                             /* before the improvement test, improvement is strict (<);      */
                             /* 0 (default): the AD variant's (improvement first, <=)        */
-    int32_t reserved[1];
+    int32_t n_devices;      /* co_optimize_ex: 0 / 1 = the handle's device. 2..8: the trees */
+                            /* are split into cost-balanced shards (longest first on        */
+                            /* nodes x (1 + K)) fitted concurrently on device_ids[0..n-1],  */
+                            /* one host thread and context each (the handle's own where a   */
+                            /* listed device is its device), outputs in the caller's order  */
+    int32_t device_ids[CO_MAX_DEVICES];
+    int32_t reserved[2];
 } CoOptions;
 
 #define CO_AD_AUTO    0
