@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include "program.h"
 #include "eval_kernel.cuh"
+#include "warp_linalg.cuh"
 
 namespace cusr {
 
@@ -47,9 +48,31 @@ constexpr uint8_t IM_DAMP_ALWAYS = 2;
 
 constexpr int STEP_THREADS = 256;
 constexpr int STEP_WARPS = STEP_THREADS / 32;
-// per-warp shared memory (doubles): sums [561 T] + A[32*32] + b[32]
+// per-warp shared memory (doubles): sums [561 T] + the damped system (K rows of WL_LD)
 constexpr int STEP_SUMS_D = 576;
-constexpr int STEP_WARP_D = STEP_SUMS_D + CO_MAX_K * CO_MAX_K + CO_MAX_K;
+constexpr int STEP_WARP_D = STEP_SUMS_D + CO_MAX_K * WL_LD;
+
+// Lane i < K of a warp writes row i of the damped system's lower triangle (packed block b):
+// a_il = JtJ_il, the diagonal damped by diag * (1 + lam) (batch_lm_ad.cu:152-159) or, with
+// `floored`, by diag + lam * max(diag, fl) (fl = damping floor * the largest diagonal).
+template <typename T>
+__device__ __forceinline__ void step_build_rows(double *W, const T *b, int K, int lane,
+                                                double lam, double fac, bool floored,
+                                                double floor_frac) {
+    double dg = 0.0;
+    if (lane < K) {
+        const T *row = b + lane * (lane + 1) / 2;
+        for (int l = 0; l <= lane; ++l) W[lane * WL_LD + l] = (double)row[l];
+        dg = W[lane * WL_LD + lane];
+    }
+    if (floored) {
+        const double fl = wl_max(dg) * floor_frac;
+        if (lane < K) W[lane * WL_LD + lane] = dg + lam * (dg > fl ? dg : fl);
+    } else if (lane < K) {
+        W[lane * WL_LD + lane] = dg * fac;
+    }
+    __syncwarp();
+}
 
 // One warp per tree. Mirrors the reference LM iteration (co_lib.cu:343-483 with the AD
 // ordering of :438-455, batch_lm_revad.cu:396-500):
@@ -61,13 +84,15 @@ constexpr int STEP_WARP_D = STEP_SUMS_D + CO_MAX_K * CO_MAX_K + CO_MAX_K;
 //   lambda *= 10, > 1e12 -> FAIL_CHOLESKY; else c_try = c + delta is queued for evaluation.
 // The J/JtJ/Jtr of an accepted trial were built by the same pass that computed its loss, so
 // an accept needs no re-evaluation and a reject re-solves from the stored block.
+// Lane 0 keeps the per-tree bookkeeping; the K-vectors and the factorisation are spread over
+// the lanes (lane i: constant i, row i of the system), so a K = 32 solve takes O(K^2) warp
+// steps (wl_chol_left: the reference's serial operation order per element).
 template <typename T>
 __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<T> p) {
     extern __shared__ double step_sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     T *sums = reinterpret_cast<T *>(step_sm + warp * STEP_WARP_D);
-    double *A = step_sm + warp * STEP_WARP_D + STEP_SUMS_D;
-    double *bv = A + CO_MAX_K * CO_MAX_K;
+    double *W = step_sm + warp * STEP_WARP_D + STEP_SUMS_D;
     for (int m = blockIdx.x * STEP_WARPS + warp; m < p.M; m += gridDim.x * STEP_WARPS) {
         int st = p.status[m];
         if (st != ST_RUNNING) continue;
@@ -91,10 +116,23 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                 }
             }
         }
+        // |delta|^2 and |c_try|^2 of the evaluated trial, lane k holding constant k
+        const bool trial = pend && !initial;
+        T ck = T(0), dn2 = T(0), cn2 = T(0);
+        if (trial) {
+            T dk = T(0);
+            if (lane < K) {
+                dk = p.delta[d.c_off + lane];
+                ck = p.ctry[d.c_off + lane];
+            }
+            dn2 = wl_sum_t(dk * dk);
+            cn2 = wl_sum_t(ck * ck);
+        }
         __syncwarp();
         int accept = 0;
+        T lam = T(0);
         if (lane == 0) {
-            T lam = p.lam[m];
+            lam = p.lam[m];
             if (pend) {
                 p.pending[m] = 0;
                 p.n_eval[m] += 1;
@@ -110,35 +148,16 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                     if (!Mth<T>::finite(ltry)) {
                         st = STATUS_FAIL_NAN;
                     } else {
-                        T dn2 = T(0), cn2 = T(0);
-                        for (int k = 0; k < K; ++k) {
-                            const T dk = p.delta[d.c_off + k], ck = p.ctry[d.c_off + k];
-                            dn2 += dk * dk;
-                            cn2 += ck * ck;
-                        }
                         const T dn = Mth<T>::sqrt(dn2), cn = Mth<T>::sqrt(cn2);
-                        if (p.fd_order) {
-                            // FD variant: a small step converges (and is kept) first, then
-                            // a strict improvement is accepted
-                            if (dn < p.xtol * (cn + p.xtol) || ltry < p.loss[m]) {
-                                accept = 1;
-                                p.loss[m] = ltry;
-                                for (int k = 0; k < K; ++k) p.c[d.c_off + k] = p.ctry[d.c_off + k];
-                                if (dn < p.xtol * (cn + p.xtol)) {
-                                    st = STATUS_CONVERGED;
-                                } else {
-                                    lam *= T(0.1);
-                                    if (lam < T(1e-12)) lam = T(1e-12);
-                                }
-                            } else {
-                                lam *= T(10);
-                                if (lam > T(1e12)) st = STATUS_FAIL_NAN;
-                            }
-                        } else if (ltry <= p.loss[m]) {
+                        const bool small = dn < p.xtol * (cn + p.xtol);
+                        // FD variant: a small step converges (and is kept) first, then a
+                        // strict improvement is accepted; AD: improvement first
+                        const bool better = p.fd_order ? (small || ltry < p.loss[m])
+                                                       : ltry <= p.loss[m];
+                        if (better) {
                             accept = 1;
                             p.loss[m] = ltry;
-                            for (int k = 0; k < K; ++k) p.c[d.c_off + k] = p.ctry[d.c_off + k];
-                            if (dn < p.xtol * (cn + p.xtol)) {
+                            if (small) {
                                 st = STATUS_CONVERGED;
                             } else {
                                 lam *= T(0.1);
@@ -151,92 +170,51 @@ __global__ void __launch_bounds__(STEP_THREADS) lm_step_kernel(const StepParams<
                     }
                 }
             }
-            p.lam[m] = lam;
-        }
-        accept = __shfl_sync(0xffffffffu, accept, 0);
-        st = __shfl_sync(0xffffffffu, st, 0);
-        if (accept)
-            for (int e = lane; e < P; e += 32) p.blk[d.q_off + e] = sums[e];
-        __syncwarp();
-        if (lane == 0) {
             // every running fit takes one LM iteration per pass (an evaluated trial or a
             // factorisation failure); after max_iter of them it stops
             if (st == ST_RUNNING && p.iters[m] >= p.max_iter) st = STATUS_MAXITER;
-            if (st == ST_RUNNING) {
-                T lam = p.lam[m];
-                const T *b = p.blk + d.q_off;
-                const int tri = K * (K + 1) / 2;
-                const double fac = (double)(T(1) + lam);
-                // damped system; `floored`: diag + lam * max(diag, floor * max diag)
-                auto build = [&](bool floored) {
-                    double fl = 0.0;
-                    if (floored) {
-                        for (int i = 0; i < K; ++i) fl = fmax(fl, (double)b[i * (i + 1) / 2 + i]);
-                        fl *= p.damping_floor;
-                    }
-                    for (int i = 0; i < K; ++i) {
-                        bv[i] = -(double)b[tri + i];
-                        for (int l = 0; l <= i; ++l) {
-                            const double v = (double)b[i * (i + 1) / 2 + l];
-                            A[i * K + l] = v;
-                            A[l * K + i] = v;
-                        }
-                        if (floored) {
-                            const double v = A[i * K + i];
-                            A[i * K + i] = v + (double)lam * (v > fl ? v : fl);
-                        } else {
-                            A[i * K + i] *= fac;
-                        }
-                    }
-                };
-                auto cholesky = [&]() -> bool {
-                    for (int j = 0; j < K; ++j) {
-                        double s = A[j * K + j];
-                        for (int k = 0; k < j; ++k) s -= A[j * K + k] * A[j * K + k];
-                        if (s <= 0.0) return false;
-                        A[j * K + j] = sqrt(s);
-                        for (int i = j + 1; i < K; ++i) {
-                            double t = A[i * K + j];
-                            for (int k = 0; k < j; ++k) t -= A[i * K + k] * A[j * K + k];
-                            A[i * K + j] = t / A[j * K + j];
-                        }
-                    }
-                    return true;
-                };
-                const bool always = p.damping_floor > 0.0 &&
-                                    (p.damping_always || (mode & IM_DAMP_ALWAYS));
-                build(always);
-                bool ok = cholesky();
-                // robust mode: a system the reference damping cannot factor (a zero or
-                // negligible Jacobian column) is retried with the damping floor
-                if (!ok && p.damping_floor > 0.0 && !always) {
-                    build(true);
-                    ok = cholesky();
-                }
-                if (!ok) {
+        }
+        accept = __shfl_sync(0xffffffffu, accept, 0);
+        st = __shfl_sync(0xffffffffu, st, 0);
+        lam = __shfl_sync(0xffffffffu, lam, 0);
+        if (accept) {
+            for (int e = lane; e < P; e += 32) p.blk[d.q_off + e] = sums[e];
+            if (trial && lane < K) p.c[d.c_off + lane] = ck;
+        }
+        if (st == ST_RUNNING) {
+            // the accepted point's block: this pass's sums after an accept, else the stored one
+            const T *b = accept ? sums : p.blk + d.q_off;
+            const int tri = K * (K + 1) / 2;
+            const double fac = (double)(T(1) + lam);
+            const bool always = p.damping_floor > 0.0 &&
+                                (p.damping_always || (mode & IM_DAMP_ALWAYS));
+            step_build_rows(W, b, K, lane, (double)lam, fac, always, p.damping_floor);
+            bool ok = wl_chol_left(W, K, lane);
+            // robust mode: a system the reference damping cannot factor (a zero or
+            // negligible Jacobian column) is retried with the damping floor
+            if (!ok && p.damping_floor > 0.0 && !always) {
+                step_build_rows(W, b, K, lane, (double)lam, fac, true, p.damping_floor);
+                ok = wl_chol_left(W, K, lane);
+            }
+            if (!ok) {
+                if (lane == 0) {
                     p.iters[m] += 1;
                     lam *= T(10);
                     if (lam > T(1e12)) st = STATUS_FAIL_CHOLESKY;
-                    p.lam[m] = lam;
-                } else {
-                    for (int i = 0; i < K; ++i) {
-                        double s = bv[i];
-                        for (int k = 0; k < i; ++k) s -= A[i * K + k] * bv[k];
-                        bv[i] = s / A[i * K + i];
-                    }
-                    for (int i = K - 1; i >= 0; --i) {
-                        double s = bv[i];
-                        for (int k = i + 1; k < K; ++k) s -= A[k * K + i] * bv[k];
-                        bv[i] = s / A[i * K + i];
-                    }
-                    for (int k = 0; k < K; ++k) {
-                        const T dk = (T)bv[k];
-                        p.delta[d.c_off + k] = dk;
-                        p.ctry[d.c_off + k] = p.c[d.c_off + k] + dk;
-                    }
-                    p.pending[m] = 1;
                 }
+            } else {
+                const double y = wl_fsub(W, K, lane, lane < K ? -(double)b[tri + lane] : 0.0);
+                const double x = wl_bsub(W, K, lane, y);
+                if (lane < K) {
+                    const T dk = (T)x;
+                    p.delta[d.c_off + lane] = dk;
+                    p.ctry[d.c_off + lane] = p.c[d.c_off + lane] + dk;
+                }
+                if (lane == 0) p.pending[m] = 1;
             }
+        }
+        if (lane == 0) {
+            p.lam[m] = lam;
             p.status[m] = st;
             if (st == ST_RUNNING) atomicAdd(p.n_running, 1);
         }

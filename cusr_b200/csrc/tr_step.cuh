@@ -27,6 +27,7 @@
 #include <float.h>
 #include <stdint.h>
 #include "lm_kernels.cuh"
+#include "warp_linalg.cuh"
 
 namespace cusr {
 
@@ -51,68 +52,8 @@ struct TrParams {
 
 constexpr int TR_THREADS = 128;
 constexpr int TR_WARPS = TR_THREADS / 32;
-constexpr int TR_LD = CO_MAX_K + 1;                     // padded row stride (doubles)
 // per warp: A, W (K x K, full symmetric), the summed block (561 values, as doubles)
-constexpr int TR_WARP_D = 2 * CO_MAX_K * TR_LD + 576;
-
-__device__ __forceinline__ double tr_wsum(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-__device__ __forceinline__ double tr_wmax(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-// Euclidean norm of a lane-distributed vector (the lanes >= K hold 0)
-__device__ __forceinline__ double tr_norm(double v) { return sqrt(tr_wsum(v * v)); }
-
-// W (rows 0..K-1 owned by lanes) = L L^T in place (lower triangle), unpivoted. false if a
-// pivot is not positive (the test reads shared memory every lane sees: warp-uniform).
-__device__ bool tr_chol(double *W, int K, int lane) {
-    for (int j = 0; j < K; ++j) {
-        __syncwarp();
-        const double djj = W[j * TR_LD + j];
-        if (!(djj > 0.0)) return false;
-        const double ljj = sqrt(djj);
-        __syncwarp();
-        if (lane > j && lane < K) W[lane * TR_LD + j] /= ljj;
-        if (lane == j) W[j * TR_LD + j] = ljj;
-        __syncwarp();
-        if (lane > j && lane < K) {
-            const double lij = W[lane * TR_LD + j];
-            for (int k = j + 1; k <= lane; ++k) W[lane * TR_LD + k] -= lij * W[k * TR_LD + j];
-        }
-    }
-    __syncwarp();
-    return true;
-}
-
-// solve L y = b (lane i holds b_i, returns y_i), L lower in W
-__device__ double tr_fsub(const double *W, int K, int lane, double b) {
-    double y = 0.0;
-    for (int k = 0; k < K; ++k) {
-        double yk = 0.0;
-        if (lane == k) yk = b / W[k * TR_LD + k];
-        yk = __shfl_sync(0xffffffffu, yk, k);
-        if (lane == k) y = yk;
-        if (lane > k && lane < K) b -= W[lane * TR_LD + k] * yk;
-    }
-    return y;
-}
-// solve L^T x = y (lane i holds y_i, returns x_i)
-__device__ double tr_bsub(const double *W, int K, int lane, double y) {
-    double x = 0.0;
-    for (int k = K - 1; k >= 0; --k) {
-        double xk = 0.0;
-        if (lane == k) xk = y / W[k * TR_LD + k];
-        xk = __shfl_sync(0xffffffffu, xk, k);
-        if (lane == k) x = xk;
-        if (lane < k) y -= W[k * TR_LD + lane] * xk;
-    }
-    return x;
-}
+constexpr int TR_WARP_D = 2 * CO_MAX_K * WL_LD + 576;
 
 // Symmetrically pivoted Cholesky of W = A (full, lanes own rows): at step b the largest
 // remaining diagonal is the pivot perm[b]; the column values l_i are kept in W[i][perm[b]].
@@ -122,7 +63,7 @@ __device__ int tr_pchol(double *W, int K, int lane, int *perm) {
     int r = 0;
     for (int b = 0; b < K; ++b) {
         __syncwarp();
-        double v = done ? -1.0 : W[lane * TR_LD + lane];
+        double v = done ? -1.0 : W[lane * WL_LD + lane];
         int p = lane;
         // argmax with ties to the lower index: every lane ends with the same (v, p)
 #pragma unroll
@@ -134,17 +75,17 @@ __device__ int tr_pchol(double *W, int K, int lane, int *perm) {
         if (!(v > 0.0)) break;
         const double lpp = sqrt(v);
         double li = 0.0;
-        if (!done && lane != p) li = W[lane * TR_LD + p] / lpp;
+        if (!done && lane != p) li = W[lane * WL_LD + p] / lpp;
         __syncwarp();
-        if (!done && lane != p) W[lane * TR_LD + p] = li;
-        if (lane == p) { W[p * TR_LD + p] = lpp; done = true; }
+        if (!done && lane != p) W[lane * WL_LD + p] = li;
+        if (lane == p) { W[p * WL_LD + p] = lpp; done = true; }
         if (lane == 0) perm[b] = p;
         // trailing update of the rows and columns still remaining
         const bool act = !done;
         for (int k = 0; k < K; ++k) {
             const double lk = __shfl_sync(0xffffffffu, li, k);
             const int dk = __shfl_sync(0xffffffffu, (int)done, k);
-            if (act && !dk) W[lane * TR_LD + k] -= li * lk;
+            if (act && !dk) W[lane * WL_LD + k] -= li * lk;
         }
         ++r;
     }
@@ -163,19 +104,19 @@ __device__ double tr_gn_step(const double *W, int r, int lane, const int *perm, 
     for (int k = 0; k < r; ++k) {          // forward: L y = b
         const int pk = perm[k];
         double yk = 0.0;
-        if (lane == k) yk = b / W[pk * TR_LD + pk];
+        if (lane == k) yk = b / W[pk * WL_LD + pk];
         yk = __shfl_sync(0xffffffffu, yk, k);
         if (lane == k) y = yk;
-        if (lane > k && lane < r) b -= W[pa * TR_LD + pk] * yk;
+        if (lane > k && lane < r) b -= W[pa * WL_LD + pk] * yk;
     }
     double z = 0.0;
     for (int k = r - 1; k >= 0; --k) {     // back: L^T z = y
         const int pk = perm[k];
         double zk = 0.0;
-        if (lane == k) zk = y / W[pk * TR_LD + pk];
+        if (lane == k) zk = y / W[pk * WL_LD + pk];
         zk = __shfl_sync(0xffffffffu, zk, k);
         if (lane == k) z = zk;
-        if (lane < k) y -= W[pk * TR_LD + pa] * zk;
+        if (lane < k) y -= W[pk * WL_LD + pa] * zk;
     }
     // back to the original order: lane i takes z of the pivot position holding i
     double x = 0.0;
@@ -195,20 +136,20 @@ __device__ double tr_pfsub_norm(const double *W, int K, int lane, const int *per
     for (int k = 0; k < K; ++k) {
         const int pk = perm[k];
         double wk = 0.0;
-        if (lane == k) wk = b / W[pk * TR_LD + pk];
+        if (lane == k) wk = b / W[pk * WL_LD + pk];
         wk = __shfl_sync(0xffffffffu, wk, k);
         if (lane == k) w = wk;
-        if (lane > k && lane < K) b -= W[pa * TR_LD + pk] * wk;
+        if (lane > k && lane < K) b -= W[pa * WL_LD + pk] * wk;
     }
-    return tr_norm(w);
+    return wl_norm(w);
 }
 
 // W = A + par diag(d^2), rows owned by lanes
 __device__ __forceinline__ void tr_load(double *W, const double *A, int K, int lane, double par,
                                         double d) {
     if (lane < K) {
-        for (int k = 0; k < K; ++k) W[lane * TR_LD + k] = A[lane * TR_LD + k];
-        W[lane * TR_LD + lane] += par * d * d;
+        for (int k = 0; k < K; ++k) W[lane * WL_LD + k] = A[lane * WL_LD + k];
+        W[lane * WL_LD + lane] += par * d * d;
     }
     __syncwarp();
 }
@@ -223,7 +164,7 @@ __device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lan
     const int r = tr_pchol(W, K, lane, perm);
     double x = r > 0 ? tr_gn_step(W, r, lane, perm, g) : 0.0;
     if (lane >= K) x = 0.0;
-    double dxnorm = tr_norm(d * x);
+    double dxnorm = wl_norm(d * x);
     double fp = dxnorm - delta;
     if (fp <= 0.1 * delta) {
         par = 0.0;
@@ -237,7 +178,7 @@ __device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lan
         parl = ((fp / delta) / t) / t;
     }
     // upper bound
-    const double gnorm = tr_norm(lane < K ? g / d : 0.0);
+    const double gnorm = wl_norm(lane < K ? g / d : 0.0);
     double paru = gnorm / delta;
     if (paru == 0.0) paru = dwarf / fmin(delta, 0.1);
     par = fmax(par, parl);
@@ -249,23 +190,23 @@ __device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lan
         // a system that rounding left indefinite (dependent columns, par tiny against the
         // scale of J^T J) is factored with par raised until it is positive definite
         int guard = 0;
-        while (!tr_chol(W, K, lane) && guard < 64) {
-            const double amax = tr_wmax(lane < K ? fabs(A[lane * TR_LD + lane]) : 0.0);
-            const double dmin = -tr_wmax(lane < K ? -(d * d) : -DBL_MAX);
+        while (!wl_chol(W, K, lane) && guard < 64) {
+            const double amax = wl_max(lane < K ? fabs(A[lane * WL_LD + lane]) : 0.0);
+            const double dmin = -wl_max(lane < K ? -(d * d) : -DBL_MAX);
             par = fmax(fmax(2.0 * par, 1e-15 * amax / dmin), dwarf);
             tr_load(W, A, K, lane, par, d);
             ++guard;
         }
-        const double y = tr_fsub(W, K, lane, lane < K ? -g : 0.0);
-        x = tr_bsub(W, K, lane, y);
+        const double y = wl_fsub(W, K, lane, lane < K ? -g : 0.0);
+        x = wl_bsub(W, K, lane, y);
         if (lane >= K) x = 0.0;
-        dxnorm = tr_norm(d * x);
+        dxnorm = wl_norm(d * x);
         const double temp = fp;
         fp = dxnorm - delta;
         if (fabs(fp) <= 0.1 * delta || (parl == 0.0 && fp <= temp && temp < 0.0) || iter == 10)
             return x;
         const double v = lane < K ? d * (d * x) / dxnorm : 0.0;
-        const double t = tr_norm(tr_fsub(W, K, lane, v));
+        const double t = wl_norm(wl_fsub(W, K, lane, v));
         const double parc = ((fp / delta) / t) / t;
         if (fp > 0.0) parl = fmax(parl, par);
         if (fp < 0.0) paru = fmin(paru, par);
@@ -280,8 +221,8 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
     __shared__ int s_perm[TR_WARPS][CO_MAX_K];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     double *A = tr_sm + warp * TR_WARP_D;
-    double *W = A + CO_MAX_K * TR_LD;
-    double *sums = W + CO_MAX_K * TR_LD;
+    double *W = A + CO_MAX_K * WL_LD;
+    double *sums = W + CO_MAX_K * WL_LD;
     int *perm = s_perm[warp];
     const double eps = sizeof(T) == 8 ? DBL_EPSILON : (double)FLT_EPSILON;
     for (int m = blockIdx.x * TR_WARPS + warp; m < p.M; m += gridDim.x * TR_WARPS) {
@@ -331,7 +272,7 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
                     ap += (double)bq[hi * (hi + 1) / 2 + lo] * pl;
                 }
             }
-            const double jp2 = fmax(tr_wsum(pk * ap), 0.0);
+            const double jp2 = fmax(wl_sum(pk * ap), 0.0);
             const double actred = (0.1 * fnorm1 < fnorm) ? 1.0 - (fnorm1 / fnorm) * (fnorm1 / fnorm) : -1.0;
             const double t1 = sqrt(jp2) / fnorm, t2 = sqrt(par) * pnorm / fnorm;
             const double prered = t1 * t1 + t2 * t2 / 0.5;
@@ -351,7 +292,7 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
                 fnorm = fnorm1;
                 outer += 1;
                 const double cn = lane < K ? d * (double)p.ctry[dsc.c_off + lane] : 0.0;
-                xnorm = tr_norm(cn);
+                xnorm = wl_norm(cn);
                 if (lane < K) p.c[dsc.c_off + lane] = p.ctry[dsc.c_off + lane];
                 if (lane == 0) p.loss[m] = ltry;
             }
@@ -384,22 +325,22 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
             if (lane < K)
                 for (int l = 0; l < K; ++l) {
                     const int hi = lane > l ? lane : l, lo = lane > l ? l : lane;
-                    A[lane * TR_LD + l] = (double)bq[hi * (hi + 1) / 2 + lo];
+                    A[lane * WL_LD + l] = (double)bq[hi * (hi + 1) / 2 + lo];
                 }
             __syncwarp();
             const double g = lane < K ? (double)bq[tri + lane] : 0.0;
             if (accept) {
                 // outer iteration: column norms, the scaling, the gradient test
-                const double acn = lane < K ? sqrt(fmax(A[lane * TR_LD + lane], 0.0)) : 0.0;
+                const double acn = lane < K ? sqrt(fmax(A[lane * WL_LD + lane], 0.0)) : 0.0;
                 if (outer == 1) {
                     d = (lane < K && acn != 0.0) ? acn : 1.0;
                     const double cn = lane < K ? d * (double)p.c[dsc.c_off + lane] : 0.0;
-                    xnorm = tr_norm(cn);
+                    xnorm = wl_norm(cn);
                     delta = xnorm != 0.0 ? p.factor * xnorm : p.factor;
                 }
                 double gl = 0.0;
                 if (fnorm != 0.0 && lane < K && acn != 0.0) gl = fabs(g / fnorm) / acn;
-                gnorm = tr_wmax(gl);
+                gnorm = wl_max(gl);
                 if (gnorm <= p.gtol || gnorm <= eps) {
                     st = STATUS_CONVERGED;
                     done = true;
@@ -408,7 +349,7 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
             }
             if (!done) {
                 const double x = tr_lmpar(A, W, perm, K, lane, g, d, delta, par);
-                pnorm = tr_norm(lane < K ? d * x : 0.0);
+                pnorm = wl_norm(lane < K ? d * x : 0.0);
                 if (outer == 1) delta = fmin(delta, pnorm);
                 if (lane < K) {
                     const T xk = (T)x;
