@@ -19,7 +19,8 @@ the public extended entry point (co_optimize_ex) from pinned host buffers, H2D a
 scipy least_squares LM per tree, one process per host core) on a bounded sample of trees; its
 line also carries `reference_gpu`, the reference's own CUDA LM path (batch_lm_revad built from
 its sources for sm_100a by oracle/Makefile) timed on the same 16,384-tree population, when that
-binary is present. `--impl reference_gpu` prints that measurement as its own line.
+binary is present. `--impl reference_gpu` prints that measurement as its own line, and the
+default arm (one GPU) carries it as `vs_reference_gpu` {ours, ref, ratio}.
 
 Reports that are files (the nvidia-smi clock samples) go to --out-dir, default
 $CUSR_REPORT_DIR, else a temporary directory.
@@ -450,6 +451,14 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
     }
     if world == 1 and not args.no_parity_mode:
         line["parity_mode"] = parity_mode(co, pop)
+    if world == 1 and not args.no_reference_gpu:
+        # the reference's own CUDA path on the same population and box (a subprocess of its
+        # binary); its convention counts the LM loop only, as `value` does
+        rg = reference_gpu(pop, runs=2, warmup=1)
+        line["vs_reference_gpu"] = {
+            "ours": line["value"], "ref": rg.get("value"),
+            "ratio": (line["value"] / rg["value"]) if rg.get("value") else None,
+            "same_population": True, "reference_gpu": rg}
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(pop)
     print(json.dumps(line), flush=True)
@@ -582,7 +591,7 @@ def main() -> None:
     ap.add_argument("--no-parity-mode", action="store_true",
                     help="skip the parity-grade mode's measurement")
     ap.add_argument("--no-reference-gpu", action="store_true",
-                    help="--impl reference: skip timing the reference's CUDA path")
+                    help="skip timing the reference's CUDA path (--impl reference and the default arm)")
     ap.add_argument("--out-dir", default=None,
                     help="directory for report files (default $CUSR_REPORT_DIR, else a temp dir)")
     ap.add_argument("--profile-case", action="store_true",

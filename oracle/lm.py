@@ -41,8 +41,21 @@ def _cholesky_solve(A: np.ndarray, b: np.ndarray):
     return x
 
 
-def fit_tree(nt, nv, ci, xs, y, c0, max_iter=50, dtype=np.float64, lambda0=1e-3, xtol=1e-6):
-    """LM fit of one tree. Returns (c_final, status, loss_init, loss_final, iters)."""
+def _chunked(fn, n, chunk):
+    """fn(lo, hi) summed over sample ranges of `chunk` in sequence (chunk None: one range)."""
+    if not chunk:
+        return fn(0, n)
+    acc = fn(0, min(chunk, n))
+    for lo in range(chunk, n, chunk):
+        acc = acc + fn(lo, min(lo + chunk, n))
+    return acc
+
+
+def fit_tree(nt, nv, ci, xs, y, c0, max_iter=50, dtype=np.float64, lambda0=1e-3, xtol=1e-6,
+             sum_chunk=None):
+    """LM fit of one tree. Returns (c_final, status, loss_init, loss_final, iters).
+    sum_chunk: sums over samples (loss, JtJ, Jtr) taken as a sequence of per-chunk sums, the
+    way a chunked device reduction orders them (None: numpy's order over all samples)."""
     T = np.dtype(dtype).type
     c = np.asarray(c0, dtype).copy()
     K = c.size
@@ -50,7 +63,8 @@ def fit_tree(nt, nv, ci, xs, y, c0, max_iter=50, dtype=np.float64, lambda0=1e-3,
     with np.errstate(all="ignore"):
         f, J = interp.value_and_jacobian(nt, nv, ci, xs, c, dtype=dtype, jacobian=K > 0)
         r = f - y
-        loss = T(0.5) * T(np.sum(r * r, dtype=dtype))
+        n = r.shape[0]
+        loss = T(0.5) * T(_chunked(lambda a, b: np.sum(r[a:b] * r[a:b], dtype=dtype), n, sum_chunk))
     loss_init = loss
     if K == 0:
         return c, K0_SKIP, loss_init, loss, 0
@@ -63,8 +77,8 @@ def fit_tree(nt, nv, ci, xs, y, c0, max_iter=50, dtype=np.float64, lambda0=1e-3,
     for _ in range(max_iter):
         iters += 1
         with np.errstate(all="ignore"):
-            JtJ = (J.T @ J).astype(np.float64)
-            Jtr = (J.T @ r).astype(np.float64)
+            JtJ = _chunked(lambda a, b: J[a:b].T @ J[a:b], n, sum_chunk).astype(np.float64)
+            Jtr = _chunked(lambda a, b: J[a:b].T @ r[a:b], n, sum_chunk).astype(np.float64)
         A = JtJ.copy()
         A[np.diag_indices(K)] *= float(T(1) + lam)
         sol = _cholesky_solve(A, -Jtr) if np.all(np.isfinite(A)) else None
@@ -81,7 +95,8 @@ def fit_tree(nt, nv, ci, xs, y, c0, max_iter=50, dtype=np.float64, lambda0=1e-3,
         with np.errstate(all="ignore"):
             f_t, J_t = interp.value_and_jacobian(nt, nv, ci, xs, c_try, dtype=dtype)
             r_t = f_t - y
-            loss_try = T(0.5) * T(np.sum(r_t * r_t, dtype=dtype))
+            loss_try = T(0.5) * T(_chunked(lambda a, b: np.sum(r_t[a:b] * r_t[a:b], dtype=dtype),
+                                           n, sum_chunk))
         if not np.isfinite(loss_try):
             status = FAIL_NAN
             break
@@ -111,7 +126,7 @@ def loss64(nt, nv, ci, xs, y, c) -> float:
 
 
 def fit_pop(pop: dict, max_iter=50, dtype=np.float64, lambda0=1e-3, xtol=1e-6, audit=None,
-            trees=None) -> dict:
+            trees=None, sum_chunk=None) -> dict:
     """Fit every tree (or the subset `trees`) of a pop dict. fp32 fits get the fp64 audit
     unless audit=False. Returns arrays over the selected trees."""
     idx = np.arange(int(pop["M"])) if trees is None else np.asarray(trees)
@@ -122,7 +137,8 @@ def fit_pop(pop: dict, max_iter=50, dtype=np.float64, lambda0=1e-3, xtol=1e-6, a
         nt, nv, ci, y, K = interp.tree_view(pop, int(m))
         c_off = int(pop["metas"][m][2])
         c0 = np.asarray(pop["c_init"][c_off:c_off + K])
-        c, s, l0, l1, it = fit_tree(nt, nv, ci, pop["xs"], y, c0, max_iter, dtype, lambda0, xtol)
+        c, s, l0, l1, it = fit_tree(nt, nv, ci, pop["xs"], y, c0, max_iter, dtype, lambda0, xtol,
+                                    sum_chunk)
         if audit and K > 0:
             lf64 = loss64(nt, nv, ci, pop["xs"], y, c)
             li64 = loss64(nt, nv, ci, pop["xs"], y, c0)
