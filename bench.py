@@ -525,15 +525,22 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
         co.fit_loaded(max_iter=max_iter, sample_sharded=sharded)
     barrier(world)
     dev, launches, nodes = [], 0, 0
+    split = {"eval_ms": 0.0, "comm_ms": 0.0, "step_ms": 0.0}
     for _ in range(args.steps):
         co.fit_loaded(max_iter=max_iter, sample_sharded=sharded)
         st = co.stats()
         dev.append(st["device_ms"])
         launches += st["kernel_launches"]
         nodes += st["node_evals"]
+        for k in split:
+            split[k] += st[k] / args.steps
+        passes = int(st["iters_run"]) + 1
     barrier(world)
     total_ms = max_over_ranks(float(sum(dev)), world)
     nodes_all = sum_over_ranks(float(nodes), world)
+    # per-fit device time split of the slowest rank's figures (comm: chunk sum + all-reduce,
+    # waiting for the other ranks included)
+    split = {k: max_over_ranks(v, world) for k, v in split.items()}
     if rank != 0:
         return
     M = int(pop["M"])
@@ -547,7 +554,8 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
         "config": {"workload": "sharded", "trees": M, "N": int(pop["N"]),
                    "max_iter": max_iter, "parallelism": f"sample-sharded x{world} "
                    "(NCCL all-reduce of JtJ/Jtr/loss per iteration)"},
-        "node_evals_per_s": nodes_all / (total_ms / 1e3), "gpu_launches": launches}),
+        "node_evals_per_s": nodes_all / (total_ms / 1e3), "gpu_launches": launches,
+        "per_fit_ms": {**split, "passes": passes}}),
         flush=True)
 
 

@@ -120,7 +120,7 @@ class CoStats(ctypes.Structure):
         ("y_shared", ctypes.c_int32), ("precision", ctypes.c_int32),
         ("n_reverted", ctypes.c_int32), ("n_starts", ctypes.c_int32),
         ("fits_run", ctypes.c_int64), ("trees_retired", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 3),
+        ("reserved", ctypes.c_int32), ("comm_ms", ctypes.c_double),
     ]
 
 

@@ -673,7 +673,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         if (e) cudaEventRecord(e, s);
         return e;
     };
-    std::vector<std::pair<size_t, size_t>> eval_spans, step_spans;
+    std::vector<std::pair<size_t, size_t>> eval_spans, step_spans, comm_spans;
     // the step kernels of one pass (and the wave update), counting running fits into n_running
     auto steps = [&](int *n_running) -> int {
         CK(cudaMemsetAsync(n_running, 0, sizeof(int), s));
@@ -704,16 +704,19 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     size_t e0 = ev_i; rec();
     rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true);
     if (rc) return rc;
+    size_t e1 = ev_i; rec();
+    eval_spans.push_back({e0, e1});
     if (sharded) {
         rc = shard_reduce_blocks<T>(ctx, M_fit, sc.block_elems);
         if (rc) return rc;
         sp.reduced = P<T>(ctx->red);
+        size_t ec = ev_i; rec();
+        comm_spans.push_back({e1, ec});
+        e1 = ec;
     }
-    size_t e1 = ev_i; rec();
     rc = steps(P<int>(ctx->n_run));
     if (rc) return rc;
     size_t e2 = ev_i; rec();
-    eval_spans.push_back({e0, e1});
     step_spans.push_back({e1, e2});
     rc = sync_stream(ctx, sharded);
     if (rc) return rc;
@@ -739,15 +742,18 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         size_t a = ev_i; rec();
         rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true);
         if (rc) return rc;
+        size_t b = ev_i; rec();
+        eval_spans.push_back({a, b});
         if (sharded) {
             rc = shard_reduce_blocks<T>(ctx, M_fit, sc.block_elems);
             if (rc) return rc;
+            size_t bc = ev_i; rec();
+            comm_spans.push_back({b, bc});
+            b = bc;
         }
-        size_t b = ev_i; rec();
         rc = steps(P<int>(ctx->n_run) + slot);
         if (rc) return rc;
         size_t c = ev_i; rec();
-        eval_spans.push_back({a, b});
         step_spans.push_back({b, c});
         if (opt.early_exit) {
             CK(cudaMemcpyAsync(ctx->h_nrun + slot, P<int>(ctx->n_run) + slot, sizeof(int),
@@ -868,19 +874,19 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     st.fits_run = fits_run;
 
     // device-time split from the recorded events
-    double eval_ms = 0.0, step_ms = 0.0;
-    for (auto &sp_ : eval_spans) {
-        float x = 0.f;
-        if (cudaEventElapsedTime(&x, ctx->events[sp_.first], ctx->events[sp_.second]) == cudaSuccess)
-            eval_ms += x;
-    }
-    for (auto &sp_ : step_spans) {
-        float x = 0.f;
-        if (cudaEventElapsedTime(&x, ctx->events[sp_.first], ctx->events[sp_.second]) == cudaSuccess)
-            step_ms += x;
-    }
-    st.eval_ms = eval_ms;
-    st.step_ms = step_ms;
+    auto span_ms = [&](const std::vector<std::pair<size_t, size_t>> &spans) {
+        double t = 0.0;
+        for (auto &sp_ : spans) {
+            float x = 0.f;
+            if (cudaEventElapsedTime(&x, ctx->events[sp_.first], ctx->events[sp_.second]) ==
+                cudaSuccess)
+                t += x;
+        }
+        return t;
+    };
+    st.eval_ms = span_ms(eval_spans);
+    st.step_ms = span_ms(step_spans);
+    st.comm_ms = span_ms(comm_spans);
     st.finish_ms = ms_since(t_fin);
     g_last_setup_ms = st.setup_ms;
     g_last_loop_ms = st.loop_ms;
@@ -1296,6 +1302,7 @@ static int optimize_multi(Ctx *ctx, const PopHeader *h, const int32_t *nt, const
         agg.finish_ms = std::max(agg.finish_ms, s_.finish_ms);
         agg.eval_ms = std::max(agg.eval_ms, s_.eval_ms);
         agg.step_ms = std::max(agg.step_ms, s_.step_ms);
+        agg.comm_ms = std::max(agg.comm_ms, s_.comm_ms);
         agg.device_ms = std::max(agg.device_ms, s_.device_ms);
         agg.flops += s_.flops;
         agg.node_evals += s_.node_evals;

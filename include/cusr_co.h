@@ -232,7 +232,10 @@ typedef struct CoStats {
     int32_t n_starts;       /* fits per tree of the call                                */
     int64_t fits_run;       /* fits (tree x start) evaluated at least once              */
     int32_t trees_retired;  /* trees whose later starts were retired unrun (wave1)      */
-    int32_t reserved[3];
+    int32_t reserved0;
+    double  comm_ms;        /* sample-sharded mode: device time of the per-pass chunk sum
+                               and NCCL all-reduce (events; waiting for the slowest rank
+                               included); 0 otherwise. eval_ms excludes it               */
 } CoStats;
 
 /* Resident problem: co_load compiles, schedules and uploads a population (programs,
