@@ -574,7 +574,7 @@ def run_profile_case(args) -> None:
         bins[str(kc)] = {"trees": int(sel.sum()), "nodes": int(metas[sel, 1].sum()),
                          "tree_samples": int(sel.sum()) * int(pop["N"])}
     print(json.dumps({"profile_bins": bins}), flush=True)
-    co = InProcessCO(device_id=0)
+    co = InProcessCO(device_id=0, lib_path=args.profile_lib)
     precision = args.profile_precision or pop["precision"]
     co.load(pop, precision=precision)
     kw = {}
@@ -582,10 +582,11 @@ def run_profile_case(args) -> None:
         kw = dict(algorithm="trust_region", xtol=1e-10)
     res = co.fit_loaded(max_iter=args.profile_iters, **kw)
     st = co.stats()
-    print(json.dumps({"profile_case": True, "trees": int(pop["M"]), "N": int(pop["N"]),
+    print(json.dumps({"profile_case": True, "lib": args.profile_lib or "in-tree",
+                      "trees": int(pop["M"]), "N": int(pop["N"]),
                       "iters": args.profile_iters, "device_ms": st["device_ms"],
                       "eval_launches": st["eval_launches"], "flops": st["flops"],
-                      "eval_ms": st["eval_ms"],
+                      "eval_ms": st["eval_ms"], "node_evals": st["node_evals"],
                       "statuses": np.bincount(res["status"], minlength=5).tolist()}), flush=True)
 
 
@@ -608,6 +609,9 @@ def main() -> None:
     ap.add_argument("--profile-trees", type=int, default=8192)
     ap.add_argument("--profile-alg", choices=["reference", "trust_region"], default="reference",
                     help="--profile-case: the LM algorithm of the fit")
+    ap.add_argument("--profile-lib", default=None,
+                    help="--profile-case: a variant build of the library (python -m "
+                         "cusr_b200.build --define ... --lib PATH)")
     ap.add_argument("--profile-precision", default=None,
                     help="--profile-case: fp32 | fp64 | fp32_fast (default: the config's)")
     ap.add_argument("--config", default=None,

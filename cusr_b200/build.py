@@ -116,8 +116,19 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--define", action="append", default=[],
+                    help="extra preprocessor define of a variant build (e.g. CUSR_IEEE_F32: the "
+                         "fp32 interpreter with the accurate library transcendentals instead "
+                         "of the SFU arithmetic); needs --lib")
+    ap.add_argument("--lib", default=None,
+                    help="output path of a variant library (objects beside it in _build/); "
+                         "the in-tree library and its aliases are left as they are")
     a = ap.parse_args()
-    print(build(force=a.force, verbose=a.verbose))
+    if a.define and not a.lib:
+        ap.error("--define builds a variant: give --lib")
+    lib = Path(a.lib).resolve() if a.lib else None
+    print(build(force=a.force, verbose=a.verbose, defines=tuple(a.define),
+                obj_dir=lib.parent / "_build" if lib else None, lib=lib))
 
 
 if __name__ == "__main__":
