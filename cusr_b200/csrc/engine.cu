@@ -202,7 +202,7 @@ int check_args(const Problem &pr) {
 template <typename T>
 int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cdev, T *partials,
                 const PopHeader &hd, int64_t ldx, bool grad, T *vals = nullptr, T *jac = nullptr,
-                int jac_kmax = 0) {
+                int jac_kmax = 0, const uint8_t *imode = nullptr) {
     const int n_bins = (int)sc.bins.size();
     {
         ItemsParams ip;
@@ -244,6 +244,7 @@ int launch_pass(Ctx *ctx, const Schedule &sc, const PackResult &pk, const T *cde
         p.vals = vals;
         p.jac = jac;
         p.jac_kmax = jac_kmax;
+        p.imode = imode;
         const int kc = grad ? bin.kc : 4;
         // Block width: the narrow (EVAL_NT) or the wide (EVAL_NT_WIDE) instantiation, whichever
         // keeps more warps resident (registers and shared memory both counted); a bin whose
@@ -702,7 +703,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
 
     // ---- initial pass at the start points + solve of iteration 0 ----
     size_t e0 = ev_i; rec();
-    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true);
+    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true, nullptr,
+                        nullptr, 0, P<uint8_t>(ctx->imode));
     if (rc) return rc;
     size_t e1 = ev_i; rec();
     eval_spans.push_back({e0, e1});
@@ -740,7 +742,8 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         }
         iters_run++;
         size_t a = ev_i; rec();
-        rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true);
+        rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true,
+                            nullptr, nullptr, 0, P<uint8_t>(ctx->imode));
         if (rc) return rc;
         size_t b = ev_i; rec();
         eval_spans.push_back({a, b});

@@ -62,7 +62,17 @@ struct EvalParams {
     T *vals;                 // optional: per-sample values, [tree][N]
     T *jac;                  // optional: per-sample gradients, [tree][jac_kmax][N]
     int jac_kmax;
+    // optional per-fit mode bits (indexed like desc); IM_SENTINEL fits take the residual
+    // convention of the reference's scipy backend
+    const uint8_t *imode = nullptr;
 };
+
+// Per-fit mode bit: a non-finite residual counts as the sentinel 1e6 with a zero gradient
+// row, the objective the reference's scipy backend hands to MINPACK
+// (cusr/benchmark/backends.py:105-110: np.where(np.isfinite(r), r, 1e6); a forward
+// difference across two sentinel values is 0). Set for the trust-region fits.
+constexpr uint8_t IM_SENTINEL = 4;
+constexpr double RESIDUAL_SENTINEL = 1e6;
 
 __host__ __device__ constexpr inline size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
 
@@ -546,7 +556,7 @@ lm_eval_kernel(const EvalParams<T> p) {
     constexpr int NTRI = KC * (KC + 1) / 2;
 
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int s_item;
+    __shared__ int s_item, s_sent;
     const L lay(p.code_cap, p.n_vars, p.spill_cap, p.tape_cap, !TG);
     uint32_t *code_s = reinterpret_cast<uint32_t *>(smem + lay.code);
     T *c_s = reinterpret_cast<T *>(smem + lay.cval);
@@ -580,6 +590,9 @@ lm_eval_kernel(const EvalParams<T> p) {
         const TreeDesc d = p.desc[wi.x];
         const int K = d.K;
         const bool grad = GRAD && K > 0;
+        // the fit's sentinel bit, read back from shared memory where needed (no register is
+        // held across the sweeps for it)
+        if (tid == 0) s_sent = p.imode ? (p.imode[wi.x] & IM_SENTINEL) : 0;
         // forward program; for reverse mode the reverse program and its row table follow
         const int n_code = REV ? d.n_instr + d.n_bwd + row_table_words(K) : d.n_instr;
         for (int i = tid; i < n_code; i += NT) code_s[i] = p.code[d.code_off + i];
@@ -640,12 +653,30 @@ lm_eval_kernel(const EvalParams<T> p) {
             CUSR_FOR_V {
                 valid[j] = si + j < p.N;
                 r[j] = valid[j] ? f[j] - (T)yv.v[j] : T(0);
-                lsum += r[j] * r[j];
             }
+            // sentinel fits: non-finite residuals become the sentinel, their samples' gradient
+            // entries are dropped (bit j of the mask); applied where the gradients are final
+            auto sentinel_mask = [&]() -> unsigned {
+                unsigned mk = 0u;
+                if (s_sent) {
+                    CUSR_FOR_V {
+                        if (!Mth<T>::finite(r[j])) {
+                            r[j] = T(RESIDUAL_SENTINEL);
+                            mk |= 1u << j;
+                        }
+                    }
+                }
+                return mk;
+            };
             if (p.vals) {
                 CUSR_FOR_V if (valid[j]) p.vals[(int64_t)wi.x * p.N + si + j] = f[j];
             }
             if constexpr (FWD) {
+              const unsigned mk = sentinel_mask();
+              CUSR_FOR_V {
+                  if ((mk >> j) & 1u) valid[j] = false;
+                  lsum += r[j] * r[j];
+              }
               if (grad) {
                 if (p.jac) {
                     T *jrow = p.jac + (int64_t)wi.x * p.jac_kmax * p.N;
@@ -666,8 +697,13 @@ lm_eval_kernel(const EvalParams<T> p) {
                     }
                 }
               }
-            } else if (grad) {
+            } else if (!grad) {
+                sentinel_mask();
+                CUSR_FOR_V lsum += r[j] * r[j];
+            } else {
                 reverse_sweep<T, V, NT, TSTR, RSTR, TG>(bcode_s, d.n_bwd, c_s, xt, spt, tpt, rc);
+                const unsigned mk = sentinel_mask();
+                CUSR_FOR_V lsum += r[j] * r[j];
                 if (p.jac) {
                     T *jrow = p.jac + (int64_t)wi.x * p.jac_kmax * p.N;
                     for (int k = 0; k < K; ++k) {
@@ -675,14 +711,14 @@ lm_eval_kernel(const EvalParams<T> p) {
                         CUSR_FOR_V if (valid[j]) jrow[(int64_t)k * p.N + si + j] = g.v[j];
                     }
                 }
-                // residual row; gradients of samples past N are zeroed (only the last round
-                // of a tree's last chunk has any)
+                // residual row; gradients of samples past N (only the last round of a tree's
+                // last chunk has any) and of sentinel samples are zeroed
                 *rc.at(K, rtab[K]) = pack<T, V>(r);
-                if (si + V > p.N) {
+                if (si + V > p.N || mk) {
                     for (int k = 0; k < K; ++k) {
                         VecT<T, V> *q = rc.at(k, rtab[k]);
                         VecT<T, V> g = *q;
-                        CUSR_FOR_V if (!valid[j]) g.v[j] = T(0);
+                        CUSR_FOR_V if (!valid[j] || ((mk >> j) & 1u)) g.v[j] = T(0);
                         *q = g;
                     }
                 }

@@ -80,7 +80,7 @@ __global__ void init_starts_kernel(const StartsParams<T> p) {
             p.diag[d.c_off + k] = 1.0;
         }
         uint8_t mode = 0;
-        if (s < p.tr_starts) mode = IM_TR;
+        if (s < p.tr_starts) mode = IM_TR | IM_SENTINEL;
         else if (p.damp_alternate && ((s - p.tr_starts) & 1)) mode = IM_DAMP_ALWAYS;
         p.imode[i] = mode;
         const bool first = p.wave1 <= 0 || s < p.wave1;

@@ -8,6 +8,7 @@ reference's uv.lock), whose published steps are restated here: scaling D = runni
 Jacobian column norms, initial trust radius 100 |D c0|, the ratio test actred / prered with the
 radius updates of Moré's paper, acceptance at ratio >= 1e-4, the ftol / xtol / gtol / maxfev
 tests, and the LM parameter from lmpar's safeguarded Newton iteration on 1/|Dp| - 1/Delta.
+The residual is the reference backend's: non-finite entries count as the sentinel 1e6.
 The Jacobian is the exact (reverse-mode) one of oracle.interp, the linear algebra Cholesky
 factors of J^T J + par D^2 (the engine's formulation; MINPACK uses QR of J): the Gauss-Newton
 step takes symmetric pivoting and stops at the first non-positive pivot, the basic solution on
@@ -24,6 +25,8 @@ import numpy as np
 
 from . import interp
 
+SENTINEL = 1e6
+RANKDEF_BOUNDARY = False
 DWARF = np.finfo(np.float64).tiny
 EPS = np.finfo(np.float64).eps
 
@@ -88,6 +91,8 @@ def lmpar(A, g, d, delta, par):
         x[perm[:r]] = -_bsub(Lr, _fsub(Lr, g[perm][:r]))
     dxnorm = np.linalg.norm(d * x)
     fp = dxnorm - delta
+    if RANKDEF_BOUNDARY and r < n:
+        dxnorm, fp = np.inf, np.inf
     if fp <= 0.1 * delta:
         return 0.0, x
     parl = 0.0
@@ -135,8 +140,16 @@ def fit_tree(nt, nv, ci, xs, y, c0, max_nfev=200, ftol=1e-10, xtol=1e-10, gtol=1
     xs = np.asarray(xs)
 
     def fj(c, jac):
+        # the reference scipy backend's residual (backends.py:105-110): a non-finite residual
+        # is the sentinel 1e6, whose forward difference, and so Jacobian row, is 0
         v, J = interp.value_and_jacobian(nt, nv, ci, xs, c, jacobian=jac)
-        return v - y64, J
+        r = v - y64
+        bad = ~np.isfinite(r)
+        if bad.any():
+            r = np.where(bad, SENTINEL, r)
+            if J is not None:
+                J = np.where(bad[:, None], 0.0, J)
+        return r, J
 
     x = np.asarray(c0, np.float64).copy()
     with np.errstate(all="ignore"):
