@@ -26,7 +26,6 @@ import numpy as np
 from . import interp
 
 SENTINEL = 1e6
-RANKDEF_BOUNDARY = False
 DWARF = np.finfo(np.float64).tiny
 EPS = np.finfo(np.float64).eps
 
@@ -91,8 +90,6 @@ def lmpar(A, g, d, delta, par):
         x[perm[:r]] = -_bsub(Lr, _fsub(Lr, g[perm][:r]))
     dxnorm = np.linalg.norm(d * x)
     fp = dxnorm - delta
-    if RANKDEF_BOUNDARY and r < n:
-        dxnorm, fp = np.inf, np.inf
     if fp <= 0.1 * delta:
         return 0.0, x
     parl = 0.0

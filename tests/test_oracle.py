@@ -216,3 +216,18 @@ def test_lm_trajectory_sensitivity_to_summation_order():
     np.testing.assert_allclose(a["loss_init"], b["loss_init"], rtol=1e-13)
     assert 0.8 <= same < 0.99, same
     assert 0.9 <= status < 1.0, status
+
+
+def test_reference_fit_reproducibility_floor():
+    """The reference fit is not reproducible at the rounding level: ScipyPop re-run on PR1
+    with every c_init moved by one float32 ulp ends within 1e-6 of (or better than) its own
+    golden fit on only ~84% of trees, with the targets moved by one ulp on ~91% (a plain re-run:
+    100%). On the mid / long / metric grammars the figures are lower still
+    (`python -m oracle.scipy_floor NAME`). A fit that reaches >= 99% against one reference run
+    is therefore better than the reference against itself."""
+    from oracle import scipy_floor
+
+    z = np.load(GOLDEN / "pr1_scipy.npz")
+    out = scipy_floor.perturbation_floor(load_npz_pop(z, "pop"), z["scipy/loss64"])
+    assert out["rerun"] == 1.0
+    assert out["c_init+1ulp"] < 0.95 and out["y+1ulp"] < 0.97, out
