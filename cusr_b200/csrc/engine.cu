@@ -484,14 +484,26 @@ int sync_stream(Ctx *ctx, bool sharded) {
     return shard_wait_event(ctx->shard, ctx->ev_sync);
 }
 
+// chunks per tree from which the step's chunk sums run as their own block-parallel kernel
+constexpr int64_t PRESUM_CHUNKS = 64;
+
+// Per-tree sums of the chunk partials into ctx->red (chunk_sum_kernel).
+template <typename T>
+int chunk_sums(Ctx *ctx, int M, int64_t block_elems, cudaStream_t s) {
+    GROW(ctx->red, (size_t)block_elems * sizeof(T));
+    const int grid = std::max(1, std::min(M, 8 * ctx->sm_count));
+    chunk_sum_kernel<T><<<grid, CSUM_THREADS, 0, s>>>(P<TreeDesc>(ctx->desc), M,
+                                                      P<T>(ctx->partials), P<T>(ctx->red));
+    CK(cudaGetLastError());
+    ctx->stats.kernel_launches++;
+    return CO_OK;
+}
+
 // Sample-sharded mode: sum this rank's chunk partials per tree and all-reduce them.
 template <typename T>
 int shard_reduce_blocks(Ctx *ctx, int M, int64_t block_elems) {
-    GROW(ctx->red, (size_t)block_elems * sizeof(T));
-    reduce_chunks_kernel<T><<<grid_for(ctx, M), 256, 0, ctx->stream>>>(
-        P<TreeDesc>(ctx->desc), M, P<T>(ctx->partials), P<T>(ctx->red));
-    CK(cudaGetLastError());
-    ctx->stats.kernel_launches++;
+    const int rc = chunk_sums<T>(ctx, M, block_elems, ctx->stream);
+    if (rc) return rc;
     return shard_allreduce(ctx->shard, ctx->red.ptr, (size_t)block_elems, sizeof(T) == 8,
                            ctx->stream);
 }
@@ -701,6 +713,11 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         return CO_OK;
     };
 
+    // with hundreds of chunks per tree (N of millions) the chunk partials are summed by a
+    // block per tree before the step, instead of by the step kernel's one warp per tree
+    const int64_t n_chunks = ((int64_t)h->N + sc.chunk - 1) / std::max(sc.chunk, 1);
+    const bool presum = !sharded && n_chunks >= PRESUM_CHUNKS;
+
     // ---- initial pass at the start points + solve of iteration 0 ----
     size_t e0 = ev_i; rec();
     rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true, nullptr,
@@ -715,6 +732,10 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         size_t ec = ev_i; rec();
         comm_spans.push_back({e1, ec});
         e1 = ec;
+    } else if (presum) {
+        rc = chunk_sums<T>(ctx, M_fit, sc.block_elems, s);
+        if (rc) return rc;
+        sp.reduced = P<T>(ctx->red);
     }
     rc = steps(P<int>(ctx->n_run));
     if (rc) return rc;
@@ -753,6 +774,9 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
             size_t bc = ev_i; rec();
             comm_spans.push_back({b, bc});
             b = bc;
+        } else if (presum) {
+            rc = chunk_sums<T>(ctx, M_fit, sc.block_elems, s);
+            if (rc) return rc;
         }
         rc = steps(P<int>(ctx->n_run) + slot);
         if (rc) return rc;

@@ -345,17 +345,37 @@ __global__ void fd_column_kernel(const TreeDesc *desc, int M, int N, int k, int 
     }
 }
 
-// Sample-sharded mode: per-tree sums of this rank's chunk partials, in chunk order (raw sums,
-// the all-reduce input).
+// Per-tree sums of the chunk partials for populations with many chunks per tree (the
+// sample-sharded all-reduce input, and the step kernels' input when N spans hundreds of
+// chunks): one block per tree (grid-stride over trees), its warps take interleaved chunk
+// slices and its lanes 32 consecutive elements (coalesced reads of a chunk's partial row);
+// the slice sums of an element are then added in slice order, a fixed order, so the sums are
+// the same run to run. Raw sums (the step kernel halves the loss element itself).
+constexpr int CSUM_THREADS = 256;
 template <typename T>
-__global__ void reduce_chunks_kernel(const TreeDesc *desc, int M, const T *partials, T *out) {
-    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+__global__ void __launch_bounds__(CSUM_THREADS)
+chunk_sum_kernel(const TreeDesc *desc, int M, const T *partials, T *out) {
+    constexpr int NW = CSUM_THREADS / 32;
+    __shared__ T part[NW][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int m = blockIdx.x; m < M; m += gridDim.x) {
         const TreeDesc d = desc[m];
         const int P = nblock_size(d.K);
-        for (int e = 0; e < P; ++e) {
+        for (int e0 = 0; e0 < P; e0 += 32) {
+            const int e = e0 + lane;
             T s = T(0);
-            for (int ch = 0; ch < d.n_chunks; ++ch) s += partials[d.p_off + (int64_t)ch * P + e];
-            out[d.q_off + e] = s;
+            if (e < P)
+                for (int ch = warp; ch < d.n_chunks; ch += NW)
+                    s += partials[d.p_off + (int64_t)ch * P + e];
+            part[warp][lane] = s;
+            __syncthreads();
+            if (warp == 0 && e < P) {
+                T t = part[0][lane];
+#pragma unroll
+                for (int w = 1; w < NW; ++w) t += part[w][lane];
+                out[d.q_off + e] = t;
+            }
+            __syncthreads();
         }
     }
 }

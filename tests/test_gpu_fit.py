@@ -542,3 +542,22 @@ def test_fp32_honesty_regression(co, precision, max_iter):
                                                      "converged_but_worse": conv_worse})
     assert n == 257 and serious_base == 208
     assert conv_worse == []
+
+
+def test_many_chunk_fit_sums(co):
+    """N of 300,000 (74 chunks per tree): the step's per-tree sums run as their own
+    block-parallel kernel (chunk_sum_kernel). The fp64 loss elements it hands the step equal
+    the oracle's losses at c_init and at c_final, and the fits follow the oracle's LM
+    iteration (same algorithm, fp64) on the trees whose trajectory is not chaotic."""
+    pop = synth.make_config("pr1", M=16, N=300_000, seed=4)
+    res = co.optimize_ex(pop, max_iter=20, precision="fp64")
+    li = interp.loss_pop(pop, np.asarray(pop["c_init"], np.float64))
+    lf = interp.loss_pop(pop, res["c_final"])
+    K = np.asarray(pop["metas"])[:, 3]
+    fin = (K > 0) & np.isfinite(li)
+    np.testing.assert_allclose(res["loss_init"][fin], li[fin], rtol=1e-11)
+    ok = np.isfinite(lf) & fin
+    np.testing.assert_allclose(res["loss_final"][ok], lf[ok], rtol=1e-10)
+    ref = lm.fit_pop(pop, max_iter=20, dtype=np.float64, trees=np.arange(8))
+    same = np.abs(res["loss_final"][:8] - ref["loss_final"]) <= 1e-6 * np.abs(ref["loss_final"]) + 1e-12
+    assert np.mean(same[np.isfinite(ref["loss_final"])]) >= 0.6
