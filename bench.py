@@ -298,8 +298,8 @@ def run_reference(args, world: int, rank: int) -> None:
 
 
 def parity_mode(co, pop: dict) -> dict:
-    """The parity-grade fit (cusr_b200.multistart defaults: 64 starts per tree on the device,
-    16 trust-region / 48 reference-schedule, two waves, fp64, trust-region polish): fits/s on a
+    """The parity-grade fit (cusr_b200.multistart defaults: 96 trust-region starts per tree on
+    the device, two waves, fp64, trust-region polish): fits/s on a
     2,048-tree stratified slice of the metric population (device time of the multi-start call
     plus the polish call), and the north-star fraction — fp64 loss within 1e-6 of, or better
     than, the reference scipy fit — on the 256-tree scipy sample of the same population
@@ -329,8 +329,8 @@ def parity_mode(co, pop: dict) -> dict:
             "within_1e-6_or_better": frac, "starts": int(st["n_starts"]),
             "fits_run": int(st["fits_run"]), "trees_retired": int(st["trees_retired"]),
             "trees": int(sub["M"]), "dtype": "f64", "device_ms": ms,
-            "note": "the parity-grade mode (64 device-side starts, trust-region + reference "
-                    "schedule, fp64) on a 2,048-tree slice of the metric population; the "
+            "note": "the parity-grade mode (96 device-side trust-region starts, fp64) on a "
+                    "2,048-tree slice of the metric population; the "
                     "fraction on the 256-tree reference scipy sample of that population"}
 
 

@@ -127,13 +127,14 @@ def test_pr1_fit_parity_vs_reference_scipy(co):
 
 def _multistart_parity(co, name, pop, ref, **kw):
     """North-star parity with the parity-grade fit (cusr_b200.multistart defaults, the device
-    start axis: 64 starts per tree — 16 trust-region, 48 reference-schedule with the damping
-    floor — in two waves, fp64, a trust-region polish of the best; the best final loss kept):
+    start axis: 96 trust-region starts per tree in two waves, fp64, a trust-region polish of
+    the best; the best final loss kept):
     the fraction of trees whose fp64 loss is within 1e-6 relative of, or better than, the
     reference scipy fit. Divergent trees are listed. The bars are the measured levels: on
-    the mid / long / metric grammars a few trees in a hundred keep a local minimum worse than
-    MINPACK's (whose QR steps along rank-deficient directions reach regions no start of ours
-    does)."""
+    the mid grammar a few trees in a hundred keep a local minimum worse than MINPACK's, whose
+    steps on Jacobians rank-deficient to machine precision are rounding-driven (the reference
+    itself, re-run with its inputs moved by one ulp, reaches its own fit on 66-74% of mid
+    trees: oracle/scipy_floor.py)."""
     from cusr_b200 import multistart
 
     res = multistart.fit_multistart(co, pop, **kw)
@@ -166,12 +167,12 @@ def test_pop1000_multistart_parity_vs_reference_scipy(co):
     assert _multistart_parity(co, "pop1000", pop, g["scipy/loss64"]) >= 0.99
 
 
-@pytest.mark.parametrize("name,bar", [("mid", 0.95), ("physics", 0.99), ("long", 0.96),
-                                      ("scale", 0.99)])
+@pytest.mark.parametrize("name,bar", [("mid", 0.95), ("physics", 0.99), ("long", 0.98),
+                                      ("scale", 0.98)])
 def test_config_multistart_parity_vs_reference_scipy(co, name, bar):
     """64-tree samples of the other BASELINE configurations (reduced N) with the reference's
-    scipy fits (tests/golden/configs_scipy.npz); measured mid 96.9%, physics 100%, long 98.4%,
-    scale 100%."""
+    scipy fits (tests/golden/configs_scipy.npz); measured mid 96.9%, physics 100%, long 100%,
+    scale 98.4-100% (one tree of 64 at 1.0036 in some start mixes)."""
     z = np.load(GOLDEN / "configs_scipy.npz")
     pop = load_npz_pop(z, name)
     assert _multistart_parity(co, name, pop, z[f"{name}/scipy/loss64"]) >= bar
@@ -230,8 +231,8 @@ def test_metric_sample_parity_modes(co):
     rep["parity_mode_trees_retired"] = int(st["trees_retired"])
     rep["parity_mode_device_ms"] = st["device_ms"]
     _report("metric_sample_modes_vs_scipy", rep)
-    # measured: single fp32 52%, fp64 62%, one trust-region start 74%, parity mode 96.4%
-    assert rep["single_fp32"] >= 0.45 and rep["parity_mode"] >= 0.95, rep
+    # measured: single fp32 52%, fp64 62%, one trust-region start 74%, parity mode 99.2%
+    assert rep["single_fp32"] >= 0.45 and rep["parity_mode"] >= 0.98, rep
 
 
 def test_trust_region_fp64_matches_oracle(co):

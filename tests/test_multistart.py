@@ -78,7 +78,7 @@ def test_parity_preset_reaches_options():
     co_inproc.start_options(opt, **{k: v for k, v in co_inproc.PARITY.items()
                                     if k in ("algorithm", "n_starts", "tr_starts", "wave1",
                                              "ftol", "gtol")})
-    assert opt.algorithm == 1 and opt.n_starts == 64 and opt.tr_starts == 16 and opt.wave1 == 8
+    assert opt.algorithm == 1 and opt.n_starts == 96 and opt.tr_starts == 96 and opt.wave1 == 8
     assert opt.ftol == 1e-10 and opt.gtol == 1e-8
     with pytest.raises(ValueError):
         co_inproc.start_options(opt, algorithm="newton")
