@@ -30,11 +30,10 @@ class FitResult:
 
 
 class B200Pop:
-    """In-process engine backend. precision 'fp32' (IEEE functions), 'fp32_fast' (the
+    """In-process engine backend. precision 'fp32' (the SFU arithmetic), 'fp32_fast' (the
     reference kernel's fast-math arithmetic) or 'fp64'; shared target rows are detected and
     uploaded once. starts > 1: the parity-grade multi-start fit (cusr_b200.multistart: the
-    device start axis, trust-region and reference-schedule starts; max_iter then defaults to
-    200)."""
+    device start axis, trust-region starts; max_iter then defaults to 200)."""
 
     def __init__(self, max_iter: int | None = None, precision: str = "fp32", device_id: int = 0,
                  name: str | None = None, starts: int = 1):
