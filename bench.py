@@ -303,35 +303,47 @@ def parity_mode(co, pop: dict) -> dict:
     2,048-tree stratified slice of the metric population (device time of the multi-start call
     plus the polish call), and the north-star fraction — fp64 loss within 1e-6 of, or better
     than, the reference scipy fit — on the 256-tree scipy sample of the same population
-    (tests/golden/metric_scipy.npz, made by the reference's ScipyPop)."""
-    from cusr_b200 import multistart, popio
+    (tests/golden/metric_scipy.npz, made by the reference's ScipyPop). `fast`: the same for
+    co_inproc.PARITY_FAST (fp32 exploration, fp64 polish)."""
+    from cusr_b200 import co_inproc, multistart, popio
 
     sub = popio.slice_pop(pop, np.unique(np.linspace(0, int(pop["M"]) - 1, 2048).astype(np.int64)))
-    multistart.fit_multistart(co, popio.slice_pop(sub, 64))            # warm-up
-    res = multistart.fit_multistart(co, sub)
-    st = res["stats"]
-    ms = st["device_ms"] + co.stats()["device_ms"]
     golden = ROOT / "tests" / "golden" / "metric_scipy.npz"
-    frac = None
+    sample = ref = None
     if golden.exists():
         z = np.load(golden)
         sample = {k: z[f"pop/{k}"] for k in ("nt", "nv", "ci", "metas", "c_init", "xs", "ym")}
         sample.update({k: int(z[f"pop/{k}"]) for k in ("M", "total_nodes", "total_c", "N",
                                                         "n_vars", "K_max", "max_stack")})
-        r = multistart.fit_multistart(co, sample)
-        blk = co.evaluate(sample, c=r["c_final"], precision="fp64", values=False,
-                          blocks=True)["blocks"]
-        l64 = np.array([b[-1] for b in blk])
         ref = z["scipy/loss64"]
-        elig = (sample["metas"][:, 3] > 0) & np.isfinite(ref)
-        frac = float(np.mean((l64 <= ref * (1 + 1e-6) + 1e-12)[elig]))
-    return {"value": int(sub["M"]) / (ms / 1e3), "unit": "fits/s",
-            "within_1e-6_or_better": frac, "starts": int(st["n_starts"]),
-            "fits_run": int(st["fits_run"]), "trees_retired": int(st["trees_retired"]),
-            "trees": int(sub["M"]), "dtype": "f64", "device_ms": ms,
-            "note": "the parity-grade mode (96 device-side trust-region starts, fp64) on a "
-                    "2,048-tree slice of the metric population; the "
-                    "fraction on the 256-tree reference scipy sample of that population"}
+
+    def measure(kw: dict) -> dict:
+        multistart.fit_multistart(co, popio.slice_pop(sub, 64), **kw)            # warm-up
+        res = multistart.fit_multistart(co, sub, **kw)
+        st = res["stats"]
+        ms = st["device_ms"] + co.stats()["device_ms"]
+        frac = None
+        if sample is not None:
+            r = multistart.fit_multistart(co, sample, **kw)
+            blk = co.evaluate(sample, c=r["c_final"], precision="fp64", values=False,
+                              blocks=True)["blocks"]
+            l64 = np.array([b[-1] for b in blk])
+            elig = (sample["metas"][:, 3] > 0) & np.isfinite(ref)
+            frac = float(np.mean((l64 <= ref * (1 + 1e-6) + 1e-12)[elig]))
+        return {"value": int(sub["M"]) / (ms / 1e3), "unit": "fits/s",
+                "within_1e-6_or_better": frac, "starts": int(st["n_starts"]),
+                "fits_run": int(st["fits_run"]), "trees_retired": int(st["trees_retired"]),
+                "trees": int(sub["M"]), "device_ms": ms}
+
+    out = measure(multistart.preset_kwargs(co_inproc.PARITY))
+    out.update(dtype="f64", note="the parity-grade mode (co_inproc.PARITY: 96 device-side "
+               "trust-region starts, fp64) on a 2,048-tree slice of the metric population; the "
+               "fraction on the 256-tree reference scipy sample of that population")
+    fast = measure(multistart.preset_kwargs(co_inproc.PARITY_FAST))
+    fast.update(dtype="f32 starts, f64 polish", note="co_inproc.PARITY_FAST: 128 trust-region "
+                "starts in fp32 (50 evaluations), then the fp64 trust-region polish")
+    out["fast"] = fast
+    return out
 
 
 def run_ours(args, world: int, rank: int, local: int) -> None:

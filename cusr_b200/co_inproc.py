@@ -260,6 +260,14 @@ PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
               algorithm="trust_region", n_starts=96, tr_starts=96, wave1=8, ftol=1e-10,
               gtol=1e-8, polish=True)
 
+# The fast parity-grade fit: the same trust-region start axis with 128 starts explored in
+# fp32 (50 evaluations, ftol = xtol = 1e-6), then the fp64 trust-region polish of each tree's
+# best (200 evaluations, scipy's tolerances). Measured on the scipy samples: about five times
+# faster than PARITY, the same north-star fraction on the metric sample, a few more divergent
+# trees on the mid / long grammars.
+PARITY_FAST = dict(PARITY, n_starts=128, tr_starts=128, explore_precision="fp32",
+                   explore_max_iter=50, explore_tol=1e-6)
+
 
 class InProcessCO:
     """One persistent engine context on one device. CUDA context creation is paid once in

@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .co_inproc import PARITY
+from .co_inproc import PARITY, PARITY_FAST
 
 KINDS = ("scale", "shift", "fresh1", "fresh3")   # start kinds after c_init, cycled
 
@@ -71,23 +71,41 @@ def start_points(pop: dict, starts: int, seed: int = 0) -> np.ndarray:
     return v.astype(np.float32)
 
 
+def preset_kwargs(preset: dict = PARITY_FAST) -> dict:
+    """fit_multistart keyword arguments of a preset dict (co_inproc.PARITY / PARITY_FAST)."""
+    return {("starts" if k == "n_starts" else k): v for k, v in preset.items() if k != "algorithm"}
+
+
 def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
                    max_iter: int = PARITY["max_iter"], xtol: float = PARITY["xtol"],
                    precision: str = PARITY["precision"], seed: int = 0,
                    damping_floor: float = PARITY["damping_floor"],
                    tr_starts: int = PARITY["tr_starts"], wave1: int = PARITY["wave1"],
-                   polish: bool = PARITY["polish"], **kw) -> dict:
+                   polish: bool = PARITY["polish"], explore_precision: str | None = None,
+                   explore_max_iter: int | None = None, explore_tol: float | None = None,
+                   **kw) -> dict:
     """Fit every tree of `pop` from `starts` starting points (the first is its c_init) in one
     device call (InProcessCO.optimize_ex with n_starts) and return the best start's
     c_final / status / loss_init / loss_final / iters with its index ('start').
     polish: a second device call continues every tree's best fit with the trust-region LM
     (from its constants rounded to the fp32 of the ABI) and keeps whichever is lower.
 
+    explore_precision / explore_max_iter / explore_tol: run the multi-start call in another
+    precision (e.g. "fp32": about five times faster), with its own evaluation budget and
+    ftol = xtol; the polish then runs in `precision` with max_iter / xtol and its result is
+    kept wherever it is finite and no worse (co_inproc.PARITY_FAST).
+
     Defaults: the parity preset (co_inproc.PARITY)."""
     algorithm = "trust_region" if tr_starts > 0 else kw.pop("algorithm", "reference")
-    res = co.optimize_ex(pop, max_iter=max_iter, precision=precision, xtol=xtol,
+    explore = explore_precision is not None and explore_precision != precision
+    x_kw = dict(kw)
+    if explore and explore_tol is not None:
+        x_kw["ftol"] = explore_tol
+    res = co.optimize_ex(pop, max_iter=explore_max_iter if explore and explore_max_iter else max_iter,
+                         precision=explore_precision if explore else precision,
+                         xtol=explore_tol if explore and explore_tol is not None else xtol,
                          damping_floor=damping_floor, algorithm=algorithm, n_starts=starts,
-                         tr_starts=tr_starts, wave1=wave1, seed=seed, **kw)
+                         tr_starts=tr_starts, wave1=wave1, seed=seed, **x_kw)
     if not polish:
         return res
     stats = co.stats()
@@ -97,7 +115,14 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     pol = co.optimize_ex(again, max_iter=max_iter, precision=precision, xtol=xtol,
                          algorithm="trust_region", **{k: v for k, v in kw.items()
                                                       if k in ("y_shared", "ftol", "gtol")})
-    better = np.asarray(pol["loss_final"]) < np.asarray(res["loss_final"])
+    lp, lr = np.asarray(pol["loss_final"]), np.asarray(res["loss_final"])
+    if explore:
+        # the polish starts at the explore stage's (float32) constants and only accepts
+        # improvements: its loss is the better one unless it failed; the two stages' losses
+        # come from different precisions, hence the tolerance
+        better = np.isfinite(lp) & (lp <= lr * (1 + 1e-5) + 1e-30)
+    else:
+        better = lp < lr
     M = int(pop["M"])
     K = np.asarray(pop["metas"], np.int64).reshape(M, 4)[:, 3]
     out = {k: np.where(better, pol[k], res[k]) for k in ("status", "loss_final", "iters")}

@@ -82,3 +82,10 @@ def test_parity_preset_reaches_options():
     assert opt.ftol == 1e-10 and opt.gtol == 1e-8
     with pytest.raises(ValueError):
         co_inproc.start_options(opt, algorithm="newton")
+
+
+def test_fast_preset_keywords():
+    kw = multistart.preset_kwargs(co_inproc.PARITY_FAST)
+    assert kw["starts"] == 128 and kw["tr_starts"] == 128 and "algorithm" not in kw
+    assert kw["explore_precision"] == "fp32" and kw["precision"] == "fp64"
+    assert multistart.preset_kwargs(co_inproc.PARITY)["starts"] == co_inproc.PARITY["n_starts"]
