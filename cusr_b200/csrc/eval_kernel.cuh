@@ -538,9 +538,14 @@ __device__ __forceinline__ void dmma_884(double (&c)[2], double a, double b) {
 // blocks per SM, as many as shared memory allows for the common tape sizes); the K <= 32
 // class keeps its 15 accumulator tiles in registers at four blocks; fp64 (twice the shared
 // memory per thread) is held to six and two blocks.
+#ifndef CUSR_F64_THREADS_PER_SM
+// fp64 classes K <= 16: resident threads per SM (768: 85 registers, small spills; 512 removes
+// the spills and measured 0.7-4% slower on the parity mode and the physics configuration)
+#define CUSR_F64_THREADS_PER_SM 768
+#endif
 template <typename T, int V, int NT, int KC, bool GRAD, bool TG, bool FAST>
 __global__ void __launch_bounds__(
-    NT, (sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : 768)) / NT)
+    NT, (sizeof(T) == 4 ? (KC > 16 ? 512 : 1024) : (KC > 16 ? 256 : CUSR_F64_THREADS_PER_SM)) / NT)
 lm_eval_kernel(const EvalParams<T> p) {
     typedef EvalSmem<T, V, NT, KC> L;
     constexpr bool FWD = GRAD && L::kFwd;    // forward-mode tangents (KC = 1, 2)
