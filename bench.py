@@ -47,6 +47,7 @@ CONFIG = "metric"
 M_PER_GPU = 16384
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 PROFILE_SUMMARY = ROOT / "profiles" / "lm_eval_kernel_metric.md"
+INST_SUMMARY = ROOT / "profiles" / "lm_eval_kernel_sfu_vs_ieee_instructions.md"
 
 
 def dist_setup():
@@ -166,14 +167,14 @@ def out_dir(args) -> Path:
     return p
 
 
-def profile_value(key: str):
-    """A figure recorded in the committed ncu summary of the evaluation kernel
-    (profiles/lm_eval_kernel_metric.md, lines `key: value`): NOT measured by this run, so it is
-    returned with its source and the commit it was captured at."""
-    if not PROFILE_SUMMARY.exists():
+def profile_value(key: str, summary: Path = PROFILE_SUMMARY):
+    """A figure recorded in a committed ncu summary (default profiles/lm_eval_kernel_metric.md,
+    lines `key: value`): NOT measured by this run, so it is returned with its source and the
+    commit it was captured at."""
+    if not summary.exists():
         return None
     val, commit = None, None
-    for line in PROFILE_SUMMARY.read_text().splitlines():
+    for line in summary.read_text().splitlines():
         t = line.strip()
         if t.startswith(key + ":"):
             try:
@@ -184,8 +185,29 @@ def profile_value(key: str):
             commit = t.split(":", 1)[1].strip()
     if val is None:
         return None
-    return {"value": val, "source": str(PROFILE_SUMMARY.relative_to(ROOT)),
+    return {"value": val, "source": str(summary.relative_to(ROOT)),
             "captured_at": commit, "measured_in_this_run": False}
+
+
+def issue_estimate(node_evals: float, eval_ms: float, clk: dict):
+    """Issue-slot fraction of the timed evaluation launches, estimated live: the committed
+    capture's thread-instructions per node-eval (a per-workload constant of the interpreter)
+    x this run's node-evals / eval time, over the issue peak 148 SMs x 4 schedulers x the
+    sampled SM clock x 32 threads."""
+    ipn = profile_value("thread_instructions_per_node_eval", INST_SUMMARY)
+    mhz = clk.get("sm_mhz") if isinstance(clk, dict) else None
+    if not ipn or not mhz or eval_ms <= 0:
+        return None
+    try:
+        import torch
+
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+    except Exception:  # noqa: BLE001
+        sms = 148
+    peak = sms * 4 * mhz * 1e6 * 32
+    rate = ipn["value"] * node_evals / (eval_ms / 1e3)
+    return {"frac": rate / peak, "thread_inst_per_s": rate, "peak_thread_inst_per_s": peak,
+            "inst_per_node_eval": ipn}
 
 
 def cpu_baseline(pop: dict, target_s: float = 15.0) -> dict:
@@ -432,7 +454,8 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
         "issue": {"bound": "issue", "achieved_pct": profile_value("issue_active_pct"),
                   "note": "issue slots busy on the evaluation kernel, from the committed ncu "
                           "capture (not measured in this run): the interpreter is bound by "
-                          "instruction issue, not FMA or HBM throughput"},
+                          "instruction issue, not FMA or HBM throughput",
+                  "live_estimate": issue_estimate(float(node_evals), eval_ms, clk)},
         "avg_launch_ms": avg_launch_ms,
         "flops_def": "per evaluated (tree, sample): 2 per operator node (value + adjoint) + "
                      "2 per normal-equation entry (K+1)(K+2)/2",
