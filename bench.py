@@ -499,10 +499,12 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
     print(json.dumps(line), flush=True)
 
 
-def run_config(args) -> None:
-    """One BASELINE configuration on one GPU (pr1, mid, physics, long, scale, sharded):
-    resident-input fits/s and node-evals/s, device-timed, with its CPU baseline sample."""
-    from cusr_b200 import InProcessCO, synth
+def run_config(args, world: int = 1, rank: int = 0, local: int = 0) -> None:
+    """One BASELINE configuration (pr1, mid, physics, long, scale, sharded): resident-input
+    fits/s and node-evals/s, device-timed, with its CPU baseline sample. Under torchrun the
+    configuration's population is split into cost-balanced expression shards, one per rank
+    (strong scaling: the population is fixed), time = max over ranks."""
+    from cusr_b200 import InProcessCO, shard, synth
 
     name = args.config
     pop = synth.make_config(name, M=args.M, N=args.N, seed=0)
@@ -510,10 +512,12 @@ def run_config(args) -> None:
     if args.fast_math and precision == "fp32":
         precision = "fp32_fast"
     shared = np.asarray(pop["ym"]).ndim == 1
-    co = InProcessCO(device_id=0)
-    co.load(pop, precision=precision, y_shared=shared)
+    mine = shard.shard(pop, rank, world)[0] if world > 1 else pop
+    co = InProcessCO(device_id=local if world > 1 else 0)
+    co.load(mine, precision=precision, y_shared=shared)
     for _ in range(args.warmup):
         co.fit_loaded(max_iter=max_iter)
+    barrier(world)
     dev, nodes, launches, res = [], 0, 0, None
     for _ in range(args.steps):
         res = co.fit_loaded(max_iter=max_iter)
@@ -521,18 +525,25 @@ def run_config(args) -> None:
         dev.append(st["device_ms"])
         nodes += st["node_evals"]
         launches += st["kernel_launches"]
-    total_ms = float(sum(dev))
+    barrier(world)
+    total_ms = max_over_ranks(float(sum(dev)), world)
+    nodes = sum_over_ranks(float(nodes), world)
+    if rank != 0:
+        return
     M = int(pop["M"])
     line = {"metric": f"LM fits/sec ({name}: M={M}, N={pop['N']}, {max_iter} iters, {precision})",
-            "value": M * args.steps / (total_ms / 1e3), "unit": "fits/s", "n_gpus": 1,
+            "value": M * args.steps / (total_ms / 1e3), "unit": "fits/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "f64" if precision == "fp64" else "f32", "data": "synthetic",
             "config": {"workload": name, "trees": M, "N": int(pop["N"]), "max_iter": max_iter,
                        "y_shared": bool(shared), "precision": precision},
             "node_evals_per_s": nodes / (total_ms / 1e3), "gpu_launches": launches,
             "statuses": np.bincount(res["status"], minlength=5).tolist()}
-    if not args.no_cpu_baseline:
+    if world > 1:
+        line["config"]["parallelism"] = f"expression-sharded x{world} (LPT cost-balanced)"
+    if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(pop, target_s=10.0)
     print(json.dumps(line), flush=True)
 
@@ -662,12 +673,11 @@ def main() -> None:
     if args.profile_case:
         run_profile_case(args)
         return
-    if args.config:
-        run_config(args)
-        return
     world, rank, local = dist_setup()
     try:
-        if args.sample_sharded:
+        if args.config:
+            run_config(args, world, rank, local)
+        elif args.sample_sharded:
             run_sample_sharded(args, world, rank, local)
         elif args.impl == "reference":
             run_reference(args, world, rank)
