@@ -112,6 +112,40 @@ def build(force: bool = False, verbose: bool = False, defines: tuple = (), obj_d
     return LIB
 
 
+def ptxas_report() -> str:
+    """Markdown table of every kernel's registers, stack frame and spills (ptxas -v) for the
+    CUDA sources, compiled as the library build compiles them."""
+    import re
+    import tempfile
+
+    nvcc = _nvcc()
+    rows = []
+    with tempfile.TemporaryDirectory() as tmp:
+        for src in [s for s in SOURCES if s.endswith(".cu")]:
+            cmd = [nvcc, *NVCC_FLAGS, *FILE_FLAGS.get(src, []), "-Xptxas", "-v", "-c",
+                   str(CSRC / src), "-o", str(Path(tmp) / "x.o")]
+            err = subprocess.run(cmd, capture_output=True, text=True).stderr.splitlines()
+            name, frame = None, None
+            for i, line in enumerate(err):
+                m = re.search(r"Function properties for (\S+)", line)
+                if m:
+                    name = m.group(1)
+                    frame = err[i + 1] if i + 1 < len(err) else ""
+                    continue
+                m = re.search(r"Used (\d+) registers", line)
+                if m and name and name.startswith("_Z"):
+                    st = re.search(r"(\d+) bytes stack frame, (\d+) bytes spill stores, "
+                                   r"(\d+) bytes spill loads", frame or "")
+                    demangled = subprocess.run(["c++filt", name], capture_output=True,
+                                               text=True).stdout.strip().replace("cusr::", "")
+                    if st:
+                        rows.append(f"| {src} | `{demangled}` | {m.group(1)} | {st.group(1)} | "
+                                    f"{st.group(2)}/{st.group(3)} |")
+                    name = None
+    head = ["| file | kernel | registers | stack B | spill st/ld B |", "|---|---|---|---|---|"]
+    return "\n".join(head + rows)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -120,10 +154,15 @@ def main() -> None:
                     help="extra preprocessor define of a variant build (e.g. CUSR_IEEE_F32: the "
                          "fp32 interpreter with the accurate library transcendentals instead "
                          "of the SFU arithmetic); needs --lib")
+    ap.add_argument("--ptxas-report", action="store_true",
+                    help="print every kernel's registers / stack / spills (ptxas -v) and exit")
     ap.add_argument("--lib", default=None,
                     help="output path of a variant library (objects beside it in _build/); "
                          "the in-tree library and its aliases are left as they are")
     a = ap.parse_args()
+    if a.ptxas_report:
+        print(ptxas_report())
+        return
     if a.define and not a.lib:
         ap.error("--define builds a variant: give --lib")
     lib = Path(a.lib).resolve() if a.lib else None
