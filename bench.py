@@ -320,13 +320,14 @@ def run_reference(args, world: int, rank: int) -> None:
 
 
 def parity_mode(co, pop: dict) -> dict:
-    """The parity-grade fit (cusr_b200.multistart defaults: 96 trust-region starts per tree on
-    the device, two waves, fp64, trust-region polish): fits/s on a
+    """The parity-grade fit (cusr_b200.multistart defaults, co_inproc.PARITY: 128 trust-region
+    starts per tree explored in fp32 on the device, two waves, fp64 polish from 16 starts
+    around each tree's best): fits/s on a
     2,048-tree stratified slice of the metric population (device time of the multi-start call
     plus the polish call), and the north-star fraction — fp64 loss within 1e-6 of, or better
     than, the reference scipy fit — on the 256-tree scipy sample of the same population
     (tests/golden/metric_scipy.npz, made by the reference's ScipyPop). `fast`: the same for
-    co_inproc.PARITY_FAST (fp32 exploration, fp64 polish)."""
+    co_inproc.PARITY_FAST (single-start polish)."""
     from cusr_b200 import co_inproc, multistart, popio
 
     sub = popio.slice_pop(pop, np.unique(np.linspace(0, int(pop["M"]) - 1, 2048).astype(np.int64)))
@@ -358,12 +359,14 @@ def parity_mode(co, pop: dict) -> dict:
                 "trees": int(sub["M"]), "device_ms": ms}
 
     out = measure(multistart.preset_kwargs(co_inproc.PARITY))
-    out.update(dtype="f64", note="the parity-grade mode (co_inproc.PARITY: 96 device-side "
-               "trust-region starts, fp64) on a 2,048-tree slice of the metric population; the "
-               "fraction on the 256-tree reference scipy sample of that population")
+    out.update(dtype="f32 starts, f64 polish", note="the parity-grade mode (co_inproc.PARITY: "
+               "128 device-side trust-region starts explored in fp32, then each tree's best "
+               "polished in fp64 from 16 starts around it) on a 2,048-tree slice of the metric "
+               "population; the fraction on the 256-tree reference scipy sample of that "
+               "population")
     fast = measure(multistart.preset_kwargs(co_inproc.PARITY_FAST))
-    fast.update(dtype="f32 starts, f64 polish", note="co_inproc.PARITY_FAST: 128 trust-region "
-                "starts in fp32 (50 evaluations), then the fp64 trust-region polish")
+    fast.update(dtype="f32 starts, f64 polish", note="co_inproc.PARITY_FAST: the same with a "
+                "single-start fp64 polish")
     out["fast"] = fast
     return out
 

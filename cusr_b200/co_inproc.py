@@ -250,23 +250,28 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
     return opt
 
 
-# The parity-grade fit: every tree fitted from 96 starts in one device batch, all with the
-# trust-region LM of the reference's scipy backend, in two waves (trees whose first 8 fits
-# agree skip the other 88), fp64, scipy's tolerances, then a trust-region polish of each
-# tree's best fit; the lowest final loss is kept. (Measured on the metric, mid and long scipy
-# samples: trust-region starts reach the reference fit more often than reference-schedule
-# starts and cost less; 96 of them cost what 16 + 48 mixed starts did.)
+# The parity-grade fit, in two device calls: every tree's 128 starts explored at once with the
+# trust-region LM of the reference's scipy backend in fp32 (50 evaluations, ftol = xtol = 1e-6,
+# two waves: trees whose first 8 fits agree skip the rest), then each tree's best fit polished
+# in fp64 with scipy's tolerances (200 evaluations) from 16 starts around it (the best itself
+# and 15 perturbations of it); the lower final loss is kept. Measured on the eight scipy
+# samples (about 800 trees): 7 trees not within 1e-6 of the reference fit, against 8 for 96
+# fp64 starts (PARITY_FP64) at 2.3 times its device time.
 PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
-              algorithm="trust_region", n_starts=96, tr_starts=96, wave1=8, ftol=1e-10,
-              gtol=1e-8, polish=True)
+              algorithm="trust_region", n_starts=128, tr_starts=128, wave1=8, ftol=1e-10,
+              gtol=1e-8, polish=True, explore_precision="fp32", explore_max_iter=50,
+              explore_tol=1e-6, polish_starts=16)
 
-# The fast parity-grade fit: the same trust-region start axis with 128 starts explored in
-# fp32 (50 evaluations, ftol = xtol = 1e-6), then the fp64 trust-region polish of each tree's
-# best (200 evaluations, scipy's tolerances). Measured on the scipy samples: about five times
-# faster than PARITY, the same north-star fraction on the metric sample, a few more divergent
-# trees on the mid / long grammars.
-PARITY_FAST = dict(PARITY, n_starts=128, tr_starts=128, explore_precision="fp32",
-                   explore_max_iter=50, explore_tol=1e-6)
+# The same with a single-start polish: half the device time of PARITY, 12 of about 800 trees
+# off the reference fit.
+PARITY_FAST = dict(PARITY, polish_starts=1)
+
+# Every stage in fp64: 96 trust-region starts (200 evaluations, scipy's tolerances), then a
+# single-start polish of each tree's best.
+PARITY_FP64 = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
+                   algorithm="trust_region", n_starts=96, tr_starts=96, wave1=8, ftol=1e-10,
+                   gtol=1e-8, polish=True, explore_precision=None, explore_max_iter=None,
+                   explore_tol=None, polish_starts=1)
 
 
 class InProcessCO:

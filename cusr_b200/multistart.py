@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from .co_inproc import PARITY, PARITY_FAST
+from .co_inproc import PARITY
 
 KINDS = ("scale", "shift", "fresh1", "fresh3")   # start kinds after c_init, cycled
 
@@ -71,8 +71,9 @@ def start_points(pop: dict, starts: int, seed: int = 0) -> np.ndarray:
     return v.astype(np.float32)
 
 
-def preset_kwargs(preset: dict = PARITY_FAST) -> dict:
-    """fit_multistart keyword arguments of a preset dict (co_inproc.PARITY / PARITY_FAST)."""
+def preset_kwargs(preset: dict = PARITY) -> dict:
+    """fit_multistart keyword arguments of a preset dict (co_inproc.PARITY, PARITY_FAST,
+    PARITY_FP64)."""
     return {("starts" if k == "n_starts" else k): v for k, v in preset.items() if k != "algorithm"}
 
 
@@ -81,9 +82,11 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
                    precision: str = PARITY["precision"], seed: int = 0,
                    damping_floor: float = PARITY["damping_floor"],
                    tr_starts: int = PARITY["tr_starts"], wave1: int = PARITY["wave1"],
-                   polish: bool = PARITY["polish"], explore_precision: str | None = None,
-                   explore_max_iter: int | None = None, explore_tol: float | None = None,
-                   **kw) -> dict:
+                   polish: bool = PARITY["polish"],
+                   explore_precision: str | None = PARITY["explore_precision"],
+                   explore_max_iter: int | None = PARITY["explore_max_iter"],
+                   explore_tol: float | None = PARITY["explore_tol"],
+                   polish_starts: int = PARITY["polish_starts"], **kw) -> dict:
     """Fit every tree of `pop` from `starts` starting points (the first is its c_init) in one
     device call (InProcessCO.optimize_ex with n_starts) and return the best start's
     c_final / status / loss_init / loss_final / iters with its index ('start').
@@ -93,7 +96,9 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     explore_precision / explore_max_iter / explore_tol: run the multi-start call in another
     precision (e.g. "fp32": about five times faster), with its own evaluation budget and
     ftol = xtol; the polish then runs in `precision` with max_iter / xtol and its result is
-    kept wherever it is finite and no worse (co_inproc.PARITY_FAST).
+    kept wherever it is finite and no worse.
+    polish_starts: the polish call's starts per tree — the best fit itself and perturbations
+    of it (the start kinds of the start axis, around the best).
 
     Defaults: the parity preset (co_inproc.PARITY)."""
     algorithm = "trust_region" if tr_starts > 0 else kw.pop("algorithm", "reference")
@@ -112,9 +117,11 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     again = dict(pop)
     with np.errstate(over="ignore"):            # fits that ran off to huge constants
         again["c_init"] = np.asarray(res["c_final"], np.float32)
+    ps = max(1, int(polish_starts))
     pol = co.optimize_ex(again, max_iter=max_iter, precision=precision, xtol=xtol,
-                         algorithm="trust_region", **{k: v for k, v in kw.items()
-                                                      if k in ("y_shared", "ftol", "gtol")})
+                         algorithm="trust_region", n_starts=ps, tr_starts=ps,
+                         wave1=min(8, ps - 1) if ps > 1 else 0, seed=seed + 1,
+                         **{k: v for k, v in kw.items() if k in ("y_shared", "ftol", "gtol")})
     lp, lr = np.asarray(pol["loss_final"]), np.asarray(res["loss_final"])
     if explore:
         # the polish starts at the explore stage's (float32) constants and only accepts

@@ -78,14 +78,22 @@ def test_parity_preset_reaches_options():
     co_inproc.start_options(opt, **{k: v for k, v in co_inproc.PARITY.items()
                                     if k in ("algorithm", "n_starts", "tr_starts", "wave1",
                                              "ftol", "gtol")})
-    assert opt.algorithm == 1 and opt.n_starts == 96 and opt.tr_starts == 96 and opt.wave1 == 8
+    assert opt.algorithm == 1 and opt.n_starts == 128 and opt.tr_starts == 128 and opt.wave1 == 8
     assert opt.ftol == 1e-10 and opt.gtol == 1e-8
     with pytest.raises(ValueError):
         co_inproc.start_options(opt, algorithm="newton")
 
 
-def test_fast_preset_keywords():
-    kw = multistart.preset_kwargs(co_inproc.PARITY_FAST)
+def test_preset_keywords():
+    kw = multistart.preset_kwargs(co_inproc.PARITY)
     assert kw["starts"] == 128 and kw["tr_starts"] == 128 and "algorithm" not in kw
     assert kw["explore_precision"] == "fp32" and kw["precision"] == "fp64"
-    assert multistart.preset_kwargs(co_inproc.PARITY)["starts"] == co_inproc.PARITY["n_starts"]
+    assert kw["polish_starts"] == 16
+    assert multistart.preset_kwargs(co_inproc.PARITY_FAST)["polish_starts"] == 1
+    fp64 = multistart.preset_kwargs(co_inproc.PARITY_FP64)
+    assert fp64["starts"] == 96 and fp64["explore_precision"] is None
+    # every preset key is a fit_multistart parameter
+    import inspect
+    params = inspect.signature(multistart.fit_multistart).parameters
+    for p in (co_inproc.PARITY, co_inproc.PARITY_FAST, co_inproc.PARITY_FP64):
+        assert set(multistart.preset_kwargs(p)) <= set(params) | {"ftol", "gtol"}
