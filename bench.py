@@ -368,6 +368,11 @@ def parity_mode(co, pop: dict) -> dict:
     fast.update(dtype="f32 starts, f64 polish", note="co_inproc.PARITY_FAST: the same with a "
                 "single-start fp64 polish")
     out["fast"] = fast
+    top = measure(multistart.preset_kwargs(co_inproc.PARITY_MAX))
+    top.update(dtype="f32 starts, f64 polish, dd-f64 starts", note="co_inproc.PARITY_MAX: "
+               "PARITY and 16 fp64 trust-region starts from c_init on double-double normal "
+               "equations")
+    out["max"] = top
     return out
 
 

@@ -105,7 +105,7 @@ class CoOptions(ctypes.Structure):
         ("ftol", ctypes.c_double), ("gtol", ctypes.c_double), ("agree_tol", ctypes.c_double),
         ("start_seed", ctypes.c_uint64), ("fd_ordering", ctypes.c_int32),
         ("n_devices", ctypes.c_int32), ("device_ids", ctypes.c_int32 * 8),
-        ("reserved", ctypes.c_int32 * 2),
+        ("tr_dd", ctypes.c_int32), ("reserved", ctypes.c_int32),
     ]
 
 
@@ -226,7 +226,7 @@ def build_header(pop: dict) -> PopHeader:
 
 def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 1,
                   tr_starts: int = 0, wave1: int = 0, ftol: float = 1e-10, gtol: float = 1e-8,
-                  agree_tol: float = 1e-7, seed: int = 0) -> CoOptions:
+                  agree_tol: float = 1e-7, seed: int = 0, tr_dd: bool = False) -> CoOptions:
     """Fill the algorithm / start-axis fields of `opt`:
       algorithm  'reference' (the reference LM schedule) | 'trust_region' (MINPACK lmder: max_iter
                  then counts function evaluations, the first included, like scipy's max_nfev)
@@ -235,7 +235,8 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
                  schedule (alternately with the floored damping on every solve)
       wave1      0 < wave1 < n_starts: run starts 0..wave1-1 first, then the rest only for trees
                  whose first-wave fits do not agree within agree_tol
-      ftol, gtol trust-region tolerances; seed: start points"""
+      ftol, gtol trust-region tolerances; seed: start points
+      tr_dd      trust-region fits (fp64) with double-double normal equations"""
     try:
         opt.algorithm = ALGORITHMS[algorithm]
     except KeyError:
@@ -247,6 +248,7 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
     opt.gtol = float(gtol)
     opt.agree_tol = float(agree_tol)
     opt.start_seed = int(seed) & (2 ** 64 - 1)
+    opt.tr_dd = 1 if tr_dd else 0
     return opt
 
 
@@ -260,18 +262,23 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
 PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
               algorithm="trust_region", n_starts=128, tr_starts=128, wave1=8, ftol=1e-10,
               gtol=1e-8, polish=True, explore_precision="fp32", explore_max_iter=50,
-              explore_tol=1e-6, polish_starts=16)
+              explore_tol=1e-6, polish_starts=16, dd_starts=0)
 
 # The same with a single-start polish: half the device time of PARITY, 12 of about 800 trees
 # off the reference fit.
 PARITY_FAST = dict(PARITY, polish_starts=1)
+
+# PARITY and a third call: 16 fp64 trust-region starts from c_init on double-double normal
+# equations (CoOptions.tr_dd). On the eight scipy samples 5 trees off the reference fit
+# (PARITY 9) at 3.4 times PARITY's device time.
+PARITY_MAX = dict(PARITY, dd_starts=16)
 
 # Every stage in fp64: 96 trust-region starts (200 evaluations, scipy's tolerances), then a
 # single-start polish of each tree's best.
 PARITY_FP64 = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
                    algorithm="trust_region", n_starts=96, tr_starts=96, wave1=8, ftol=1e-10,
                    gtol=1e-8, polish=True, explore_precision=None, explore_max_iter=None,
-                   explore_tol=None, polish_starts=1)
+                   explore_tol=None, polish_starts=1, dd_starts=0)
 
 
 class InProcessCO:

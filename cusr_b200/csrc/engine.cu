@@ -76,7 +76,8 @@ struct Ctx {
     DBuf c, ctry, delta, cinit_f, lam, loss, loss_init, status, iters, pending, n_run, n_eval;
     DBuf partials, blk;
     DBuf c64, l64, n_rev;
-    DBuf vals, jac;
+    DBuf vals, jac;            // per-sample values / Jacobians (co_evaluate; tr_dd fits)
+    DBuf dd_g, dd_blk;         // double-double sums of a pass / accepted blocks (tr_dd fits)
     // start axis and trust-region state (per fit), tree-level inputs and outputs
     DBuf c_tree, tree_coff, imode, tr, diag, outer, resolved, n_retired;
     DBuf out_c, out_status, out_li, out_lf, out_iters, out_start;
@@ -486,6 +487,8 @@ int sync_stream(Ctx *ctx, bool sharded) {
 
 // chunks per tree from which the step's chunk sums run as their own block-parallel kernel
 constexpr int64_t PRESUM_CHUNKS = 64;
+// largest per-sample Jacobian kept for double-double trust-region fits (fits x K_max x N x 8 B)
+constexpr double DD_JAC_MAX_BYTES = 64.0 * (1 << 30);
 
 // Per-tree sums of the chunk partials into ctx->red (chunk_sum_kernel).
 template <typename T>
@@ -573,6 +576,17 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     const int tr_fits = opt.tr_starts > 0 ? std::min(opt.tr_starts, S)
                                           : (opt.algorithm == CO_ALG_TRUST_REGION ? S : 0);
     const bool has_tr = tr_fits > 0, has_ref = tr_fits < S;
+    // trust-region fits in double-double: per-sample values and Jacobians stay on the device
+    const bool tr_dd = fp64 && has_tr && opt.tr_dd != 0;
+    const int dd_kmax = std::max(h->K_max, 1);
+    if (tr_dd) {
+        const double jac_bytes = (double)M_fit * dd_kmax * h->N * sizeof(double);
+        if (jac_bytes > DD_JAC_MAX_BYTES) return CO_ERR_BOUNDS;
+        GROW(ctx->vals, (size_t)M_fit * h->N * sizeof(double));
+        GROW(ctx->jac, (size_t)M_fit * dd_kmax * h->N * sizeof(double));
+        GROW(ctx->dd_g, 2 * (size_t)sc.block_elems * sizeof(double));
+        GROW(ctx->dd_blk, 2 * (size_t)sc.block_elems * sizeof(double));
+    }
     const int wave1 = (S > 1 && opt.wave1 > 0 && opt.wave1 < S) ? opt.wave1 : 0;
     if (sharded && has_tr) return CO_ERR_NULLARG;   // sample-sharded fits: reference schedule
     CK(cudaEventRecord(ctx->ev_fit[0], s));
@@ -586,6 +600,7 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         ip.wave1 = wave1;
         ip.tr_starts = tr_fits;
         ip.damp_alternate = (S > 1 && opt.damping_floor > 0.0) ? 1 : 0;
+        ip.tr_dd = tr_dd ? 1 : 0;
         ip.seed = opt.start_seed;
         ip.lam0 = (T)opt.lambda0;
         ip.c_start = P<float>(ctx->cinit_f);
@@ -611,23 +626,29 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
 
     // ---- step-kernel launch geometry ----
     const size_t step_smem = (size_t)STEP_WARPS * STEP_WARP_D * sizeof(double);
-    const size_t tr_smem = (size_t)TR_WARPS * TR_WARP_D * sizeof(double);
+    const size_t tr_smem = (size_t)(TR_THREADS / 32) * TR_WARP_D * sizeof(double);
+    const size_t tr_smem_dd = (size_t)(TR_THREADS_DD / 32) * TR_WARP_D * sizeof(DD);
     if (!ctx->step_attr_set[fp64 ? 1 : 0]) {
         CK(cudaFuncSetAttribute(lm_step_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)step_smem));
-        CK(cudaFuncSetAttribute(lm_tr_step_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)tr_smem));
+        CK(cudaFuncSetAttribute(lm_tr_step_kernel_s<T, double>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tr_smem));
+        if constexpr (sizeof(T) == 8)
+            CK(cudaFuncSetAttribute(lm_tr_step_kernel_s<double, DD>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tr_smem_dd));
         ctx->step_attr_set[fp64 ? 1 : 0] = true;
     }
     int step_occ = 0, tr_occ = 0;
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&step_occ, lm_step_kernel<T>, STEP_THREADS,
                                                      step_smem));
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&tr_occ, lm_tr_step_kernel<T>, TR_THREADS,
-                                                     tr_smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&tr_occ, lm_tr_step_kernel_s<T, double>,
+                                                     TR_THREADS, tr_smem));
     const int step_grid = std::max(1, std::min((M_fit + STEP_WARPS - 1) / STEP_WARPS,
                                                std::max(1, step_occ) * ctx->sm_count));
     const int tr_grid = std::max(1, std::min((M_fit + TR_WARPS - 1) / TR_WARPS,
                                              std::max(1, tr_occ) * ctx->sm_count));
+    const int tr_grid_dd = std::max(1, std::min((M_fit + 1) / 2, 2 * ctx->sm_count));
+    const int ddg_grid = std::max(1, std::min(M_fit, 8 * ctx->sm_count));
 
     StepParams<T> sp;
     sp.desc = P<TreeDesc>(ctx->desc);
@@ -675,6 +696,22 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
     tp.xtol = opt.xtol;
     tp.gtol = opt.gtol;
     tp.factor = 100.0;
+    tp.ddg = tr_dd ? P<double>(ctx->dd_g) : nullptr;
+    tp.blk_dd = tr_dd ? P<double>(ctx->dd_blk) : nullptr;
+    // double-double fits: the pass also writes per-sample values and Jacobians, from which
+    // dd_gram_kernel forms their normal equations
+    T *dd_vals = tr_dd ? P<T>(ctx->vals) : nullptr;
+    T *dd_jac = tr_dd ? P<T>(ctx->jac) : nullptr;
+    auto dd_gram = [&]() -> int {
+        if (!tr_dd) return CO_OK;
+        dd_gram_kernel<<<ddg_grid, DDG_THREADS, 0, s>>>(
+            P<TreeDesc>(ctx->desc), M_fit, P<uint8_t>(ctx->imode), P<int32_t>(ctx->status),
+            P<int32_t>(ctx->pending), P<double>(ctx->vals), P<double>(ctx->jac), dd_kmax,
+            P<float>(ctx->ym), h->N, P<double>(ctx->dd_g));
+        CK(cudaGetLastError());
+        st.kernel_launches++;
+        return CO_OK;
+    };
 
     // passes: one per LM iteration (reference) / per function evaluation after the first
     // (trust region); a second wave can start as late as the first wave's last pass
@@ -698,9 +735,16 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         }
         if (has_tr) {
             tp.n_running = n_running;
-            lm_tr_step_kernel<T><<<tr_grid, TR_THREADS, tr_smem, s>>>(tp);
+            lm_tr_step_kernel_s<T, double><<<tr_grid, TR_THREADS, tr_smem, s>>>(tp);
             CK(cudaGetLastError());
             st.kernel_launches++;
+            if constexpr (sizeof(T) == 8) {
+                if (tr_dd) {
+                    lm_tr_step_kernel_s<double, DD><<<tr_grid_dd, TR_THREADS_DD, tr_smem_dd, s>>>(tp);
+                    CK(cudaGetLastError());
+                    st.kernel_launches++;
+                }
+            }
         }
         if (wave1) {
             waves_kernel<T><<<grid_for(ctx, M), 256, 0, s>>>(
@@ -720,8 +764,10 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
 
     // ---- initial pass at the start points + solve of iteration 0 ----
     size_t e0 = ev_i; rec();
-    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true, nullptr,
-                        nullptr, 0, P<uint8_t>(ctx->imode));
+    rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->c), P<T>(ctx->partials), *h, ldx, true, dd_vals,
+                        dd_jac, tr_dd ? dd_kmax : 0, P<uint8_t>(ctx->imode));
+    if (rc) return rc;
+    rc = dd_gram();
     if (rc) return rc;
     size_t e1 = ev_i; rec();
     eval_spans.push_back({e0, e1});
@@ -764,7 +810,9 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
         iters_run++;
         size_t a = ev_i; rec();
         rc = launch_pass<T>(ctx, sc, pk, P<T>(ctx->ctry), P<T>(ctx->partials), *h, ldx, true,
-                            nullptr, nullptr, 0, P<uint8_t>(ctx->imode));
+                            dd_vals, dd_jac, tr_dd ? dd_kmax : 0, P<uint8_t>(ctx->imode));
+        if (rc) return rc;
+        rc = dd_gram();
         if (rc) return rc;
         size_t b = ev_i; rec();
         eval_spans.push_back({a, b});
@@ -1078,6 +1126,7 @@ static bool valid_fit_options(const CoOptions &o) {
     return o.lambda0 > 0.0 && o.xtol >= 0.0 && o.ftol >= 0.0 && o.gtol >= 0.0 &&
            o.agree_tol >= 0.0 && o.n_starts >= 0 && o.n_starts <= CO_MAX_STARTS &&
            o.tr_starts >= 0 && o.wave1 >= 0 &&
+           (o.tr_dd == 0 || (o.tr_dd == 1 && o.precision == CO_PREC_FP64)) &&
            (o.algorithm == CO_ALG_REFERENCE || o.algorithm == CO_ALG_TRUST_REGION);
 }
 
@@ -1586,6 +1635,7 @@ void co_teardown(void *handle) {
                     &ctx->cinit_f, &ctx->lam, &ctx->loss, &ctx->loss_init, &ctx->status,
                     &ctx->iters, &ctx->pending, &ctx->n_run, &ctx->n_eval, &ctx->partials, &ctx->blk,
                     &ctx->c64, &ctx->l64, &ctx->n_rev, &ctx->vals, &ctx->jac, &ctx->red,
+                    &ctx->dd_g, &ctx->dd_blk,
                     &ctx->c_tree, &ctx->tree_coff, &ctx->imode, &ctx->tr, &ctx->diag,
                     &ctx->outer, &ctx->resolved, &ctx->n_retired, &ctx->out_c,
                     &ctx->out_status, &ctx->out_li, &ctx->out_lf, &ctx->out_iters,

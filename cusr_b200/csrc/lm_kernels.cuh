@@ -45,6 +45,9 @@ struct StepParams {
 // skipped here), and the floored damping on every solve for a reference-schedule fit
 constexpr uint8_t IM_TR = 1;
 constexpr uint8_t IM_DAMP_ALWAYS = 2;
+// a trust-region fit whose normal equations are formed and factored in double-double
+// (dd_gram_kernel, lm_tr_step_kernel_dd): fp64 fits with CoOptions.tr_dd
+constexpr uint8_t IM_TR_DD = 8;
 
 constexpr int STEP_THREADS = 256;
 constexpr int STEP_WARPS = STEP_THREADS / 32;

@@ -45,6 +45,7 @@ struct StartsParams {
     const float *c_tree;       // the caller's c_init (per tree)
     int M_fit, S, wave1, tr_starts;
     int damp_alternate;        // reference fits alternate the floored damping on every solve
+    int tr_dd;                 // trust-region fits take double-double normal equations
     uint64_t seed;
     T lam0;
     float *c_start;            // per fit constant: the start point (the audit's c_init)
@@ -80,7 +81,7 @@ __global__ void init_starts_kernel(const StartsParams<T> p) {
             p.diag[d.c_off + k] = 1.0;
         }
         uint8_t mode = 0;
-        if (s < p.tr_starts) mode = IM_TR | IM_SENTINEL;
+        if (s < p.tr_starts) mode = IM_TR | IM_SENTINEL | (p.tr_dd ? IM_TR_DD : 0);
         else if (p.damp_alternate && ((s - p.tr_starts) & 1)) mode = IM_DAMP_ALWAYS;
         p.imode[i] = mode;
         const bool first = p.wave1 <= 0 || s < p.wave1;

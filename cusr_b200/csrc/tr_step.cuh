@@ -48,33 +48,40 @@ struct TrParams {
     int *n_running;
     int max_nfev;        // evaluations per fit, the initial one included
     double ftol, xtol, gtol, factor;
+    const double *ddg = nullptr;   // double-double sums of the pass (dd_gram_kernel), or null
+    double *blk_dd = nullptr;      // double-double block at the accepted point (IM_TR_DD fits)
 };
 
 constexpr int TR_THREADS = 128;
 constexpr int TR_WARPS = TR_THREADS / 32;
-// per warp: A, W (K x K, full symmetric), the summed block (561 values, as doubles)
+constexpr int TR_THREADS_DD = 64;     // the double-double variant: twice the shared memory
+// per warp, in scalars S: A, W (K x K, full symmetric), the summed block (561 values)
 constexpr int TR_WARP_D = 2 * CO_MAX_K * WL_LD + 576;
+template <typename S> __host__ __device__ constexpr int tr_threads() {
+    return sizeof(S) == 8 ? TR_THREADS : TR_THREADS_DD;
+}
 
 // Symmetrically pivoted Cholesky of W = A (full, lanes own rows): at step b the largest
 // remaining diagonal is the pivot perm[b]; the column values l_i are kept in W[i][perm[b]].
 // Returns the rank r (pivots taken before the first non-positive one).
-__device__ int tr_pchol(double *W, int K, int lane, int *perm) {
+template <typename S>
+__device__ int tr_pchol(S *W, int K, int lane, int *perm) {
     bool done = lane >= K;
     int r = 0;
     for (int b = 0; b < K; ++b) {
         __syncwarp();
-        double v = done ? -1.0 : W[lane * WL_LD + lane];
+        S v = done ? S(-1.0) : W[lane * WL_LD + lane];
         int p = lane;
         // argmax with ties to the lower index: every lane ends with the same (v, p)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const double v2 = __shfl_xor_sync(0xffffffffu, v, o);
+            const S v2 = shfl_xor(v, o);
             const int p2 = __shfl_xor_sync(0xffffffffu, p, o);
             if (v2 > v || (v2 == v && p2 < p)) { v = v2; p = p2; }
         }
-        if (!(v > 0.0)) break;
-        const double lpp = sqrt(v);
-        double li = 0.0;
+        if (!(v > S(0.0))) break;
+        const S lpp = sqrt(v);
+        S li = S(0.0);
         if (!done && lane != p) li = W[lane * WL_LD + p] / lpp;
         __syncwarp();
         if (!done && lane != p) W[lane * WL_LD + p] = li;
@@ -83,7 +90,7 @@ __device__ int tr_pchol(double *W, int K, int lane, int *perm) {
         // trailing update of the rows and columns still remaining
         const bool act = !done;
         for (int k = 0; k < K; ++k) {
-            const double lk = __shfl_sync(0xffffffffu, li, k);
+            const S lk = shfl(li, k);
             const int dk = __shfl_sync(0xffffffffu, (int)done, k);
             if (act && !dk) W[lane * WL_LD + k] -= li * lk;
         }
@@ -96,48 +103,50 @@ __device__ int tr_pchol(double *W, int K, int lane, int *perm) {
 // Gauss-Newton step on the pivoted factor: x = -(A^+) g on the r independent columns,
 // 0 on the others (lane i holds g_i, returns x_i). Lanes work in pivot order: lane a takes
 // row perm[a]; L[a][k] = W[perm[a]][perm[k]].
-__device__ double tr_gn_step(const double *W, int r, int lane, const int *perm, double g) {
+template <typename S>
+__device__ S tr_gn_step(const S *W, int r, int lane, const int *perm, S g) {
     const int pa = lane < r ? perm[lane] : 0;
-    double b = __shfl_sync(0xffffffffu, -g, pa);
-    if (lane >= r) b = 0.0;
-    double y = 0.0;
+    S b = shfl(-g, pa);
+    if (lane >= r) b = S(0.0);
+    S y = S(0.0);
     for (int k = 0; k < r; ++k) {          // forward: L y = b
         const int pk = perm[k];
-        double yk = 0.0;
+        S yk = S(0.0);
         if (lane == k) yk = b / W[pk * WL_LD + pk];
-        yk = __shfl_sync(0xffffffffu, yk, k);
+        yk = shfl(yk, k);
         if (lane == k) y = yk;
         if (lane > k && lane < r) b -= W[pa * WL_LD + pk] * yk;
     }
-    double z = 0.0;
+    S z = S(0.0);
     for (int k = r - 1; k >= 0; --k) {     // back: L^T z = y
         const int pk = perm[k];
-        double zk = 0.0;
+        S zk = S(0.0);
         if (lane == k) zk = y / W[pk * WL_LD + pk];
-        zk = __shfl_sync(0xffffffffu, zk, k);
+        zk = shfl(zk, k);
         if (lane == k) z = zk;
         if (lane < k) y -= W[pk * WL_LD + pa] * zk;
     }
     // back to the original order: lane i takes z of the pivot position holding i
-    double x = 0.0;
+    S x = S(0.0);
     for (int a = 0; a < r; ++a) {
-        const double za = __shfl_sync(0xffffffffu, z, a);
+        const S za = shfl(z, a);
         if (lane == perm[a]) x = za;
     }
     return x;
 }
 
 // forward solve with the full-rank pivoted factor (L w = v[perm]), returns |w|
-__device__ double tr_pfsub_norm(const double *W, int K, int lane, const int *perm, double v) {
+template <typename S>
+__device__ double tr_pfsub_norm(const S *W, int K, int lane, const int *perm, S v) {
     const int pa = lane < K ? perm[lane] : 0;
-    double b = __shfl_sync(0xffffffffu, v, pa);
-    if (lane >= K) b = 0.0;
-    double w = 0.0;
+    S b = shfl(v, pa);
+    if (lane >= K) b = S(0.0);
+    S w = S(0.0);
     for (int k = 0; k < K; ++k) {
         const int pk = perm[k];
-        double wk = 0.0;
+        S wk = S(0.0);
         if (lane == k) wk = b / W[pk * WL_LD + pk];
-        wk = __shfl_sync(0xffffffffu, wk, k);
+        wk = shfl(wk, k);
         if (lane == k) w = wk;
         if (lane > k && lane < K) b -= W[pa * WL_LD + pk] * wk;
     }
@@ -145,26 +154,28 @@ __device__ double tr_pfsub_norm(const double *W, int K, int lane, const int *per
 }
 
 // W = A + par diag(d^2), rows owned by lanes
-__device__ __forceinline__ void tr_load(double *W, const double *A, int K, int lane, double par,
+template <typename S>
+__device__ __forceinline__ void tr_load(S *W, const S *A, int K, int lane, double par,
                                         double d) {
     if (lane < K) {
         for (int k = 0; k < K; ++k) W[lane * WL_LD + k] = A[lane * WL_LD + k];
-        W[lane * WL_LD + lane] += par * d * d;
+        W[lane * WL_LD + lane] += S(par * d * d);
     }
     __syncwarp();
 }
 
 // The LM parameter and step for trust radius delta (MINPACK lmpar, on normal equations).
 // Lane i holds g_i = (J^T f)_i and d_i; returns x_i (the step) and updates par.
-__device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lane, double g,
-                           double d, double delta, double &par) {
+template <typename S>
+__device__ S tr_lmpar(const S *A, S *W, int *perm, int K, int lane, S g, double d,
+                      double delta, double &par) {
     const double dwarf = DBL_MIN;
     // Gauss-Newton direction
     tr_load(W, A, K, lane, 0.0, d);
     const int r = tr_pchol(W, K, lane, perm);
-    double x = r > 0 ? tr_gn_step(W, r, lane, perm, g) : 0.0;
-    if (lane >= K) x = 0.0;
-    double dxnorm = wl_norm(d * x);
+    S x = r > 0 ? tr_gn_step(W, r, lane, perm, g) : S(0.0);
+    if (lane >= K) x = S(0.0);
+    double dxnorm = wl_norm(S(d) * x);
     double fp = dxnorm - delta;
     if (fp <= 0.1 * delta) {
         par = 0.0;
@@ -173,12 +184,12 @@ __device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lan
     // lower bound (J of full rank): the Newton step of 1/|Dx| - 1/delta at par = 0
     double parl = 0.0;
     if (r == K) {
-        const double v = lane < K ? d * (d * x) / dxnorm : 0.0;
+        const S v = lane < K ? S(d) * (S(d) * x) / S(dxnorm) : S(0.0);
         const double t = tr_pfsub_norm(W, K, lane, perm, v);
         parl = ((fp / delta) / t) / t;
     }
     // upper bound
-    const double gnorm = wl_norm(lane < K ? g / d : 0.0);
+    const double gnorm = wl_norm(lane < K ? g / S(d) : S(0.0));
     double paru = gnorm / delta;
     if (paru == 0.0) paru = dwarf / fmin(delta, 0.1);
     par = fmax(par, parl);
@@ -191,21 +202,21 @@ __device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lan
         // scale of J^T J) is factored with par raised until it is positive definite
         int guard = 0;
         while (!wl_chol(W, K, lane) && guard < 64) {
-            const double amax = wl_max(lane < K ? fabs(A[lane * WL_LD + lane]) : 0.0);
+            const double amax = to_double(wl_max(lane < K ? fabs(A[lane * WL_LD + lane]) : S(0.0)));
             const double dmin = -wl_max(lane < K ? -(d * d) : -DBL_MAX);
             par = fmax(fmax(2.0 * par, 1e-15 * amax / dmin), dwarf);
             tr_load(W, A, K, lane, par, d);
             ++guard;
         }
-        const double y = wl_fsub(W, K, lane, lane < K ? -g : 0.0);
+        const S y = wl_fsub(W, K, lane, lane < K ? -g : S(0.0));
         x = wl_bsub(W, K, lane, y);
-        if (lane >= K) x = 0.0;
-        dxnorm = wl_norm(d * x);
+        if (lane >= K) x = S(0.0);
+        dxnorm = wl_norm(S(d) * x);
         const double temp = fp;
         fp = dxnorm - delta;
         if (fabs(fp) <= 0.1 * delta || (parl == 0.0 && fp <= temp && temp < 0.0) || iter == 10)
             return x;
-        const double v = lane < K ? d * (d * x) / dxnorm : 0.0;
+        const S v = lane < K ? S(d) * (S(d) * x) / S(dxnorm) : S(0.0);
         const double t = wl_norm(wl_fsub(W, K, lane, v));
         const double parc = ((fp / delta) / t) / t;
         if (fp > 0.0) parl = fmax(parl, par);
@@ -214,32 +225,41 @@ __device__ double tr_lmpar(const double *A, double *W, int *perm, int K, int lan
     }
 }
 
-// One trust-region step for every running fit of mode IM_TR whose trial was evaluated.
-template <typename T>
-__global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T> p) {
+// One trust-region step for every running fit of mode IM_TR whose trial was evaluated. S is
+// the scalar of the normal equations: double (lm_tr_step_kernel), or double-double for the
+// IM_TR_DD fits (lm_tr_step_kernel_dd: sums from dd_gram_kernel, accepted block in blk_dd).
+template <typename T, typename S>
+__global__ void __launch_bounds__(tr_threads<S>()) lm_tr_step_kernel_s(const TrParams<T> p) {
+    constexpr bool DDM = sizeof(S) == 16;
+    constexpr int NWARP = tr_threads<S>() / 32;
     extern __shared__ double tr_sm[];
-    __shared__ int s_perm[TR_WARPS][CO_MAX_K];
+    __shared__ int s_perm[NWARP][CO_MAX_K];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    double *A = tr_sm + warp * TR_WARP_D;
-    double *W = A + CO_MAX_K * WL_LD;
-    double *sums = W + CO_MAX_K * WL_LD;
+    S *A = reinterpret_cast<S *>(tr_sm) + warp * TR_WARP_D;
+    S *W = A + CO_MAX_K * WL_LD;
+    S *sums = W + CO_MAX_K * WL_LD;
     int *perm = s_perm[warp];
     const double eps = sizeof(T) == 8 ? DBL_EPSILON : (double)FLT_EPSILON;
-    for (int m = blockIdx.x * TR_WARPS + warp; m < p.M; m += gridDim.x * TR_WARPS) {
-        if (!(p.imode[m] & IM_TR)) continue;
+    for (int m = blockIdx.x * NWARP + warp; m < p.M; m += gridDim.x * NWARP) {
+        const uint8_t mode = p.imode[m];
+        if (!(mode & IM_TR) || ((mode & IM_TR_DD) != 0) != DDM) continue;
         int st = p.status[m];
         if (st != ST_RUNNING || !p.pending[m]) continue;
         const TreeDesc dsc = p.desc[m];
         const int K = dsc.K, P = nblock_size(K), tri = K * (K + 1) / 2;
         for (int e = lane; e < P; e += 32) {
-            const T *src = p.partials + dsc.p_off + e;
-            T s = T(0);
-            for (int ch = 0; ch < dsc.n_chunks; ++ch) s += src[(int64_t)ch * P];
-            sums[e] = (double)s;
+            if constexpr (DDM) {
+                sums[e] = S(p.ddg[2 * (dsc.q_off + e)], p.ddg[2 * (dsc.q_off + e) + 1]);
+            } else {
+                const T *src = p.partials + dsc.p_off + e;
+                T s = T(0);
+                for (int ch = 0; ch < dsc.n_chunks; ++ch) s += src[(int64_t)ch * P];
+                sums[e] = (double)s;
+            }
         }
         __syncwarp();
         double *trs = p.tr + (int64_t)m * TR_FIELDS;
-        const double ssq = sums[P - 1];              // |f_try|^2
+        const double ssq = to_double(sums[P - 1]);   // |f_try|^2
         const T ltry = T(0.5) * (T)ssq;
         const int ne = p.n_eval[m];                  // evaluations before this one
         const bool initial = ne == 0;
@@ -264,15 +284,18 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
             // |J p|^2 = p^T A p with A = the accepted point's J^T J (packed lower in blk)
             const T *bq = p.blk + dsc.q_off;
             const double pk = lane < K ? (double)p.delta[dsc.c_off + lane] : 0.0;
-            double ap = 0.0;
+            S ap = S(0.0);
             for (int l = 0; l < K; ++l) {
                 const double pl = __shfl_sync(0xffffffffu, pk, l);
                 if (lane < K) {
                     const int hi = lane > l ? lane : l, lo = lane > l ? l : lane;
-                    ap += (double)bq[hi * (hi + 1) / 2 + lo] * pl;
+                    const int64_t e = dsc.q_off + hi * (hi + 1) / 2 + lo;
+                    if constexpr (DDM) ap += S(p.blk_dd[2 * e], p.blk_dd[2 * e + 1]) * S(pl);
+                    else ap += S((double)p.blk[e]) * S(pl);
                 }
             }
-            const double jp2 = fmax(wl_sum(pk * ap), 0.0);
+            (void)bq;
+            const double jp2 = fmax(to_double(wl_sum(S(pk) * ap)), 0.0);
             const double actred = (0.1 * fnorm1 < fnorm) ? 1.0 - (fnorm1 / fnorm) * (fnorm1 / fnorm) : -1.0;
             const double t1 = sqrt(jp2) / fnorm, t2 = sqrt(par) * pnorm / fnorm;
             const double prered = t1 * t1 + t2 * t2 / 0.5;
@@ -316,22 +339,32 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
                 st = STATUS_FAIL_NAN;
                 done = true;
             }
-            for (int e = lane; e < P; e += 32) p.blk[dsc.q_off + e] = (T)sums[e];
+            for (int e = lane; e < P; e += 32) {
+                p.blk[dsc.q_off + e] = (T)to_double(sums[e]);
+                if constexpr (DDM) {
+                    p.blk_dd[2 * (dsc.q_off + e)] = sums[e].hi;
+                    p.blk_dd[2 * (dsc.q_off + e) + 1] = sums[e].lo;
+                }
+            }
         }
         __syncwarp();
         if (!done) {
             // current point's J^T J (full) and J^T f, from the accepted block
-            const T *bq = p.blk + dsc.q_off;
+            auto blk_at = [&](int64_t e) -> S {
+                if constexpr (DDM) return S(p.blk_dd[2 * e], p.blk_dd[2 * e + 1]);
+                else return S((double)p.blk[e]);
+            };
             if (lane < K)
                 for (int l = 0; l < K; ++l) {
                     const int hi = lane > l ? lane : l, lo = lane > l ? l : lane;
-                    A[lane * WL_LD + l] = (double)bq[hi * (hi + 1) / 2 + lo];
+                    A[lane * WL_LD + l] = blk_at(dsc.q_off + hi * (hi + 1) / 2 + lo);
                 }
             __syncwarp();
-            const double g = lane < K ? (double)bq[tri + lane] : 0.0;
+            const S g = lane < K ? blk_at(dsc.q_off + tri + lane) : S(0.0);
             if (accept) {
                 // outer iteration: column norms, the scaling, the gradient test
-                const double acn = lane < K ? sqrt(fmax(A[lane * WL_LD + lane], 0.0)) : 0.0;
+                const double acn =
+                    lane < K ? sqrt(fmax(to_double(A[lane * WL_LD + lane]), 0.0)) : 0.0;
                 if (outer == 1) {
                     d = (lane < K && acn != 0.0) ? acn : 1.0;
                     const double cn = lane < K ? d * (double)p.c[dsc.c_off + lane] : 0.0;
@@ -339,7 +372,7 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
                     delta = xnorm != 0.0 ? p.factor * xnorm : p.factor;
                 }
                 double gl = 0.0;
-                if (fnorm != 0.0 && lane < K && acn != 0.0) gl = fabs(g / fnorm) / acn;
+                if (fnorm != 0.0 && lane < K && acn != 0.0) gl = fabs(to_double(g) / fnorm) / acn;
                 gnorm = wl_max(gl);
                 if (gnorm <= p.gtol || gnorm <= eps) {
                     st = STATUS_CONVERGED;
@@ -348,7 +381,7 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
                 d = fmax(d, acn);
             }
             if (!done) {
-                const double x = tr_lmpar(A, W, perm, K, lane, g, d, delta, par);
+                const double x = to_double(tr_lmpar(A, W, perm, K, lane, g, d, delta, par));
                 pnorm = wl_norm(lane < K ? d * x : 0.0);
                 if (outer == 1) delta = fmin(delta, pnorm);
                 if (lane < K) {
@@ -368,6 +401,81 @@ __global__ void __launch_bounds__(TR_THREADS) lm_tr_step_kernel(const TrParams<T
             if (st == ST_RUNNING) atomicAdd(p.n_running, 1);
         }
         __syncwarp();
+    }
+}
+
+}  // namespace cusr
+
+namespace cusr {
+
+// Normal equations of the trust-region fits that take them in double-double (IM_TR_DD), from
+// the pass's per-sample values (vals[fit][N]) and Jacobian (jac[fit][jac_kmax][N], fp64):
+// ddg holds, per fit at its q_off, the packed (K+1) x (K+1) lower triangle of the Gram matrix
+// of [g_0 .. g_{K-1}; r] as (hi, lo) pairs — J^T J, J^T r, sum r^2 — each product exact
+// (dd_two_prod) and the sums double-double. r = f - y with the sentinel convention of the
+// fused pass (a non-finite residual counts as RESIDUAL_SENTINEL and its Jacobian row as 0).
+// One block per fit, its threads over the Gram entries, samples staged through shared memory
+// in tiles; the order of the sums is fixed.
+constexpr int DDG_THREADS = 256;
+constexpr int DDG_TILE = 64;
+constexpr int DDG_LD = DDG_TILE + 1;          // odd row stride: rows read at one column spread
+constexpr int DDG_PER_THREAD = (nblock_size(CO_MAX_K) + DDG_THREADS - 1) / DDG_THREADS;
+
+__global__ void __launch_bounds__(DDG_THREADS)
+dd_gram_kernel(const TreeDesc *desc, int M, const uint8_t *imode, const int32_t *status,
+               const int32_t *pending, const double *vals, const double *jac, int jac_kmax,
+               const float *ym, int N, double *ddg) {
+    __shared__ double tile[(CO_MAX_K + 1) * DDG_LD];
+    for (int m = blockIdx.x; m < M; m += gridDim.x) {
+        if (!(imode[m] & IM_TR_DD) || status[m] != ST_RUNNING || !pending[m]) continue;
+        const TreeDesc d = desc[m];
+        const int K = d.K, P = nblock_size(K);
+        int ei[DDG_PER_THREAD], el[DDG_PER_THREAD];
+        DD acc[DDG_PER_THREAD];
+#pragma unroll
+        for (int q = 0; q < DDG_PER_THREAD; ++q) {
+            const int e = threadIdx.x + q * DDG_THREADS;
+            int i = 0;
+            while ((i + 1) * (i + 2) / 2 <= e) ++i;
+            ei[q] = i;
+            el[q] = e - i * (i + 1) / 2;
+            acc[q] = DD(0.0);
+        }
+        const double *vrow = vals + (int64_t)m * N;
+        const float *yrow = ym + d.y_off;
+        const double *jrow = jac + (int64_t)m * jac_kmax * N;
+        for (int s0 = 0; s0 < N; s0 += DDG_TILE) {
+            __syncthreads();
+            for (int idx = threadIdx.x; idx < (K + 1) * DDG_TILE; idx += DDG_THREADS) {
+                const int row = idx / DDG_TILE, j = idx - row * DDG_TILE, s = s0 + j;
+                double v = 0.0;
+                if (s < N) {
+                    const double r = vrow[s] - (double)yrow[s];
+                    const bool bad = !::isfinite(r);
+                    if (row == K) v = bad ? RESIDUAL_SENTINEL : r;
+                    else v = bad ? 0.0 : jrow[(int64_t)row * N + s];
+                }
+                tile[row * DDG_LD + j] = v;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int q = 0; q < DDG_PER_THREAD; ++q) {
+                if (threadIdx.x + q * DDG_THREADS < P) {
+                    const double *a = tile + ei[q] * DDG_LD, *b = tile + el[q] * DDG_LD;
+                    DD s = acc[q];
+                    for (int j = 0; j < DDG_TILE; ++j) s += dd_two_prod(a[j], b[j]);
+                    acc[q] = s;
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < DDG_PER_THREAD; ++q) {
+            const int e = threadIdx.x + q * DDG_THREADS;
+            if (e < P) {
+                ddg[2 * (d.q_off + e)] = acc[q].hi;
+                ddg[2 * (d.q_off + e) + 1] = acc[q].lo;
+            }
+        }
     }
 }
 

@@ -86,7 +86,8 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
                    explore_precision: str | None = PARITY["explore_precision"],
                    explore_max_iter: int | None = PARITY["explore_max_iter"],
                    explore_tol: float | None = PARITY["explore_tol"],
-                   polish_starts: int = PARITY["polish_starts"], **kw) -> dict:
+                   polish_starts: int = PARITY["polish_starts"],
+                   dd_starts: int = PARITY["dd_starts"], **kw) -> dict:
     """Fit every tree of `pop` from `starts` starting points (the first is its c_init) in one
     device call (InProcessCO.optimize_ex with n_starts) and return the best start's
     c_final / status / loss_init / loss_final / iters with its index ('start').
@@ -99,6 +100,10 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     kept wherever it is finite and no worse.
     polish_starts: the polish call's starts per tree — the best fit itself and perturbations
     of it (the start kinds of the start axis, around the best).
+    dd_starts > 0 (precision fp64): a third call fits every tree again from its c_init and
+    dd_starts - 1 generated starts with the trust-region LM on double-double normal equations
+    (CoOptions.tr_dd), which keeps the small singular directions of rank-deficient Jacobians
+    as MINPACK's QR does; the lowest final loss of the three calls is kept.
 
     Defaults: the parity preset (co_inproc.PARITY)."""
     algorithm = "trust_region" if tr_starts > 0 else kw.pop("algorithm", "reference")
@@ -138,4 +143,15 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     out["polished"] = better
     out["c_final"] = np.where(np.repeat(better, K), pol["c_final"], res["c_final"])
     out["stats"] = stats
+    if dd_starts > 0 and precision == "fp64":
+        ds = int(dd_starts)
+        dd = co.optimize_ex(pop, max_iter=max_iter, precision=precision, xtol=xtol,
+                            algorithm="trust_region", n_starts=ds, tr_starts=ds,
+                            wave1=min(8, ds - 1) if ds > 1 else 0, seed=seed + 2, tr_dd=True,
+                            **{k: v for k, v in kw.items() if k in ("y_shared", "ftol", "gtol")})
+        take = np.isfinite(dd["loss_final"]) & (np.asarray(dd["loss_final"]) < out["loss_final"])
+        for k in ("status", "loss_final", "iters"):
+            out[k] = np.where(take, dd[k], out[k])
+        out["c_final"] = np.where(np.repeat(take, K), dd["c_final"], out["c_final"])
+        out["dd"] = take
     return out

@@ -182,7 +182,12 @@ typedef struct CoOptions {
                             /* one host thread and context each (the handle's own where a   */
                             /* listed device is its device), outputs in the caller's order  */
     int32_t device_ids[CO_MAX_DEVICES];
-    int32_t reserved[2];
+    int32_t tr_dd;          /* 1: trust-region fits (fp64 only) form and factor their normal  */
+                            /* equations in double-double: J^T J keeps the small singular     */
+                            /* directions of Jacobians rank-deficient to machine precision,   */
+                            /* as MINPACK's QR of J does. Per-sample values and Jacobians of  */
+                            /* the fits are kept on the device (fits x K_max x N doubles).    */
+    int32_t reserved[1];
 } CoOptions;
 
 #define CO_AD_AUTO    0

@@ -167,15 +167,18 @@ def test_pop1000_multistart_parity_vs_reference_scipy(co):
     assert _multistart_parity(co, "pop1000", pop, g["scipy/loss64"]) >= 0.99
 
 
-@pytest.mark.parametrize("name,bar", [("mid", 0.95), ("physics", 0.99), ("long", 0.98),
+@pytest.mark.parametrize("name,bar", [("mid", 0.98), ("physics", 0.99), ("long", 0.99),
                                       ("scale", 0.98)])
 def test_config_multistart_parity_vs_reference_scipy(co, name, bar):
     """64-tree samples of the other BASELINE configurations (reduced N) with the reference's
     scipy fits (tests/golden/configs_scipy.npz); measured mid 96.9%, physics 100%, long 100%,
     scale 98.4-100% (one tree of 64 at 1.0036 in some start mixes)."""
+    from cusr_b200 import multistart
+
     z = np.load(GOLDEN / "configs_scipy.npz")
     pop = load_npz_pop(z, name)
-    assert _multistart_parity(co, name, pop, z[f"{name}/scipy/loss64"]) >= bar
+    kw = multistart.preset_kwargs(co_inproc.PARITY_MAX)
+    assert _multistart_parity(co, name, pop, z[f"{name}/scipy/loss64"], **kw) >= bar
 
 
 def _digest(pop):
@@ -187,7 +190,7 @@ def _digest(pop):
     return h.hexdigest()
 
 
-@pytest.mark.parametrize("name,bar", [("mid", 0.93), ("physics", 0.99), ("long", 0.9),
+@pytest.mark.parametrize("name,bar", [("mid", 0.96), ("physics", 0.99), ("long", 0.93),
                                       ("scale", 0.96)])
 def test_config_multistart_parity_full_n(co, name, bar):
     """32-tree samples of the configurations at their own N (mid 10,000, physics 100,000,
@@ -197,7 +200,10 @@ def test_config_multistart_parity_full_n(co, name, bar):
     z = np.load(GOLDEN / "configs_full_scipy.npz")
     pop = synth.make_config(name, M=int(z[f"{name}/M"]), seed=11)
     assert _digest(pop) == str(z[f"{name}/digest"])
-    assert _multistart_parity(co, f"{name}_fullN", pop, z[f"{name}/scipy/loss64"]) >= bar
+    from cusr_b200 import multistart
+
+    kw = multistart.preset_kwargs(co_inproc.PARITY_MAX)
+    assert _multistart_parity(co, f"{name}_fullN", pop, z[f"{name}/scipy/loss64"], **kw) >= bar
 
 
 def test_metric_sample_parity_modes(co):
@@ -569,3 +575,32 @@ def test_many_chunk_fit_sums(co):
     ref = lm.fit_pop(pop, max_iter=20, dtype=np.float64, trees=np.arange(8))
     same = np.abs(res["loss_final"][:8] - ref["loss_final"]) <= 1e-6 * np.abs(ref["loss_final"]) + 1e-12
     assert np.mean(same[np.isfinite(ref["loss_final"])]) >= 0.6
+
+
+def test_trust_region_double_double_on_rank_deficient_trees(co):
+    """Trees whose Jacobian is rank-deficient to machine precision at their start (metric
+    sample 53 and 116, long full-N 16): one trust-region start from c_init on double-double
+    normal equations (CoOptions.tr_dd) reaches the reference scipy fit or better (measured
+    0.92, 0.85, 0.75 of its loss, the levels of MINPACK with the exact Jacobian and of the
+    32-digit restatement oracle/tr_lm_dd.py), where the fp64 normal equations end 8-10,000
+    times above it. tr_dd is an fp64 option."""
+    cases = []
+    z = np.load(GOLDEN / "metric_scipy.npz")
+    cases.append((load_npz_pop(z, "pop"), z["scipy/loss64"], [53, 116]))
+    zf = np.load(GOLDEN / "configs_full_scipy.npz")
+    cases.append((synth.make_config("long", M=int(zf["long/M"]), seed=11), zf["long/scipy/loss64"], [16]))
+    rep = {}
+    for pop, ref, trees in cases:
+        sub = popio.slice_pop(pop, np.asarray(trees))
+        kw = dict(precision="fp64", max_iter=200, xtol=1e-10, ftol=1e-10, gtol=1e-8,
+                  algorithm="trust_region")
+        l64 = interp.loss_pop(sub, co.optimize_ex(sub, **kw)["c_final"])
+        ldd = interp.loss_pop(sub, co.optimize_ex(sub, tr_dd=True, **kw)["c_final"])
+        for i, t in enumerate(trees):
+            rep[str(t)] = {"fp64": float(l64[i] / ref[t]), "dd": float(ldd[i] / ref[t])}
+            assert ldd[i] <= ref[t] * (1 + 1e-6), rep
+            assert l64[i] > 2.0 * ref[t], rep
+    _report("trust_region_double_double", rep)
+    with pytest.raises(co_inproc.COError):
+        co.optimize_ex(popio.slice_pop(cases[0][0], 4), precision="fp32", algorithm="trust_region",
+                       tr_dd=True)

@@ -90,10 +90,11 @@ def test_preset_keywords():
     assert kw["explore_precision"] == "fp32" and kw["precision"] == "fp64"
     assert kw["polish_starts"] == 16
     assert multistart.preset_kwargs(co_inproc.PARITY_FAST)["polish_starts"] == 1
+    assert multistart.preset_kwargs(co_inproc.PARITY_MAX)["dd_starts"] == 16
     fp64 = multistart.preset_kwargs(co_inproc.PARITY_FP64)
     assert fp64["starts"] == 96 and fp64["explore_precision"] is None
     # every preset key is a fit_multistart parameter
     import inspect
     params = inspect.signature(multistart.fit_multistart).parameters
-    for p in (co_inproc.PARITY, co_inproc.PARITY_FAST, co_inproc.PARITY_FP64):
+    for p in (co_inproc.PARITY, co_inproc.PARITY_FAST, co_inproc.PARITY_FP64, co_inproc.PARITY_MAX):
         assert set(multistart.preset_kwargs(p)) <= set(params) | {"ftol", "gtol"}

@@ -231,3 +231,31 @@ def test_reference_fit_reproducibility_floor():
     out = scipy_floor.perturbation_floor(load_npz_pop(z, "pop"), z["scipy/loss64"])
     assert out["rerun"] == 1.0
     assert out["c_init+1ulp"] < 0.95 and out["y+1ulp"] < 0.97, out
+
+
+def test_trust_region_double_double_restatement_reaches_minpack():
+    """Metric-sample tree 53 has a Jacobian rank-deficient to machine precision at its start
+    (the column-scaled J's two smallest singular values are ~1e-16). MINPACK (the reference
+    scipy backend) fits it to a loss the fp64 normal-equation restatement misses by a factor
+    of ~8 (its step takes the basic solution); the same algorithm with the normal equations at
+    32 digits (oracle/tr_lm_dd.py, the arithmetic of the engine's tr_dd fits) reaches it."""
+    from oracle import tr_lm, tr_lm_dd
+
+    z = np.load(GOLDEN / "metric_scipy.npz")
+    pop = load_npz_pop(z, "pop")
+    ref = z["scipy/loss64"]
+    m = 53
+    nt, nv, ci, y, K = interp.tree_view(pop, m)
+    off = int(pop["metas"][m][2])
+    c0 = pop["c_init"][off:off + K]
+    y64 = np.asarray(y, np.float64)
+
+    def loss(c):
+        f = interp.eval_tree_arrays(nt, nv, ci, pop["xs"], np.asarray(c, np.float64))
+        return 0.5 * float(np.sum((f - y64) ** 2))
+
+    with np.errstate(all="ignore"):
+        l64 = loss(tr_lm.fit_tree(nt, nv, ci, pop["xs"], y, c0)[0])
+        ldd = loss(tr_lm_dd.fit_tree(nt, nv, ci, pop["xs"], y, c0)[0])
+    assert l64 > 2.0 * ref[m]
+    assert ldd <= ref[m] * (1 + 1e-6)
