@@ -633,7 +633,7 @@ def run_profile_case(args) -> None:
     co.load(pop, precision=precision)
     kw = {}
     if args.profile_alg == "trust_region":
-        kw = dict(algorithm="trust_region", xtol=1e-10)
+        kw = dict(algorithm="trust_region", xtol=1e-10, tr_dd=args.profile_tr_dd)
     res = co.fit_loaded(max_iter=args.profile_iters, **kw)
     st = co.stats()
     print(json.dumps({"profile_case": True, "lib": args.profile_lib or "in-tree",
@@ -663,6 +663,9 @@ def main() -> None:
     ap.add_argument("--profile-trees", type=int, default=8192)
     ap.add_argument("--profile-alg", choices=["reference", "trust_region"], default="reference",
                     help="--profile-case: the LM algorithm of the fit")
+    ap.add_argument("--profile-tr-dd", action="store_true",
+                    help="--profile-case with --profile-alg trust_region: double-double normal "
+                         "equations (CoOptions.tr_dd; fp64)")
     ap.add_argument("--profile-lib", default=None,
                     help="--profile-case: a variant build of the library (python -m "
                          "cusr_b200.build --define ... --lib PATH)")

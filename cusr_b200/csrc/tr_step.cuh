@@ -411,11 +411,15 @@ namespace cusr {
 // Normal equations of the trust-region fits that take them in double-double (IM_TR_DD), from
 // the pass's per-sample values (vals[fit][N]) and Jacobian (jac[fit][jac_kmax][N], fp64):
 // ddg holds, per fit at its q_off, the packed (K+1) x (K+1) lower triangle of the Gram matrix
-// of [g_0 .. g_{K-1}; r] as (hi, lo) pairs — J^T J, J^T r, sum r^2 — each product exact
-// (dd_two_prod) and the sums double-double. r = f - y with the sentinel convention of the
-// fused pass (a non-finite residual counts as RESIDUAL_SENTINEL and its Jacobian row as 0).
-// One block per fit, its threads over the Gram entries, samples staged through shared memory
-// in tiles; the order of the sums is fixed.
+// of [g_0 .. g_{K-1}; r] as (hi, lo) pairs — J^T J, J^T r, sum r^2. r = f - y with the
+// sentinel convention of the fused pass (a non-finite residual counts as RESIDUAL_SENTINEL
+// and its Jacobian row as 0).
+// One block per fit; samples are staged through shared memory in tiles of DDG_TILE. Each
+// Gram entry is taken by G = DDG_THREADS / P threads (P entries), thread g of an entry
+// summing the tile's samples g, g + G, ...: within a tile by Dot2 (Ogita, Rump & Oishi 2005,
+// "Accurate sum and dot product": TwoProduct by fma, TwoSum of the running sum, the error
+// terms summed apart), the tile's pair then added to the thread's double-double total; the G
+// totals of an entry are added in g order at the end. The order of every sum is fixed.
 constexpr int DDG_THREADS = 256;
 constexpr int DDG_TILE = 64;
 constexpr int DDG_LD = DDG_TILE + 1;          // odd row stride: rows read at one column spread
@@ -426,15 +430,21 @@ dd_gram_kernel(const TreeDesc *desc, int M, const uint8_t *imode, const int32_t 
                const int32_t *pending, const double *vals, const double *jac, int jac_kmax,
                const float *ym, int N, double *ddg) {
     __shared__ double tile[(CO_MAX_K + 1) * DDG_LD];
+    __shared__ DD red[DDG_THREADS];
     for (int m = blockIdx.x; m < M; m += gridDim.x) {
         if (!(imode[m] & IM_TR_DD) || status[m] != ST_RUNNING || !pending[m]) continue;
         const TreeDesc d = desc[m];
         const int K = d.K, P = nblock_size(K);
-        int ei[DDG_PER_THREAD], el[DDG_PER_THREAD];
+        const int G = P <= DDG_THREADS ? DDG_THREADS / P : 1;   // threads per entry
+        int ei[DDG_PER_THREAD], el[DDG_PER_THREAD], eg[DDG_PER_THREAD];
+        bool on[DDG_PER_THREAD];
         DD acc[DDG_PER_THREAD];
 #pragma unroll
         for (int q = 0; q < DDG_PER_THREAD; ++q) {
-            const int e = threadIdx.x + q * DDG_THREADS;
+            const int u = threadIdx.x + q * DDG_THREADS;
+            on[q] = u < G * P;
+            const int e = on[q] ? u % P : 0;
+            eg[q] = on[q] ? u / P : 0;
             int i = 0;
             while ((i + 1) * (i + 2) / 2 <= e) ++i;
             ei[q] = i;
@@ -460,20 +470,40 @@ dd_gram_kernel(const TreeDesc *desc, int M, const uint8_t *imode, const int32_t 
             __syncthreads();
 #pragma unroll
             for (int q = 0; q < DDG_PER_THREAD; ++q) {
-                if (threadIdx.x + q * DDG_THREADS < P) {
+                if (on[q]) {
                     const double *a = tile + ei[q] * DDG_LD, *b = tile + el[q] * DDG_LD;
-                    DD s = acc[q];
-                    for (int j = 0; j < DDG_TILE; ++j) s += dd_two_prod(a[j], b[j]);
-                    acc[q] = s;
+                    double ps = 0.0, err = 0.0;          // Dot2 over this thread's samples
+                    for (int j = eg[q]; j < DDG_TILE; j += G) {
+                        const double h = a[j] * b[j];
+                        const double rr = fma(a[j], b[j], -h);
+                        const double t = ps + h;
+                        const double bb = t - ps;
+                        err += ((ps - (t - bb)) + (h - bb)) + rr;
+                        ps = t;
+                    }
+                    acc[q] += dd_two_sum(ps, err);
                 }
             }
         }
+        // the G partial totals of each entry, added in thread order
 #pragma unroll
         for (int q = 0; q < DDG_PER_THREAD; ++q) {
-            const int e = threadIdx.x + q * DDG_THREADS;
-            if (e < P) {
-                ddg[2 * (d.q_off + e)] = acc[q].hi;
-                ddg[2 * (d.q_off + e) + 1] = acc[q].lo;
+            const int u = threadIdx.x + q * DDG_THREADS;
+            if (G == 1) {
+                if (on[q]) {
+                    ddg[2 * (d.q_off + u)] = acc[q].hi;
+                    ddg[2 * (d.q_off + u) + 1] = acc[q].lo;
+                }
+            } else if (q == 0) {
+                __syncthreads();
+                red[threadIdx.x] = on[0] ? acc[0] : DD(0.0);
+                __syncthreads();
+                if (threadIdx.x < P) {
+                    DD t = red[threadIdx.x];
+                    for (int g = 1; g < G; ++g) t += red[g * P + threadIdx.x];
+                    ddg[2 * (d.q_off + threadIdx.x)] = t.hi;
+                    ddg[2 * (d.q_off + threadIdx.x) + 1] = t.lo;
+                }
             }
         }
     }
