@@ -414,7 +414,8 @@ namespace cusr {
 // of [g_0 .. g_{K-1}; r] as (hi, lo) pairs — J^T J, J^T r, sum r^2. r = f - y with the
 // sentinel convention of the fused pass (a non-finite residual counts as RESIDUAL_SENTINEL
 // and its Jacobian row as 0).
-// One block per fit; samples are staged through shared memory in tiles of DDG_TILE. Each
+// One block per fit; samples are staged through shared memory in tiles of DDG_TILE, the next
+// tile's loads in flight in registers while a tile is summed. Each
 // Gram entry is taken by G = DDG_THREADS / P threads (P entries), thread g of an entry
 // summing the tile's samples g, g + G, ...: within a tile by Dot2 (Ogita, Rump & Oishi 2005,
 // "Accurate sum and dot product": TwoProduct by fma, TwoSum of the running sum, the error
@@ -424,6 +425,8 @@ constexpr int DDG_THREADS = 256;
 constexpr int DDG_TILE = 64;
 constexpr int DDG_LD = DDG_TILE + 1;          // odd row stride: rows read at one column spread
 constexpr int DDG_PER_THREAD = (nblock_size(CO_MAX_K) + DDG_THREADS - 1) / DDG_THREADS;
+// tile elements a thread stages: (K + 1) rows x DDG_TILE samples over the block
+constexpr int DDG_NV = ((CO_MAX_K + 1) * DDG_TILE + DDG_THREADS - 1) / DDG_THREADS;
 
 __global__ void __launch_bounds__(DDG_THREADS)
 dd_gram_kernel(const TreeDesc *desc, int M, const uint8_t *imode, const int32_t *status,
@@ -454,19 +457,47 @@ dd_gram_kernel(const TreeDesc *desc, int M, const uint8_t *imode, const int32_t 
         const double *vrow = vals + (int64_t)m * N;
         const float *yrow = ym + d.y_off;
         const double *jrow = jac + (int64_t)m * jac_kmax * N;
+        const int n_el = (K + 1) * DDG_TILE;
+        // the next tile's raw values in registers (loads in flight while a tile is summed):
+        // element idx = row * DDG_TILE + j, row K the value f (with its target), rows < K J
+        double nv[DDG_NV];
+        float ny[DDG_NV];
+        auto fetch = [&](int s0) {
+#pragma unroll
+            for (int q = 0; q < DDG_NV; ++q) {
+                const int idx = threadIdx.x + q * DDG_THREADS;
+                const int row = idx / DDG_TILE, s = s0 + idx - row * DDG_TILE;
+                nv[q] = 0.0;
+                ny[q] = 0.f;
+                if (idx < n_el && s < N) {
+                    if (row == K) {
+                        nv[q] = vrow[s];
+                        ny[q] = yrow[s];
+                    } else {
+                        nv[q] = jrow[(int64_t)row * N + s];
+                    }
+                }
+            }
+        };
+        fetch(0);
         for (int s0 = 0; s0 < N; s0 += DDG_TILE) {
             __syncthreads();
-            for (int idx = threadIdx.x; idx < (K + 1) * DDG_TILE; idx += DDG_THREADS) {
-                const int row = idx / DDG_TILE, j = idx - row * DDG_TILE, s = s0 + j;
-                double v = 0.0;
-                if (s < N) {
-                    const double r = vrow[s] - (double)yrow[s];
-                    const bool bad = !::isfinite(r);
-                    if (row == K) v = bad ? RESIDUAL_SENTINEL : r;
-                    else v = bad ? 0.0 : jrow[(int64_t)row * N + s];
+#pragma unroll
+            for (int q = 0; q < DDG_NV; ++q) {
+                const int idx = threadIdx.x + q * DDG_THREADS;
+                if (idx < n_el) {
+                    const int row = idx / DDG_TILE, j = idx - row * DDG_TILE;
+                    tile[row * DDG_LD + j] = row == K ? nv[q] - (double)ny[q] : nv[q];
                 }
-                tile[row * DDG_LD + j] = v;
             }
+            __syncthreads();
+            // the sentinel convention: a non-finite residual counts as RESIDUAL_SENTINEL and
+            // its sample's Jacobian row as 0 (samples past N stay 0)
+            if (threadIdx.x < DDG_TILE && !::isfinite(tile[K * DDG_LD + threadIdx.x])) {
+                tile[K * DDG_LD + threadIdx.x] = RESIDUAL_SENTINEL;
+                for (int row = 0; row < K; ++row) tile[row * DDG_LD + threadIdx.x] = 0.0;
+            }
+            if (s0 + DDG_TILE < N) fetch(s0 + DDG_TILE);
             __syncthreads();
 #pragma unroll
             for (int q = 0; q < DDG_PER_THREAD; ++q) {
