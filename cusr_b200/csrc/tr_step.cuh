@@ -281,8 +281,8 @@ __global__ void __launch_bounds__(tr_threads<S>()) lm_tr_step_kernel_s(const TrP
         } else {
             if (lane == 0) p.iters[m] += 1;
             const double fnorm1 = isfinite(ssq) ? sqrt(ssq) : INFINITY;
-            // |J p|^2 = p^T A p with A = the accepted point's J^T J (packed lower in blk)
-            const T *bq = p.blk + dsc.q_off;
+            // |J p|^2 = p^T A p with A = the accepted point's J^T J (packed lower in blk, or
+            // blk_dd for double-double fits)
             const double pk = lane < K ? (double)p.delta[dsc.c_off + lane] : 0.0;
             S ap = S(0.0);
             for (int l = 0; l < K; ++l) {
@@ -294,7 +294,6 @@ __global__ void __launch_bounds__(tr_threads<S>()) lm_tr_step_kernel_s(const TrP
                     else ap += S((double)p.blk[e]) * S(pl);
                 }
             }
-            (void)bq;
             const double jp2 = fmax(to_double(wl_sum(S(pk) * ap)), 0.0);
             const double actred = (0.1 * fnorm1 < fnorm) ? 1.0 - (fnorm1 / fnorm) * (fnorm1 / fnorm) : -1.0;
             const double t1 = sqrt(jp2) / fnorm, t2 = sqrt(par) * pnorm / fnorm;
