@@ -321,7 +321,7 @@ def run_reference(args, world: int, rank: int) -> None:
 
 def parity_mode(co, pop: dict) -> dict:
     """The parity-grade fit (cusr_b200.multistart defaults, co_inproc.PARITY: 128 trust-region
-    starts per tree explored in fp32 on the device, two waves, fp64 polish from 16 starts
+    starts per tree explored in fp32 on the device, two waves, fp64 polish from 8 starts
     around each tree's best): fits/s on a
     2,048-tree stratified slice of the metric population (device time of the multi-start call
     plus the polish call), and the north-star fraction — fp64 loss within 1e-6 of, or better
@@ -361,7 +361,7 @@ def parity_mode(co, pop: dict) -> dict:
     out = measure(multistart.preset_kwargs(co_inproc.PARITY))
     out.update(dtype="f32 starts, f64 polish", note="the parity-grade mode (co_inproc.PARITY: "
                "128 device-side trust-region starts explored in fp32, then each tree's best "
-               "polished in fp64 from 16 starts around it) on a 2,048-tree slice of the metric "
+               "polished in fp64 from 8 starts around it) on a 2,048-tree slice of the metric "
                "population; the fraction on the 256-tree reference scipy sample of that "
                "population")
     fast = measure(multistart.preset_kwargs(co_inproc.PARITY_FAST))

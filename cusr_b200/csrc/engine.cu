@@ -647,7 +647,12 @@ int fit_loaded(Ctx *ctx, const CoOptions &opt, const Outputs &out,
                                                std::max(1, step_occ) * ctx->sm_count));
     const int tr_grid = std::max(1, std::min((M_fit + TR_WARPS - 1) / TR_WARPS,
                                              std::max(1, tr_occ) * ctx->sm_count));
-    const int tr_grid_dd = std::max(1, std::min((M_fit + 1) / 2, 2 * ctx->sm_count));
+    int tr_occ_dd = 0;
+    if constexpr (sizeof(T) == 8)
+        CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&tr_occ_dd, lm_tr_step_kernel_s<double, DD>,
+                                                         TR_THREADS_DD, tr_smem_dd));
+    const int tr_grid_dd = std::max(1, std::min((M_fit + TR_THREADS_DD / 32 - 1) / (TR_THREADS_DD / 32),
+                                                std::max(1, tr_occ_dd) * ctx->sm_count));
     const int ddg_grid = std::max(1, std::min(M_fit, 8 * ctx->sm_count));
 
     StepParams<T> sp;

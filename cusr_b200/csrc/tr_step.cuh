@@ -55,8 +55,11 @@ struct TrParams {
 constexpr int TR_THREADS = 128;
 constexpr int TR_WARPS = TR_THREADS / 32;
 constexpr int TR_THREADS_DD = 64;     // the double-double variant: twice the shared memory
-// per warp, in scalars S: A, W (K x K, full symmetric), the summed block (561 values)
-constexpr int TR_WARP_D = 2 * CO_MAX_K * WL_LD + 576;
+// per warp, in scalars S: A, W (K x K, full symmetric); the summed block of the pass (at most
+// 561 values) shares W's space: it is read (loss, finiteness, the accepted block) before the
+// step's factorisations write W
+constexpr int TR_WARP_D = 2 * CO_MAX_K * WL_LD;
+static_assert(CO_MAX_K * WL_LD >= nblock_size(CO_MAX_K), "the block fits in W");
 template <typename S> __host__ __device__ constexpr int tr_threads() {
     return sizeof(S) == 8 ? TR_THREADS : TR_THREADS_DD;
 }
@@ -237,7 +240,7 @@ __global__ void __launch_bounds__(tr_threads<S>()) lm_tr_step_kernel_s(const TrP
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     S *A = reinterpret_cast<S *>(tr_sm) + warp * TR_WARP_D;
     S *W = A + CO_MAX_K * WL_LD;
-    S *sums = W + CO_MAX_K * WL_LD;
+    S *sums = W;
     int *perm = s_perm[warp];
     const double eps = sizeof(T) == 8 ? DBL_EPSILON : (double)FLT_EPSILON;
     for (int m = blockIdx.x * NWARP + warp; m < p.M; m += gridDim.x * NWARP) {

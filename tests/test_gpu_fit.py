@@ -128,7 +128,7 @@ def test_pr1_fit_parity_vs_reference_scipy(co):
 def _multistart_parity(co, name, pop, ref, **kw):
     """North-star parity with the parity-grade fit (cusr_b200.multistart defaults, the device
     start axis: 128 trust-region starts per tree explored in fp32 in two waves, then each
-    tree's best polished in fp64 from 16 starts around it; the best final loss kept):
+    tree's best polished in fp64 from 8 starts around it; the best final loss kept):
     the fraction of trees whose fp64 loss is within 1e-6 relative of, or better than, the
     reference scipy fit. Divergent trees are listed. The bars are the measured levels: on
     the mid grammar a few trees in a hundred keep a local minimum worse than MINPACK's, whose
@@ -243,7 +243,7 @@ def test_metric_sample_parity_modes(co):
     rep["parity_fp64"] = frac(f64["c_final"])
     _report("metric_sample_modes_vs_scipy", rep)
     # measured: single fp32 52%, fp64 62%, one trust-region start 74%; the parity presets
-    # (fp32 exploration + 16-start fp64 polish / single-start polish / all fp64) 99.2-99.6%
+    # (fp32 exploration + 8-start fp64 polish / single-start polish / all fp64) 99.2-99.6%
     assert rep["single_fp32"] >= 0.45 and rep["parity_mode"] >= 0.99, rep
     assert rep["parity_fast"] >= 0.98 and rep["parity_fp64"] >= 0.98, rep
 

@@ -88,7 +88,7 @@ def test_preset_keywords():
     kw = multistart.preset_kwargs(co_inproc.PARITY)
     assert kw["starts"] == 128 and kw["tr_starts"] == 128 and "algorithm" not in kw
     assert kw["explore_precision"] == "fp32" and kw["precision"] == "fp64"
-    assert kw["polish_starts"] == 16
+    assert kw["polish_starts"] == 8 and kw["explore_max_iter"] == 30
     assert multistart.preset_kwargs(co_inproc.PARITY_FAST)["polish_starts"] == 1
     assert multistart.preset_kwargs(co_inproc.PARITY_MAX)["dd_starts"] == 16
     fp64 = multistart.preset_kwargs(co_inproc.PARITY_FP64)
