@@ -255,19 +255,19 @@ def start_options(opt: CoOptions, algorithm: str = "reference", n_starts: int = 
 # The parity-grade fit, in two device calls: every tree's 128 starts explored at once with the
 # trust-region LM of the reference's scipy backend in fp32 (30 evaluations, ftol = xtol = 1e-6,
 # two waves: trees whose first 8 fits agree skip the rest), then each tree's best fit polished
-# in fp64 with scipy's tolerances (200 evaluations) from 8 starts around it (the best itself
-# and 7 perturbations of it); the lower final loss is kept. Measured on the eight scipy
-# samples (about 800 trees): 9 trees not within 1e-6 of the reference fit, as for 50
-# exploration evaluations and a 16-start polish at 1.34 times the device time, and 8 for 96
-# fp64 starts (PARITY_FP64) at 3.2 times it.
+# in fp64 with scipy's tolerances (100 evaluations) from 8 starts around it (the best itself
+# and 7 perturbations of it, one wave); the lower final loss is kept. Measured on the eight
+# scipy samples (about 800 trees): 9 trees not within 1e-6 of the reference fit (the same with
+# 60 or 200 polish evaluations), as for 50 exploration evaluations and a 16-start polish at
+# twice the device time, and 8 for 96 fp64 starts (PARITY_FP64) at about five times it.
 PARITY = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
               algorithm="trust_region", n_starts=128, tr_starts=128, wave1=8, ftol=1e-10,
               gtol=1e-8, polish=True, explore_precision="fp32", explore_max_iter=30,
-              explore_tol=1e-6, polish_starts=8, dd_starts=0)
+              explore_tol=1e-6, polish_starts=8, polish_max_iter=100, dd_starts=0)
 
 # 50 exploration evaluations and a single-start polish: 11-12 of about 800 trees off the
 # reference fit, the lowest device time.
-PARITY_FAST = dict(PARITY, explore_max_iter=50, polish_starts=1)
+PARITY_FAST = dict(PARITY, explore_max_iter=50, polish_starts=1, polish_max_iter=200)
 
 # PARITY and a third call: 16 fp64 trust-region starts from c_init on double-double normal
 # equations (CoOptions.tr_dd). On the eight scipy samples 5 trees off the reference fit
@@ -279,7 +279,7 @@ PARITY_MAX = dict(PARITY, dd_starts=16)
 PARITY_FP64 = dict(precision="fp64", max_iter=200, xtol=1e-10, damping_floor=1e-3,
                    algorithm="trust_region", n_starts=96, tr_starts=96, wave1=8, ftol=1e-10,
                    gtol=1e-8, polish=True, explore_precision=None, explore_max_iter=None,
-                   explore_tol=None, polish_starts=1, dd_starts=0)
+                   explore_tol=None, polish_starts=1, polish_max_iter=None, dd_starts=0)
 
 
 class InProcessCO:

@@ -87,6 +87,7 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
                    explore_max_iter: int | None = PARITY["explore_max_iter"],
                    explore_tol: float | None = PARITY["explore_tol"],
                    polish_starts: int = PARITY["polish_starts"],
+                   polish_max_iter: int | None = PARITY["polish_max_iter"],
                    dd_starts: int = PARITY["dd_starts"], **kw) -> dict:
     """Fit every tree of `pop` from `starts` starting points (the first is its c_init) in one
     device call (InProcessCO.optimize_ex with n_starts) and return the best start's
@@ -99,7 +100,8 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     ftol = xtol; the polish then runs in `precision` with max_iter / xtol and its result is
     kept wherever it is finite and no worse.
     polish_starts: the polish call's starts per tree — the best fit itself and perturbations
-    of it (the start kinds of the start axis, around the best).
+    of it (the start kinds of the start axis, around the best), in one wave;
+    polish_max_iter: its evaluation budget (default max_iter).
     dd_starts > 0 (precision fp64): a third call fits every tree again from its c_init and
     dd_starts - 1 generated starts with the trust-region LM on double-double normal equations
     (CoOptions.tr_dd), which keeps the small singular directions of rank-deficient Jacobians
@@ -123,9 +125,9 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     with np.errstate(over="ignore"):            # fits that ran off to huge constants
         again["c_init"] = np.asarray(res["c_final"], np.float32)
     ps = max(1, int(polish_starts))
-    pol = co.optimize_ex(again, max_iter=max_iter, precision=precision, xtol=xtol,
-                         algorithm="trust_region", n_starts=ps, tr_starts=ps,
-                         wave1=min(8, ps - 1) if ps > 1 else 0, seed=seed + 1,
+    pol = co.optimize_ex(again, max_iter=polish_max_iter or max_iter, precision=precision,
+                         xtol=xtol, algorithm="trust_region", n_starts=ps, tr_starts=ps, wave1=0,
+                         seed=seed + 1,
                          **{k: v for k, v in kw.items() if k in ("y_shared", "ftol", "gtol")})
     lp, lr = np.asarray(pol["loss_final"]), np.asarray(res["loss_final"])
     if explore:
