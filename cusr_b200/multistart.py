@@ -71,6 +71,31 @@ def start_points(pop: dict, starts: int, seed: int = 0) -> np.ndarray:
     return v.astype(np.float32)
 
 
+# device memory one double-double call may take for its fits' per-sample Jacobians and values
+DD_BATCH_BYTES = 16 << 30
+
+
+def _dd_stage(co, pop: dict, ds: int, max_iter: int, xtol: float, seed: int, kw: dict) -> dict:
+    """The double-double trust-region starts of every tree (CoOptions.tr_dd), in batches of
+    consecutive trees so that a call keeps at most DD_BATCH_BYTES of per-sample Jacobians and
+    values on the device; outputs in tree order."""
+    from .popio import slice_pop
+
+    M, N = int(pop["M"]), int(pop["N"])
+    kmax = max(1, int(np.asarray(pop["metas"]).reshape(M, 4)[:, 3].max(initial=0)))
+    per_tree = ds * (kmax + 1) * N * 8
+    batch = max(1, int(DD_BATCH_BYTES // per_tree))
+    call = dict(max_iter=max_iter, precision="fp64", xtol=xtol, algorithm="trust_region",
+                n_starts=ds, tr_starts=ds, wave1=min(8, ds - 1) if ds > 1 else 0, seed=seed,
+                tr_dd=True, **kw)
+    if batch >= M:
+        return co.optimize_ex(pop, **call)
+    parts = [co.optimize_ex(slice_pop(pop, np.arange(a, min(a + batch, M))), **call)
+             for a in range(0, M, batch)]
+    return {k: np.concatenate([np.asarray(p[k]) for p in parts])
+            for k in ("c_final", "status", "loss_final", "iters")}
+
+
 def preset_kwargs(preset: dict = PARITY) -> dict:
     """fit_multistart keyword arguments of a preset dict (co_inproc.PARITY, PARITY_FAST,
     PARITY_FP64)."""
@@ -146,11 +171,8 @@ def fit_multistart(co, pop: dict, starts: int = PARITY["n_starts"],
     out["c_final"] = np.where(np.repeat(better, K), pol["c_final"], res["c_final"])
     out["stats"] = stats
     if dd_starts > 0 and precision == "fp64":
-        ds = int(dd_starts)
-        dd = co.optimize_ex(pop, max_iter=max_iter, precision=precision, xtol=xtol,
-                            algorithm="trust_region", n_starts=ds, tr_starts=ds,
-                            wave1=min(8, ds - 1) if ds > 1 else 0, seed=seed + 2, tr_dd=True,
-                            **{k: v for k, v in kw.items() if k in ("y_shared", "ftol", "gtol")})
+        dd = _dd_stage(co, pop, int(dd_starts), max_iter, xtol, seed + 2,
+                       {k: v for k, v in kw.items() if k in ("y_shared", "ftol", "gtol")})
         take = np.isfinite(dd["loss_final"]) & (np.asarray(dd["loss_final"]) < out["loss_final"])
         for k in ("status", "loss_final", "iters"):
             out[k] = np.where(take, dd[k], out[k])

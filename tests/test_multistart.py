@@ -98,3 +98,31 @@ def test_preset_keywords():
     params = inspect.signature(multistart.fit_multistart).parameters
     for p in (co_inproc.PARITY, co_inproc.PARITY_FAST, co_inproc.PARITY_FP64, co_inproc.PARITY_MAX):
         assert set(multistart.preset_kwargs(p)) <= set(params) | {"ftol", "gtol"}
+
+
+def test_dd_stage_batches_by_memory(monkeypatch):
+    """The double-double stage splits a population into batches of consecutive trees when its
+    per-sample Jacobians would exceed DD_BATCH_BYTES, and returns the outputs in tree order."""
+    pop = synth.make_config("pr1", M=10, N=64, seed=2)
+    calls = []
+
+    class FakeCo:
+        def optimize_ex(self, p, **kw):
+            assert kw["tr_dd"] and kw["precision"] == "fp64"
+            M = int(p["M"])
+            calls.append(M)
+            K = np.asarray(p["metas"]).reshape(M, 4)[:, 3]
+            # each tree's constants, status and loss name the tree by its first constant
+            return {"c_final": np.asarray(p["c_init"], np.float64),
+                    "status": np.zeros(M, np.int32),
+                    "loss_final": np.asarray([p["c_init"][o] if k else 0.0 for o, k in
+                                              zip(np.asarray(p["metas"])[:, 2], K)]),
+                    "iters": np.full(M, 3, np.int32)}
+
+    kmax = int(np.asarray(pop["metas"])[:, 3].max())
+    per_tree = 4 * (kmax + 1) * 64 * 8
+    monkeypatch.setattr(multistart, "DD_BATCH_BYTES", 3 * per_tree)
+    out = multistart._dd_stage(FakeCo(), pop, 4, 50, 1e-10, 0, {})
+    assert calls == [3, 3, 3, 1]
+    np.testing.assert_array_equal(out["c_final"], np.asarray(pop["c_init"], np.float64))
+    assert out["status"].shape == (10,)
