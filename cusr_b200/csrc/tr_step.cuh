@@ -55,10 +55,11 @@ struct TrParams {
 constexpr int TR_THREADS = 128;
 constexpr int TR_WARPS = TR_THREADS / 32;
 constexpr int TR_THREADS_DD = 64;     // the double-double variant: twice the shared memory
-// per warp, in scalars S: A, W (K x K, full symmetric); the summed block of the pass (at most
-// 561 values) shares W's space: it is read (loss, finiteness, the accepted block) before the
-// step's factorisations write W
-constexpr int TR_WARP_D = 2 * CO_MAX_K * WL_LD;
+// per warp, in scalars S: the factorisation workspace W (K x K); the summed block of the pass
+// (at most 561 values) shares its space: it is read (loss, finiteness, the accepted block)
+// before the step's factorisations write W. J^T J itself is read from the accepted block in
+// global memory (TrA).
+constexpr int TR_WARP_D = CO_MAX_K * WL_LD;
 static_assert(CO_MAX_K * WL_LD >= nblock_size(CO_MAX_K), "the block fits in W");
 template <typename S> __host__ __device__ constexpr int tr_threads() {
     return sizeof(S) == 8 ? TR_THREADS : TR_THREADS_DD;
@@ -156,12 +157,27 @@ __device__ double tr_pfsub_norm(const S *W, int K, int lane, const int *perm, S 
     return wl_norm(w);
 }
 
+// J^T J of the accepted point, read from its packed lower-triangle block in global memory
+// (T values, or (hi, lo) pairs for double-double fits); the block is read where it is needed
+// instead of being kept in shared memory, so more warps stay resident
+template <typename T, typename S>
+struct TrA {
+    const T *blk;          // packed block of the fit (its q_off applied)
+    const double *blk_dd;  // the same as (hi, lo) pairs, double-double fits
+    __device__ __forceinline__ S operator()(int i, int l) const {
+        const int hi = i > l ? i : l, lo = i > l ? l : i;
+        const int e = hi * (hi + 1) / 2 + lo;
+        if constexpr (sizeof(S) == 16) return S(blk_dd[2 * e], blk_dd[2 * e + 1]);
+        else return S((double)blk[e]);
+    }
+};
+
 // W = A + par diag(d^2), rows owned by lanes
-template <typename S>
-__device__ __forceinline__ void tr_load(S *W, const S *A, int K, int lane, double par,
+template <typename S, typename AV>
+__device__ __forceinline__ void tr_load(S *W, const AV A, int K, int lane, double par,
                                         double d) {
     if (lane < K) {
-        for (int k = 0; k < K; ++k) W[lane * WL_LD + k] = A[lane * WL_LD + k];
+        for (int k = 0; k < K; ++k) W[lane * WL_LD + k] = A(lane, k);
         W[lane * WL_LD + lane] += S(par * d * d);
     }
     __syncwarp();
@@ -169,8 +185,8 @@ __device__ __forceinline__ void tr_load(S *W, const S *A, int K, int lane, doubl
 
 // The LM parameter and step for trust radius delta (MINPACK lmpar, on normal equations).
 // Lane i holds g_i = (J^T f)_i and d_i; returns x_i (the step) and updates par.
-template <typename S>
-__device__ S tr_lmpar(const S *A, S *W, int *perm, int K, int lane, S g, double d,
+template <typename S, typename AV>
+__device__ __forceinline__ S tr_lmpar(const AV A, S *W, int *perm, int K, int lane, S g, double d,
                       double delta, double &par) {
     const double dwarf = DBL_MIN;
     // Gauss-Newton direction
@@ -205,7 +221,7 @@ __device__ S tr_lmpar(const S *A, S *W, int *perm, int K, int lane, S g, double 
         // scale of J^T J) is factored with par raised until it is positive definite
         int guard = 0;
         while (!wl_chol(W, K, lane) && guard < 64) {
-            const double amax = to_double(wl_max(lane < K ? fabs(A[lane * WL_LD + lane]) : S(0.0)));
+            const double amax = to_double(wl_max(lane < K ? fabs(A(lane, lane)) : S(0.0)));
             const double dmin = -wl_max(lane < K ? -(d * d) : -DBL_MAX);
             par = fmax(fmax(2.0 * par, 1e-15 * amax / dmin), dwarf);
             tr_load(W, A, K, lane, par, d);
@@ -238,8 +254,7 @@ __global__ void __launch_bounds__(tr_threads<S>()) lm_tr_step_kernel_s(const TrP
     extern __shared__ double tr_sm[];
     __shared__ int s_perm[NWARP][CO_MAX_K];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    S *A = reinterpret_cast<S *>(tr_sm) + warp * TR_WARP_D;
-    S *W = A + CO_MAX_K * WL_LD;
+    S *W = reinterpret_cast<S *>(tr_sm) + warp * TR_WARP_D;
     S *sums = W;
     int *perm = s_perm[warp];
     const double eps = sizeof(T) == 8 ? DBL_EPSILON : (double)FLT_EPSILON;
@@ -351,22 +366,19 @@ __global__ void __launch_bounds__(tr_threads<S>()) lm_tr_step_kernel_s(const TrP
         }
         __syncwarp();
         if (!done) {
-            // current point's J^T J (full) and J^T f, from the accepted block
-            auto blk_at = [&](int64_t e) -> S {
-                if constexpr (DDM) return S(p.blk_dd[2 * e], p.blk_dd[2 * e + 1]);
-                else return S((double)p.blk[e]);
-            };
-            if (lane < K)
-                for (int l = 0; l < K; ++l) {
-                    const int hi = lane > l ? lane : l, lo = lane > l ? l : lane;
-                    A[lane * WL_LD + l] = blk_at(dsc.q_off + hi * (hi + 1) / 2 + lo);
-                }
+            // current point's J^T J and J^T f, from the accepted block (written above by this
+            // warp; the warp barrier orders those writes before these reads)
             __syncwarp();
-            const S g = lane < K ? blk_at(dsc.q_off + tri + lane) : S(0.0);
+            const TrA<T, S> A{p.blk + dsc.q_off, DDM ? p.blk_dd + 2 * dsc.q_off : nullptr};
+            S g = S(0.0);
+            if (lane < K) {
+                if constexpr (DDM) g = S(p.blk_dd[2 * (dsc.q_off + tri + lane)],
+                                         p.blk_dd[2 * (dsc.q_off + tri + lane) + 1]);
+                else g = S((double)p.blk[dsc.q_off + tri + lane]);
+            }
             if (accept) {
                 // outer iteration: column norms, the scaling, the gradient test
-                const double acn =
-                    lane < K ? sqrt(fmax(to_double(A[lane * WL_LD + lane]), 0.0)) : 0.0;
+                const double acn = lane < K ? sqrt(fmax(to_double(A(lane, lane)), 0.0)) : 0.0;
                 if (outer == 1) {
                     d = (lane < K && acn != 0.0) ? acn : 1.0;
                     const double cn = lane < K ? d * (double)p.c[dsc.c_off + lane] : 0.0;
