@@ -48,6 +48,8 @@ M_PER_GPU = 16384
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 PROFILE_SUMMARY = ROOT / "profiles" / "lm_eval_kernel_metric.md"
 INST_SUMMARY = ROOT / "profiles" / "lm_eval_kernel_sfu_vs_ieee_instructions.md"
+L2_BYTES = 126 << 20     # B200 L2
+CPU_BASELINE_MAX_N = 1_000_000   # larger N: a single scipy fit outlasts the bounded sample
 
 
 def dist_setup():
@@ -208,6 +210,59 @@ def issue_estimate(node_evals: float, eval_ms: float, clk: dict):
     rate = ipn["value"] * node_evals / (eval_ms / 1e3)
     return {"frac": rate / peak, "thread_inst_per_s": rate, "peak_thread_inst_per_s": peak,
             "inst_per_node_eval": ipn}
+
+
+def measured_hbm_peak():
+    """(GB/s, source) of the copy bandwidth in MEASURED_PEAKS.json (driver-measured on this
+    pool's B200s), else the pool's earlier measurement (6,650 GB/s, "fallback")."""
+    try:
+        return float(json.loads(PEAKS.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback (earlier measurement on this pool)"
+
+
+def config_roofline(st_sum: dict, pop: dict, precision: str, fp_peaks: tuple) -> dict:
+    """Live roofline of the evaluation kernel over a configuration's timed fits, from the
+    engine's own counters (summed over the timed steps): FLOPs of the interpreter and
+    normal equations (2 per operator node + 2 per block entry, per evaluated tree-sample)
+    over its device time, against the in-run FMA probe peak of the fit's precision; for
+    per-tree targets (a target row per tree, streamed from HBM every pass) also the target
+    bytes (4 per evaluated tree-sample) over the same time, against the measured copy
+    bandwidth. `bound` is the roof with the larger fraction."""
+    eval_s = st_sum["eval_ms"] / 1e3
+    if eval_s <= 0:
+        return {"unavailable": "no evaluation time recorded"}
+    fp64 = precision == "fp64"
+    peak = fp_peaks[1] if fp64 else fp_peaks[0]
+    tf = st_sum["flops"] / eval_s / 1e12
+    fp = {"bound": "fp64" if fp64 else "fp32", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+          "frac": tf / peak if peak else None,
+          "peak_source": "measured FMA probe (co_probe_peak, same run)"}
+    out = {"kernel": "lm_eval_kernel", "fp": fp, "eval_ms": st_sum["eval_ms"],
+           "avg_launch_ms": st_sum["eval_ms"] / max(1, st_sum["eval_launches"]),
+           "node_evals_per_s_eval": st_sum["node_evals"] / eval_s}
+    ym = np.asarray(pop["ym"])
+    per_tree_y = ym.ndim == 2 and ym.shape[0] > 1
+    N, n_vars = int(pop["N"]), int(pop["n_vars"])
+    x_in_l2 = 4 * N * (n_vars + 1) <= L2_BYTES
+    if per_tree_y or not x_in_l2:
+        per_sample = (4 if per_tree_y else 0) + (0 if x_in_l2 else 4 * (n_vars + (0 if per_tree_y else 1)))
+        gbs = per_sample * st_sum["sample_evals"] / eval_s / 1e9
+        hpk, src = measured_hbm_peak()
+        what = ("the tree's target" if per_tree_y else "") + \
+               ("" if x_in_l2 else (" and " if per_tree_y else "") + "the sample's inputs" +
+                ("" if per_tree_y else " and shared target"))
+        out["hbm"] = {"bound": "hbm", "achieved": gbs, "peak": hpk, "unit": "GB/s",
+                      "frac": gbs / hpk, "peak_source": src,
+                      "bytes_def": f"{per_sample} B per evaluated (tree, sample): {what} "
+                                   f"({'X is L2-resident' if x_in_l2 else 'X and y exceed L2'})"}
+    else:
+        out["hbm_note"] = "one shared target row and X are L2-resident: no HBM stream per pass"
+    best = max((r for r in (fp, out.get("hbm")) if r and r.get("frac") is not None),
+               key=lambda r: r["frac"], default=fp)
+    out.update(bound=best["bound"], achieved=best["achieved"], peak=best["peak"],
+               unit=best["unit"], frac=best["frac"])
+    return out
 
 
 def cpu_baseline(pop: dict, target_s: float = 15.0) -> dict:
@@ -563,17 +618,23 @@ def run_config(args, world: int = 1, rank: int = 0, local: int = 0) -> None:
     shared = np.asarray(pop["ym"]).ndim == 1
     mine = shard.shard(pop, rank, world)[0] if world > 1 else pop
     co = InProcessCO(device_id=local if world > 1 else 0)
+    peaks = co.probe_peak()
     co.load(mine, precision=precision, y_shared=shared)
     for _ in range(args.warmup):
         co.fit_loaded(max_iter=max_iter)
     barrier(world)
+    clocks = ClockSampler(local if world > 1 else 0, out_dir(args) / f"clocks_{name}_rank{rank}.csv")
     dev, nodes, launches, res = [], 0, 0, None
+    st_sum = dict.fromkeys(("eval_ms", "flops", "node_evals", "sample_evals", "eval_launches"), 0)
     for _ in range(args.steps):
         res = co.fit_loaded(max_iter=max_iter)
         st = co.stats()
         dev.append(st["device_ms"])
         nodes += st["node_evals"]
         launches += st["kernel_launches"]
+        for k in st_sum:
+            st_sum[k] += st[k]
+    clk = clocks.stop()
     barrier(world)
     total_ms = max_over_ranks(float(sum(dev)), world)
     nodes = sum_over_ranks(float(nodes), world)
@@ -589,11 +650,17 @@ def run_config(args, world: int = 1, rank: int = 0, local: int = 0) -> None:
             "config": {"workload": name, "trees": M, "N": int(pop["N"]), "max_iter": max_iter,
                        "y_shared": bool(shared), "precision": precision},
             "node_evals_per_s": nodes / (total_ms / 1e3), "gpu_launches": launches,
-            "statuses": np.bincount(res["status"], minlength=5).tolist()}
+            "statuses": np.bincount(res["status"], minlength=5).tolist(),
+            "roofline": config_roofline(st_sum, mine, precision, peaks), "clocks": clk}
     if world > 1:
         line["config"]["parallelism"] = f"expression-sharded x{world} (LPT cost-balanced)"
     if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(pop, target_s=10.0)
+        if int(pop["N"]) > CPU_BASELINE_MAX_N:
+            # one scipy fit over 10^7 samples takes about a minute per core: no bounded sample
+            line["cpu_baseline"] = {"unavailable": f"N = {pop['N']}: one scipy fit per core "
+                                                   "exceeds the bounded sample's time"}
+        else:
+            line["cpu_baseline"] = cpu_baseline(pop, target_s=10.0)
     print(json.dumps(line), flush=True)
 
 
@@ -608,6 +675,7 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
     precision, max_iter = pop["precision"], int(pop["max_iter"])
     mine = shard.sample_slice(pop, rank, world) if world > 1 else pop
     co = InProcessCO(device_id=local if world > 1 else 0)
+    peaks = co.probe_peak()
     if world > 1:
         import torch.distributed as dist
 
@@ -619,8 +687,10 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
     for _ in range(args.warmup):
         co.fit_loaded(max_iter=max_iter, sample_sharded=sharded)
     barrier(world)
+    clocks = ClockSampler(local if world > 1 else 0, out_dir(args) / f"clocks_sharded_rank{rank}.csv")
     dev, launches, nodes = [], 0, 0
     split = {"eval_ms": 0.0, "comm_ms": 0.0, "step_ms": 0.0}
+    st_sum = dict.fromkeys(("eval_ms", "flops", "node_evals", "sample_evals", "eval_launches"), 0)
     for _ in range(args.steps):
         co.fit_loaded(max_iter=max_iter, sample_sharded=sharded)
         st = co.stats()
@@ -629,7 +699,10 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
         nodes += st["node_evals"]
         for k in split:
             split[k] += st[k] / args.steps
+        for k in st_sum:
+            st_sum[k] += st[k]
         passes = int(st["iters_run"]) + 1
+    clk = clocks.stop()
     barrier(world)
     total_ms = max_over_ranks(float(sum(dev)), world)
     nodes_all = sum_over_ranks(float(nodes), world)
@@ -650,7 +723,9 @@ def run_sample_sharded(args, world: int, rank: int, local: int) -> None:
                    "max_iter": max_iter, "parallelism": f"sample-sharded x{world} "
                    "(NCCL all-reduce of JtJ/Jtr/loss per iteration)"},
         "node_evals_per_s": nodes_all / (total_ms / 1e3), "gpu_launches": launches,
-        "per_fit_ms": {**split, "passes": passes}}),
+        "per_fit_ms": {**split, "passes": passes},
+        "roofline": {**config_roofline(st_sum, mine, precision, peaks), "rank": 0},
+        "clocks": clk}),
         flush=True)
 
 
