@@ -588,7 +588,10 @@ def run_ours(args, world: int, rank: int, local: int) -> None:
         "node_evals_per_s": roofline["node_evals_per_s"],
     }
     if world == 1 and not args.no_parity_mode:
-        line["fit_parity"] = headline_parity(co)
+        try:
+            line["fit_parity"] = headline_parity(co)
+        except Exception as e:  # noqa: BLE001 - a report field; the measured line stands
+            line["fit_parity"] = {"unavailable": f"{type(e).__name__}: {str(e)[:300]}"}
         line["parity_mode"] = parity_mode(co, pop)
     if world == 1 and not args.no_reference_gpu:
         # the reference's own CUDA path on the same population and box (a subprocess of its

@@ -29,6 +29,9 @@ Everything written here comes from the reference's own code and files:
   configs_full_scipy.npz         reference ScipyPop fits of 32-tree samples of the mid,
                                  physics, long and scale configurations at their own N
                                  (--configs-full; inputs stored as a digest)
+  sharded_scipy.npz              reference ScipyPop fits of an 8-tree sample of the
+                                 sample-sharded configuration at its own N = 10,000,000
+                                 (--sharded; inputs stored as a digest)
 The tests read only these files; the reference is not needed at test time.
 """
 from __future__ import annotations
@@ -163,6 +166,34 @@ def make_config_samples_full() -> None:
     np.savez_compressed(HERE / "configs_full_scipy.npz", **arr)
 
 
+# trees of sharded_scipy.npz: the sample-sharded configuration at N = 10^7, where one
+# reference fit takes minutes per core
+SHARDED_SAMPLE = 8
+
+
+def make_sharded_sample() -> None:
+    """sharded_scipy.npz: reference ScipyPop fits of the sample-sharded configuration's
+    grammar at its full N (10^7 samples), inputs stored as a digest."""
+    REF = _reference()
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(ROOT))
+    from cusr.benchmark import backends, interp  # reference code
+
+    from cusr_b200 import synth
+
+    pop = synth.make_config("sharded", M=SHARDED_SAMPLE, seed=11)
+    ref_pop = _as_ref(pop)
+    sc = backends.ScipyPop(nproc=os.cpu_count()).fit_pop(ref_pop)
+    arr = {k: v for k, v in _pop_arrays("sharded", pop).items()
+           if not k.endswith(("/xs", "/ym"))}
+    arr["sharded/digest"] = np.asarray(pop_digest(pop))
+    arr["sharded/scipy/c_final"] = sc.c_final
+    arr["sharded/scipy/status"] = sc.status
+    arr["sharded/scipy/loss64"] = interp.loss_pop(ref_pop, sc.c_final)
+    arr["sharded/init/loss64"] = interp.loss_pop(ref_pop, pop["c_init"].astype(np.float64))
+    np.savez_compressed(HERE / "sharded_scipy.npz", **arr)
+
+
 def make_fd_golden() -> None:
     """fd_pop1000.npz: the reference FD variant's outputs on its pop.bin fixture
     (cusr/kernel/tests/golden/fd/pop1000: status, c_final; 50 iterations,
@@ -216,6 +247,9 @@ def main() -> None:
         return
     if "--configs-full" in sys.argv:
         make_config_samples_full()
+        return
+    if "--sharded" in sys.argv:
+        make_sharded_sample()
         return
     REF = _reference()
     sys.path.insert(0, str(REF))
