@@ -72,3 +72,25 @@ def test_configs_are_seeded_and_in_range(name):
         off = int(a["metas"][m][2])
         y = interp.eval_tree_arrays(nt, nv, ci, a["xs"][:64], a["c_init"][off:off + Km])
         assert np.all(np.isfinite(y))
+
+
+@pytest.mark.parametrize("fixture,name", [("configs_full_scipy.npz", "mid"),
+                                          ("configs_full_scipy.npz", "physics"),
+                                          ("configs_full_scipy.npz", "long"),
+                                          ("configs_full_scipy.npz", "scale"),
+                                          ("sharded_scipy.npz", "sharded")])
+def test_full_n_fixtures_regenerate_from_the_seeded_generator(fixture, name):
+    """The full-N scipy fixtures store their inputs as a digest; the GPU parity tests
+    regenerate them with the seeded generator. Same bytes here, on the CPU."""
+    import hashlib
+
+    from _helpers import GOLDEN
+
+    z = np.load(GOLDEN / fixture)
+    pop = synth.make_config(name, M=int(z[f"{name}/M"]), seed=11)
+    h = hashlib.sha256()
+    for k in ("nt", "nv", "ci", "metas", "c_init", "xs", "ym"):
+        h.update(np.ascontiguousarray(pop[k]).tobytes())
+    assert h.hexdigest() == str(z[f"{name}/digest"])
+    for k in ("nt", "ci", "metas", "c_init"):
+        np.testing.assert_array_equal(np.asarray(pop[k]), z[f"{name}/{k}"])
